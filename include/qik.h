@@ -1,0 +1,169 @@
+/*
+ * qik.h -- C ABI of the B200-native (sm_100a) Qwen-Image FP8 DiT hot path.
+ *
+ * One shared library (libqik.so) exports these entry points.  They take plain
+ * device pointers, sizes and a CUDA stream (as void*, a cudaStream_t; NULL = the
+ * legacy default stream); no framework types cross the boundary.  Every entry
+ * point is asynchronous on the given stream, allocates nothing, and returns a
+ * status code (QIK_OK = 0); qik_last_error() gives the message of the last
+ * failure on the calling thread.  Kernels never trap: a device-side failure (a
+ * bounded wait that ran out) is written to the optional `status` word, which the
+ * caller reads when it synchronizes.
+ *
+ * Each entry point names the reference interface it replaces
+ * (gomezcojj-coder/qwen-image-kernel, file:line).
+ */
+#ifndef QIK_H_
+#define QIK_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QIK_OK 0
+#define QIK_ERR_INVALID 1     /* bad pointer, shape, stride or alignment */
+#define QIK_ERR_CUDA 2        /* a CUDA runtime/driver call failed */
+#define QIK_ERR_UNSUPPORTED 3 /* valid request this build does not implement */
+
+/* Element types used in `dtype` arguments. */
+#define QIK_DTYPE_BF16 0
+#define QIK_DTYPE_F32 1
+#define QIK_DTYPE_E4M3 2
+
+/* Device-side status word values (written to `status` when non-NULL). */
+#define QIK_STATUS_OK 0
+#define QIK_STATUS_TIMEOUT 1
+
+/* Library version (major*10000 + minor*100 + patch). */
+int qik_version(void);
+/* Message for the last non-zero status returned on this thread. */
+const char* qik_last_error(void);
+
+/* Bytes of scratch `ws` the quantizer entry points need (16-byte aligned). */
+size_t qik_quant_workspace_bytes(void);
+
+/*
+ * Dynamic per-tensor scale: *scale_out = clamp_min(amax|x| * fl32(1/448), 1e-12),
+ * fp32, on the device.  Replaces compute_scale (qwen_image_kernel/fp8.py:24-26),
+ * evaluated as the reference evaluates it on CUDA.
+ *   x: n elements of `dtype` (BF16 or F32), contiguous.
+ */
+int qik_compute_scale(const void* x, int dtype, int64_t n, float* scale_out, void* ws, void* stream);
+
+/*
+ * Dynamic per-tensor e4m3 activation quantization: scale as qik_compute_scale,
+ * q[i] = e4m3_rn_satfinite(fl32(x[i]) * (1/scale)).  Replaces quantize_tensorwise
+ * + _scale_cast_fp8_kernel (qwen_image_kernel/fp8.py:29-53).
+ *   x: n bf16, contiguous; q: n bytes; scale_out: 1 fp32 (device).
+ */
+int qik_quantize_act(const void* x, int64_t n, uint8_t* q, float* scale_out, void* ws, void* stream);
+
+/*
+ * e4m3 activation pack with a scale already on the device (the second half of
+ * qik_quantize_act, used after a producer kernel accumulated the amax):
+ *   amax_bits: fp32 bit pattern of max|x| (as written by qik_fp8_gemm's amax_out).
+ * Writes *scale_out and q as qik_quantize_act does.
+ */
+int qik_quantize_act_from_amax(const void* x, int64_t n, const uint32_t* amax_bits, uint8_t* q, float* scale_out,
+                               void* stream);
+
+/*
+ * Static per-tensor e4m3 weight quantization: scale as qik_compute_scale,
+ * q[i] = e4m3(clamp(fl32(w[i]) / scale, -448, 448)) with IEEE division.
+ * Replaces quantize_weight_tensorwise (qwen_image_kernel/fp8.py:56-60) and the
+ * per-linear step of _staged_quantize (qwen_image_kernel/quantize_offline.py:19-26).
+ *   w: n elements of `dtype` (BF16 or F32), contiguous.
+ */
+int qik_quantize_weight(const void* w, int dtype, int64_t n, uint8_t* q, float* scale_out, void* ws, void* stream);
+
+/* Epilogue selectors for qik_fp8_gemm. */
+#define QIK_EPI_SCALE 0      /* y = acc * sa * sb (+ bias) */
+#define QIK_EPI_GELU_TANH 1  /* y = gelu_tanh(bf16(acc * sa * sb (+ bias))) */
+
+/*
+ * FP8 GEMM on tcgen05: C[M,N] = epilogue(A[M,K] . B[N,K]^T), e4m3 x e4m3 with
+ * fp32 accumulation in tensor memory.  Replaces the torch._scaled_mm call of
+ * FP8Linear.forward (qwen_image_kernel/fp8.py:87-88).
+ *   A: row-major [M, K] e4m3, row pitch lda bytes (lda % 16 == 0, K % 16 == 0)
+ *   B: row-major [N, K] e4m3 (the FP8Linear weight buffer), row pitch ldb bytes
+ *   scale_a, scale_b: 1 fp32 each (device)
+ *   bias: N bf16 or NULL
+ *   C: row-major [M, N] of out_dtype (BF16 or F32), row pitch ldc elements
+ *      (N % 16 == 0, ldc % 8 == 0, C 16-byte aligned)
+ *   epilogue: QIK_EPI_*
+ *   amax_out: NULL, or a u32 that receives atomicMax of the fp32 bit patterns of
+ *      |C| (BF16 output only): the amax of the next dynamic quantization.
+ *   status: NULL or a device int set to QIK_STATUS_TIMEOUT on a failed wait.
+ */
+int qik_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                 const float* scale_a, const float* scale_b, const void* bias, void* C, int64_t ldc, int out_dtype,
+                 int epilogue, uint32_t* amax_out, int* status, void* stream);
+
+/* Attention flags. */
+#define QIK_ATTN_HAS_CACHE 1     /* keys/values = virtual concat [cache ; fresh] */
+#define QIK_ATTN_HAS_KEY_VALID 2 /* per-(batch, key) validity bytes */
+#define QIK_ATTN_UNIFORM 4       /* every row attends to [0, P+SN): L unused */
+#define QIK_ATTN_V_FP8 8         /* cache V is e4m3 with per-(batch, head) scales */
+
+/* Strides are in elements of the tensor they describe. */
+typedef struct qik_attn_args {
+  const void* q;       /* [B, SQ, H, D] bf16 */
+  const void* k;       /* [B, SN, H, D] bf16 fresh keys */
+  const void* v;       /* [B, SN, H, D] bf16 fresh values */
+  const void* cache_k; /* [B, P, H, D] bf16, or NULL */
+  const void* cache_v; /* [B, P, H, D] bf16 or e4m3, or NULL */
+  const float* cache_v_scale; /* [B, H] fp32 (V_FP8 only) */
+  const int32_t* L;    /* [SQ]: row attends kv iff 0 <= kv <= L[row]; -1 -> no key */
+  const uint8_t* key_valid; /* [B, P + SN] bytes, non-zero = valid (HAS_KEY_VALID) */
+  void* out;           /* [B, SQ, H, D] bf16 */
+  int64_t B, SQ, SN, P, H, D;
+  int64_t q_sb, q_ss, q_sh;
+  int64_t k_sb, k_ss, k_sh;
+  int64_t v_sb, v_ss, v_sh;
+  int64_t ck_sb, ck_ss, ck_sh;
+  int64_t cv_sb, cv_ss, cv_sh;
+  int64_t o_sb, o_ss, o_sh;
+  int64_t kv_sb;       /* key_valid batch stride */
+  float sm_scale;      /* softmax scale, D^-0.5 in the reference */
+  int flags;           /* QIK_ATTN_* */
+} qik_attn_args;
+
+/*
+ * Block-causal flash attention over [prefix slab ; fresh K/V] with per-row
+ * prefix lengths, optional key validity and an e4m3 slab V dequantized in the
+ * loop as bf16(fl32(v8) * scale[b, h]).  Replaces block_causal_flash_attention
+ * + _qwen21_attn_fwd (qwen_image_kernel/triton_attention.py:35-260).
+ * Requires D == 128 and unit stride along D; rows with no allowed key give 0.
+ */
+int qik_block_causal_attention(const qik_attn_args* args, int* status, void* stream);
+
+/*
+ * Prefix-KV slab store for one layer: K copied to [B, H, Pmax, D] bf16; V either
+ * copied (bf16) or quantized per (b, h): s = clamp_min(amax * fl32(1/448), 1e-12),
+ * v8 = e4m3(clamp(fl32(v) / s, -448, 448)).  Replaces _LayerView.store
+ * (qwen_image_kernel/kv_cache.py:30-45).
+ *   k, v: [B, P, H, D] bf16 with element strides (sb, sp, sh) and unit D stride
+ *   k_layer: K slab of the layer, [B, H, pmax, D] bf16 dense
+ *   v_layer: V slab of the layer, [B, H, pmax, D] (bf16, or e4m3 when v_fp8)
+ *   v_scale_layer: [B, H] fp32 (v_fp8 only); ws: qik_quant_workspace_bytes() * B*H
+ */
+int qik_kv_store(const void* k, const void* v, int64_t B, int64_t P, int64_t H, int64_t D, int64_t k_sb,
+                 int64_t k_sp, int64_t k_sh, int64_t v_sb, int64_t v_sp, int64_t v_sh, void* k_layer, void* v_layer,
+                 int64_t pmax, int v_fp8, float* v_scale_layer, void* ws, void* stream);
+
+/*
+ * Self-test of the bounded-wait machinery: launches one CTA that waits on an
+ * mbarrier nothing will ever complete, with a limit of `wait_ns` nanoseconds, and
+ * writes QIK_STATUS_TIMEOUT to *status when the wait gives up.  The GPU context
+ * stays usable afterwards.
+ */
+int qik_selftest_wait_timeout(int* status, uint64_t wait_ns, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QIK_H_ */

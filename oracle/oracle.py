@@ -285,3 +285,27 @@ def bf16_ulp(x: torch.Tensor) -> torch.Tensor:
     e = torch.floor(torch.log2(a))
     return torch.pow(2.0, e - 7)
 
+
+
+_RECIP_TABLE: dict[int, int] | None = None
+
+
+def act_reciprocal(s: float) -> float:
+    """fp32 value of ``1.0 / s`` as the reference's activation cast forms it
+    (fp8.py:39, an fp32 division inside a Triton kernel).
+
+    It equals the IEEE round-to-nearest reciprocal except for the scales listed in
+    tests/golden/act_reciprocal.npz, which tests/golden/make_act_reciprocal.py measured
+    on a B200 by evaluating that same Triton expression for every scale a bf16
+    tensor can produce.  Without the table this is the IEEE reciprocal."""
+    global _RECIP_TABLE
+    if _RECIP_TABLE is None:
+        path = _HERE.parent / "tests" / "golden" / "act_reciprocal.npz"
+        _RECIP_TABLE = {}
+        if path.exists():
+            g = np.load(path)
+            _RECIP_TABLE = dict(zip(g["scale_bits"].tolist(), g["inv_bits"].tolist()))
+    sb = int(np.float32(s).view(np.uint32))
+    if sb in _RECIP_TABLE:
+        return float(np.uint32(_RECIP_TABLE[sb]).view(np.float32))
+    return reciprocal_rn(s)

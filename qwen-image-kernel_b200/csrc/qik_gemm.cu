@@ -1,0 +1,316 @@
+// qik_gemm.cu -- FP8 (e4m3 x e4m3 -> fp32) GEMM on the sm_100a tensor core.
+//
+// C[M,N] = epilogue(A[M,K] . B[N,K]^T): the W8A8 per-tensor linear of
+// FP8Linear.forward (qwen_image_kernel/fp8.py:78-90), whose reference computes it
+// with torch._scaled_mm.  Design:
+//   * persistent CTAs (one per SM), tiles of 128 x BN outputs visited round-robin;
+//   * warp 0: TMA producer -- one 128x128 A box and one BNx128 B box per stage,
+//     128-byte swizzle, no cluster multicast (each CTA loads its own tiles; L2
+//     absorbs the cross-CTA reuse);
+//   * warp 1: one thread issues tcgen05.mma.kind::f8f6f4 (M=128, N=BN, K=32 per
+//     instruction) into a double-buffered fp32 accumulator in tensor memory and
+//     releases smem stages / accumulators with tcgen05.commit;
+//   * warps 2-5: epilogue -- tcgen05.ld of one accumulator row per thread, scale by
+//     sa*sb, optional bias and GELU-tanh, bf16/fp32 stores, optional amax of the
+//     bf16 output for the next dynamic quantization.
+// The epilogue of tile i overlaps the MMAs of tile i+1.
+#include "qik_device.cuh"
+#include "qik_host.h"
+
+namespace qik {
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 128;  // e4m3 elements (= bytes) of K per pipeline stage
+constexpr int kGemmThreads = 192;
+
+struct GemmParams {
+  int M, N, K;
+  const float* scale_a;
+  const float* scale_b;
+  const __nv_bfloat16* bias;
+  void* C;
+  int64_t ldc;
+  int out_f32;
+  int epilogue;
+  uint32_t* amax_out;
+  int* status;
+};
+
+template <int BN, int STAGES>
+struct GemmLayout {
+  static constexpr int kABytes = kGemmBM * kGemmBK;
+  static constexpr int kBBytes = BN * kGemmBK;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kBarBytes = (2 * STAGES + 4) * 8 + 16;
+  static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;  // + alignment slack
+  static constexpr int kTmemCols = 2 * BN;
+};
+
+__device__ __forceinline__ float gelu_tanh_f32(float x) {
+  // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
+  const float k0 = 0.7978845608028654f;
+  const float k1 = 0.044715f;
+  const float x3 = x * x * x;
+  return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x3)));
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const GemmParams p) {
+  using Lay = GemmLayout<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * Lay::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lay::kBarOffset);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Lay::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m = (p.M + kGemmBM - 1) / kGemmBM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_k = (p.K + kGemmBK - 1) / kGemmBK;
+  const int tiles = num_m * num_n;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        const int mb = tile / num_n, nb = tile % num_n;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status)) goto producer_done;
+          mbar_arrive_expect_tx(&full[stage], Lay::kStageBytes);
+          tma_load_2d(sA + stage * Lay::kABytes, &tmA, kb * kGemmBK, mb * kGemmBM, &full[stage]);
+          tma_load_2d(sB + stage * Lay::kBBytes, &tmB, kb * kGemmBK, nb * BN, &full[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f32acc(0, 0, 0, 0, kGemmBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.status)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * Lay::kABytes);
+          const uint32_t b_addr = smem_u32(sB + stage * Lay::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 32; ++k) {
+            const uint64_t ad = sdesc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(b_addr + k * 32, 16, 1024);
+            umma_f8f6f4_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+      }
+    }
+  } else {
+    // epilogue warps 2..5: TMEM lane quarter = warp % 4
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    const float s = __ldg(p.scale_a) * __ldg(p.scale_b);
+    uint32_t amax_local = 0;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status)) break;
+      tc_fence_after();
+      const int mb = tile / num_n, nb = tile % num_n;
+      const int row = mb * kGemmBM + row_in_tile;
+      const bool row_ok = row < p.M;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN + c * 32),
+                  r);
+        const int col0 = nb * BN + c * 32;
+        if (!row_ok || col0 >= p.N) continue;
+        const int ncols = min(32, p.N - col0);  // 16 or 32 (N % 16 == 0)
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * s;
+        if (p.bias) {
+          const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (q * 8 >= ncols) break;
+            const uint4 bb = __ldg(bp + q);
+            const uint32_t bw[4] = {bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              v[q * 8 + 2 * t] += __uint_as_float(bw[t] << 16);
+              v[q * 8 + 2 * t + 1] += __uint_as_float(bw[t] & 0xFFFF0000u);
+            }
+          }
+        }
+        if (p.out_f32) {
+          float* dst = static_cast<float*>(p.C) + static_cast<int64_t>(row) * p.ldc + col0;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            if (q * 4 >= ncols) break;
+            reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          }
+        } else {
+          uint32_t w[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float lo = v[2 * j], hi = v[2 * j + 1];
+            if (p.epilogue == QIK_EPI_GELU_TANH) {
+              lo = gelu_tanh_f32(__bfloat162float(__float2bfloat16_rn(lo)));
+              hi = gelu_tanh_f32(__bfloat162float(__float2bfloat16_rn(hi)));
+            }
+            w[j] = pack_bf16x2(lo, hi);
+          }
+          if (p.amax_out) {
+            uint32_t m2 = 0;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (2 * j < ncols) m2 = __vmaxu2(m2, w[j] & 0x7FFF7FFFu);
+            amax_local = max(amax_local, max(m2 & 0xFFFFu, m2 >> 16));
+          }
+          __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.C) + static_cast<int64_t>(row) * p.ldc + col0;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (q * 8 >= ncols) break;
+            reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+    if (p.amax_out) {
+      amax_local = __reduce_max_sync(0xffffffffu, amax_local);
+      if (lane == 0 && amax_local != 0u) atomicMax(p.amax_out, amax_local << 16);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Lay::kTmemCols);
+  }
+}
+
+template <int BN, int STAGES>
+static int launch_gemm(const uint8_t* A, const uint8_t* B, const GemmParams& p, int64_t lda, int64_t ldb,
+                       cudaStream_t st) {
+  using Lay = GemmLayout<BN, STAGES>;
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, static_cast<uint64_t>(p.K),
+                        static_cast<uint64_t>(p.M), static_cast<uint64_t>(lda), kGemmBK, kGemmBM,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.N),
+                    static_cast<uint64_t>(ldb), kGemmBK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  QIK_TRY_CUDA(cudaGetDevice(&dev));
+  if (dev < 64 && !attr_set[dev]) {
+    QIK_TRY_CUDA(cudaFuncSetAttribute(fp8_gemm_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      Lay::kSmemBytes));
+    attr_set[dev] = true;
+  }
+  const int tiles = ((p.M + kGemmBM - 1) / kGemmBM) * ((p.N + BN - 1) / BN);
+  const int grid = min(tiles, sm_count());
+  fp8_gemm_kernel<BN, STAGES><<<grid, kGemmThreads, Lay::kSmemBytes, st>>>(ta, tb, p);
+  return check_launch("fp8_gemm_kernel");
+}
+
+}  // namespace qik
+
+using namespace qik;
+
+extern "C" int qik_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda,
+                            int64_t ldb, const float* scale_a, const float* scale_b, const void* bias, void* C,
+                            int64_t ldc, int out_dtype, int epilogue, uint32_t* amax_out, int* status,
+                            void* stream) {
+  QIK_REQUIRE(M >= 0 && N >= 0 && K >= 0, "qik_fp8_gemm: negative size");
+  if (M == 0 || N == 0) return QIK_OK;
+  QIK_REQUIRE(K > 0, "qik_fp8_gemm: K must be positive");
+  QIK_REQUIRE(M <= (1ll << 31) - 1 && N <= (1ll << 31) - 1 && K <= (1ll << 31) - 1, "qik_fp8_gemm: size above 2^31");
+  QIK_REQUIRE(A && B && C && scale_a && scale_b, "qik_fp8_gemm: NULL operand");
+  QIK_REQUIRE(K % 16 == 0, "qik_fp8_gemm: K=%lld must be a multiple of 16", (long long)K);
+  QIK_REQUIRE(lda >= K && lda % 16 == 0 && ldb >= K && ldb % 16 == 0,
+              "qik_fp8_gemm: lda/ldb must be >= K and multiples of 16 bytes");
+  QIK_REQUIRE(aligned16(A) && aligned16(B) && aligned16(C), "qik_fp8_gemm: A, B, C must be 16-byte aligned");
+  QIK_REQUIRE(N % 16 == 0, "qik_fp8_gemm: N=%lld must be a multiple of 16", (long long)N);
+  QIK_REQUIRE(ldc >= N && ldc % 8 == 0, "qik_fp8_gemm: ldc must be >= N and a multiple of 8");
+  QIK_REQUIRE(out_dtype == QIK_DTYPE_BF16 || out_dtype == QIK_DTYPE_F32, "qik_fp8_gemm: out_dtype must be BF16/F32");
+  QIK_REQUIRE(epilogue == QIK_EPI_SCALE || epilogue == QIK_EPI_GELU_TANH, "qik_fp8_gemm: unknown epilogue");
+  QIK_REQUIRE(!(out_dtype == QIK_DTYPE_F32 && (epilogue != QIK_EPI_SCALE || amax_out)),
+              "qik_fp8_gemm: GELU and amax need BF16 output");
+  QIK_REQUIRE(!bias || aligned16(bias), "qik_fp8_gemm: bias must be 16-byte aligned");
+  GemmParams p;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.scale_a = scale_a;
+  p.scale_b = scale_b;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.C = C;
+  p.ldc = ldc;
+  p.out_f32 = out_dtype == QIK_DTYPE_F32;
+  p.epilogue = epilogue;
+  p.amax_out = amax_out;
+  p.status = status;
+  return launch_gemm<256, 4>(A, B, p, lda, ldb, static_cast<cudaStream_t>(stream));
+}

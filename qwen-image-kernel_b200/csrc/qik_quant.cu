@@ -1,0 +1,361 @@
+// qik_quant.cu -- per-tensor e4m3 quantizers and the prefix-KV slab store.
+//
+// HBM-bound byte work: 16-byte vector loads/stores, grids sized to a multiple of
+// the SM count, one atomic per CTA for the global amax.  Scales are computed on
+// the device exactly as the reference's torch expressions evaluate on CUDA:
+//   s   = clamp_min(fl32(amax) * fl32(1/448), 1e-12)     (fp8.py:24-26; a CUDA
+//         division by a host scalar is a multiplication by its fp32 reciprocal)
+//   act:    q = e4m3_rn_satfinite(fl32(x) * inv), inv = 1/s  (fp8.py:39-41)
+//   weight: q = e4m3(clamp(fl32(w) / s, -448, 448))          (fp8.py:59, IEEE div)
+//   slab V: per (b, h), as weight                              (kv_cache.py:36-42)
+// The amax is kept as the fp32 bit pattern of |x|: for non-negative floats the
+// unsigned order is the numeric order and NaN patterns sort above +inf, so an
+// integer atomicMax reproduces torch.amax including NaN propagation.
+#include "qik_device.cuh"
+#include "qik_host.h"
+
+namespace qik {
+
+struct QuantWs {
+  uint32_t amax_bits;
+  uint32_t pad[3];
+};
+
+constexpr int kQuantThreads = 256;
+
+__device__ __forceinline__ float scale_from_amax_bits(uint32_t bits) {
+  const float amax = __uint_as_float(bits);
+  float s = amax * (1.0f / 448.0f);
+  if (s < 1e-12f) s = 1e-12f;  // NaN compares false and passes through
+  return s;
+}
+
+// 1/s as the activation cast forms it (fp8.py:39 `1.0 / tl.load(...)`): Triton
+// lowers an fp32 division to PTX div.full.f32; QIK_ACT_RECIP_RN selects the
+// IEEE round-to-nearest reciprocal instead.
+__device__ __forceinline__ float act_inverse(float s) {
+#ifdef QIK_ACT_RECIP_RN
+  return __frcp_rn(s);
+#else
+  float r;
+  asm("div.full.f32 %0, %1, %2;" : "=f"(r) : "f"(1.0f), "f"(s));
+  return r;
+#endif
+}
+
+__device__ __forceinline__ uint32_t block_max_u32(uint32_t v) {
+  __shared__ uint32_t red[32];
+  v = __reduce_max_sync(0xffffffffu, v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    v = lane < (blockDim.x >> 5) ? red[lane] : 0u;
+    v = __reduce_max_sync(0xffffffffu, v);
+  }
+  return v;  // valid in warp 0
+}
+
+// ---------------------------------------------------------------- amax
+// bf16: |x| as 16-bit patterns; __vmaxu2 takes the halfword max of two at once.
+__global__ void __launch_bounds__(kQuantThreads) amax_bf16_kernel(const uint16_t* __restrict__ x, int64_t n,
+                                                                  uint32_t* __restrict__ amax_bits) {
+  uint32_t m2 = 0;  // two running halfword maxima
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const bool vec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+  int64_t done = 0;
+  if (vec) {
+    const int64_t nvec = n >> 3;
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    int64_t i = tid;
+    for (; i + 3 * nthreads < nvec; i += 4 * nthreads) {
+      uint4 a = __ldg(xv + i), b = __ldg(xv + i + nthreads), c = __ldg(xv + i + 2 * nthreads),
+            d = __ldg(xv + i + 3 * nthreads);
+      m2 = __vmaxu2(m2, __vmaxu2(__vmaxu2(a.x & 0x7FFF7FFFu, a.y & 0x7FFF7FFFu),
+                                 __vmaxu2(a.z & 0x7FFF7FFFu, a.w & 0x7FFF7FFFu)));
+      m2 = __vmaxu2(m2, __vmaxu2(__vmaxu2(b.x & 0x7FFF7FFFu, b.y & 0x7FFF7FFFu),
+                                 __vmaxu2(b.z & 0x7FFF7FFFu, b.w & 0x7FFF7FFFu)));
+      m2 = __vmaxu2(m2, __vmaxu2(__vmaxu2(c.x & 0x7FFF7FFFu, c.y & 0x7FFF7FFFu),
+                                 __vmaxu2(c.z & 0x7FFF7FFFu, c.w & 0x7FFF7FFFu)));
+      m2 = __vmaxu2(m2, __vmaxu2(__vmaxu2(d.x & 0x7FFF7FFFu, d.y & 0x7FFF7FFFu),
+                                 __vmaxu2(d.z & 0x7FFF7FFFu, d.w & 0x7FFF7FFFu)));
+    }
+    for (; i < nvec; i += nthreads) {
+      uint4 a = __ldg(xv + i);
+      m2 = __vmaxu2(m2, __vmaxu2(__vmaxu2(a.x & 0x7FFF7FFFu, a.y & 0x7FFF7FFFu),
+                                 __vmaxu2(a.z & 0x7FFF7FFFu, a.w & 0x7FFF7FFFu)));
+    }
+    done = nvec << 3;
+  }
+  for (int64_t i = done + tid; i < n; i += nthreads) m2 = __vmaxu2(m2, static_cast<uint32_t>(x[i] & 0x7FFFu));
+  uint32_t m = max(m2 & 0xFFFFu, m2 >> 16);
+  m = block_max_u32(m);
+  if (threadIdx.x == 0 && m != 0u) atomicMax(amax_bits, m << 16);
+}
+
+__global__ void __launch_bounds__(kQuantThreads) amax_f32_kernel(const float* __restrict__ x, int64_t n,
+                                                                 uint32_t* __restrict__ amax_bits) {
+  uint32_t m = 0;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t done = 0;
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+    const int64_t nvec = n >> 2;
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    for (int64_t i = tid; i < nvec; i += nthreads) {
+      uint4 a = __ldg(xv + i);
+      m = max(max(max(m, a.x & 0x7FFFFFFFu), max(a.y & 0x7FFFFFFFu, a.z & 0x7FFFFFFFu)), a.w & 0x7FFFFFFFu);
+    }
+    done = nvec << 2;
+  }
+  for (int64_t i = done + tid; i < n; i += nthreads) m = max(m, __float_as_uint(x[i]) & 0x7FFFFFFFu);
+  m = block_max_u32(m);
+  if (threadIdx.x == 0 && m != 0u) atomicMax(amax_bits, m);
+}
+
+__global__ void scale_finalize_kernel(const uint32_t* __restrict__ amax_bits, float* __restrict__ scale_out) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) scale_out[0] = scale_from_amax_bits(*amax_bits);
+}
+
+// ---------------------------------------------------------------- packs
+// Activation: 16 bf16 -> 16 e4m3 per thread iteration (two 16-byte loads, one
+// 16-byte store).
+__global__ void __launch_bounds__(kQuantThreads) pack_act_kernel(const uint16_t* __restrict__ x, int64_t n,
+                                                                 const uint32_t* __restrict__ amax_bits,
+                                                                 uint8_t* __restrict__ q,
+                                                                 float* __restrict__ scale_out) {
+  const float s = scale_from_amax_bits(__ldg(amax_bits));
+  const float inv = act_inverse(s);
+  if (blockIdx.x == 0 && threadIdx.x == 0 && scale_out) scale_out[0] = s;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t done = 0;
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (reinterpret_cast<uintptr_t>(q) & 15u) == 0) {
+    const int64_t nvec = n >> 4;
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    uint4* qv = reinterpret_cast<uint4*>(q);
+    for (int64_t i = tid; i < nvec; i += nthreads) {
+      const uint4 a = __ldg(xv + 2 * i), b = __ldg(xv + 2 * i + 1);
+      const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t u0 = w[2 * j], u1 = w[2 * j + 1];
+        const uint16_t lo = cvt_e4m3x2(__uint_as_float(u0 << 16) * inv, __uint_as_float(u0 & 0xFFFF0000u) * inv);
+        const uint16_t hi = cvt_e4m3x2(__uint_as_float(u1 << 16) * inv, __uint_as_float(u1 & 0xFFFF0000u) * inv);
+        o[j] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+      }
+      qv[i] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    done = nvec << 4;
+  }
+  for (int64_t i = done + tid; i < n; i += nthreads) {
+    const float v = __uint_as_float(static_cast<uint32_t>(x[i]) << 16) * inv;
+    q[i] = static_cast<uint8_t>(cvt_e4m3x2(v, 0.0f) & 0xFFu);
+  }
+}
+
+// Weight / slab V element: clamp(w / s) then round to e4m3; NaN keeps its sign
+// like c10's conversion (after the clamp every other value is finite).
+__device__ __forceinline__ uint8_t weight_code(float w, float s) {
+  float v = __fdiv_rn(w, s);
+  if (v != v) return static_cast<uint8_t>(0x7Fu | ((__float_as_uint(v) >> 24) & 0x80u));
+  v = fminf(fmaxf(v, -448.0f), 448.0f);
+  return static_cast<uint8_t>(cvt_e4m3x2(v, 0.0f) & 0xFFu);
+}
+
+template <typename T>
+__device__ __forceinline__ float load_as_f32(const T* p, int64_t i);
+template <>
+__device__ __forceinline__ float load_as_f32<uint16_t>(const uint16_t* p, int64_t i) {
+  return __uint_as_float(static_cast<uint32_t>(__ldg(p + i)) << 16);
+}
+template <>
+__device__ __forceinline__ float load_as_f32<float>(const float* p, int64_t i) {
+  return __ldg(p + i);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kQuantThreads) pack_weight_kernel(const T* __restrict__ w, int64_t n,
+                                                                    const uint32_t* __restrict__ amax_bits,
+                                                                    uint8_t* __restrict__ q,
+                                                                    float* __restrict__ scale_out) {
+  const float s = scale_from_amax_bits(__ldg(amax_bits));
+  if (blockIdx.x == 0 && threadIdx.x == 0) scale_out[0] = s;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  // 4 elements per thread iteration, one 4-byte store.
+  const int64_t n4 = ((reinterpret_cast<uintptr_t>(q) & 3u) == 0) ? (n >> 2) : 0;
+  for (int64_t i = tid; i < n4; i += nthreads) {
+    const uint32_t o = static_cast<uint32_t>(weight_code(load_as_f32(w, 4 * i), s)) |
+                       (static_cast<uint32_t>(weight_code(load_as_f32(w, 4 * i + 1), s)) << 8) |
+                       (static_cast<uint32_t>(weight_code(load_as_f32(w, 4 * i + 2), s)) << 16) |
+                       (static_cast<uint32_t>(weight_code(load_as_f32(w, 4 * i + 3), s)) << 24);
+    reinterpret_cast<uint32_t*>(q)[i] = o;
+  }
+  for (int64_t i = (n4 << 2) + tid; i < n; i += nthreads) q[i] = weight_code(load_as_f32(w, i), s);
+}
+
+// ---------------------------------------------------------------- slab store
+// grid (row chunks, B*H); rows of D contiguous elements.
+__global__ void __launch_bounds__(kQuantThreads) kv_amax_kernel(const uint16_t* __restrict__ v, int64_t P, int64_t H,
+                                                                int64_t D, int64_t sb, int64_t sp, int64_t sh,
+                                                                int rows_per_block, uint32_t* __restrict__ amax_bits) {
+  const int64_t bh = blockIdx.y;
+  const int64_t b = bh / H, h = bh % H;
+  const int64_t p0 = static_cast<int64_t>(blockIdx.x) * rows_per_block;
+  const int64_t p1 = min(P, p0 + rows_per_block);
+  const uint16_t* base = v + b * sb + h * sh;
+  uint32_t m = 0;
+  const int64_t cnt = (p1 - p0) * D;
+  for (int64_t e = threadIdx.x; e < cnt; e += blockDim.x) {
+    const int64_t p = p0 + e / D, d = e % D;
+    m = max(m, static_cast<uint32_t>(base[p * sp + d] & 0x7FFFu));
+  }
+  m = block_max_u32(m);
+  if (threadIdx.x == 0 && m != 0u) atomicMax(amax_bits + bh, m << 16);
+}
+
+__global__ void __launch_bounds__(kQuantThreads) kv_store_kernel(
+    const uint16_t* __restrict__ k, const uint16_t* __restrict__ v, int64_t P, int64_t H, int64_t D, int64_t k_sb,
+    int64_t k_sp, int64_t k_sh, int64_t v_sb, int64_t v_sp, int64_t v_sh, uint16_t* __restrict__ k_layer,
+    void* __restrict__ v_layer, int64_t pmax, int v_fp8, const uint32_t* __restrict__ amax_bits,
+    float* __restrict__ v_scale_layer, int rows_per_block) {
+  const int64_t bh = blockIdx.y;
+  const int64_t b = bh / H, h = bh % H;
+  const int64_t p0 = static_cast<int64_t>(blockIdx.x) * rows_per_block;
+  const int64_t p1 = min(P, p0 + rows_per_block);
+  const uint16_t* kb = k + b * k_sb + h * k_sh;
+  const uint16_t* vb = v + b * v_sb + h * v_sh;
+  const int64_t dst0 = bh * pmax * D;
+  const int64_t cnt = (p1 - p0) * D;
+  float s = 1.0f;
+  if (v_fp8) {
+    s = scale_from_amax_bits(__ldg(amax_bits + bh));
+    if (blockIdx.x == 0 && threadIdx.x == 0) v_scale_layer[bh] = s;
+  }
+  for (int64_t e = threadIdx.x; e < cnt; e += blockDim.x) {
+    const int64_t p = p0 + e / D, d = e % D;
+    const int64_t dst = dst0 + p * D + d;
+    k_layer[dst] = kb[p * k_sp + d];
+    const uint16_t vv = vb[p * v_sp + d];
+    if (v_fp8)
+      static_cast<uint8_t*>(v_layer)[dst] = weight_code(__uint_as_float(static_cast<uint32_t>(vv) << 16), s);
+    else
+      static_cast<uint16_t*>(v_layer)[dst] = vv;
+  }
+}
+
+static int grid_for(int64_t work_items, int per_thread) {
+  const int64_t want = (work_items + static_cast<int64_t>(kQuantThreads) * per_thread - 1) /
+                       (static_cast<int64_t>(kQuantThreads) * per_thread);
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+  int64_t g = want < cap ? want : cap;
+  return static_cast<int>(g < 1 ? 1 : g);
+}
+
+static int launch_amax(const void* x, int dtype, int64_t n, uint32_t* amax_bits, cudaStream_t st) {
+  if (n <= 0) return QIK_OK;
+  if (dtype == QIK_DTYPE_BF16) {
+    amax_bf16_kernel<<<grid_for(n, 32), kQuantThreads, 0, st>>>(static_cast<const uint16_t*>(x), n, amax_bits);
+  } else {
+    amax_f32_kernel<<<grid_for(n, 16), kQuantThreads, 0, st>>>(static_cast<const float*>(x), n, amax_bits);
+  }
+  return check_launch("amax kernel");
+}
+
+}  // namespace qik
+
+using namespace qik;
+
+extern "C" {
+
+size_t qik_quant_workspace_bytes(void) { return sizeof(QuantWs); }
+
+int qik_compute_scale(const void* x, int dtype, int64_t n, float* scale_out, void* ws, void* stream) {
+  QIK_REQUIRE(x || n == 0, "qik_compute_scale: x is NULL");
+  QIK_REQUIRE(scale_out && ws, "qik_compute_scale: scale_out/ws is NULL");
+  QIK_REQUIRE(dtype == QIK_DTYPE_BF16 || dtype == QIK_DTYPE_F32, "qik_compute_scale: dtype must be BF16 or F32");
+  QIK_REQUIRE(n >= 0, "qik_compute_scale: negative n");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  QuantWs* w = static_cast<QuantWs*>(ws);
+  QIK_TRY_CUDA(cudaMemsetAsync(&w->amax_bits, 0, sizeof(uint32_t), st));
+  int rc = launch_amax(x, dtype, n, &w->amax_bits, st);
+  if (rc) return rc;
+  scale_finalize_kernel<<<1, 32, 0, st>>>(&w->amax_bits, scale_out);
+  return check_launch("scale_finalize_kernel");
+}
+
+int qik_quantize_act_from_amax(const void* x, int64_t n, const uint32_t* amax_bits, uint8_t* q, float* scale_out,
+                               void* stream) {
+  QIK_REQUIRE((x && q) || n == 0, "qik_quantize_act_from_amax: x/q is NULL");
+  QIK_REQUIRE(amax_bits, "qik_quantize_act_from_amax: amax_bits is NULL");
+  QIK_REQUIRE(n >= 0, "qik_quantize_act_from_amax: negative n");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  pack_act_kernel<<<grid_for(n, 16), kQuantThreads, 0, st>>>(static_cast<const uint16_t*>(x), n, amax_bits, q,
+                                                               scale_out);
+  return check_launch("pack_act_kernel");
+}
+
+int qik_quantize_act(const void* x, int64_t n, uint8_t* q, float* scale_out, void* ws, void* stream) {
+  QIK_REQUIRE(ws && scale_out, "qik_quantize_act: ws/scale_out is NULL");
+  QIK_REQUIRE((x && q) || n == 0, "qik_quantize_act: x/q is NULL");
+  QIK_REQUIRE(n >= 0, "qik_quantize_act: negative n");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  QuantWs* w = static_cast<QuantWs*>(ws);
+  QIK_TRY_CUDA(cudaMemsetAsync(&w->amax_bits, 0, sizeof(uint32_t), st));
+  int rc = launch_amax(x, QIK_DTYPE_BF16, n, &w->amax_bits, st);
+  if (rc) return rc;
+  return qik_quantize_act_from_amax(x, n, &w->amax_bits, q, scale_out, stream);
+}
+
+int qik_quantize_weight(const void* w, int dtype, int64_t n, uint8_t* q, float* scale_out, void* ws, void* stream) {
+  QIK_REQUIRE(ws && scale_out, "qik_quantize_weight: ws/scale_out is NULL");
+  QIK_REQUIRE((w && q) || n == 0, "qik_quantize_weight: w/q is NULL");
+  QIK_REQUIRE(dtype == QIK_DTYPE_BF16 || dtype == QIK_DTYPE_F32, "qik_quantize_weight: dtype must be BF16 or F32");
+  QIK_REQUIRE(n >= 0, "qik_quantize_weight: negative n");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  QuantWs* ws_ = static_cast<QuantWs*>(ws);
+  QIK_TRY_CUDA(cudaMemsetAsync(&ws_->amax_bits, 0, sizeof(uint32_t), st));
+  int rc = launch_amax(w, dtype, n, &ws_->amax_bits, st);
+  if (rc) return rc;
+  const int g = grid_for(n, 4);
+  if (dtype == QIK_DTYPE_BF16)
+    pack_weight_kernel<uint16_t><<<g, kQuantThreads, 0, st>>>(static_cast<const uint16_t*>(w), n, &ws_->amax_bits,
+                                                               q, scale_out);
+  else
+    pack_weight_kernel<float><<<g, kQuantThreads, 0, st>>>(static_cast<const float*>(w), n, &ws_->amax_bits, q,
+                                                            scale_out);
+  return check_launch("pack_weight_kernel");
+}
+
+int qik_kv_store(const void* k, const void* v, int64_t B, int64_t P, int64_t H, int64_t D, int64_t k_sb,
+                 int64_t k_sp, int64_t k_sh, int64_t v_sb, int64_t v_sp, int64_t v_sh, void* k_layer, void* v_layer,
+                 int64_t pmax, int v_fp8, float* v_scale_layer, void* ws, void* stream) {
+  QIK_REQUIRE(B >= 0 && P >= 0 && H >= 0 && D >= 0, "qik_kv_store: negative size");
+  QIK_REQUIRE(P <= pmax, "qik_kv_store: P=%lld exceeds slab capacity %lld", (long long)P, (long long)pmax);
+  if (B == 0 || H == 0 || P == 0 || D == 0) return QIK_OK;
+  QIK_REQUIRE(k && v && k_layer && v_layer, "qik_kv_store: NULL tensor");
+  QIK_REQUIRE(!v_fp8 || (v_scale_layer && ws), "qik_kv_store: fp8 V needs v_scale_layer and ws");
+  QIK_REQUIRE(B * H <= 65535, "qik_kv_store: B*H above 65535");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t rows_want = 8192 / D;
+  const int rows = static_cast<int>(rows_want < 1 ? 1 : (rows_want > P ? P : rows_want));
+  dim3 grid(static_cast<unsigned>((P + rows - 1) / rows), static_cast<unsigned>(B * H));
+  uint32_t* amax = static_cast<uint32_t*>(ws);
+  if (v_fp8) {
+    QIK_TRY_CUDA(cudaMemsetAsync(amax, 0, sizeof(uint32_t) * B * H, st));
+    kv_amax_kernel<<<grid, kQuantThreads, 0, st>>>(static_cast<const uint16_t*>(v), P, H, D, v_sb, v_sp, v_sh, rows,
+                                                   amax);
+    int rc = check_launch("kv_amax_kernel");
+    if (rc) return rc;
+  }
+  kv_store_kernel<<<grid, kQuantThreads, 0, st>>>(static_cast<const uint16_t*>(k), static_cast<const uint16_t*>(v), P,
+                                                  H, D, k_sb, k_sp, k_sh, v_sb, v_sp, v_sh,
+                                                  static_cast<uint16_t*>(k_layer), v_layer, pmax, v_fp8, amax,
+                                                  v_scale_layer, rows);
+  return check_launch("kv_store_kernel");
+}
+
+}  // extern "C"

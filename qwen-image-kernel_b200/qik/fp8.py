@@ -1,0 +1,231 @@
+"""FP8 (W8A8, per-tensor e4m3) linear layers on the sm_100a tensor core.
+
+Drop-in for ``qwen_image_kernel/fp8.py`` of gomezcojj-coder/qwen-image-kernel: the
+same names, module buffers and return conventions, with the arithmetic done by the
+hand-written CUDA kernels of libqik.so instead of Triton + torch._scaled_mm:
+
+  compute_scale               fp8.py:24-26   -> qik_compute_scale
+  quantize_tensorwise         fp8.py:44-53   -> qik_quantize_act (amax + e4m3 pack)
+  quantize_weight_tensorwise  fp8.py:56-60   -> qik_quantize_weight
+  FP8Linear.forward           fp8.py:78-90   -> qik_quantize_act + qik_fp8_gemm
+  FP8Linear.from_linear       fp8.py:92-101
+  convert_linears_fp8         fp8.py:104-120
+  fp8_state_dict              fp8.py:123-127
+
+Scales stay on the device (no host synchronization), as in the reference.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from . import _lib as L
+
+FP8_E4M3_MAX = 448.0
+
+
+def _ws(device: torch.device) -> torch.Tensor:
+    return torch.empty(16, dtype=torch.uint8, device=device)
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.bfloat16:
+        return L.DTYPE_BF16
+    if t.dtype == torch.float32:
+        return L.DTYPE_F32
+    raise TypeError(f"qik: unsupported dtype {t.dtype} (bf16 or fp32)")
+
+
+def _require_cuda(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"qik: {name} must be a CUDA tensor (the kernels have no CPU path)")
+
+
+def compute_scale(x: torch.Tensor) -> torch.Tensor:
+    """Dynamic per-tensor fp8 activation scale (fp32 0-dim tensor, on the device):
+    clamp_min(amax|x| / 448, 1e-12), evaluated as the reference does on CUDA."""
+    _require_cuda(x, "x")
+    lib = L.load()
+    xc = x.contiguous()
+    s = torch.empty((), dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        L.check(lib.qik_compute_scale(xc.data_ptr(), _dtype_code(xc), xc.numel(), s.data_ptr(),
+                                      _ws(x.device).data_ptr(), L.stream_ptr()), "qik_compute_scale")
+    return s
+
+
+def quantize_tensorwise(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """[..., K] bf16 -> (e4m3 of the same shape, scale fp32 [1]).  One amax reduction
+    and one scale+cast pass: q = e4m3_rn_satfinite(x * (1/s))."""
+    _require_cuda(x, "x")
+    if x.dtype != torch.bfloat16:
+        raise TypeError("qik.quantize_tensorwise: bf16 activations only")
+    lib = L.load()
+    xc = x.contiguous()
+    q = torch.empty(x.shape, dtype=torch.float8_e4m3fn, device=x.device)
+    s = torch.empty(1, dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        L.check(lib.qik_quantize_act(xc.data_ptr(), xc.numel(), q.data_ptr(), s.data_ptr(),
+                                     _ws(x.device).data_ptr(), L.stream_ptr()), "qik_quantize_act")
+    return q, s
+
+
+def quantize_from_amax(x: torch.Tensor, amax_bits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """The pack half of quantize_tensorwise when a producer kernel already accumulated
+    max|x| (fp32 bit pattern in ``amax_bits``, int32 [1])."""
+    lib = L.load()
+    xc = x.contiguous()
+    q = torch.empty(x.shape, dtype=torch.float8_e4m3fn, device=x.device)
+    s = torch.empty(1, dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        L.check(lib.qik_quantize_act_from_amax(xc.data_ptr(), xc.numel(), amax_bits.data_ptr(), q.data_ptr(),
+                                               s.data_ptr(), L.stream_ptr()), "qik_quantize_act_from_amax")
+    return q, s
+
+
+def quantize_weight_tensorwise(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """[N, K] -> (fp8 [N, K], scale fp32 [1]); q = e4m3(clamp(w / s, +-448)).
+
+    Runs on the GPU.  A CPU weight is staged to the current CUDA device and the
+    results are returned on the weight's device, as the reference's offline
+    quantizer does (quantize_offline.py:19-26)."""
+    src_dev = w.device
+    wd = w if w.is_cuda else w.to(torch.device("cuda", torch.cuda.current_device()), non_blocking=True)
+    lib = L.load()
+    wc = wd.contiguous()
+    q = torch.empty(w.shape, dtype=torch.float8_e4m3fn, device=wd.device)
+    s = torch.empty(1, dtype=torch.float32, device=wd.device)
+    with torch.cuda.device(wd.device):
+        L.check(lib.qik_quantize_weight(wc.data_ptr(), _dtype_code(wc), wc.numel(), q.data_ptr(), s.data_ptr(),
+                                        _ws(wd.device).data_ptr(), L.stream_ptr()), "qik_quantize_weight")
+    if src_dev.type != "cuda":
+        return q.to(src_dev), s.to(src_dev)
+    return q, s
+
+
+def fp8_gemm(xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
+             bias: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
+             epilogue: int = L.EPI_SCALE, amax_out: torch.Tensor | None = None,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """y[M, N] = epilogue((xq . wq^T) * sx * sw (+ bias)) on the tensor core.
+
+    xq [M, K] e4m3 (row pitch a multiple of 16 bytes), wq [N, K] e4m3, sx/sw fp32 [1]
+    on the device, bias bf16 [N] or None.  out_dtype bf16, or fp32 for the pre-cast
+    parity output.  ``amax_out`` (int32 [1], zeroed by the caller) receives the
+    amax of the bf16 output for the next dynamic quantization."""
+    lib = L.load()
+    if xq.dtype != torch.float8_e4m3fn or wq.dtype != torch.float8_e4m3fn:
+        raise TypeError("qik.fp8_gemm: operands must be float8_e4m3fn")
+    if xq.stride(-1) != 1:
+        xq = xq.contiguous()
+    if wq.stride(-1) != 1:
+        wq = wq.contiguous()
+    M, K = xq.shape
+    N, K2 = wq.shape
+    if K2 != K:
+        raise ValueError(f"qik.fp8_gemm: K mismatch {K} vs {K2}")
+    if out is None:
+        out = torch.empty(M, N, dtype=out_dtype, device=xq.device)
+    if bias is not None:
+        bias = bias.to(torch.bfloat16).contiguous()
+    status = L.status_word(xq.device)
+    with torch.cuda.device(xq.device):
+        L.check(lib.qik_fp8_gemm(xq.data_ptr(), wq.data_ptr(), M, N, K, xq.stride(0), wq.stride(0), sx.data_ptr(),
+                                 sw.data_ptr(), L.ptr(bias), out.data_ptr(), out.stride(0),
+                                 L.DTYPE_F32 if out.dtype == torch.float32 else L.DTYPE_BF16, epilogue,
+                                 L.ptr(amax_out), status.data_ptr(), L.stream_ptr()), "qik_fp8_gemm")
+    return out
+
+
+class FP8Linear(nn.Module):
+    """Drop-in replacement for nn.Linear with e4m3 weights (static per-tensor scale)
+    and dynamic per-tensor activation quantization, computed by the qik tcgen05 GEMM.
+
+    Buffers (state-dict compatible with the reference's e4m3 cache):
+      weight        float8_e4m3fn [out_features, in_features]
+      weight_scale  float32 [1]
+      bias          bfloat16 [out_features] or None
+    """
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = False):
+        super().__init__()
+        self.in_features = in_features
+        self.out_features = out_features
+        self.register_buffer("weight", torch.zeros(out_features, in_features, dtype=torch.float8_e4m3fn))
+        self.register_buffer("weight_scale", torch.ones(1, dtype=torch.float32))
+        if bias:
+            self.register_buffer("bias", torch.zeros(out_features, dtype=torch.bfloat16))
+        else:
+            self.bias = None
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.in_features < 256:
+            # Same rule as the reference (fp8.py:79-84): skinny-K linears (img_in,
+            # K=64) dequantize the weight and run a bf16 linear.
+            w = self.weight.to(torch.bfloat16).float() * self.weight_scale
+            out = torch.nn.functional.linear(x, w.to(x.dtype), self.bias)
+            return out.to(x.dtype)
+        x2 = x.reshape(-1, x.shape[-1])
+        xq, s_a = quantize_tensorwise(x2)
+        out = fp8_gemm(xq, s_a, self.weight, self.weight_scale, self.bias)
+        out = out.reshape(*x.shape[:-1], self.out_features)
+        return out.to(x.dtype) if out.dtype != x.dtype else out
+
+    def forward_fp32(self, x: torch.Tensor) -> torch.Tensor:
+        """Same computation with the fp32 GEMM output before the bf16 cast (parity mode)."""
+        x2 = x.reshape(-1, x.shape[-1])
+        xq, s_a = quantize_tensorwise(x2)
+        out = fp8_gemm(xq, s_a, self.weight, self.weight_scale, self.bias, out_dtype=torch.float32)
+        return out.reshape(*x.shape[:-1], self.out_features)
+
+    @staticmethod
+    def from_linear(linear: nn.Linear) -> "FP8Linear":
+        """Convert a loaded bf16 nn.Linear (weights on CPU or GPU; quantized on the GPU)."""
+        mod = FP8Linear(linear.in_features, linear.out_features, bias=linear.bias is not None)
+        wq, s = quantize_weight_tensorwise(linear.weight.data.float())
+        mod.weight = wq.to(linear.weight.device)
+        mod.weight_scale = s.to(linear.weight.device)
+        if linear.bias is not None:
+            mod.bias = linear.bias.data.to(torch.bfloat16).clone()
+        return mod.to(linear.weight.device)
+
+    def extra_repr(self) -> str:
+        return f"in_features={self.in_features}, out_features={self.out_features}, bias={self.bias is not None}"
+
+
+def convert_linears_fp8(module: nn.Module, skip_patterns: tuple[str, ...] = (), prefix: str = "") -> list[str]:
+    """Recursively replace nn.Linear submodules with FP8Linear (in place); returns the
+    converted fully-qualified names.  Names containing any of ``skip_patterns`` are
+    left alone."""
+    converted = []
+    for name, child in list(module.named_children()):
+        full = f"{prefix}.{name}" if prefix else name
+        if any(p in full for p in skip_patterns):
+            continue
+        if isinstance(child, nn.Linear):
+            setattr(module, name, FP8Linear.from_linear(child))
+            converted.append(full)
+        else:
+            converted.extend(convert_linears_fp8(child, skip_patterns, full))
+    return converted
+
+
+def fp8_state_dict(model: nn.Module) -> dict[str, torch.Tensor]:
+    """State dict where converted linears expose fp8 ``weight`` + ``weight_scale``."""
+    return {k: v for k, v in model.state_dict().items()}
+
+
+def fp8_ffn_gelu(x: torch.Tensor, up: FP8Linear, down: FP8Linear) -> torch.Tensor:
+    """DiT FFN pair: down(gelu_tanh(up(x))) with both linears FP8 per-tensor and the
+    hidden activation re-quantized dynamically between them.
+
+    The up-projection epilogue applies GELU-tanh to the bf16 linear output and
+    accumulates max|h| on the fly, so the hidden tensor is quantized with one pack
+    pass (no separate amax read)."""
+    x2 = x.reshape(-1, x.shape[-1])
+    xq, sx = quantize_tensorwise(x2)
+    amax = torch.zeros(1, dtype=torch.int32, device=x.device)
+    h = fp8_gemm(xq, sx, up.weight, up.weight_scale, up.bias, epilogue=L.EPI_GELU_TANH, amax_out=amax)
+    hq, sh = quantize_from_amax(h, amax)
+    y = fp8_gemm(hq, sh, down.weight, down.weight_scale, down.bias)
+    return y.reshape(*x.shape[:-1], down.out_features)

@@ -1,0 +1,173 @@
+"""GPU parity: the tcgen05 FP8 GEMM (qik_fp8_gemm) and FP8Linear against the oracle.
+
+Gates: the fp32 (pre-cast) GEMM output within
+max-abs <= 2e-2 and relative Frobenius <= 5e-3 of the fp32 dequant oracle; the
+bf16 production output within 1 bf16 ulp (+1e-6) of bf16(oracle) element-wise and
+relF <= 5e-3.  Small-integer operands make fp32 accumulation exact, so those cases
+must match bit for bit whatever the summation order.
+"""
+import numpy as np
+import pytest
+import torch
+
+import golden_inputs as GI
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-2
+RELF = 5e-3
+
+
+@pytest.fixture(scope="module")
+def fp8():
+    from qik import fp8 as F
+    return F
+
+
+def _e4m3_small_ints(seed: int, shape, lo=-4, hi=4) -> torch.Tensor:
+    g = np.random.default_rng(seed)
+    return torch.from_numpy(g.integers(lo, hi + 1, size=shape).astype(np.float32)).to(torch.float8_e4m3fn)
+
+
+def _one():
+    return torch.ones(1, dtype=torch.float32, device="cuda")
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 128), (128, 256, 256), (256, 512, 384), (1, 16, 16),
+                                   (2, 48, 32), (127, 272, 112), (129, 256, 144), (300, 3072, 3072),
+                                   (4352, 256, 128)])
+def test_gemm_exact_small_ints(fp8, M, N, K):
+    """Exact integer products: any layout/descriptor/tail error shows up as a mismatch."""
+    a = _e4m3_small_ints(M * 7 + K, (M, K))
+    b = _e4m3_small_ints(N * 3 + K, (N, K))
+    ref = a.float() @ b.float().t()
+    y = fp8.fp8_gemm(a.cuda(), _one(), b.cuda(), _one(), out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert torch.equal(y.cpu(), ref)
+
+
+def test_gemm_scales_and_bias(fp8):
+    M, N, K = 200, 320, 256
+    a = _e4m3_small_ints(1, (M, K))
+    b = _e4m3_small_ints(2, (N, K))
+    bias = GI.randn_bf16(3, (N,))
+    sa = torch.tensor([0.25], device="cuda")
+    sb = torch.tensor([0.5], device="cuda")
+    y = fp8.fp8_gemm(a.cuda(), sa, b.cuda(), sb, bias=bias.cuda(), out_dtype=torch.float32)
+    ref = (a.float() @ b.float().t()) * 0.125 + bias.float()
+    assert torch.allclose(y.cpu(), ref, rtol=0, atol=1e-5)
+    yb = fp8.fp8_gemm(a.cuda(), sa, b.cuda(), sb, bias=bias.cuda())
+    assert torch.equal(yb.cpu(), ref.to(torch.bfloat16))
+
+
+def _linear_case(seed, M, N, K, outliers=True):
+    x = GI.outlier_activations(seed, M, K) if outliers else GI.randn_bf16(seed, (M, K))
+    w = GI.randn_bf16(seed + 1, (N, K), 0.02)
+    return x, w
+
+
+@pytest.mark.parametrize("M,N,K", [(4352, 3072, 3072), (256, 9216, 3072), (1024, 12288, 3072),
+                                   (256, 3072, 12288), (2, 18432, 3072)])
+def test_fp8_linear_parity(fp8, M, N, K):
+    """BASELINE config 1 (and sweep shapes): dynamic activation quant + FP8 GEMM vs the
+    fp32 dequant path of the reference, on the same quantized operands."""
+    x, w = _linear_case(M + N, M, N, K)
+    lin = fp8.FP8Linear(K, N).cuda()
+    wq, sw = fp8.quantize_weight_tensorwise(w.cuda())
+    lin.weight.copy_(wq)
+    lin.weight_scale.copy_(sw)
+    xd = x.cuda()
+    y32 = lin.forward_fp32(xd)
+    y16 = lin(xd)
+    torch.cuda.synchronize()
+    xq, sx = fp8.quantize_tensorwise(xd)
+    ref = O.fp8_linear(xq.cpu(), float(sx.item()), wq.cpu(), float(sw.item()))
+    d = (y32.cpu() - ref).abs().max().item()
+    assert d <= MAX_ABS, d
+    assert O.relf(y32.cpu(), ref) <= RELF
+    ref16 = ref.to(torch.bfloat16).float()
+    err16 = (y16.cpu().float() - ref16).abs()
+    assert (err16 <= O.bf16_ulp(ref16) + 1e-6).all(), err16.max().item()
+    assert O.relf(y16.cpu(), ref) <= RELF
+    # the reference's own gate vs the unquantized product (tests/test_fp8.py:27-28)
+    assert O.relf(y16.cpu(), x.float() @ w.float().t()) < 0.06
+
+
+def test_fp8_linear_bias_and_leading_dims(fp8):
+    x = GI.randn_bf16(70, (2, 37, 512))
+    w = GI.randn_bf16(71, (384, 512), 0.02)
+    b = GI.randn_bf16(72, (384,), 0.1)
+    lin = torch.nn.Linear(512, 384, bias=True, dtype=torch.bfloat16)
+    with torch.no_grad():
+        lin.weight.copy_(w)
+        lin.bias.copy_(b)
+    f = fp8.FP8Linear.from_linear(lin.cuda())
+    y = f(x.cuda())
+    assert y.shape == (2, 37, 384) and y.dtype == torch.bfloat16
+    xq, sx = fp8.quantize_tensorwise(x.cuda().reshape(-1, 512))
+    ref = O.fp8_linear(xq.cpu(), float(sx.item()), f.weight.cpu(), float(f.weight_scale.item()), b)
+    assert O.relf(y.reshape(-1, 384).cpu(), ref) <= RELF
+
+
+def test_fp8_linear_skinny_k_dequant_path(fp8):
+    """in_features < 256 follows the reference's dequantized bf16 linear."""
+    lin = torch.nn.Linear(64, 128, bias=False, dtype=torch.bfloat16).cuda()
+    f = fp8.FP8Linear.from_linear(lin)
+    x = GI.randn_bf16(80, (10, 64)).cuda()
+    w = (f.weight.to(torch.bfloat16).float() * f.weight_scale).to(torch.bfloat16)
+    assert torch.equal(f(x), torch.nn.functional.linear(x, w))
+
+
+def test_gelu_epilogue_and_amax(fp8):
+    """GEMM1 of the FFN: y = gelu_tanh(bf16(acc*s)), amax of the bf16 output."""
+    M, N, K = 512, 1024, 3072
+    x, w = _linear_case(5, M, N, K)
+    xq, sx = fp8.quantize_tensorwise(x.cuda())
+    wq, sw = fp8.quantize_weight_tensorwise(w.cuda())
+    amax = torch.zeros(1, dtype=torch.int32, device="cuda")
+    from qik import _lib as L
+    h = fp8.fp8_gemm(xq, sx, wq, sw, epilogue=L.EPI_GELU_TANH, amax_out=amax)
+    plain = fp8.fp8_gemm(xq, sx, wq, sw)
+    torch.cuda.synchronize()
+    ref_h = torch.nn.functional.gelu(plain.float(), approximate="tanh").to(torch.bfloat16)
+    d = (h.float() - ref_h.float()).abs()
+    assert (d <= O.bf16_ulp(ref_h.float()) + 1e-6).all()
+    got_amax = np.array([amax.item()], dtype=np.int32).view(np.float32)[0]
+    assert got_amax == h.float().abs().max().item()
+
+
+def test_ffn_pair_parity(fp8):
+    """BASELINE config 2 at reduced M: FFN 3072 -> 12288 (GELU-tanh) -> 3072, both FP8,
+    hidden re-quantized dynamically; vs the fp32 dequant oracle on the same operands."""
+    M, K, Hd = 512, 3072, 12288
+    x = GI.outlier_activations(90, M, K)
+    up = fp8.FP8Linear(K, Hd).cuda()
+    down = fp8.FP8Linear(Hd, K).cuda()
+    for lin, seed in ((up, 91), (down, 92)):
+        wq, sw = fp8.quantize_weight_tensorwise(GI.randn_bf16(seed, (lin.out_features, lin.in_features), 0.02).cuda())
+        lin.weight.copy_(wq)
+        lin.weight_scale.copy_(sw)
+    y = fp8.fp8_ffn_gelu(x.cuda(), up, down)
+    torch.cuda.synchronize()
+    # oracle: same dynamic quantizations, fp32 dequant GEMMs, bf16 rounding points of
+    # the reference module chain (linear -> bf16, gelu -> bf16, linear -> bf16)
+    xq, sx = O.quantize_act(x)
+    y1 = O.fp8_linear(xq, sx, up.weight.cpu(), float(up.weight_scale.item())).to(torch.bfloat16)
+    h = O.gelu_tanh(y1)
+    hq, sh = O.quantize_act(h, inv=O.act_reciprocal(O.compute_scale(h)))
+    ref = O.fp8_linear(hq, sh, down.weight.cpu(), float(down.weight_scale.item()))
+    assert (y.cpu().float() - ref).abs().max().item() <= 5 * MAX_ABS
+    assert O.relf(y.cpu(), ref) <= RELF
+
+
+def test_gemm_rejects_bad_shapes(fp8):
+    from qik import _lib as L
+    a = torch.zeros(4, 24, dtype=torch.float8_e4m3fn, device="cuda")
+    b = torch.zeros(32, 24, dtype=torch.float8_e4m3fn, device="cuda")
+    with pytest.raises(L.QikError):
+        fp8.fp8_gemm(a, _one(), b, _one())                               # K % 16 != 0
+    a = torch.zeros(4, 32, dtype=torch.float8_e4m3fn, device="cuda")
+    b = torch.zeros(40, 32, dtype=torch.float8_e4m3fn, device="cuda")
+    with pytest.raises(L.QikError):
+        fp8.fp8_gemm(a, _one(), b, _one())                               # N % 16 != 0
