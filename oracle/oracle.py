@@ -137,12 +137,12 @@ def quantize_act(x: torch.Tensor, mode: int = SCALE_CUDA, inv: float | None = No
     """quantize_tensorwise (fp8.py:44-53): s = compute_scale(x); q = e4m3(x * (1/s)).
 
     ``inv`` is the fp32 value of ``1/s`` the device formed (fp8.py:39); by default
-    the IEEE round-to-nearest reciprocal.  Returns (q uint8 ndarray, s float).
+    the reference's form (act_reciprocal).  Returns (q uint8 ndarray, s float).
     """
     bits = _bf16_bits(x)
     s = compute_scale(x, mode)
     if inv is None:
-        inv = reciprocal_rn(s)
+        inv = act_reciprocal(s)
     q = np.empty(bits.shape, dtype=np.uint8)
     lib().qik_oracle_pack_act_bf16(_ptr(bits), bits.size, inv, _ptr(q))
     return q, s

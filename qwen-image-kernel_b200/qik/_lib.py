@@ -78,11 +78,20 @@ def load(require_cuda: bool = True) -> ctypes.CDLL:
                 raise QikError(f"qik: {LIB_PATH} is missing; build it with qwen-image-kernel_b200/build.py")
             lib = ctypes.CDLL(str(LIB_PATH))
             for name, (res, args) in SIGNATURES.items():
-                fn = getattr(lib, name)
+                try:
+                    fn = getattr(lib, name)
+                except AttributeError:
+                    continue   # reported by missing_symbols(); calling it raises
                 fn.restype = res
                 fn.argtypes = args
             _lib = lib
     return _lib
+
+
+def missing_symbols() -> list[str]:
+    """Entry points of include/qik.h that the loaded library does not export."""
+    lib = load(require_cuda=False)
+    return [n for n in SIGNATURES if not hasattr(lib, n)]
 
 
 def check(rc: int, what: str) -> None:
