@@ -1,0 +1,358 @@
+"""Benchmark of the FP8 DiT hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl qik|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...           (N > 1)
+
+Workload ("DiT FFN pair on 1 B200"): per GPU, M = 4352
+token rows x 3072 -> 12288 (GELU-tanh) -> 3072, both linears FP8 per-tensor with
+static e4m3 weights (N(0, 0.02) init) and dynamic per-tensor activation scales,
+the hidden activation re-quantized between them, bf16 output.  Activations are
+N(0,1) with 8 outlier channels x20 (synthetic; no dataset is involved).
+
+A step is one FFN pair over one batch.  ``value`` = FLOPs (2*M*N*K summed over both
+linears and all ranks) / device time of the K timed steps (CUDA events on the
+launching stream, max over ranks); L2 is flushed (256 MiB write) between steps,
+outside the timed events.  ``e2e`` is the same metric through the public API
+with the step's input copied from pinned host memory and its output copied back
+inside the timed region.  ``roofline`` covers the dominant kernel (the tcgen05 FP8
+GEMM): algorithmic FLOPs per launch / its average CUDA-event duration.
+
+Multi-GPU: token-row shards, one process per GPU, no collective on the data path
+(weak scaling).  ``--impl reference`` times the reference's arithmetic (fp8
+quantize + dequantized-fp32 matmuls, restated in PyTorch) on the host CPU cores
+on a bounded row sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import shutil
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "qwen-image-kernel_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "FP8 linear TFLOPS/GPU & % dense-FP8 peak at DiT shapes; DiT-block ms @1024px"
+M_ROWS, K_IN, HIDDEN = 4352, 3072, 12288
+FLOPS_PER_LINEAR = 2.0 * M_ROWS * K_IN * HIDDEN
+FLOPS_PER_STEP = 2 * FLOPS_PER_LINEAR
+NOMINAL_FP8_TFLOPS = 4500.0
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"fp8_tflops": 2.0 * float(d["bf16_tflops_sustained"]),
+                "fp8_tflops_burst": 2.0 * float(d["bf16_tflops"]), "hbm_gbs": float(d["hbm_gbs"]),
+                "source": "measured (MEASURED_PEAKS.json): FP8 dense = 2 x measured bf16 cuBLAS, sustained"}
+    return {"fp8_tflops": 2.0 * 1400.0, "fp8_tflops_burst": 2.0 * 1590.0, "hbm_gbs": 6650.0,
+            "source": "fallback: 2 x 1.40 PFLOP/s sustained bf16, 6.65 TB/s"}
+
+
+# ------------------------------------------------------------------------------ inputs
+def make_inputs(seed: int, device: torch.device):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(M_ROWS, K_IN, generator=g)
+    x[:, :8] *= 20.0
+    x = x.to(torch.bfloat16)
+    w1 = (torch.randn(HIDDEN, K_IN, generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(K_IN, HIDDEN, generator=g) * 0.02).to(torch.bfloat16)
+    return x, w1, w2
+
+
+# ------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        if shutil.which("nvidia-smi") is None:
+            return self
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        self.fh = open(self.path, "w")
+        self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits", "-lms", "200"],
+                                     stdout=self.fh, stderr=subprocess.DEVNULL)
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self) -> dict:
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        smax = max(r[1] for r in rows)
+        load = [r for r in rows if r[0] >= 0.5 * smax] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[2]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in load), "sm_max_mhz": smax, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ------------------------------------------------------------------------------ qik arm
+def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
+    from qik import fp8 as F
+    from qik import _lib as L
+
+    x_cpu, w1, w2 = make_inputs(1234 + rank, device)
+    up = F.FP8Linear(K_IN, HIDDEN).to(device)
+    down = F.FP8Linear(HIDDEN, K_IN).to(device)
+    for lin, w in ((up, w1), (down, w2)):
+        wq, sw = F.quantize_weight_tensorwise(w.to(device))
+        lin.weight.copy_(wq)
+        lin.weight_scale.copy_(sw)
+    x = x_cpu.to(device)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step(xin: torch.Tensor, ev=None):
+        # the public FP8 FFN path, split to time the GEMM launches individually
+        x2 = xin.reshape(-1, K_IN)
+        xq, sx = F.quantize_tensorwise(x2)
+        amax = torch.zeros(1, dtype=torch.int32, device=device)
+        if ev is not None:
+            ev[0].record(stream)
+        h = F.fp8_gemm(xq, sx, up.weight, up.weight_scale, up.bias, epilogue=L.EPI_GELU_TANH, amax_out=amax)
+        if ev is not None:
+            ev[1].record(stream)
+        hq, sh = F.quantize_from_amax(h, amax)
+        if ev is not None:
+            ev[2].record(stream)
+        y = F.fp8_gemm(hq, sh, down.weight, down.weight_scale, down.bias)
+        if ev is not None:
+            ev[3].record(stream)
+        return y
+
+    launches_per_step = 5  # amax, pack, gemm (GELU+amax), pack, gemm
+    for _ in range(args.warmup):
+        step(x)
+    torch.cuda.synchronize(device)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+
+    # ---- device-resident timed region
+    ev_step = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+    ev_k = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    barrier()
+    with ClockSampler(device.index if device.index is not None else 0) as clk:
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            ev_step[i][0].record(stream)
+            step(x, ev_k[i])
+            ev_step[i][1].record(stream)
+        barrier()
+    clocks = clk.summary()
+    t_steps = sum(a.elapsed_time(b) for a, b in ev_step) / 1e3            # seconds
+    t_gemm = [ev[0].elapsed_time(ev[1]) for ev in ev_k] + [ev[2].elapsed_time(ev[3]) for ev in ev_k]
+    gemm_ms = sum(t_gemm) / len(t_gemm)
+
+    # ---- end-to-end through the public API with host buffers
+    x_host = x_cpu.pin_memory()
+    y_host = torch.empty(M_ROWS, K_IN, dtype=torch.bfloat16).pin_memory()
+    for _ in range(2):
+        y_host.copy_(F.fp8_ffn_gelu(x_host.to(device, non_blocking=True), up, down), non_blocking=True)
+    barrier()
+    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.fill_(float(i))
+        e2e_ev[i][0].record(stream)
+        xd = x_host.to(device, non_blocking=True)
+        y_host.copy_(F.fp8_ffn_gelu(xd, up, down), non_blocking=True)
+        e2e_ev[i][1].record(stream)
+    barrier()
+    t_e2e = sum(a.elapsed_time(b) for a, b in e2e_ev) / 1e3
+
+    status = L.device_status(device)
+    t = torch.tensor([t_steps, t_e2e, gemm_ms, float(status)], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    t_steps, t_e2e, gemm_ms, status = t.tolist()
+    if rank != 0:
+        return None
+
+    pk = peaks()
+    total_flops = FLOPS_PER_STEP * args.steps * world
+    value = total_flops / t_steps / 1e12
+    achieved = FLOPS_PER_LINEAR / (gemm_ms / 1e3) / 1e12
+    out = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t_steps / args.steps * 1e3, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "e4m3 x e4m3 -> fp32 accumulate, bf16 out",
+        "data": "synthetic: N(0,1) activations with 8 outlier channels x20, N(0,0.02) random-init weights",
+        "config": {"workload": "configs[1] DiT FFN pair: M=4352 x 3072 -> 12288 (GELU-tanh) -> 3072, FP8 "
+                               "per-tensor, dynamic activation re-quantization, bf16 out",
+                   "rows_per_gpu": M_ROWS, "global_rows": M_ROWS * world,
+                   "l2": "flushed between timed steps (256 MiB write outside the timed events)",
+                   "parallelism": f"dp{world}: token-row shards, no data-path collective"},
+        "per_gpu_tflops": round(value / world, 2),
+        "pct_dense_fp8_peak": round(100.0 * value / world / pk["fp8_tflops"], 1),
+        "pct_nominal_fp8_4500": round(100.0 * value / world / NOMINAL_FP8_TFLOPS, 1),
+        "e2e": {"value": round(total_flops / t_e2e / 1e12, 2), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": M_ROWS * K_IN * 2, "d2h_bytes_per_step": M_ROWS * K_IN * 2,
+                "ms_per_step": round(t_e2e / args.steps * 1e3, 4)},
+        "roofline": {"kernel": "qik::fp8_gemm_kernel (tcgen05 kind::f8f6f4)", "bound": "tensor",
+                     "achieved": round(achieved, 1), "peak": round(pk["fp8_tflops"], 1), "unit": "TFLOP/s",
+                     "frac": round(achieved / pk["fp8_tflops"], 3), "traffic": traffic_from_profile(),
+                     "peak_source": pk["source"], "avg_launch_ms": round(gemm_ms, 4),
+                     "flops_per_launch": FLOPS_PER_LINEAR},
+        "gpu_launches": launches_per_step * args.steps * 2,
+        "device_status": int(status),
+        "clocks": clocks,
+    }
+    if world == 1:
+        out["cpu_baseline"] = cpu_baseline(args)
+    return out
+
+
+def traffic_from_profile():
+    """DRAM bytes per GEMM launch from the committed ncu summary, if present."""
+    p = ROOT / "profiles" / "fp8_gemm_ffn_cfg2.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get("dram_bytes_per_launch")
+        except (OSError, ValueError):
+            return None
+    return None
+
+
+# ------------------------------------------------------------------------------ CPU arm
+def cpu_ffn_reference(x: torch.Tensor, w1q, s1, w2q, s2) -> torch.Tensor:
+    """The reference's arithmetic on CPU tensors, in PyTorch: dynamic per-tensor e4m3
+    quantization (fp8.py:24-53), dequantized fp32 matmul (the fp32-accumulated path
+    of fp8.py:87), bf16 output, GELU-tanh, re-quantization, second matmul."""
+    def quant(a):
+        s = (a.abs().amax().float() / 448.0).clamp_min(1e-12)
+        return (a.float() * (1.0 / s)).to(torch.float8_e4m3fn), s
+
+    xq, sx = quant(x)
+    y1 = ((xq.float() * sx) @ (w1q.float() * s1).t()).to(torch.bfloat16)
+    h = torch.nn.functional.gelu(y1.float(), approximate="tanh").to(torch.bfloat16)
+    hq, sh = quant(h)
+    return ((hq.float() * sh) @ (w2q.float() * s2).t()).to(torch.bfloat16)
+
+
+def cpu_baseline(args, budget_s: float = 12.0, rows: int = 512) -> dict:
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    x, w1, w2 = make_inputs(4321, torch.device("cpu"))
+    xs = x[:rows].contiguous()
+
+    def wquant(w):
+        s = (w.abs().amax().float() / 448.0).clamp_min(1e-12)
+        return (w.float() / s).clamp(-448, 448).to(torch.float8_e4m3fn), s
+
+    w1q, s1 = wquant(w1)
+    w2q, s2 = wquant(w2)
+    cpu_ffn_reference(xs[:64], w1q, s1, w2q, s2)                         # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        cpu_ffn_reference(xs, w1q, s1, w2q, s2)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= 50:
+            break
+    flops = 2 * (2.0 * rows * K_IN * HIDDEN) * reps
+    return {"value": round(flops / el / 1e12, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} x FFN pair on {rows} of the {M_ROWS} rows (same shapes/weights), "
+                      f"{el:.1f} s wall, PyTorch CPU fp32 dequant matmuls"}
+
+
+def run_reference(args, rank: int, world: int) -> dict | None:
+    if rank != 0:
+        return None
+    cb = cpu_baseline(args, budget_s=max(5.0, min(60.0, 2.0 * (args.steps + args.warmup))))
+    return {"metric": METRIC, "value": cb["value"], "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "e4m3 quantize + fp32 dequant matmul (CPU)", "data": "synthetic",
+            "config": {"workload": "configs[1] DiT FFN pair (row sample)", "rows_per_gpu": M_ROWS},
+            "impl": "reference", "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["qik", "reference"], default="qik")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return 0
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+    try:
+        res = run_qik(args, rank, world, device)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+    if res is not None:
+        print(json.dumps(res), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
