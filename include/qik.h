@@ -62,6 +62,27 @@ int qik_compute_scale(const void* x, int dtype, int64_t n, float* scale_out, voi
 int qik_quantize_act(const void* x, int64_t n, uint8_t* q, float* scale_out, void* ws, void* stream);
 
 /*
+ * qik_quantize_act without a workspace argument, for callers that cannot
+ * allocate device memory: plugin hosts and serving runtimes that hand a kernel
+ * only its inputs and outputs from a pre-planned pool, and code that must not
+ * call cudaMalloc (or torch's allocator) on its launch path.  Same result as
+ * qik_quantize_act (bytes and scale).  No counterpart in the reference: it is an
+ * addition of this library.
+ *
+ * The scratch lives in one file-scope __device__ array of
+ * QIK_NOALLOC_SCRATCH_BYTES bytes that every GPU loading the library holds until
+ * the process exits; this entry point needs qik_quant_workspace_bytes() of it for
+ * any n and returns QIK_ERR_INVALID if that ever exceeds the array.  The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress);
+ * make that first call before any stream capture.  All calls share the array and
+ * its amax word is cleared on the stream at the start of each call, so calls
+ * that overlap on the GPU (different streams, or different host threads on one
+ * device) race; serialize them.
+ */
+#define QIK_NOALLOC_SCRATCH_BYTES 256
+int qik_quantize_act_noalloc(const void* x, int64_t n, uint8_t* q, float* scale_out, void* stream);
+
+/*
  * e4m3 activation pack with a scale already on the device (the second half of
  * qik_quantize_act, used after a producer kernel accumulated the amax):
  *   amax_bits: fp32 bit pattern of max|x| (as written by qik_fp8_gemm's amax_out).

@@ -11,6 +11,8 @@
 // The amax is kept as the fp32 bit pattern of |x|: for non-negative floats the
 // unsigned order is the numeric order and NaN patterns sort above +inf, so an
 // integer atomicMax reproduces torch.amax including NaN propagation.
+#include <mutex>
+
 #include "qik_device.cuh"
 #include "qik_host.h"
 
@@ -359,3 +361,48 @@ int qik_kv_store(const void* k, const void* v, int64_t B, int64_t P, int64_t H, 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- no-alloc variant
+// Scratch of qik_quantize_act_noalloc, for callers that cannot allocate device
+// memory.  Host code cannot use the array's name as a device pointer (on the host
+// it names a stand-in object), so its device address is looked up once per
+// device with cudaGetSymbolAddress, with that device current, and passed to the
+// kernels like any workspace.
+static __device__ __align__(256) uint8_t qik_noalloc_scratch[QIK_NOALLOC_SCRATCH_BYTES];
+
+namespace qik {
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {nullptr};
+
+int noalloc_scratch_ptr(void** out) {
+  int dev = 0;
+  QIK_TRY_CUDA(cudaGetDevice(&dev));
+  QIK_REQUIRE(dev >= 0 && dev < 64, "qik_quantize_act_noalloc: device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, qik_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(qik_noalloc_scratch)");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return QIK_OK;
+}
+}  // namespace
+}  // namespace qik
+
+extern "C" int qik_quantize_act_noalloc(const void* x, int64_t n, uint8_t* q, float* scale_out, void* stream) {
+  QIK_REQUIRE(scale_out, "qik_quantize_act_noalloc: scale_out is NULL");
+  QIK_REQUIRE((x && q) || n == 0, "qik_quantize_act_noalloc: x/q is NULL");
+  QIK_REQUIRE(n >= 0, "qik_quantize_act_noalloc: negative n");
+  const size_t need = qik_quant_workspace_bytes();
+  QIK_REQUIRE(need <= QIK_NOALLOC_SCRATCH_BYTES,
+              "qik_quantize_act_noalloc: needs %zu bytes of scratch, the static array holds %d", need,
+              QIK_NOALLOC_SCRATCH_BYTES);
+  void* ws = nullptr;
+  const int rc = qik::noalloc_scratch_ptr(&ws);
+  if (rc) return rc;
+  // qik_quantize_act clears the amax word on the stream before accumulating.
+  return qik_quantize_act(x, n, q, scale_out, ws, stream);
+}

@@ -49,6 +49,7 @@ SIGNATURES = {
     "qik_compute_scale": (_i32, [_vp, _i32, _i64, _vp, _vp, _vp]),
     "qik_quantize_act": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp]),
     "qik_quantize_act_from_amax": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp]),
+    "qik_quantize_act_noalloc": (_i32, [_vp, _i64, _vp, _vp, _vp]),
     "qik_quantize_weight": (_i32, [_vp, _i32, _i64, _vp, _vp, _vp, _vp]),
     "qik_fp8_gemm": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _vp,
                             _vp, _vp]),
