@@ -69,18 +69,24 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
   return QIK_OK;
 }
 
-int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, const uint64_t dims[3],
-                 const uint64_t strides_bytes[2], const uint32_t box[3], CUtensorMapSwizzle swizzle) {
+int make_tmap_nd(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int rank, const uint64_t* dims,
+                 const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return set_error(QIK_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
-  cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
-  cuuint64_t s[2] = {strides_bytes[0], strides_bytes[1]};
-  cuuint32_t b[3] = {box[0], box[1], box[2]};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, dtype, 3, const_cast<void*>(base), d, s, b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (rank < 1 || rank > 5) return set_error(QIK_ERR_INVALID, "tensor map rank %d out of range", rank);
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i + 1 < rank) st[i] = strides_bytes[i];
+  }
+  CUresult r = fn(map, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, st, b, e,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
-    return set_error(QIK_ERR_CUDA, "cuTensorMapEncodeTiled(3d) failed (%d)", static_cast<int>(r));
+    return set_error(QIK_ERR_CUDA, "cuTensorMapEncodeTiled(%dd) failed (%d)", rank, static_cast<int>(r));
   return QIK_OK;
 }
 

@@ -1,0 +1,483 @@
+// qik_attn.cu -- block-causal flash attention over [prefix slab ; fresh K/V] on the
+// sm_100a tensor core.
+//
+// Semantics of block_causal_flash_attention / _qwen21_attn_fwd
+// (qwen_image_kernel/triton_attention.py:35-260): query row r of (b, h) attends to
+// the keys kv of the virtual concatenation [cache (P keys) ; fresh (SN keys)] with
+// kv <= L[r] (all keys when UNIFORM) and key_valid[b, kv] != 0 (when given);
+// softmax in base 2 with the scores scaled by sm_scale * log2(e); the e4m3 slab V
+// is dequantized as bf16(fl32(v8) * scale[b, h]) (triton_attention.py:154-159); P
+// is rounded to bf16 before P.V; fp32 accumulation; rows with no allowed key are 0.
+//
+// One CTA per (128-query tile, b, h):
+//   warp 0     TMA producer: Q once (two 64-column halves, 128-byte swizzle), then
+//              per key tile K (bf16) and V (bf16, or e4m3 raw for the fp8 slab)
+//              into a 2-stage ring;
+//   warp 1     MMA issuer (one thread): S_t = Q K_t^T (kind::f16, M=N=128, K=16 x 8)
+//              into a double-buffered TMEM S, then O += P_t V_t with P_t read from
+//              TMEM (A operand) and V_t from shared memory (MN-major B operand);
+//   warps 2-3  e4m3 -> bf16 V converters for slab tiles when V is fp8;
+//   warps 4-7  softmax: thread = query row; reads S_t from TMEM, masks, online
+//              max/sum (the accumulator O is rescaled in TMEM only when the running
+//              max grows by more than 2^8, which leaves the final O/l unchanged),
+//              writes bf16 P_t to TMEM; finally O / l -> bf16 -> global.
+// TMEM columns: S0 [0,128) S1 [128,256) O [256,384) P0 [384,448) P1 [448,512).
+#include "qik_device.cuh"
+#include "qik_host.h"
+
+namespace qik {
+
+constexpr int kAttnBM = 128;
+constexpr int kAttnBN = 128;
+constexpr int kAttnD = 128;
+constexpr int kAttnThreads = 256;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when the max grows by > 2^8
+
+struct AttnSmem {
+  static constexpr int kQ = 0;            // 32 KB: two 16 KB halves (d 0-63, d 64-127)
+  static constexpr int kStage0 = 32768;
+  static constexpr int kK = 0;            // per stage: K bf16 32 KB
+  static constexpr int kV = 32768;        //            V bf16 32 KB
+  static constexpr int kV8 = 65536;       //            V e4m3 raw 16 KB
+  static constexpr int kStageBytes = 81920;
+  static constexpr int kStages = 2;
+  static constexpr int kBar = kStage0 + kStages * kStageBytes;
+  static constexpr int kBytes = kBar + 256 + 1024;  // barriers + alignment slack
+};
+
+struct AttnDev {
+  const int32_t* L;
+  const uint8_t* key_valid;
+  const float* v_scale;
+  __nv_bfloat16* out;
+  int64_t o_sb, o_ss, o_sh, kv_sb;
+  int SQ, SN, P, H;
+  float qk_scale_log2;
+  int flags;
+  int* status;
+};
+
+// Two boxes of 64 d-columns x 128 keys (rows) of one (b, h).
+__device__ __forceinline__ void load_bf16_tile(const CUtensorMap* tm, void* dst, int key0, int h, int b,
+                                               uint64_t* bar) {
+  tma_load_4d(dst, tm, 0, key0, h, b, bar);
+  tma_load_4d(static_cast<uint8_t*>(dst) + 16384, tm, 64, key0, h, b, bar);
+}
+
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_ck,
+                    const __grid_constant__ CUtensorMap tm_cv, const AttnDev a) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + AttnSmem::kBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* v_full = bars + 3;    // [2] V bf16 ready (TMA or converters)
+  uint64_t* v8_full = bars + 5;   // [2] raw e4m3 V landed
+  uint64_t* kv_empty = bars + 7;  // [2] stage free (after P.V)
+  uint64_t* s_full = bars + 9;    // [2]
+  uint64_t* p_full = bars + 11;   // [2]
+  uint64_t* pv_done = bars + 13;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* lmax_slot = reinterpret_cast<int*>(tmem_slot + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kAttnBM;
+  const int bh = blockIdx.y;
+  const int b = bh / a.H, h = bh % a.H;
+  const bool has_cache = (a.flags & QIK_ATTN_HAS_CACHE) && a.P > 0;
+  const bool uniform = (a.flags & QIK_ATTN_UNIFORM) != 0;
+  const bool v_fp8 = has_cache && (a.flags & QIK_ATTN_V_FP8);
+  const bool has_kv = (a.flags & QIK_ATTN_HAS_KEY_VALID) != 0;
+  const int P = has_cache ? a.P : 0;
+  const int kv_total = P + a.SN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v8_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&p_full[s], 4);
+      mbar_init(&pv_done[s], 1);
+    }
+    *abort_flag = 0;
+    *lmax_slot = -1;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  // per-row limits; the largest L of the tile decides how many key tiles exist
+  int my_L = -1;
+  if (warp >= 4) {
+    const int r = m0 + (threadIdx.x - 128);
+    if (r < a.SQ) my_L = uniform ? kv_total - 1 : min(__ldg(a.L + r), kv_total - 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp >= 4) {
+    const int wmax = __reduce_max_sync(0xffffffffu, my_L);
+    if (lane == 0) atomicMax(lmax_slot, wmax);
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int lmax = *lmax_slot;
+  const int tiles_slab_all = (P + kAttnBN - 1) / kAttnBN;
+  const int n_slab = lmax < 0 ? 0 : min(tiles_slab_all, lmax / kAttnBN + 1);
+  const int n_fresh = lmax < P ? 0 : min((a.SN + kAttnBN - 1) / kAttnBN, (lmax - P) / kAttnBN + 1);
+  const int n_tiles = n_slab + n_fresh;
+
+  uint8_t* sQ = smem + AttnSmem::kQ;
+  auto stage_ptr = [&](int s) { return smem + AttnSmem::kStage0 + s * AttnSmem::kStageBytes; };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && n_tiles > 0) {
+      tma_prefetch_desc(&tm_q);
+      mbar_arrive_expect_tx(q_full, 32768);
+      load_bf16_tile(&tm_q, sQ, m0, h, b, q_full);
+      for (int t = 0; t < n_tiles; ++t) {
+        const int s = t & 1;
+        const uint32_t ph = (t >> 1) & 1;
+        if (!mbar_wait(&kv_empty[s], ph ^ 1u, abort_flag, a.status)) break;
+        uint8_t* st = stage_ptr(s);
+        const bool slab = t < n_slab;
+        const int key0 = slab ? t * kAttnBN : (t - n_slab) * kAttnBN;
+        mbar_arrive_expect_tx(&k_full[s], 32768);
+        load_bf16_tile(slab ? &tm_ck : &tm_k, st + AttnSmem::kK, key0, h, b, &k_full[s]);
+        if (slab && v_fp8) {
+          mbar_arrive_expect_tx(&v8_full[s], 16384);
+          tma_load_4d(st + AttnSmem::kV8, &tm_cv, 0, key0, h, b, &v8_full[s]);
+        } else {
+          mbar_arrive_expect_tx(&v_full[s], 32768);
+          load_bf16_tile(slab ? &tm_cv : &tm_v, st + AttnSmem::kV, key0, h, b, &v_full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && n_tiles > 0) {
+      constexpr uint32_t idesc_s = idesc_f32acc(1, 1, 0, 0, kAttnBM, kAttnBN);
+      constexpr uint32_t idesc_o = idesc_f32acc(1, 1, 0, 1, kAttnBM, kAttnD);
+      const uint32_t tS[2] = {tmem + 0u, tmem + 128u};
+      const uint32_t tO = tmem + 256u;
+      const uint32_t tP[2] = {tmem + 384u, tmem + 448u};
+      bool ok = mbar_wait(q_full, 0, abort_flag, a.status);
+      const uint32_t q_addr = smem_u32(sQ);
+      auto issue_pv = [&](int t) -> bool {
+        const int s = t & 1;
+        const uint32_t ph = (t >> 1) & 1;
+        if (!mbar_wait(&p_full[s], ph, abort_flag, a.status)) return false;
+        if (!mbar_wait(&v_full[s], ph, abort_flag, a.status)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(stage_ptr(s) + AttnSmem::kV);
+#pragma unroll
+        for (int k = 0; k < kAttnBN / 16; ++k) {
+          // 16 keys per step: V rows [16k, 16k+16) (2048 B); d halves 16 KB apart
+          const uint64_t vd = sdesc_sw128(v_addr + k * 2048, 16384, 1024);
+          umma_f16_ts(tO, tP[s] + k * 8, vd, idesc_o, (t > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&pv_done[s]);
+        umma_commit(&kv_empty[s]);
+        return true;
+      };
+      for (int t = 0; ok && t < n_tiles; ++t) {
+        const int s = t & 1;
+        const uint32_t ph = (t >> 1) & 1;
+        if (!mbar_wait(&k_full[s], ph, abort_flag, a.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(stage_ptr(s) + AttnSmem::kK);
+#pragma unroll
+        for (int k = 0; k < kAttnD / 16; ++k) {
+          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+          const uint64_t qd = sdesc_sw128(q_addr + off, 16, 1024);
+          const uint64_t kd = sdesc_sw128(k_addr + off, 16, 1024);
+          umma_f16_ss(tS[s], qd, kd, idesc_s, k > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[s]);
+        if (t > 0 && !issue_pv(t - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok) issue_pv(n_tiles - 1);
+    }
+  } else if (warp < 4) {
+    // ------------------------------------------------------------ V converters
+    if (v_fp8 && n_slab > 0) {
+      const float vsc = __ldg(a.v_scale + static_cast<int64_t>(b) * a.H + h);
+      const int ct = threadIdx.x - 64;  // 0..63
+      for (int t = 0; t < n_slab; ++t) {
+        const int s = t & 1;
+        const uint32_t ph = (t >> 1) & 1;
+        if (!mbar_wait(&v8_full[s], ph, abort_flag, a.status)) break;
+        const uint8_t* raw = stage_ptr(s) + AttnSmem::kV8;
+        uint8_t* dst = stage_ptr(s) + AttnSmem::kV;
+        // 2048 chunks of 8 values: chunk g -> key row g / 16, d-chunk g % 16; the
+        // bf16 tile is written in the 128-byte-swizzled layout TMA would produce.
+        for (int g = ct; g < 2048; g += 64) {
+          const int r = g >> 4, dc = g & 15;
+          const uint2 w = *reinterpret_cast<const uint2*>(raw + r * 128 + dc * 8);
+          const uint32_t bytes[2] = {w.x, w.y};
+          uint32_t o[4];
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const uint32_t h0 = cvt_e4m3x2_to_f16x2(static_cast<uint16_t>(bytes[i] & 0xFFFFu));
+            const uint32_t h1 = cvt_e4m3x2_to_f16x2(static_cast<uint16_t>(bytes[i] >> 16));
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&h0));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&h1));
+            o[2 * i] = pack_bf16x2(f0.x * vsc, f0.y * vsc);
+            o[2 * i + 1] = pack_bf16x2(f1.x * vsc, f1.y * vsc);
+          }
+          const int hd = dc >> 3, c = dc & 7;
+          *reinterpret_cast<uint4*>(dst + hd * 16384 + r * 128 + ((c ^ (r & 7)) << 4)) =
+              make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(1, 64);
+        if (ct == 0) mbar_arrive(&v_full[s]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int quarter = warp & 3;
+    const int row = threadIdx.x - 128;  // == quarter * 32 + lane
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t tS[2] = {tmem + lane_base, tmem + lane_base + 128u};
+    const uint32_t tO = tmem + lane_base + 256u;
+    const uint32_t tP[2] = {tmem + lane_base + 384u, tmem + lane_base + 448u};
+    const uint8_t* kvb = has_kv ? a.key_valid + static_cast<int64_t>(b) * a.kv_sb : nullptr;
+    float m_run = -INFINITY, l_run = 0.0f;
+    bool ok = true;
+    for (int t = 0; t < n_tiles; ++t) {
+      const int s = t & 1;
+      const uint32_t ph = (t >> 1) & 1;
+      if (!mbar_wait(&s_full[s], ph, abort_flag, a.status)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool slab = t < n_slab;
+      const int kv0 = slab ? t * kAttnBN : P + (t - n_slab) * kAttnBN;
+      const int seg_end = slab ? P : kv_total;
+      const int lim = min(my_L, seg_end - 1);  // allowed: kv0 + c <= lim
+      float sv[kAttnBN];
+#pragma unroll
+      for (int c = 0; c < kAttnBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tS[s] + c * 32, r);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sv[c * 32 + j] = __uint_as_float(r[j]);
+      }
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kAttnBN; ++c) {
+        bool allowed = kv0 + c <= lim;
+        if (has_kv && allowed) allowed = __ldg(kvb + kv0 + c) != 0;
+        sv[c] = allowed ? sv[c] * a.qk_scale_log2 : -INFINITY;
+        tmax = fmaxf(tmax, sv[c]);
+      }
+      // the running max moves (and O, l are rescaled) only when it grows by > 2^8
+      float alpha = 1.0f;
+      bool rescale_o = false;
+      if (tmax > m_run + kRescaleThreshold || (m_run == -INFINITY && tmax > -INFINITY)) {
+        alpha = (m_run == -INFINITY) ? 0.0f : ex2(m_run - tmax);
+        rescale_o = (m_run != -INFINITY);
+        m_run = tmax;
+      }
+      const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
+      float psum = 0.0f;
+      uint32_t pk[kAttnBN / 2];
+#pragma unroll
+      for (int c = 0; c < kAttnBN; c += 2) {
+        const float p0 = ex2(sv[c] - m_use);
+        const float p1 = ex2(sv[c + 1] - m_use);
+        psum += p0 + p1;
+        pk[c / 2] = pack_bf16x2(p0, p1);
+      }
+      l_run = l_run * alpha + psum;
+      // P buffer s is free once P.V of tile t-2 finished; O may be rescaled once
+      // P.V of tile t-1 finished.
+      if (t >= 2 && !mbar_wait(&pv_done[s], ((t - 2) >> 1) & 1, abort_flag, a.status)) {
+        ok = false;
+        break;
+      }
+      if (rescale_o && t >= 1) {
+        if (!mbar_wait(&pv_done[(t - 1) & 1], ((t - 1) >> 1) & 1, abort_flag, a.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < kAttnD / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tO + c * 32, r);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * alpha);
+          tmem_st32(tO + c * 32, r);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t r[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = pk[c * 32 + j];
+        tmem_st32(tP[s] + c * 32, r);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[s]);
+    }
+    // epilogue: O / l -> bf16
+    const int grow = m0 + row;
+    float o[kAttnD];
+    bool have_o = false;
+    if (ok && n_tiles > 0) {
+      const int tl = n_tiles - 1;
+      if (mbar_wait(&pv_done[tl & 1], (tl >> 1) & 1, abort_flag, a.status)) {
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < kAttnD / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tO + c * 32, r);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) o[c * 32 + j] = __uint_as_float(r[j]);
+        }
+        have_o = true;
+      }
+    }
+    if (grow < a.SQ) {
+      const bool nz = have_o && l_run > 0.0f;
+      const float inv = nz ? 1.0f / l_run : 0.0f;
+      __nv_bfloat16* dst = a.out + static_cast<int64_t>(b) * a.o_sb + static_cast<int64_t>(grow) * a.o_ss +
+                           static_cast<int64_t>(h) * a.o_sh;
+#pragma unroll
+      for (int c = 0; c < kAttnD; c += 8) {
+        uint4 w = make_uint4(0u, 0u, 0u, 0u);
+        if (nz)
+          w = make_uint4(pack_bf16x2(o[c] * inv, o[c + 1] * inv), pack_bf16x2(o[c + 2] * inv, o[c + 3] * inv),
+                         pack_bf16x2(o[c + 4] * inv, o[c + 5] * inv), pack_bf16x2(o[c + 6] * inv, o[c + 7] * inv));
+        *reinterpret_cast<uint4*>(dst + c) = w;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// 4-D map (d, s, h, b) over a [B, S, H, D] tensor with element strides (sb, ss, sh).
+static int make_bshd_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esize, int64_t B, int64_t S,
+                         int64_t H, int64_t sb, int64_t ss, int64_t sh, uint32_t box_d, CUtensorMapSwizzle sw) {
+  const uint64_t dims[4] = {static_cast<uint64_t>(kAttnD), static_cast<uint64_t>(S), static_cast<uint64_t>(H),
+                            static_cast<uint64_t>(B)};
+  const uint64_t strides[3] = {static_cast<uint64_t>(ss * esize), static_cast<uint64_t>(sh * esize),
+                               static_cast<uint64_t>(sb * esize)};
+  const uint32_t box[4] = {box_d, static_cast<uint32_t>(kAttnBN), 1, 1};
+  return make_tmap_nd(m, base, dt, 4, dims, strides, box, sw);
+}
+
+}  // namespace qik
+
+using namespace qik;
+
+extern "C" int qik_block_causal_attention(const qik_attn_args* args, int* status, void* stream) {
+  QIK_REQUIRE(args != nullptr, "qik_block_causal_attention: args is NULL");
+  const qik_attn_args& A = *args;
+  QIK_REQUIRE(A.D == kAttnD, "qik_block_causal_attention: head_dim %lld unsupported (128 only)", (long long)A.D);
+  QIK_REQUIRE(A.B >= 0 && A.SQ >= 0 && A.SN >= 0 && A.P >= 0 && A.H > 0, "qik_block_causal_attention: bad sizes");
+  if (A.B == 0 || A.SQ == 0) return QIK_OK;
+  QIK_REQUIRE(A.SN > 0, "qik_block_causal_attention: no fresh keys (SN == 0)");
+  QIK_REQUIRE(A.B * A.H <= 65535 && A.SQ <= (1ll << 30) && A.SN + A.P <= (1ll << 30),
+              "qik_block_causal_attention: size out of range");
+  QIK_REQUIRE(A.q && A.k && A.v && A.out, "qik_block_causal_attention: NULL q/k/v/out");
+  const bool has_cache = (A.flags & QIK_ATTN_HAS_CACHE) && A.P > 0;
+  const bool v_fp8 = has_cache && (A.flags & QIK_ATTN_V_FP8);
+  QIK_REQUIRE(!has_cache || (A.cache_k && A.cache_v), "qik_block_causal_attention: cache pointers missing");
+  QIK_REQUIRE(!v_fp8 || A.cache_v_scale, "qik_block_causal_attention: fp8 V needs cache_v_scale");
+  QIK_REQUIRE((A.flags & QIK_ATTN_UNIFORM) || A.L, "qik_block_causal_attention: L is NULL");
+  QIK_REQUIRE(!(A.flags & QIK_ATTN_HAS_KEY_VALID) || A.key_valid, "qik_block_causal_attention: key_valid is NULL");
+  auto ok_strides = [](int64_t sb, int64_t ss, int64_t sh, int esize) {
+    return (sb * esize) % 16 == 0 && (ss * esize) % 16 == 0 && (sh * esize) % 16 == 0 && sb >= 0 && ss > 0 && sh > 0;
+  };
+  QIK_REQUIRE(ok_strides(A.q_sb, A.q_ss, A.q_sh, 2) && ok_strides(A.k_sb, A.k_ss, A.k_sh, 2) &&
+                  ok_strides(A.v_sb, A.v_ss, A.v_sh, 2) && ok_strides(A.o_sb, A.o_ss, A.o_sh, 2),
+              "qik_block_causal_attention: q/k/v/out strides must be multiples of 16 bytes (unit stride on D)");
+  QIK_REQUIRE(aligned16(A.q) && aligned16(A.k) && aligned16(A.v) && aligned16(A.out),
+              "qik_block_causal_attention: q/k/v/out must be 16-byte aligned");
+  if (has_cache) {
+    QIK_REQUIRE(ok_strides(A.ck_sb, A.ck_ss, A.ck_sh, 2) && ok_strides(A.cv_sb, A.cv_ss, A.cv_sh, v_fp8 ? 1 : 2) &&
+                    aligned16(A.cache_k) && aligned16(A.cache_v),
+                "qik_block_causal_attention: cache strides/alignment must be 16-byte multiples");
+  }
+  CUtensorMap tq, tk, tv, tck, tcv;
+  int rc = make_bshd_map(&tq, A.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A.B, A.SQ, A.H, A.q_sb, A.q_ss, A.q_sh, 64,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc)
+    rc = make_bshd_map(&tk, A.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A.B, A.SN, A.H, A.k_sb, A.k_ss, A.k_sh, 64,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc)
+    rc = make_bshd_map(&tv, A.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A.B, A.SN, A.H, A.v_sb, A.v_ss, A.v_sh, 64,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  if (has_cache) {
+    rc = make_bshd_map(&tck, A.cache_k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A.B, A.P, A.H, A.ck_sb, A.ck_ss, A.ck_sh,
+                       64, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!rc) {
+      if (v_fp8)
+        rc = make_bshd_map(&tcv, A.cache_v, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A.B, A.P, A.H, A.cv_sb, A.cv_ss,
+                           A.cv_sh, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+      else
+        rc = make_bshd_map(&tcv, A.cache_v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A.B, A.P, A.H, A.cv_sb, A.cv_ss,
+                           A.cv_sh, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    if (rc) return rc;
+  } else {
+    tck = tk;
+    tcv = tv;
+  }
+  AttnDev d;
+  d.L = A.L;
+  d.key_valid = A.key_valid;
+  d.v_scale = A.cache_v_scale;
+  d.out = static_cast<__nv_bfloat16*>(A.out);
+  d.o_sb = A.o_sb;
+  d.o_ss = A.o_ss;
+  d.o_sh = A.o_sh;
+  d.kv_sb = A.kv_sb;
+  d.SQ = static_cast<int>(A.SQ);
+  d.SN = static_cast<int>(A.SN);
+  d.P = static_cast<int>(A.P);
+  d.H = static_cast<int>(A.H);
+  d.qk_scale_log2 = A.sm_scale * 1.4426950408889634f;
+  d.flags = A.flags;
+  d.status = status;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  QIK_TRY_CUDA(cudaGetDevice(&dev));
+  if (dev < 64 && !attr_set[dev]) {
+    QIK_TRY_CUDA(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem::kBytes));
+    attr_set[dev] = true;
+  }
+  dim3 grid(static_cast<unsigned>((A.SQ + kAttnBM - 1) / kAttnBM), static_cast<unsigned>(A.B * A.H));
+  attn_fwd_kernel<<<grid, kAttnThreads, AttnSmem::kBytes, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, tck, tcv,
+                                                                                                  d);
+  return check_launch("attn_fwd_kernel");
+}

@@ -45,8 +45,8 @@ int sm_count();
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t cols, uint64_t rows,
                  uint64_t row_pitch_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle);
 
-// 3-D map (dims innermost first) with byte strides for dims 1 and 2.
-int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, const uint64_t dims[3],
-                 const uint64_t strides_bytes[2], const uint32_t box[3], CUtensorMapSwizzle swizzle);
+// rank-D map (dims innermost first, rank <= 5) with byte strides for dims 1..rank-1.
+int make_tmap_nd(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int rank, const uint64_t* dims,
+                 const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle);
 
 }  // namespace qik
