@@ -272,7 +272,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const bool slab = t < n_slab;
       const int kv0 = slab ? t * kAttnBN : P + (t - n_slab) * kAttnBN;
       const int seg_end = slab ? P : kv_total;
-      const int lim = min(my_L, seg_end - 1);  // allowed: kv0 + c <= lim
+      const int lim_rel = min(my_L, seg_end - 1) - kv0;  // column c allowed iff c <= lim_rel (and key valid)
+      // key-valid bits of this tile: bit i of kvm[j] <-> column 32 j + i (4 warp ballots)
+      uint32_t kvm[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
+      if (has_kv) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int kv = kv0 + 32 * j + lane;
+          const bool valid = kv < seg_end && __ldg(kvb + kv) != 0;
+          kvm[j] = __ballot_sync(0xffffffffu, valid);
+        }
+      }
       float sv[kAttnBN];
 #pragma unroll
       for (int c = 0; c < kAttnBN / 32; ++c) {
@@ -281,14 +291,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) sv[c * 32 + j] = __uint_as_float(r[j]);
       }
-      float tmax = -INFINITY;
+      // raw scores stay unscaled; the scale is folded into the exponent below
+      float mx[8];
 #pragma unroll
-      for (int c = 0; c < kAttnBN; ++c) {
-        bool allowed = kv0 + c <= lim;
-        if (has_kv && allowed) allowed = __ldg(kvb + kv0 + c) != 0;
-        sv[c] = allowed ? sv[c] * a.qk_scale_log2 : -INFINITY;
-        tmax = fmaxf(tmax, sv[c]);
+      for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
+      if (lim_rel >= kAttnBN - 1 && !has_kv) {
+#pragma unroll
+        for (int c = 0; c < kAttnBN; ++c) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < kAttnBN; ++c) {
+          const bool allowed = (c <= lim_rel) && ((kvm[c >> 5] >> (c & 31)) & 1u);
+          sv[c] = allowed ? sv[c] : -INFINITY;
+          mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
+        }
       }
+      const float raw_max = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                  fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      const float tmax = raw_max * a.qk_scale_log2;  // scale > 0: max commutes with it
       // the running max moves (and O, l are rescaled) only when it grows by > 2^8
       float alpha = 1.0f;
       bool rescale_o = false;
@@ -297,16 +317,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         rescale_o = (m_run != -INFINITY);
         m_run = tmax;
       }
-      const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-      float psum = 0.0f;
+      const float neg_m = (m_run == -INFINITY) ? 0.0f : -m_run;
+      float ps[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       uint32_t pk[kAttnBN / 2];
 #pragma unroll
       for (int c = 0; c < kAttnBN; c += 2) {
-        const float p0 = ex2(sv[c] - m_use);
-        const float p1 = ex2(sv[c + 1] - m_use);
-        psum += p0 + p1;
+        const float p0 = ex2(fmaf(sv[c], a.qk_scale_log2, neg_m));
+        const float p1 = ex2(fmaf(sv[c + 1], a.qk_scale_log2, neg_m));
+        ps[(c >> 1) & 3] += p0 + p1;
         pk[c / 2] = pack_bf16x2(p0, p1);
       }
+      const float psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
       l_run = l_run * alpha + psum;
       // P buffer s is free once P.V of tile t-2 finished; O may be rescaled once
       // P.V of tile t-1 finished.
