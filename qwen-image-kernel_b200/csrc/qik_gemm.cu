@@ -41,24 +41,32 @@ struct GemmLayout {
   static constexpr int kABytes = kGemmBM * kGemmBK;
   static constexpr int kBBytes = BN * kGemmBK;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kStageOutOffset = STAGES * kStageBytes;  // 4 warps x 2 buffers x 4 KB
+  static constexpr int kOutBufBytes = 4096;                      // 32 rows x 32 cols x <= 4 B
+  static constexpr int kBarOffset = kStageOutOffset + 4 * 2 * kOutBufBytes;
   static constexpr int kBarBytes = (2 * STAGES + 4) * 8 + 16;
   static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;  // + alignment slack
   static constexpr int kTmemCols = 2 * BN;
 };
 
+// GELU, tanh form: 0.5 x (1 + tanh(u)), u = sqrt(2/pi) (x + 0.044715 x^3), evaluated
+// through the identity 0.5 (1 + tanh(u)) = 1 / (1 + e^(-2u)) with the MUFU exp2 and
+// reciprocal (PTX ex2.approx / rcp.approx, both within ~2 ulp of fp32): relative
+// accuracy stays at fp32 level on both tails, far below the bf16 rounding that follows.
 __device__ __forceinline__ float gelu_tanh_f32(float x) {
-  // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
-  const float k0 = 0.7978845608028654f;
+  const float k0 = 0.7978845608028654f;   // sqrt(2/pi)
   const float k1 = 0.044715f;
-  const float x3 = x * x * x;
-  return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x3)));
+  const float u = k0 * fmaf(k1 * x, x * x, x);
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(u * -2.8853900817779268f));  // e^(-2u) = 2^(-2u log2 e)
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+  return x * r;
 }
 
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const GemmParams p) {
+                    const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   using Lay = GemmLayout<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -88,6 +96,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Lay::kTmemCols);
@@ -160,28 +169,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // epilogue warps 2..5: TMEM lane quarter = warp % 4
+    // epilogue warps 2..5: TMEM lane quarter = warp % 4.  Each warp turns its 32
+    // accumulator rows into 32x32 output blocks: registers -> swizzled staging
+    // buffer (two per warp, alternating) -> one TMA tensor store per block, which
+    // writes whole rows coalesced and clips rows >= M / columns >= N.
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
     const float s = __ldg(p.scale_a) * __ldg(p.scale_b);
+    uint8_t* stage_out = smem + Lay::kStageOutOffset + quarter * 2 * Lay::kOutBufBytes;
     uint32_t amax_local = 0;
     int local = 0;
+    int buf = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status)) break;
       tc_fence_after();
       const int mb = tile / num_n, nb = tile % num_n;
-      const int row = mb * kGemmBM + row_in_tile;
-      const bool row_ok = row < p.M;
+      const int row0 = mb * kGemmBM + quarter * 32;
+      const bool row_ok = row0 + lane < p.M;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN + c * 32),
                   r);
         const int col0 = nb * BN + c * 32;
-        if (!row_ok || col0 >= p.N) continue;
-        const int ncols = min(32, p.N - col0);  // 16 or 32 (N % 16 == 0)
+        if (col0 >= p.N) continue;                    // warp-uniform
+        const int ncols = min(32, p.N - col0);        // 16 or 32 (N % 16 == 0)
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * s;
@@ -189,8 +203,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col0);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            if (q * 8 >= ncols) break;
-            const uint4 bb = __ldg(bp + q);
+            const uint4 bb = (q * 8 < ncols) ? __ldg(bp + q) : make_uint4(0u, 0u, 0u, 0u);
             const uint32_t bw[4] = {bb.x, bb.y, bb.z, bb.w};
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
@@ -199,13 +212,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
         }
+        // the staging buffer is free once at most one store (the other buffer's) is in flight
+        if (lane == 0) bulk_wait_read_1();
+        __syncwarp();
+        uint8_t* sb = stage_out + buf * Lay::kOutBufBytes;
         if (p.out_f32) {
-          float* dst = static_cast<float*>(p.C) + static_cast<int64_t>(row) * p.ldc + col0;
+          // 128-byte rows, 128-byte swizzle: 16-byte chunk q of row l at chunk q ^ (l & 7)
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            if (q * 4 >= ncols) break;
-            reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-          }
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(sb + lane * 128 + ((q ^ (lane & 7)) << 4)) =
+                make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
         } else {
           uint32_t w[16];
 #pragma unroll
@@ -217,25 +233,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             w[j] = pack_bf16x2(lo, hi);
           }
-          if (p.amax_out) {
+          if (p.amax_out && row_ok) {
             uint32_t m2 = 0;
 #pragma unroll
             for (int j = 0; j < 16; ++j)
               if (2 * j < ncols) m2 = __vmaxu2(m2, w[j] & 0x7FFF7FFFu);
             amax_local = max(amax_local, max(m2 & 0xFFFFu, m2 >> 16));
           }
-          __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.C) + static_cast<int64_t>(row) * p.ldc + col0;
+          // 64-byte rows, 64-byte swizzle: 16-byte chunk q of row l at chunk q ^ ((l >> 1) & 3)
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            if (q * 8 >= ncols) break;
-            reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-          }
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(sb + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) =
+                make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
         }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && row0 < p.M) {
+          tma_store_2d(&tmC, col0, row0, sb);
+          bulk_commit_group();
+        }
+        buf ^= 1;
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
+    if (lane == 0) bulk_wait_all();
     if (p.amax_out) {
       amax_local = __reduce_max_sync(0xffffffffu, amax_local);
       if (lane == 0 && amax_local != 0u) atomicMax(p.amax_out, amax_local << 16);
@@ -261,6 +284,14 @@ static int launch_gemm(const uint8_t* A, const uint8_t* B, const GemmParams& p, 
   rc = make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.N),
                     static_cast<uint64_t>(ldb), kGemmBK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
+  CUtensorMap tc;
+  if (p.out_f32)
+    rc = make_tmap_2d(&tc, p.C, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, static_cast<uint64_t>(p.N),
+                      static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.ldc) * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  else
+    rc = make_tmap_2d(&tc, p.C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<uint64_t>(p.N),
+                      static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.ldc) * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (rc) return rc;
   static bool attr_set[64] = {false};
   int dev = 0;
   QIK_TRY_CUDA(cudaGetDevice(&dev));
@@ -271,7 +302,7 @@ static int launch_gemm(const uint8_t* A, const uint8_t* B, const GemmParams& p, 
   }
   const int tiles = ((p.M + kGemmBM - 1) / kGemmBM) * ((p.N + BN - 1) / BN);
   const int grid = min(tiles, sm_count());
-  fp8_gemm_kernel<BN, STAGES><<<grid, kGemmThreads, Lay::kSmemBytes, st>>>(ta, tb, p);
+  fp8_gemm_kernel<BN, STAGES><<<grid, kGemmThreads, Lay::kSmemBytes, st>>>(ta, tb, tc, p);
   return check_launch("fp8_gemm_kernel");
 }
 

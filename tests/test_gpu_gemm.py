@@ -134,9 +134,16 @@ def test_gelu_epilogue_and_amax(fp8):
     h = fp8.fp8_gemm(xq, sx, wq, sw, epilogue=L.EPI_GELU_TANH, amax_out=amax)
     plain = fp8.fp8_gemm(xq, sx, wq, sw)
     torch.cuda.synchronize()
-    ref_h = torch.nn.functional.gelu(plain.float(), approximate="tanh").to(torch.bfloat16)
-    d = (h.float() - ref_h.float()).abs()
-    assert (d <= O.bf16_ulp(ref_h.float()) + 1e-6).all()
+    # GELU-tanh evaluated in fp64 on the kernel's own bf16 linear output, rounded to
+    # bf16; torch's fp32 form is also accepted within an absolute 1e-6 (it loses
+    # relative accuracy where 1 + tanh(u) cancels, x < -5).
+    xd = plain.double().cpu()
+    ref64 = 0.5 * xd * (1.0 + torch.tanh(0.7978845608028654 * (xd + 0.044715 * xd ** 3)))
+    ref_h = ref64.to(torch.bfloat16).float()
+    d = (h.cpu().float() - ref_h).abs()
+    assert (d <= O.bf16_ulp(ref_h) + 1e-6).all(), d.max().item()
+    torch_h = torch.nn.functional.gelu(plain.float(), approximate="tanh").to(torch.bfloat16).cpu().float()
+    assert ((h.cpu().float() - torch_h).abs() <= O.bf16_ulp(torch_h) + 1e-6).all()
     got_amax = np.array([amax.item()], dtype=np.int32).view(np.float32)[0]
     assert got_amax == h.float().abs().max().item()
 
