@@ -90,7 +90,7 @@ class ClockSampler:
         os.close(fd)
         self.fh = open(self.path, "w")
         self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
-                                      "--format=csv,noheader,nounits", "-lms", "200"],
+                                      "--format=csv,noheader,nounits", "-lms", "50"],
                                      stdout=self.fh, stderr=subprocess.DEVNULL)
         time.sleep(0.3)
         return self
@@ -162,6 +162,7 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
         return y
 
     launches_per_step = 5  # amax, pack, gemm (GELU+amax), pack, gemm
+    clk = ClockSampler(device.index if device.index is not None else 0).__enter__()
     for _ in range(args.warmup):
         step(x)
     torch.cuda.synchronize(device)
@@ -176,14 +177,15 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
                for _ in range(args.steps)]
     ev_k = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     barrier()
-    with ClockSampler(device.index if device.index is not None else 0) as clk:
-        for i in range(args.steps):
-            flush.fill_(float(i))
-            ev_step[i][0].record(stream)
-            step(x, ev_k[i])
-            ev_step[i][1].record(stream)
-        barrier()
+    for i in range(args.steps):
+        flush.fill_(float(i))
+        ev_step[i][0].record(stream)
+        step(x, ev_k[i])
+        ev_step[i][1].record(stream)
+    barrier()
+    clk.__exit__(None, None, None)
     clocks = clk.summary()
+    clocks["window"] = "sampled every 50 ms from before the warm-up to the end of the timed steps"
     t_steps = sum(a.elapsed_time(b) for a, b in ev_step) / 1e3            # seconds
     t_gemm = [ev[0].elapsed_time(ev[1]) for ev in ev_k] + [ev[2].elapsed_time(ev[3]) for ev in ev_k]
     gemm_ms = sum(t_gemm) / len(t_gemm)
@@ -205,6 +207,7 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
     barrier()
     t_e2e = sum(a.elapsed_time(b) for a, b in e2e_ev) / 1e3
 
+    ext = extras(device, flush) if (rank == 0 and not args.no_extras) else None
     status = L.device_status(device)
     t = torch.tensor([t_steps, t_e2e, gemm_ms, float(status)], dtype=torch.float64, device=device)
     if world > 1:
@@ -247,23 +250,116 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
                      "peak_source": pk["source"], "avg_launch_ms": round(gemm_ms, 4),
                      "flops_per_launch": FLOPS_PER_LINEAR},
         "gpu_launches": launches_per_step * args.steps * 2,
+        "gpu_launches_note": "qik kernels inside the timed regions (device-resident steps + e2e steps); "
+                             "the L2-flush fills and the 4-byte amax zeroing are torch's",
         "device_status": int(status),
         "clocks": clocks,
     }
+    if ext is not None:
+        out["extras"] = ext
     if world == 1:
         out["cpu_baseline"] = cpu_baseline(args)
     return out
 
 
 def traffic_from_profile():
-    """DRAM bytes per GEMM launch from the committed ncu summary, if present."""
-    p = ROOT / "profiles" / "fp8_gemm_ffn_cfg2.json"
+    """DRAM bytes per GEMM launch (read + write, averaged over the FFN's two GEMM
+    launches) from the committed ncu summary, if present."""
+    p = ROOT / "profiles" / "fp8_gemm_ffn_cfg2.md"
     if p.exists():
-        try:
-            return json.loads(p.read_text()).get("dram_bytes_per_launch")
-        except (OSError, ValueError):
-            return None
+        for line in p.read_text().splitlines():
+            if line.strip().startswith("dram_bytes_per_launch_avg"):
+                try:
+                    return int(line.split("=")[1].strip().split()[0])
+                except (IndexError, ValueError):
+                    return None
     return None
+
+
+# ------------------------------------------------------------------------------ extras
+def _time_ms(fn, iters: int, flush: torch.Tensor, stream) -> float:
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    for i in range(iters):
+        flush.fill_(float(i))
+        evs[i][0].record(stream)
+        fn()
+        evs[i][1].record(stream)
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs) / iters
+
+
+def extras(device: torch.device, flush: torch.Tensor, iters: int = 10) -> dict:
+    """Attention at BASELINE config 4 and the DiT-block time at 1024 px (configs[2] +
+    the t2i attention), each on synthetic inputs with the BASELINE shapes."""
+    from qik import fp8 as F
+    from qik import _lib as L
+    from qik.kv_cache import ContiguousKVCache
+    from qik.triton_attention import block_causal_flash_attention as attn
+    stream = torch.cuda.current_stream(device)
+    g = torch.Generator(device=device).manual_seed(7)
+    H, D = 24, 128
+    out = {}
+    # config 4, prefill form: 256 text (L = q) + 2304 cond (L = 2559) + 4096 target (L = 6655)
+    S = 6656
+    q, k, v = (torch.randn(1, S, H, D, device=device, generator=g, dtype=torch.bfloat16) for _ in range(3))
+    Lp = torch.arange(S, dtype=torch.int32, device=device)
+    Lp[256:2560] = 2559
+    Lp[2560:] = S - 1
+    fl = 4.0 * D * H * float((Lp.long() + 1).sum())
+    for _ in range(3):
+        attn(q, k, v, Lp, None)
+    ms = _time_ms(lambda: attn(q, k, v, Lp, None), iters, flush, stream)
+    out["attention_cfg4_prefill"] = {"ms": round(ms, 4), "tflops": round(fl / ms / 1e9, 1), "gflop": round(fl / 1e9, 1)}
+    # config 4, decode form: 4096 target queries over the e4m3-V slab (2560) + 4096 fresh
+    P, T = 2560, 4096
+    kp, vp = (torch.randn(1, P, H, D, device=device, generator=g, dtype=torch.bfloat16) for _ in range(2))
+    cache = ContiguousKVCache(1, 1, P, H, D, v_fp8=True, device=device)
+    cache.get_layer(0).store(kp, vp)
+    ck, cv, vs = cache.get_layer(0).views()
+    qd, kn, vn = (torch.randn(1, T, H, D, device=device, generator=g, dtype=torch.bfloat16) for _ in range(3))
+    Ld = torch.full((T,), P + T - 1, dtype=torch.int32, device=device)
+    fl = 4.0 * D * H * T * (P + T)
+    run = lambda: attn(qd, kn, vn, Ld, None, ck, cv, vs, uniform_full=True)  # noqa: E731
+    for _ in range(3):
+        run()
+    ms = _time_ms(run, iters, flush, stream)
+    out["attention_cfg4_decode_fp8_slab"] = {"ms": round(ms, 4), "tflops": round(fl / ms / 1e9, 1),
+                                             "gflop": round(fl / 1e9, 1)}
+    # DiT block @1024 px, CFG batch 2 (configs[2]): M = 2 x 4352; QKV, block-causal
+    # attention (256 text causal + 4096 image), out-proj, FFN (GELU-tanh), and the
+    # timestep modulation linear on M = 2.  Elementwise norm/RoPE/modulate/residual
+    # ops are not part of this path and are not timed.
+    M, K = 2 * 4352, 3072
+    lin = {}
+    for name, (n_out, n_in) in {"qkv": (9216, 3072), "out": (3072, 3072), "up": (12288, 3072),
+                                "down": (3072, 12288), "mod": (18432, 3072)}.items():
+        f = F.FP8Linear(n_in, n_out).to(device)
+        wq, sw = F.quantize_weight_tensorwise(torch.randn(n_out, n_in, device=device, generator=g) * 0.02)
+        f.weight.copy_(wq)
+        f.weight_scale.copy_(sw)
+        lin[name] = f
+    x = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
+    temb = torch.randn(2, K, device=device, generator=g).to(torch.bfloat16)
+    Lt = torch.arange(4352, dtype=torch.int32, device=device)
+    Lt[256:] = 4351
+
+    def block():
+        lin["mod"](temb)
+        qkv = lin["qkv"](x).view(2, 4352, 3, H, D)
+        o = attn(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2], Lt, None)
+        h = lin["out"](o.reshape(M, K))
+        return F.fp8_ffn_gelu(h, lin["up"], lin["down"])
+
+    for _ in range(3):
+        block()
+    ms = _time_ms(block, iters, flush, stream)
+    lin_fl = 2.0 * M * K * (9216 + 3072 + 12288) + 2.0 * M * 12288 * K + 2.0 * 2 * K * 18432
+    at_fl = 4.0 * D * H * 2 * float((Lt.long() + 1).sum())
+    out["dit_block_1024px_cfg2"] = {"ms": round(ms, 4), "tflops": round((lin_fl + at_fl) / ms / 1e9, 1),
+                                    "linear_gflop": round(lin_fl / 1e9, 1), "attention_gflop": round(at_fl / 1e9, 1),
+                                    "excluded": "elementwise norm/RoPE/modulate/residual ops"}
+    out["device_status"] = L.device_status(device)
+    return out
 
 
 # ------------------------------------------------------------------------------ CPU arm
@@ -326,6 +422,7 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["qik", "reference"], default="qik")
+    ap.add_argument("--no-extras", action="store_true", help="skip the attention / DiT-block measurements")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
