@@ -21,7 +21,8 @@ namespace qik {
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 128;  // e4m3 elements (= bytes) of K per pipeline stage
-constexpr int kGemmThreads = 192;
+constexpr int kGemmEpiWarps = 8;                  // two per TMEM lane quarter
+constexpr int kGemmThreads = 64 + 32 * kGemmEpiWarps;
 
 struct GemmParams {
   int M, N, K;
@@ -41,9 +42,9 @@ struct GemmLayout {
   static constexpr int kABytes = kGemmBM * kGemmBK;
   static constexpr int kBBytes = BN * kGemmBK;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStageOutOffset = STAGES * kStageBytes;  // 4 warps x 2 buffers x 4 KB
-  static constexpr int kOutBufBytes = 4096;                      // 32 rows x 32 cols x <= 4 B
-  static constexpr int kBarOffset = kStageOutOffset + 4 * 2 * kOutBufBytes;
+  static constexpr int kStageOutOffset = STAGES * kStageBytes;  // 8 warps x 2 buffers x 2 KB
+  static constexpr int kOutBufBytes = 2048;                      // 32 rows x 64 bytes
+  static constexpr int kBarOffset = kStageOutOffset + kGemmEpiWarps * 2 * kOutBufBytes;
   static constexpr int kBarBytes = (2 * STAGES + 4) * 8 + 16;
   static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;  // + alignment slack
   static constexpr int kTmemCols = 2 * BN;
@@ -90,7 +91,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], kGemmEpiWarps);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -169,14 +170,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // epilogue warps 2..5: TMEM lane quarter = warp % 4.  Each warp turns its 32
-    // accumulator rows into 32x32 output blocks: registers -> swizzled staging
-    // buffer (two per warp, alternating) -> one TMA tensor store per block, which
-    // writes whole rows coalesced and clips rows >= M / columns >= N.
+    // epilogue warps 2..9: TMEM lane quarter = warp % 4, two warps per quarter take
+    // alternate 32-column chunks.  Each warp turns its 32 accumulator rows into
+    // output blocks: registers -> swizzled staging buffer (two per warp, alternating)
+    // -> one TMA tensor store per block, which writes whole rows coalesced and clips
+    // rows >= M / columns >= N.
     const int quarter = warp & 3;
-    const int row_in_tile = quarter * 32 + lane;
+    const int half = (warp - 2) >> 2;
     const float s = __ldg(p.scale_a) * __ldg(p.scale_b);
-    uint8_t* stage_out = smem + Lay::kStageOutOffset + quarter * 2 * Lay::kOutBufBytes;
+    uint8_t* stage_out = smem + Lay::kStageOutOffset + (warp - 2) * 2 * Lay::kOutBufBytes;
     uint32_t amax_local = 0;
     int local = 0;
     int buf = 0;
@@ -189,7 +191,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int row0 = mb * kGemmBM + quarter * 32;
       const bool row_ok = row0 + lane < p.M;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half; c < BN / 32; c += 2) {
         uint32_t r[32];
         tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN + c * 32),
                   r);
@@ -212,16 +214,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
         }
-        // the staging buffer is free once at most one store (the other buffer's) is in flight
-        if (lane == 0) bulk_wait_read_1();
-        __syncwarp();
-        uint8_t* sb = stage_out + buf * Lay::kOutBufBytes;
         if (p.out_f32) {
-          // 128-byte rows, 128-byte swizzle: 16-byte chunk q of row l at chunk q ^ (l & 7)
+          // two 16-column blocks of 64-byte rows, 64-byte swizzle
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            *reinterpret_cast<float4*>(sb + lane * 128 + ((q ^ (lane & 7)) << 4)) =
-                make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          for (int hb = 0; hb < 2; ++hb) {
+            if (hb * 16 >= ncols) break;
+            if (lane == 0) bulk_wait_read_1();
+            __syncwarp();
+            uint8_t* sb = stage_out + buf * Lay::kOutBufBytes;
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              *reinterpret_cast<float4*>(sb + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) =
+                  make_float4(v[hb * 16 + 4 * q], v[hb * 16 + 4 * q + 1], v[hb * 16 + 4 * q + 2],
+                              v[hb * 16 + 4 * q + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && row0 < p.M) {
+              tma_store_2d(&tmC, col0 + hb * 16, row0, sb);
+              bulk_commit_group();
+            }
+            buf ^= 1;
+          }
         } else {
           uint32_t w[16];
 #pragma unroll
@@ -240,19 +253,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               if (2 * j < ncols) m2 = __vmaxu2(m2, w[j] & 0x7FFF7FFFu);
             amax_local = max(amax_local, max(m2 & 0xFFFFu, m2 >> 16));
           }
+          // the staging buffer is free once at most one store (the other buffer's) reads smem
+          if (lane == 0) bulk_wait_read_1();
+          __syncwarp();
+          uint8_t* sb = stage_out + buf * Lay::kOutBufBytes;
           // 64-byte rows, 64-byte swizzle: 16-byte chunk q of row l at chunk q ^ ((l >> 1) & 3)
 #pragma unroll
           for (int q = 0; q < 4; ++q)
             *reinterpret_cast<uint4*>(sb + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) =
                 make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && row0 < p.M) {
+            tma_store_2d(&tmC, col0, row0, sb);
+            bulk_commit_group();
+          }
+          buf ^= 1;
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0 && row0 < p.M) {
-          tma_store_2d(&tmC, col0, row0, sb);
-          bulk_commit_group();
-        }
-        buf ^= 1;
       }
       tc_fence_before();
       __syncwarp();
@@ -287,7 +304,7 @@ static int launch_gemm(const uint8_t* A, const uint8_t* B, const GemmParams& p, 
   CUtensorMap tc;
   if (p.out_f32)
     rc = make_tmap_2d(&tc, p.C, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, static_cast<uint64_t>(p.N),
-                      static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.ldc) * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+                      static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.ldc) * 4, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B);
   else
     rc = make_tmap_2d(&tc, p.C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<uint64_t>(p.N),
                       static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.ldc) * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
