@@ -54,6 +54,16 @@ size_t qik_quant_workspace_bytes(void);
 int qik_compute_scale(const void* x, int dtype, int64_t n, float* scale_out, void* ws, void* stream);
 
 /*
+ * max|x| accumulated into *amax_bits as the fp32 bit pattern (atomicMax; the caller
+ * zeroes it first): the `x.abs().amax()` of compute_scale
+ * (qwen_image_kernel/fp8.py:26).  Non-negative floats order like their bit
+ * patterns, so an integer MAX reduction of amax_bits across shards (e.g. a 4-byte
+ * all-reduce) yields the amax of the whole tensor; qik_quantize_act_from_amax then
+ * quantizes each shard with the global scale.
+ */
+int qik_amax(const void* x, int dtype, int64_t n, uint32_t* amax_bits, void* stream);
+
+/*
  * Dynamic per-tensor e4m3 activation quantization: scale as qik_compute_scale,
  * q[i] = e4m3_rn_satfinite(fl32(x[i]) * (1/scale)).  Replaces quantize_tensorwise
  * + _scale_cast_fp8_kernel (qwen_image_kernel/fp8.py:29-53).

@@ -289,6 +289,14 @@ int qik_compute_scale(const void* x, int dtype, int64_t n, float* scale_out, voi
   return check_launch("scale_finalize_kernel");
 }
 
+int qik_amax(const void* x, int dtype, int64_t n, uint32_t* amax_bits, void* stream) {
+  QIK_REQUIRE(x || n == 0, "qik_amax: x is NULL");
+  QIK_REQUIRE(amax_bits, "qik_amax: amax_bits is NULL");
+  QIK_REQUIRE(dtype == QIK_DTYPE_BF16 || dtype == QIK_DTYPE_F32, "qik_amax: dtype must be BF16 or F32");
+  QIK_REQUIRE(n >= 0, "qik_amax: negative n");
+  return launch_amax(x, dtype, n, amax_bits, static_cast<cudaStream_t>(stream));
+}
+
 int qik_quantize_act_from_amax(const void* x, int64_t n, const uint32_t* amax_bits, uint8_t* q, float* scale_out,
                                void* stream) {
   QIK_REQUIRE((x && q) || n == 0, "qik_quantize_act_from_amax: x/q is NULL");

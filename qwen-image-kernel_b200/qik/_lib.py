@@ -47,6 +47,7 @@ SIGNATURES = {
     "qik_last_error": (ctypes.c_char_p, []),
     "qik_quant_workspace_bytes": (ctypes.c_size_t, []),
     "qik_compute_scale": (_i32, [_vp, _i32, _i64, _vp, _vp, _vp]),
+    "qik_amax": (_i32, [_vp, _i32, _i64, _vp, _vp]),
     "qik_quantize_act": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp]),
     "qik_quantize_act_from_amax": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp]),
     "qik_quantize_act_noalloc": (_i32, [_vp, _i64, _vp, _vp, _vp]),

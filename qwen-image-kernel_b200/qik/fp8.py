@@ -70,6 +70,20 @@ def quantize_tensorwise(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return q, s
 
 
+def amax_bits(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """max|x| as the fp32 bit pattern in an int32 [1] tensor (accumulated into ``out``
+    with atomicMax when given, so several tensors can share one amax).  Integer MAX of
+    these bits across shards equals the bits of the global amax."""
+    _require_cuda(x, "x")
+    lib = L.load()
+    xc = x.contiguous()
+    if out is None:
+        out = torch.zeros(1, dtype=torch.int32, device=x.device)
+    with torch.cuda.device(x.device):
+        L.check(lib.qik_amax(xc.data_ptr(), _dtype_code(xc), xc.numel(), out.data_ptr(), L.stream_ptr()), "qik_amax")
+    return out
+
+
 def quantize_from_amax(x: torch.Tensor, amax_bits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """The pack half of quantize_tensorwise when a producer kernel already accumulated
     max|x| (fp32 bit pattern in ``amax_bits``, int32 [1])."""

@@ -1,0 +1,242 @@
+"""Multi-GPU execution of the FP8 DiT hot path: one process per GPU, torch.distributed.
+
+Two layouts (the reference itself is single-GPU; these follow the BASELINE configs):
+
+* **Shards** -- token rows (or the two CFG branches) are independent work: each rank
+  runs the unchanged single-GPU path on its own rows, with no collective on the data
+  path.  A per-tensor dynamic scale is a reduction over the whole tensor, so
+  ``quantize_sharded(..., global_amax=True)`` adds one 4-byte all-reduce(MAX) of the
+  amax bits; every shard is then quantized exactly as the 1-GPU run quantizes the
+  full tensor (fp32 bit patterns of |x| order like integers, so an int32 MAX is the
+  bits of the global amax).  Without it each shard is quantized like an independent
+  call of the reference (what the reference does per CFG branch).
+
+* **Tensor parallel block stack** -- weights are quantized once on the full tensor
+  and their e4m3 bytes are sharded, so every rank holds exactly the 1-GPU weights and
+  scale.  QKV (fused, 3 x heads) and FFN-up are column-parallel (QKV by heads, so
+  attention runs on local heads with no communication); attention-out and FFN-down
+  are row-parallel: their input scale needs the global amax (4-byte all-reduce MAX),
+  their fp32 partial products are summed with an NCCL all-reduce, and the bias is
+  added once after the sum.
+
+The arithmetic goes through an ``ops`` object: ``QikOps`` (the CUDA kernels, the
+default and the only product path) or a test double with the same methods.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from . import _lib as L
+
+
+class QikOps:
+    """The qik CUDA kernels behind the operations the parallel layer composes."""
+
+    def amax_bits(self, x: torch.Tensor) -> torch.Tensor:
+        from .fp8 import amax_bits
+        return amax_bits(x)
+
+    def pack(self, x: torch.Tensor, amax: torch.Tensor):
+        from .fp8 import quantize_from_amax
+        return quantize_from_amax(x, amax)
+
+    def gemm(self, xq, sx, wq, sw, bias=None, out_dtype=torch.bfloat16, epilogue=L.EPI_SCALE, amax_out=None):
+        from .fp8 import fp8_gemm
+        return fp8_gemm(xq, sx, wq, sw, bias=bias, out_dtype=out_dtype, epilogue=epilogue, amax_out=amax_out)
+
+    def zeros_amax(self, device) -> torch.Tensor:
+        return torch.zeros(1, dtype=torch.int32, device=device)
+
+    def attention(self, q, k, v, L):
+        from .triton_attention import block_causal_flash_attention
+        return block_causal_flash_attention(q, k, v, L, None)
+
+
+def _world(group) -> tuple[int, int]:
+    if not dist.is_available() or not dist.is_initialized():
+        return 0, 1
+    return dist.get_rank(group), dist.get_world_size(group)
+
+
+def row_range(n: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous balanced split of n rows: the first n % world ranks get one more."""
+    base, extra = divmod(n, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def allreduce_amax_(amax: torch.Tensor, group=None) -> torch.Tensor:
+    """In place: integer MAX of the amax bit patterns over the group."""
+    if _world(group)[1] > 1:
+        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=group)
+    return amax
+
+
+def quantize_sharded(x_local: torch.Tensor, group=None, global_amax: bool = True, ops=None):
+    """Dynamic per-tensor e4m3 quantization of this rank's rows.  With global_amax the
+    scale is the one of the full (concatenated) tensor."""
+    ops = ops or QikOps()
+    amax = ops.amax_bits(x_local)
+    if global_amax:
+        allreduce_amax_(amax, group)
+    return ops.pack(x_local, amax)
+
+
+# ------------------------------------------------------------------ weight sharding
+def shard_rows(w: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Output-feature (row) shard of a [N, K] weight for a column-parallel linear."""
+    n = w.shape[0]
+    if n % world:
+        raise ValueError(f"{n} output features do not split over {world} ranks")
+    step = n // world
+    return w[rank * step:(rank + 1) * step].contiguous()
+
+
+def shard_cols(w: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Input-feature (column) shard of a [N, K] weight for a row-parallel linear."""
+    k = w.shape[1]
+    if k % world:
+        raise ValueError(f"{k} input features do not split over {world} ranks")
+    step = k // world
+    return w[:, rank * step:(rank + 1) * step].contiguous()
+
+
+def shard_qkv_heads(w: torch.Tensor, heads: int, head_dim: int, rank: int, world: int) -> torch.Tensor:
+    """Rows of the fused QKV weight ([q; k; v], each heads * head_dim rows, the layout of
+    quantize_offline.py:80) that produce this rank's heads, as [q_l; k_l; v_l]."""
+    if heads % world:
+        raise ValueError(f"{heads} heads do not split over {world} ranks")
+    hl = heads // world
+    inner = heads * head_dim
+    if w.shape[0] != 3 * inner:
+        raise ValueError("fused QKV weight must have 3 * heads * head_dim rows")
+    raw = w.view(torch.uint8) if w.dtype == torch.float8_e4m3fn else w
+    parts = [raw[p * inner + rank * hl * head_dim: p * inner + (rank + 1) * hl * head_dim] for p in range(3)]
+    out = torch.cat(parts, 0).contiguous()
+    return out.view(w.dtype) if w.dtype == torch.float8_e4m3fn else out
+
+
+def shard_vector(b: torch.Tensor | None, rank: int, world: int) -> torch.Tensor | None:
+    if b is None:
+        return None
+    step = b.shape[0] // world
+    return b[rank * step:(rank + 1) * step].contiguous()
+
+
+def shard_qkv_bias(b: torch.Tensor | None, heads: int, head_dim: int, rank: int, world: int):
+    if b is None:
+        return None
+    return shard_qkv_heads(b[:, None], heads, head_dim, rank, world)[:, 0].contiguous()
+
+
+# ------------------------------------------------------------------ layers
+class ColumnParallelFP8Linear(nn.Module):
+    """y_local = x . W_local^T (+ b_local): this rank's output features.  The input is
+    the full activation, replicated on every rank, so every rank computes the same
+    dynamic scale without communicating."""
+
+    def __init__(self, weight: torch.Tensor, weight_scale: torch.Tensor, bias: torch.Tensor | None, ops=None):
+        super().__init__()
+        self.register_buffer("weight", weight)
+        self.register_buffer("weight_scale", weight_scale)
+        if bias is not None:
+            self.register_buffer("bias", bias)
+        else:
+            self.bias = None
+        self.ops = ops or QikOps()
+
+    @classmethod
+    def from_full(cls, weight, weight_scale, bias, rank, world, qkv_heads: tuple[int, int] | None = None, ops=None):
+        if qkv_heads is not None:
+            w = shard_qkv_heads(weight, qkv_heads[0], qkv_heads[1], rank, world)
+            b = shard_qkv_bias(bias, qkv_heads[0], qkv_heads[1], rank, world)
+        else:
+            w, b = shard_rows(weight, rank, world), shard_vector(bias, rank, world)
+        return cls(w, weight_scale.clone(), b, ops)
+
+    def forward(self, x: torch.Tensor, epilogue: int = L.EPI_SCALE, amax_out: torch.Tensor | None = None):
+        x2 = x.reshape(-1, x.shape[-1])
+        amax = self.ops.amax_bits(x2)
+        xq, sx = self.ops.pack(x2, amax)
+        return self.ops.gemm(xq, sx, self.weight, self.weight_scale, self.bias, epilogue=epilogue, amax_out=amax_out)
+
+
+class RowParallelFP8Linear(nn.Module):
+    """y = sum_ranks x_local . W_local^T (+ b): the input holds this rank's slice of the
+    input features.  The dynamic scale is global (4-byte all-reduce MAX of the amax
+    bits), the fp32 partial products are summed with an all-reduce, and the bias is
+    added once after the sum."""
+
+    def __init__(self, weight: torch.Tensor, weight_scale: torch.Tensor, bias: torch.Tensor | None, group=None,
+                 ops=None):
+        super().__init__()
+        self.register_buffer("weight", weight)
+        self.register_buffer("weight_scale", weight_scale)
+        if bias is not None:
+            self.register_buffer("bias", bias)
+        else:
+            self.bias = None
+        self.group = group
+        self.ops = ops or QikOps()
+
+    @classmethod
+    def from_full(cls, weight, weight_scale, bias, rank, world, group=None, ops=None):
+        return cls(shard_cols(weight, rank, world), weight_scale.clone(), bias, group, ops)
+
+    def forward_quantized(self, xq: torch.Tensor, sx: torch.Tensor) -> torch.Tensor:
+        part = self.ops.gemm(xq, sx, self.weight, self.weight_scale, None, out_dtype=torch.float32)
+        if _world(self.group)[1] > 1:
+            dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
+        if self.bias is not None:
+            part = part + self.bias.float()
+        return part.to(torch.bfloat16)
+
+    def forward(self, x_local: torch.Tensor, amax: torch.Tensor | None = None) -> torch.Tensor:
+        x2 = x_local.reshape(-1, x_local.shape[-1])
+        if amax is None:
+            amax = self.ops.amax_bits(x2)
+        allreduce_amax_(amax, self.group)
+        xq, sx = self.ops.pack(x2, amax)
+        return self.forward_quantized(xq, sx)
+
+
+def tp_ffn(x: torch.Tensor, up: ColumnParallelFP8Linear, down: RowParallelFP8Linear) -> torch.Tensor:
+    """down(gelu_tanh(up(x))) with up column-parallel and down row-parallel: the GELU
+    epilogue of the local up-projection accumulates the local amax of the hidden
+    activation, which one 4-byte all-reduce makes global before the pack."""
+    ops = up.ops
+    amax = ops.zeros_amax(x.device)
+    h = up(x, epilogue=L.EPI_GELU_TANH, amax_out=amax)
+    allreduce_amax_(amax, down.group)
+    hq, sh = ops.pack(h, amax)
+    return down.forward_quantized(hq, sh)
+
+
+class TPBlock(nn.Module):
+    """The linears + attention of one DiT block, tensor parallel over heads / hidden
+    features: QKV (column, by heads) -> block-causal attention on the local heads ->
+    attention-out (row) -> FFN up (column, GELU-tanh) -> FFN down (row)."""
+
+    def __init__(self, qkv, out, up, down, heads_local: int, head_dim: int):
+        super().__init__()
+        self.qkv, self.out, self.up, self.down = qkv, out, up, down
+        self.hl, self.d = heads_local, head_dim
+
+    @classmethod
+    def from_full(cls, full: dict, heads: int, head_dim: int, rank: int, world: int, group=None, ops=None):
+        """full: name -> (weight e4m3 [N, K], weight_scale [1], bias or None) for
+        'qkv', 'out', 'up', 'down' (unsharded, quantized once)."""
+        qkv = ColumnParallelFP8Linear.from_full(*full["qkv"], rank, world, qkv_heads=(heads, head_dim), ops=ops)
+        out = RowParallelFP8Linear.from_full(*full["out"], rank, world, group, ops)
+        up = ColumnParallelFP8Linear.from_full(*full["up"], rank, world, ops=ops)
+        down = RowParallelFP8Linear.from_full(*full["down"], rank, world, group, ops)
+        return cls(qkv, out, up, down, heads // world, head_dim)
+
+    def forward(self, x: torch.Tensor, batch: int, seq: int, prefix_lengths: torch.Tensor) -> torch.Tensor:
+        M = x.shape[0]
+        qkv = self.qkv(x).view(batch, seq, 3, self.hl, self.d)
+        o = self.qkv.ops.attention(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2], prefix_lengths)
+        h = self.out(o.reshape(M, self.hl * self.d))
+        return tp_ffn(h, self.up, self.down)
