@@ -208,6 +208,7 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
     t_e2e = sum(a.elapsed_time(b) for a, b in e2e_ev) / 1e3
 
     ext = extras(device, flush) if (rank == 0 and not args.no_extras) else None
+    tp = tp_stack(device, rank, world, flush) if not args.no_extras else None
     status = L.device_status(device)
     t = torch.tensor([t_steps, t_e2e, gemm_ms, float(status)], dtype=torch.float64, device=device)
     if world > 1:
@@ -257,6 +258,8 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
     }
     if ext is not None:
         out["extras"] = ext
+    if tp is not None:
+        out.setdefault("extras", {})["tp_stack_4block_1024px"] = tp
     if world == 1:
         out["cpu_baseline"] = cpu_baseline(args)
     return out
@@ -360,6 +363,60 @@ def extras(device: torch.device, flush: torch.Tensor, iters: int = 10) -> dict:
                                     "excluded": "elementwise norm/RoPE/modulate/residual ops"}
     out["device_status"] = L.device_status(device)
     return out
+
+
+def tp_stack(device: torch.device, rank: int, world: int, flush: torch.Tensor, iters: int = 5) -> dict:
+    """BASELINE configs[4]'s layer-stack case: 4 DiT blocks at 1024 px, CFG batch 2
+    (M = 8704), tensor parallel over `world` GPUs -- QKV by heads and FFN-up column-
+    parallel, attention on local heads, out-proj and FFN-down row-parallel with a
+    4-byte amax all-reduce(MAX) and an fp32 NCCL all-reduce(SUM) of the partial
+    products.  Strong scaling: the total work is fixed.  Time = max over ranks."""
+    from qik import fp8 as F
+    from qik import parallel as PX
+    H, D, K, HID, B, S = 24, 128, 3072, 12288, 2, 4352
+    g = torch.Generator(device=device).manual_seed(11)
+    blocks = []
+    for _ in range(4):
+        full = {}
+        for name, (n, kk) in {"qkv": (3 * H * D, K), "out": (K, H * D), "up": (HID, K), "down": (K, HID)}.items():
+            w = torch.randn(n, kk, device=device, generator=g) * 0.02
+            full[name] = (*F.quantize_weight_tensorwise(w), None)
+        blocks.append(PX.TPBlock.from_full(full, H, D, rank, world))
+    x = torch.randn(B * S, K, device=device, generator=g).to(torch.bfloat16)
+    Lt = torch.arange(S, dtype=torch.int32, device=device)
+    Lt[256:] = S - 1
+
+    def stack():
+        h = x
+        for blk in blocks:
+            h = blk(h, B, S, Lt)
+        return h
+
+    stream = torch.cuda.current_stream(device)
+    for _ in range(2):
+        stack()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    for i in range(iters):
+        flush.fill_(float(i))
+        evs[i][0].record(stream)
+        stack()
+        evs[i][1].record(stream)
+    torch.cuda.synchronize(device)
+    ms = torch.tensor([sum(a.elapsed_time(b) for a, b in evs) / iters], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+    ms = float(ms.item())
+    M = B * S
+    lin = 2.0 * M * K * (3 * H * D + K + HID) + 2.0 * M * HID * K
+    att = 4.0 * D * H * B * float((Lt.long() + 1).sum())
+    total = 4 * (lin + att)
+    return {"ms": round(ms, 4), "tflops_total": round(total / ms / 1e9, 1),
+            "tflops_per_gpu": round(total / ms / 1e9 / world, 1), "n_gpus": world, "scaling": "strong",
+            "collectives_per_stack": "8 x all-reduce(SUM) fp32 [8704, 3072] + 8 x all-reduce(MAX) 4 bytes"
+            if world > 1 else "none"}
 
 
 # ------------------------------------------------------------------------------ CPU arm
