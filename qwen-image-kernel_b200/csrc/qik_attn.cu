@@ -11,8 +11,9 @@
 //
 // One CTA per (128-query tile, b, h):
 //   warp 0     TMA producer: Q once (two 64-column halves, 128-byte swizzle), then
-//              per key tile K (bf16) and V (bf16, or e4m3 raw for the fp8 slab)
-//              into a 2-stage ring;
+//              K tiles into a 3-stage ring (freed as soon as S = Q K^T completes)
+//              and V tiles (bf16, or e4m3 raw for the fp8 slab) into a 2-stage ring
+//              (freed after P.V), V lagging K by one tile so K runs ahead;
 //   warp 1     MMA issuer (one thread): S_t = Q K_t^T (kind::f16, M=N=128, K=16 x 8)
 //              into a double-buffered TMEM S, then O += P_t V_t with P_t read from
 //              TMEM (A operand) and V_t from shared memory (MN-major B operand);
@@ -34,14 +35,13 @@ constexpr int kAttnThreads = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when the max grows by > 2^8
 
 struct AttnSmem {
-  static constexpr int kQ = 0;            // 32 KB: two 16 KB halves (d 0-63, d 64-127)
-  static constexpr int kStage0 = 32768;
-  static constexpr int kK = 0;            // per stage: K bf16 32 KB
-  static constexpr int kV = 32768;        //            V bf16 32 KB
-  static constexpr int kV8 = 65536;       //            V e4m3 raw 16 KB
-  static constexpr int kStageBytes = 81920;
-  static constexpr int kStages = 2;
-  static constexpr int kBar = kStage0 + kStages * kStageBytes;
+  static constexpr int kQ = 0;                    // 32 KB: two 16 KB halves (d 0-63, d 64-127)
+  static constexpr int kKStages = 3;
+  static constexpr int kVStages = 2;
+  static constexpr int kK0 = 32768;               // K ring: 3 x 32 KB
+  static constexpr int kV0 = kK0 + kKStages * 32768;   // V ring: 2 x 32 KB (bf16)
+  static constexpr int kV80 = kV0 + kVStages * 32768;  // raw e4m3 V: 2 x 16 KB
+  static constexpr int kBar = kV80 + kVStages * 16384;
   static constexpr int kBytes = kBar + 256 + 1024;  // barriers + alignment slack
 };
 
@@ -73,14 +73,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + AttnSmem::kBar);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;    // [2]
-  uint64_t* v_full = bars + 3;    // [2] V bf16 ready (TMA or converters)
-  uint64_t* v8_full = bars + 5;   // [2] raw e4m3 V landed
-  uint64_t* kv_empty = bars + 7;  // [2] stage free (after P.V)
-  uint64_t* s_full = bars + 9;    // [2]
-  uint64_t* p_full = bars + 11;   // [2]
-  uint64_t* pv_done = bars + 13;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* k_full = bars + 1;    // [3]
+  uint64_t* k_empty = bars + 4;   // [3] K stage free (after S = Q K^T)
+  uint64_t* v_full = bars + 7;    // [2] V bf16 ready (TMA or converters)
+  uint64_t* v8_full = bars + 9;   // [2] raw e4m3 V landed
+  uint64_t* v_empty = bars + 11;  // [2] V stage free (after P.V)
+  uint64_t* s_full = bars + 13;   // [2]
+  uint64_t* p_full = bars + 15;   // [2]
+  uint64_t* pv_done = bars + 17;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* lmax_slot = reinterpret_cast<int*>(tmem_slot + 2);
 
@@ -98,11 +99,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < AttnSmem::kKStages; ++s) {
       mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&v_full[s], 1);
       mbar_init(&v8_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&p_full[s], 4);
       mbar_init(&pv_done[s], 1);
@@ -137,7 +141,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int n_tiles = n_slab + n_fresh;
 
   uint8_t* sQ = smem + AttnSmem::kQ;
-  auto stage_ptr = [&](int s) { return smem + AttnSmem::kStage0 + s * AttnSmem::kStageBytes; };
+  auto k_ptr = [&](int s) { return smem + AttnSmem::kK0 + s * 32768; };
+  auto v_ptr = [&](int s) { return smem + AttnSmem::kV0 + s * 32768; };
+  auto v8_ptr = [&](int s) { return smem + AttnSmem::kV80 + s * 16384; };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -145,21 +151,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tma_prefetch_desc(&tm_q);
       mbar_arrive_expect_tx(q_full, 32768);
       load_bf16_tile(&tm_q, sQ, m0, h, b, q_full);
-      for (int t = 0; t < n_tiles; ++t) {
-        const int s = t & 1;
-        const uint32_t ph = (t >> 1) & 1;
-        if (!mbar_wait(&kv_empty[s], ph ^ 1u, abort_flag, a.status)) break;
-        uint8_t* st = stage_ptr(s);
-        const bool slab = t < n_slab;
-        const int key0 = slab ? t * kAttnBN : (t - n_slab) * kAttnBN;
-        mbar_arrive_expect_tx(&k_full[s], 32768);
-        load_bf16_tile(slab ? &tm_ck : &tm_k, st + AttnSmem::kK, key0, h, b, &k_full[s]);
-        if (slab && v_fp8) {
-          mbar_arrive_expect_tx(&v8_full[s], 16384);
-          tma_load_4d(st + AttnSmem::kV8, &tm_cv, 0, key0, h, b, &v8_full[s]);
-        } else {
-          mbar_arrive_expect_tx(&v_full[s], 32768);
-          load_bf16_tile(slab ? &tm_cv : &tm_v, st + AttnSmem::kV, key0, h, b, &v_full[s]);
+      // step u: K of tile u, then V of tile u - 1
+      for (int u = 0; u <= n_tiles; ++u) {
+        if (u < n_tiles) {
+          const int ks = u % AttnSmem::kKStages;
+          const uint32_t kph = (u / AttnSmem::kKStages) & 1;
+          if (!mbar_wait(&k_empty[ks], kph ^ 1u, abort_flag, a.status)) break;
+          const bool slab = u < n_slab;
+          const int key0 = slab ? u * kAttnBN : (u - n_slab) * kAttnBN;
+          mbar_arrive_expect_tx(&k_full[ks], 32768);
+          load_bf16_tile(slab ? &tm_ck : &tm_k, k_ptr(ks), key0, h, b, &k_full[ks]);
+        }
+        const int t = u - 1;
+        if (t >= 0) {
+          const int vs = t & 1;
+          const uint32_t vph = (t >> 1) & 1;
+          if (!mbar_wait(&v_empty[vs], vph ^ 1u, abort_flag, a.status)) break;
+          const bool slab = t < n_slab;
+          const int key0 = slab ? t * kAttnBN : (t - n_slab) * kAttnBN;
+          if (slab && v_fp8) {
+            mbar_arrive_expect_tx(&v8_full[vs], 16384);
+            tma_load_4d(v8_ptr(vs), &tm_cv, 0, key0, h, b, &v8_full[vs]);
+          } else {
+            mbar_arrive_expect_tx(&v_full[vs], 32768);
+            load_bf16_tile(slab ? &tm_cv : &tm_v, v_ptr(vs), key0, h, b, &v_full[vs]);
+          }
         }
       }
     }
@@ -179,7 +195,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (!mbar_wait(&p_full[s], ph, abort_flag, a.status)) return false;
         if (!mbar_wait(&v_full[s], ph, abort_flag, a.status)) return false;
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(stage_ptr(s) + AttnSmem::kV);
+        const uint32_t v_addr = smem_u32(v_ptr(s));
 #pragma unroll
         for (int k = 0; k < kAttnBN / 16; ++k) {
           // 16 keys per step: V rows [16k, 16k+16) (2048 B); d halves 16 KB apart
@@ -187,18 +203,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           umma_f16_ts(tO, tP[s] + k * 8, vd, idesc_o, (t > 0 || k > 0) ? 1u : 0u);
         }
         umma_commit(&pv_done[s]);
-        umma_commit(&kv_empty[s]);
+        umma_commit(&v_empty[s]);
         return true;
       };
       for (int t = 0; ok && t < n_tiles; ++t) {
         const int s = t & 1;
-        const uint32_t ph = (t >> 1) & 1;
-        if (!mbar_wait(&k_full[s], ph, abort_flag, a.status)) {
+        const int ks = t % AttnSmem::kKStages;
+        if (!mbar_wait(&k_full[ks], (t / AttnSmem::kKStages) & 1, abort_flag, a.status)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(stage_ptr(s) + AttnSmem::kK);
+        const uint32_t k_addr = smem_u32(k_ptr(ks));
 #pragma unroll
         for (int k = 0; k < kAttnD / 16; ++k) {
           const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
@@ -207,6 +223,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           umma_f16_ss(tS[s], qd, kd, idesc_s, k > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[s]);
+        umma_commit(&k_empty[ks]);
         if (t > 0 && !issue_pv(t - 1)) {
           ok = false;
           break;
@@ -223,8 +240,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int s = t & 1;
         const uint32_t ph = (t >> 1) & 1;
         if (!mbar_wait(&v8_full[s], ph, abort_flag, a.status)) break;
-        const uint8_t* raw = stage_ptr(s) + AttnSmem::kV8;
-        uint8_t* dst = stage_ptr(s) + AttnSmem::kV;
+        const uint8_t* raw = v8_ptr(s);
+        uint8_t* dst = v_ptr(s);
         // 2048 chunks of 8 values: chunk g -> key row g / 16, d-chunk g % 16; the
         // bf16 tile is written in the 128-byte-swizzled layout TMA would produce.
         for (int g = ct; g < 2048; g += 64) {
