@@ -219,7 +219,7 @@ def build_prefix_lengths(segments, prefix_len: int, seq_len: int) -> torch.Tenso
 
 def block_causal_attention(query, key, value, prefix_lengths, key_valid=None, cache_k=None,
                            cache_v=None, cache_v_scale=None, heads=None,
-                           out_dtype=torch.bfloat16) -> torch.Tensor:
+                           out_dtype=torch.bfloat16, slab_v_bf16: bool = True) -> torch.Tensor:
     """reference_block_causal_attention (triton_attention.py:266-293) on the CPU in fp32,
     extended with the fp8 slab-V dequant of the kernel (triton_attention.py:154-159):
     slab V = bf16(fl32(v8) * vsc[b, h]).  Computed head by head to bound memory.
@@ -229,14 +229,17 @@ def block_causal_attention(query, key, value, prefix_lengths, key_valid=None, ca
     [B,P,H,D] bf16 or e4m3 (then cache_v_scale [B,H] fp32).  Rows with no allowed key
     produce zeros (the kernel's `l == 0` epilogue, triton_attention.py:166).
     Returns [B,SQ,H,D] in ``out_dtype`` (bf16 like the reference, or fp32 for
-    tolerance checks on the pre-cast values).
+    tolerance checks on the pre-cast values).  ``slab_v_bf16=False`` keeps the slab V
+    dequant in fp32 (fl32(v8) * vsc, the BASELINE's fp32 dequant path) instead of
+    the reference kernel's per-element bf16 rounding.
     """
     B, SQ, H, D = query.shape
     P = 0 if cache_k is None else cache_k.shape[1]
     if cache_v is not None and cache_v.dtype == torch.float8_e4m3fn:
         assert cache_v_scale is not None
         cv = cache_v.detach().cpu().float() * cache_v_scale.detach().cpu().float()[:, None, :, None]
-        cache_v = cv.to(torch.bfloat16)
+        cache_v = cv.to(torch.bfloat16) if slab_v_bf16 else cv
+        value = value if slab_v_bf16 else value.detach().cpu().float()
     k_all = key if cache_k is None else torch.cat([cache_k.cpu(), key.cpu()], dim=1)
     v_all = value if cache_v is None else torch.cat([cache_v.cpu(), value.cpu()], dim=1)
     KV = k_all.shape[1]

@@ -5,9 +5,14 @@
 // (qwen_image_kernel/triton_attention.py:35-260): query row r of (b, h) attends to
 // the keys kv of the virtual concatenation [cache (P keys) ; fresh (SN keys)] with
 // kv <= L[r] (all keys when UNIFORM) and key_valid[b, kv] != 0 (when given);
-// softmax in base 2 with the scores scaled by sm_scale * log2(e); the e4m3 slab V
-// is dequantized as bf16(fl32(v8) * scale[b, h]) (triton_attention.py:154-159); P
-// is rounded to bf16 before P.V; fp32 accumulation; rows with no allowed key are 0.
+// softmax in base 2 with the scores scaled by sm_scale * log2(e); P is rounded to
+// bf16 before P.V; fp32 accumulation; rows with no allowed key are 0.
+// e4m3 slab V (triton_attention.py:154-159, which rounds fl32(v8) * scale[b, h] to
+// bf16 per element): here the slab tiles multiply e4m3-exact f16 V by f16 P (a
+// finer rounding of P than bf16) and the per-(b, h) scale multiplies the fp32
+// accumulator once at the slab -> fresh boundary, i.e. the exact fp32 dequant
+// product fl32(v8) * scale; the difference to the reference kernel's bf16 rounding
+// of each dequantized V element is below half a bf16 ulp of V.
 //
 // One CTA per (128-query tile, b, h):
 //   warp 0     TMA producer: Q once (two 64-column halves, 128-byte swizzle), then
@@ -17,7 +22,7 @@
 //   warp 1     MMA issuer (one thread): S_t = Q K_t^T (kind::f16, M=N=128, K=16 x 8)
 //              into a double-buffered TMEM S, then O += P_t V_t with P_t read from
 //              TMEM (A operand) and V_t from shared memory (MN-major B operand);
-//   warps 2-3  e4m3 -> bf16 V converters for slab tiles when V is fp8;
+//   warps 2-3  e4m3 -> f16 V converters for slab tiles when V is fp8 (exact);
 //   warps 4-7  softmax: thread = query row; reads S_t from TMEM, masks, online
 //              max/sum (the accumulator O is rescaled in TMEM only when the running
 //              max grows by more than 2^8, which leaves the final O/l unchanged),
@@ -183,7 +188,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_tiles > 0) {
       constexpr uint32_t idesc_s = idesc_f32acc(1, 1, 0, 0, kAttnBM, kAttnBN);
-      constexpr uint32_t idesc_o = idesc_f32acc(1, 1, 0, 1, kAttnBM, kAttnD);
+      constexpr uint32_t idesc_o = idesc_f32acc(1, 1, 0, 1, kAttnBM, kAttnD);      // bf16 P, bf16 V
+      constexpr uint32_t idesc_o16 = idesc_f32acc(0, 0, 0, 1, kAttnBM, kAttnD);    // f16 P, f16 V (fp8 slab)
       const uint32_t tS[2] = {tmem + 0u, tmem + 128u};
       const uint32_t tO = tmem + 256u;
       const uint32_t tP[2] = {tmem + 384u, tmem + 448u};
@@ -200,7 +206,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int k = 0; k < kAttnBN / 16; ++k) {
           // 16 keys per step: V rows [16k, 16k+16) (2048 B); d halves 16 KB apart
           const uint64_t vd = sdesc_sw128(v_addr + k * 2048, 16384, 1024);
-          umma_f16_ts(tO, tP[s] + k * 8, vd, idesc_o, (t > 0 || k > 0) ? 1u : 0u);
+          umma_f16_ts(tO, tP[s] + k * 8, vd, (v_fp8 && t < n_slab) ? idesc_o16 : idesc_o, (t > 0 || k > 0) ? 1u : 0u);
         }
         umma_commit(&pv_done[s]);
         umma_commit(&v_empty[s]);
@@ -234,7 +240,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else if (warp < 4) {
     // ------------------------------------------------------------ V converters
     if (v_fp8 && n_slab > 0) {
-      const float vsc = __ldg(a.v_scale + static_cast<int64_t>(b) * a.H + h);
       const int ct = threadIdx.x - 64;  // 0..63
       for (int t = 0; t < n_slab; ++t) {
         const int s = t & 1;
@@ -242,25 +247,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (!mbar_wait(&v8_full[s], ph, abort_flag, a.status)) break;
         const uint8_t* raw = v8_ptr(s);
         uint8_t* dst = v_ptr(s);
-        // 2048 chunks of 8 values: chunk g -> key row g / 16, d-chunk g % 16; the
-        // bf16 tile is written in the 128-byte-swizzled layout TMA would produce.
+        // 2048 chunks of 8 values: chunk g -> key row g / 16, d-chunk g % 16; the f16
+        // tile is written in the 128-byte-swizzled layout TMA would produce.
         for (int g = ct; g < 2048; g += 64) {
           const int r = g >> 4, dc = g & 15;
           const uint2 w = *reinterpret_cast<const uint2*>(raw + r * 128 + dc * 8);
-          const uint32_t bytes[2] = {w.x, w.y};
-          uint32_t o[4];
-#pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            const uint32_t h0 = cvt_e4m3x2_to_f16x2(static_cast<uint16_t>(bytes[i] & 0xFFFFu));
-            const uint32_t h1 = cvt_e4m3x2_to_f16x2(static_cast<uint16_t>(bytes[i] >> 16));
-            const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&h0));
-            const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&h1));
-            o[2 * i] = pack_bf16x2(f0.x * vsc, f0.y * vsc);
-            o[2 * i + 1] = pack_bf16x2(f1.x * vsc, f1.y * vsc);
-          }
           const int hd = dc >> 3, c = dc & 7;
           *reinterpret_cast<uint4*>(dst + hd * 16384 + r * 128 + ((c ^ (r & 7)) << 4)) =
-              make_uint4(o[0], o[1], o[2], o[3]);
+              make_uint4(cvt_e4m3x2_to_f16x2(static_cast<uint16_t>(w.x & 0xFFFFu)),
+                         cvt_e4m3x2_to_f16x2(static_cast<uint16_t>(w.x >> 16)),
+                         cvt_e4m3x2_to_f16x2(static_cast<uint16_t>(w.y & 0xFFFFu)),
+                         cvt_e4m3x2_to_f16x2(static_cast<uint16_t>(w.y >> 16)));
         }
         fence_proxy_async_smem();
         named_bar_sync(1, 64);
@@ -278,6 +275,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint8_t* kvb = has_kv ? a.key_valid + static_cast<int64_t>(b) * a.kv_sb : nullptr;
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
+    // fp8 slab: the per-(b, h) V scale is applied to O once, after the last slab tile
+    const bool slab_f16 = v_fp8 && n_slab > 0;
+    const float vsc = slab_f16 ? __ldg(a.v_scale + static_cast<int64_t>(b) * a.H + h) : 1.0f;
+    bool vsc_applied = !slab_f16;
     for (int t = 0; t < n_tiles; ++t) {
       const int s = t & 1;
       const uint32_t ph = (t >> 1) & 1;
@@ -342,7 +343,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const float p0 = ex2(fmaf(sv[c], a.qk_scale_log2, neg_m));
         const float p1 = ex2(fmaf(sv[c + 1], a.qk_scale_log2, neg_m));
         ps[(c >> 1) & 3] += p0 + p1;
-        pk[c / 2] = pack_bf16x2(p0, p1);
+        pk[c / 2] = (slab_f16 && slab) ? pack_f16x2(p0, p1) : pack_bf16x2(p0, p1);
       }
       const float psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
       l_run = l_run * alpha + psum;
@@ -352,20 +353,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         ok = false;
         break;
       }
-      if (rescale_o && t >= 1) {
+      const bool boundary = !vsc_applied && t == n_slab;  // first fresh tile after the fp8 slab
+      if ((rescale_o || boundary) && t >= 1) {
         if (!mbar_wait(&pv_done[(t - 1) & 1], ((t - 1) >> 1) & 1, abort_flag, a.status)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        const float f = (rescale_o ? alpha : 1.0f) * (boundary ? vsc : 1.0f);
 #pragma unroll
         for (int c = 0; c < kAttnD / 32; ++c) {
           uint32_t r[32];
           tmem_ld32(tO + c * 32, r);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * alpha);
+          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * f);
           tmem_st32(tO + c * 32, r);
         }
+        if (boundary) vsc_applied = true;
       }
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
@@ -399,7 +403,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     if (grow < a.SQ) {
       const bool nz = have_o && l_run > 0.0f;
-      const float inv = nz ? 1.0f / l_run : 0.0f;
+      const float inv = nz ? (vsc_applied ? 1.0f : vsc) / l_run : 0.0f;
       __nv_bfloat16* dst = a.out + static_cast<int64_t>(b) * a.o_sb + static_cast<int64_t>(grow) * a.o_ss +
                            static_cast<int64_t>(h) * a.o_sh;
 #pragma unroll

@@ -54,6 +54,9 @@ def test_golden_cases(attn, golden_dir, name):
                                                 vsc.cuda(), uniform_full=True)
         ref32 = O.block_causal_attention(c["q"], c["k"], c["v"], c["L"], c["key_valid"], c["cache_k"], v8, vsc,
                                          out_dtype=torch.float32)
+        exact = O.block_causal_attention(c["q"], c["k"], c["v"], c["L"], c["key_valid"], c["cache_k"], v8, vsc,
+                                         out_dtype=torch.float32, slab_v_bf16=False)
+        _check(out.cpu(), exact, tag=name + " vs fp32 dequant")
     else:
         out = attn.block_causal_flash_attention(c["q"].cuda(), c["k"].cuda(), c["v"].cuda(), c["L"].cuda(),
                                                 _cuda(c["key_valid"]), _cuda(c["cache_k"]), _cuda(c["cache_v"]))
@@ -140,6 +143,9 @@ def test_fp8_slab_through_kv_cache(attn):
     torch.cuda.synchronize()
     ref32 = O.block_causal_attention(q, kn, vn, L, None, ck8.cpu(), cv8.cpu(), vs.cpu(), out_dtype=torch.float32)
     _check(out8, ref32, tag="fp8 slab")
+    exact = O.block_causal_attention(q, kn, vn, L, None, ck8.cpu(), cv8.cpu(), vs.cpu(), out_dtype=torch.float32,
+                                     slab_v_bf16=False)
+    _check(out8, exact, tag="fp8 slab vs fp32 dequant")
     assert O.relf(out8.cpu(), out16.cpu()) < 0.03
 
 
@@ -181,6 +187,9 @@ def test_cfg4_decode_form_fp8_slab(attn):
     ref32 = O.block_causal_attention(q, kn, vn, L, None, ck.cpu(), cv.cpu(), vs.cpu(), heads=heads,
                                      out_dtype=torch.float32)
     _check(out, ref32, heads=heads, tag="cfg4 decode fp8 slab")
+    exact = O.block_causal_attention(q, kn, vn, L, None, ck.cpu(), cv.cpu(), vs.cpu(), heads=heads,
+                                     out_dtype=torch.float32, slab_v_bf16=False)
+    _check(out, exact, heads=heads, tag="cfg4 decode fp8 slab vs fp32 dequant")
 
 
 def test_edge_rows_and_ragged_tiles(attn):
@@ -203,6 +212,28 @@ def test_edge_rows_and_ragged_tiles(attn):
     ref32 = O.block_causal_attention(q, kn, vn, L, kv, ck, cv, out_dtype=torch.float32)
     _check(out, ref32, tag="edge")
     assert (out[:, :5].float() == 0).all()
+
+
+def test_fp8_slab_rows_ending_inside_slab(attn):
+    """Block-causal rows over an fp8-V slab where some query tiles never reach the
+    fresh keys (their whole range lies in the slab) and others cross the boundary."""
+    from qik.kv_cache import ContiguousKVCache
+    H, P, SN, SQ = 2, 300, 100, 260
+    kp = GI.randn_bf16(71, (1, P, H, 128))
+    vp = GI.randn_bf16(72, (1, P, H, 128))
+    q = GI.randn_bf16(73, (1, SQ, H, 128), 0.5)
+    kn = GI.randn_bf16(74, (1, SN, H, 128), 0.5)
+    vn = GI.randn_bf16(75, (1, SN, H, 128), 0.5)
+    cache = ContiguousKVCache(1, 1, P, H, 128, v_fp8=True, device="cuda")
+    cache.get_layer(0).store(kp.cuda(), vp.cuda())
+    ck, cv, vs = cache.get_layer(0).views()
+    L = torch.arange(SQ, dtype=torch.int32)            # rows 0..127 end inside the slab
+    L[200:] = P + SN - 1
+    out = attn.block_causal_flash_attention(q.cuda(), kn.cuda(), vn.cuda(), L.cuda(), None, ck, cv, vs)
+    torch.cuda.synchronize()
+    exact = O.block_causal_attention(q, kn, vn, L, None, ck.cpu(), cv.cpu(), vs.cpu(), out_dtype=torch.float32,
+                                     slab_v_bf16=False)
+    _check(out, exact, tag="fp8 slab partial")
 
 
 def test_status_word_clean(attn):
