@@ -133,6 +133,26 @@ int qik_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64
                  const float* scale_a, const float* scale_b, const void* bias, void* C, int64_t ldc, int out_dtype,
                  int epilogue, uint32_t* amax_out, int* status, void* stream);
 
+/*
+ * Bytes of workspace qik_fp8_ffn needs for an [M, K] input and a hidden width.
+ */
+size_t qik_fp8_ffn_workspace_bytes(int64_t M, int64_t K, int64_t hidden);
+
+/*
+ * DiT FFN pair y = down(gelu_tanh(up(x))), both linears FP8 per-tensor with the
+ * hidden activation re-quantized dynamically: two FP8Linear.forward calls
+ * (qwen_image_kernel/fp8.py:78-90) with GELU-tanh between them, run as one chain
+ * of five kernels (amax, pack, GEMM+GELU+amax, pack, GEMM) with programmatic
+ * dependent launches.
+ *   x: [M, K] bf16 row-major; w_up: [hidden, K] e4m3, s_up: 1 fp32, b_up: hidden bf16
+ *   or NULL; w_down: [K, hidden] e4m3, s_down, b_down likewise; y: [M, K] bf16.
+ *   ws: qik_fp8_ffn_workspace_bytes(M, K, hidden) bytes, 256-byte aligned (holds the
+ *   quantized input, the bf16 and e4m3 hidden activations and the scales).
+ */
+int qik_fp8_ffn(const void* x, int64_t M, int64_t K, int64_t hidden, const uint8_t* w_up, const float* s_up,
+                const void* b_up, const uint8_t* w_down, const float* s_down, const void* b_down, void* y, void* ws,
+                size_t ws_bytes, int* status, void* stream);
+
 /* Attention flags. */
 #define QIK_ATTN_HAS_CACHE 1     /* keys/values = virtual concat [cache ; fresh] */
 #define QIK_ATTN_HAS_KEY_VALID 2 /* per-(batch, key) validity bytes */

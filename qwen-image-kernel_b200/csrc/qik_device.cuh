@@ -247,6 +247,16 @@ __host__ __device__ constexpr uint32_t idesc_f32acc(uint32_t a_fmt, uint32_t b_f
          ((M >> 4) << 24);
 }
 
+// ---------------------------------------------------------------- launch chaining
+// Programmatic dependent launch: a kernel launched with the programmatic stream
+// serialization attribute may start while its predecessor in the stream is still
+// running; pdl_wait() blocks until the predecessor grid has completed and its
+// writes are visible.  pdl_trigger() lets the successor grid be scheduled once
+// every CTA of this grid has triggered or exited.  Both are no-ops for kernels
+// launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- numerics
 // fp32 pair -> e4m3 pair, round to nearest even, saturating to +-448 (NaN -> NaN).
 __device__ __forceinline__ uint16_t cvt_e4m3x2(float lo, float hi) {

@@ -1,0 +1,64 @@
+// qik_ffn.cu -- the DiT FFN pair as one chain of launches.
+//
+// y = down(gelu_tanh(up(x))) with both linears FP8 per-tensor: two applications of
+// FP8Linear.forward (qwen_image_kernel/fp8.py:78-90) with GELU-tanh between them
+// (the reference block uses SwiGLU through a fused up
+// projection, processors.py:180-187), the hidden activation re-quantized
+// dynamically.  Five kernels in one stream:
+//   amax(x) -> pack(x) -> GEMM1 (+GELU, amax(h)) -> pack(h) -> GEMM2
+// Every kernel after the first is launched as a programmatic dependent of its
+// predecessor, so its launch and set-up (TMEM allocation, barrier init, descriptor
+// prefetch) overlap the predecessor's tail; each waits for the predecessor's
+// results before reading them.  The intermediates live in the caller's workspace.
+#include "qik_device.cuh"
+#include "qik_host.h"
+
+namespace qik {
+namespace {
+struct FfnHeader {
+  uint32_t amax_x;
+  uint32_t amax_h;
+  float sx;
+  float sh;
+};
+constexpr size_t kAlign = 256;
+size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+}  // namespace
+}  // namespace qik
+
+using namespace qik;
+
+extern "C" size_t qik_fp8_ffn_workspace_bytes(int64_t M, int64_t K, int64_t hidden) {
+  if (M <= 0 || K <= 0 || hidden <= 0) return kAlign;
+  return kAlign + align_up(static_cast<size_t>(M) * K) + align_up(static_cast<size_t>(M) * hidden * 2) +
+         align_up(static_cast<size_t>(M) * hidden);
+}
+
+extern "C" int qik_fp8_ffn(const void* x, int64_t M, int64_t K, int64_t hidden, const uint8_t* w_up,
+                           const float* s_up, const void* b_up, const uint8_t* w_down, const float* s_down,
+                           const void* b_down, void* y, void* ws, size_t ws_bytes, int* status, void* stream) {
+  QIK_REQUIRE(M >= 0 && K > 0 && hidden > 0, "qik_fp8_ffn: bad sizes");
+  if (M == 0) return QIK_OK;
+  QIK_REQUIRE(x && w_up && s_up && w_down && s_down && y && ws, "qik_fp8_ffn: NULL pointer");
+  QIK_REQUIRE(ws_bytes >= qik_fp8_ffn_workspace_bytes(M, K, hidden), "qik_fp8_ffn: workspace of %zu bytes too small",
+              ws_bytes);
+  QIK_REQUIRE((reinterpret_cast<uintptr_t>(ws) & (kAlign - 1)) == 0, "qik_fp8_ffn: workspace must be 256-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  FfnHeader* hdr = reinterpret_cast<FfnHeader*>(base);
+  uint8_t* xq = base + kAlign;
+  void* h = xq + align_up(static_cast<size_t>(M) * K);
+  uint8_t* hq = static_cast<uint8_t*>(h) + align_up(static_cast<size_t>(M) * hidden * 2);
+
+  QIK_TRY_CUDA(cudaMemsetAsync(hdr, 0, 2 * sizeof(uint32_t), st));
+  int rc = launch_amax(x, QIK_DTYPE_BF16, M * K, &hdr->amax_x, st, false);
+  if (!rc) rc = launch_pack_act(x, M * K, &hdr->amax_x, xq, &hdr->sx, st, true);
+  if (!rc)
+    rc = launch_fp8_gemm(xq, w_up, M, hidden, K, K, K, &hdr->sx, s_up, b_up, h, hidden, QIK_DTYPE_BF16,
+                         QIK_EPI_GELU_TANH, &hdr->amax_h, status, st, true);
+  if (!rc) rc = launch_pack_act(h, M * hidden, &hdr->amax_h, hq, &hdr->sh, st, true);
+  if (!rc)
+    rc = launch_fp8_gemm(hq, w_down, M, K, hidden, hidden, hidden, &hdr->sh, s_down, b_down, y, K, QIK_DTYPE_BF16,
+                         QIK_EPI_SCALE, nullptr, status, st, true);
+  return rc;
+}

@@ -107,6 +107,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the set-up above overlaps the predecessor's tail; operands are read below
+  pdl_wait();
 
   const int num_m = (p.M + kGemmBM - 1) / kGemmBM;
   const int num_n = (p.N + BN - 1) / BN;
@@ -132,6 +134,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     producer_done:;
     }
+    pdl_trigger();
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f32acc(0, 0, 0, 0, kGemmBM, BN);
@@ -169,6 +172,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         umma_commit(&tfull[acc]);
       }
     }
+    pdl_trigger();
   } else {
     // epilogue warps 2..9: TMEM lane quarter = warp % 4, two warps per quarter take
     // alternate 32-column chunks.  Each warp turns its 32 accumulator rows into
@@ -187,6 +191,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status)) break;
       tc_fence_after();
+      if (tile + static_cast<int>(gridDim.x) >= tiles) pdl_trigger();  // last tile of this CTA
       const int mb = tile / num_n, nb = tile % num_n;
       const int row0 = mb * kGemmBM + quarter * 32;
       const bool row_ok = row0 + lane < p.M;
@@ -291,7 +296,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
 template <int BN, int STAGES>
 static int launch_gemm(const uint8_t* A, const uint8_t* B, const GemmParams& p, int64_t lda, int64_t ldb,
-                       cudaStream_t st) {
+                       cudaStream_t st, bool pdl) {
   using Lay = GemmLayout<BN, STAGES>;
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, static_cast<uint64_t>(p.K),
@@ -319,18 +324,14 @@ static int launch_gemm(const uint8_t* A, const uint8_t* B, const GemmParams& p, 
   }
   const int tiles = ((p.M + kGemmBM - 1) / kGemmBM) * ((p.N + BN - 1) / BN);
   const int grid = min(tiles, sm_count());
-  fp8_gemm_kernel<BN, STAGES><<<grid, kGemmThreads, Lay::kSmemBytes, st>>>(ta, tb, tc, p);
+  QIK_TRY_CUDA(launch_kernel(fp8_gemm_kernel<BN, STAGES>, dim3(grid), dim3(kGemmThreads), Lay::kSmemBytes, st, pdl,
+                             ta, tb, tc, p));
   return check_launch("fp8_gemm_kernel");
 }
 
-}  // namespace qik
-
-using namespace qik;
-
-extern "C" int qik_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda,
-                            int64_t ldb, const float* scale_a, const float* scale_b, const void* bias, void* C,
-                            int64_t ldc, int out_dtype, int epilogue, uint32_t* amax_out, int* status,
-                            void* stream) {
+int launch_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                    const float* scale_a, const float* scale_b, const void* bias, void* C, int64_t ldc, int out_dtype,
+                    int epilogue, uint32_t* amax_out, int* status, cudaStream_t stream, bool pdl) {
   QIK_REQUIRE(M >= 0 && N >= 0 && K >= 0, "qik_fp8_gemm: negative size");
   if (M == 0 || N == 0) return QIK_OK;
   QIK_REQUIRE(K > 0, "qik_fp8_gemm: K must be positive");
@@ -360,5 +361,15 @@ extern "C" int qik_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64
   p.epilogue = epilogue;
   p.amax_out = amax_out;
   p.status = status;
-  return launch_gemm<256, 4>(A, B, p, lda, ldb, static_cast<cudaStream_t>(stream));
+  return launch_gemm<256, 4>(A, B, p, lda, ldb, stream, pdl);
+}
+
+}  // namespace qik
+
+extern "C" int qik_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda,
+                            int64_t ldb, const float* scale_a, const float* scale_b, const void* bias, void* C,
+                            int64_t ldc, int out_dtype, int epilogue, uint32_t* amax_out, int* status,
+                            void* stream) {
+  return qik::launch_fp8_gemm(A, B, M, N, K, lda, ldb, scale_a, scale_b, bias, C, ldc, out_dtype, epilogue, amax_out,
+                              status, static_cast<cudaStream_t>(stream), false);
 }

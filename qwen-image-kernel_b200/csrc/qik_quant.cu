@@ -62,6 +62,7 @@ __device__ __forceinline__ uint32_t block_max_u32(uint32_t v) {
 // bf16: |x| as 16-bit patterns; __vmaxu2 takes the halfword max of two at once.
 __global__ void __launch_bounds__(kQuantThreads) amax_bf16_kernel(const uint16_t* __restrict__ x, int64_t n,
                                                                   uint32_t* __restrict__ amax_bits) {
+  pdl_wait();
   uint32_t m2 = 0;  // two running halfword maxima
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -94,6 +95,7 @@ __global__ void __launch_bounds__(kQuantThreads) amax_bf16_kernel(const uint16_t
   uint32_t m = max(m2 & 0xFFFFu, m2 >> 16);
   m = block_max_u32(m);
   if (threadIdx.x == 0 && m != 0u) atomicMax(amax_bits, m << 16);
+  pdl_trigger();
 }
 
 __global__ void __launch_bounds__(kQuantThreads) amax_f32_kernel(const float* __restrict__ x, int64_t n,
@@ -127,6 +129,7 @@ __global__ void __launch_bounds__(kQuantThreads) pack_act_kernel(const uint16_t*
                                                                  const uint32_t* __restrict__ amax_bits,
                                                                  uint8_t* __restrict__ q,
                                                                  float* __restrict__ scale_out) {
+  pdl_wait();
   const float s = scale_from_amax_bits(__ldg(amax_bits));
   const float inv = act_inverse(s);
   if (blockIdx.x == 0 && threadIdx.x == 0 && scale_out) scale_out[0] = s;
@@ -156,6 +159,7 @@ __global__ void __launch_bounds__(kQuantThreads) pack_act_kernel(const uint16_t*
     const float v = __uint_as_float(static_cast<uint32_t>(x[i]) << 16) * inv;
     q[i] = static_cast<uint8_t>(cvt_e4m3x2(v, 0.0f) & 0xFFu);
   }
+  pdl_trigger();
 }
 
 // Weight / slab V element: clamp(w / s) then round to e4m3; NaN keeps its sign
@@ -257,14 +261,22 @@ static int grid_for(int64_t work_items, int per_thread) {
   return static_cast<int>(g < 1 ? 1 : g);
 }
 
-static int launch_amax(const void* x, int dtype, int64_t n, uint32_t* amax_bits, cudaStream_t st) {
+int launch_amax(const void* x, int dtype, int64_t n, uint32_t* amax_bits, cudaStream_t st, bool pdl) {
   if (n <= 0) return QIK_OK;
   if (dtype == QIK_DTYPE_BF16) {
-    amax_bf16_kernel<<<grid_for(n, 32), kQuantThreads, 0, st>>>(static_cast<const uint16_t*>(x), n, amax_bits);
+    QIK_TRY_CUDA(launch_kernel(amax_bf16_kernel, dim3(grid_for(n, 32)), dim3(kQuantThreads), 0, st, pdl,
+                               static_cast<const uint16_t*>(x), n, amax_bits));
   } else {
     amax_f32_kernel<<<grid_for(n, 16), kQuantThreads, 0, st>>>(static_cast<const float*>(x), n, amax_bits);
   }
   return check_launch("amax kernel");
+}
+
+int launch_pack_act(const void* x, int64_t n, const uint32_t* amax_bits, uint8_t* q, float* scale_out,
+                    cudaStream_t st, bool pdl) {
+  QIK_TRY_CUDA(launch_kernel(pack_act_kernel, dim3(grid_for(n, 16)), dim3(kQuantThreads), 0, st, pdl,
+                             static_cast<const uint16_t*>(x), n, amax_bits, q, scale_out));
+  return check_launch("pack_act_kernel");
 }
 
 }  // namespace qik
@@ -283,7 +295,7 @@ int qik_compute_scale(const void* x, int dtype, int64_t n, float* scale_out, voi
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   QuantWs* w = static_cast<QuantWs*>(ws);
   QIK_TRY_CUDA(cudaMemsetAsync(&w->amax_bits, 0, sizeof(uint32_t), st));
-  int rc = launch_amax(x, dtype, n, &w->amax_bits, st);
+  int rc = launch_amax(x, dtype, n, &w->amax_bits, st, false);
   if (rc) return rc;
   scale_finalize_kernel<<<1, 32, 0, st>>>(&w->amax_bits, scale_out);
   return check_launch("scale_finalize_kernel");
@@ -294,7 +306,7 @@ int qik_amax(const void* x, int dtype, int64_t n, uint32_t* amax_bits, void* str
   QIK_REQUIRE(amax_bits, "qik_amax: amax_bits is NULL");
   QIK_REQUIRE(dtype == QIK_DTYPE_BF16 || dtype == QIK_DTYPE_F32, "qik_amax: dtype must be BF16 or F32");
   QIK_REQUIRE(n >= 0, "qik_amax: negative n");
-  return launch_amax(x, dtype, n, amax_bits, static_cast<cudaStream_t>(stream));
+  return launch_amax(x, dtype, n, amax_bits, static_cast<cudaStream_t>(stream), false);
 }
 
 int qik_quantize_act_from_amax(const void* x, int64_t n, const uint32_t* amax_bits, uint8_t* q, float* scale_out,
@@ -302,10 +314,7 @@ int qik_quantize_act_from_amax(const void* x, int64_t n, const uint32_t* amax_bi
   QIK_REQUIRE((x && q) || n == 0, "qik_quantize_act_from_amax: x/q is NULL");
   QIK_REQUIRE(amax_bits, "qik_quantize_act_from_amax: amax_bits is NULL");
   QIK_REQUIRE(n >= 0, "qik_quantize_act_from_amax: negative n");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  pack_act_kernel<<<grid_for(n, 16), kQuantThreads, 0, st>>>(static_cast<const uint16_t*>(x), n, amax_bits, q,
-                                                               scale_out);
-  return check_launch("pack_act_kernel");
+  return launch_pack_act(x, n, amax_bits, q, scale_out, static_cast<cudaStream_t>(stream), false);
 }
 
 int qik_quantize_act(const void* x, int64_t n, uint8_t* q, float* scale_out, void* ws, void* stream) {
@@ -315,7 +324,7 @@ int qik_quantize_act(const void* x, int64_t n, uint8_t* q, float* scale_out, voi
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   QuantWs* w = static_cast<QuantWs*>(ws);
   QIK_TRY_CUDA(cudaMemsetAsync(&w->amax_bits, 0, sizeof(uint32_t), st));
-  int rc = launch_amax(x, QIK_DTYPE_BF16, n, &w->amax_bits, st);
+  int rc = launch_amax(x, QIK_DTYPE_BF16, n, &w->amax_bits, st, false);
   if (rc) return rc;
   return qik_quantize_act_from_amax(x, n, &w->amax_bits, q, scale_out, stream);
 }
@@ -328,7 +337,7 @@ int qik_quantize_weight(const void* w, int dtype, int64_t n, uint8_t* q, float* 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   QuantWs* ws_ = static_cast<QuantWs*>(ws);
   QIK_TRY_CUDA(cudaMemsetAsync(&ws_->amax_bits, 0, sizeof(uint32_t), st));
-  int rc = launch_amax(w, dtype, n, &ws_->amax_bits, st);
+  int rc = launch_amax(w, dtype, n, &ws_->amax_bits, st, false);
   if (rc) return rc;
   const int g = grid_for(n, 4);
   if (dtype == QIK_DTYPE_BF16)

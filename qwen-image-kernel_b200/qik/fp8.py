@@ -229,17 +229,36 @@ def fp8_state_dict(model: nn.Module) -> dict[str, torch.Tensor]:
     return {k: v for k, v in model.state_dict().items()}
 
 
-def fp8_ffn_gelu(x: torch.Tensor, up: FP8Linear, down: FP8Linear) -> torch.Tensor:
+def fp8_ffn_gelu(x: torch.Tensor, up: FP8Linear, down: FP8Linear, workspace: torch.Tensor | None = None
+                 ) -> torch.Tensor:
     """DiT FFN pair: down(gelu_tanh(up(x))) with both linears FP8 per-tensor and the
-    hidden activation re-quantized dynamically between them.
+    hidden activation re-quantized dynamically between them (qik_fp8_ffn: one chain
+    of five kernels with programmatic dependent launches).
 
     The up-projection epilogue applies GELU-tanh to the bf16 linear output and
     accumulates max|h| on the fly, so the hidden tensor is quantized with one pack
-    pass (no separate amax read)."""
-    x2 = x.reshape(-1, x.shape[-1])
-    xq, sx = quantize_tensorwise(x2)
-    amax = torch.zeros(1, dtype=torch.int32, device=x.device)
-    h = fp8_gemm(xq, sx, up.weight, up.weight_scale, up.bias, epilogue=L.EPI_GELU_TANH, amax_out=amax)
-    hq, sh = quantize_from_amax(h, amax)
-    y = fp8_gemm(hq, sh, down.weight, down.weight_scale, down.bias)
-    return y.reshape(*x.shape[:-1], down.out_features)
+    pass.  ``workspace`` (uint8, >= qik_fp8_ffn_workspace_bytes) may be passed to
+    avoid an allocation per call."""
+    _require_cuda(x, "x")
+    if x.dtype != torch.bfloat16:
+        raise TypeError("qik.fp8_ffn_gelu: bf16 activations only")
+    lib = L.load()
+    K = x.shape[-1]
+    hidden = up.out_features
+    if up.in_features != K or down.in_features != hidden or down.out_features != K:
+        raise ValueError("qik.fp8_ffn_gelu: up must be K -> hidden and down hidden -> K")
+    x2 = x.reshape(-1, K).contiguous()
+    M = x2.shape[0]
+    nbytes = lib.qik_fp8_ffn_workspace_bytes(M, K, hidden)
+    if workspace is None or workspace.numel() < nbytes or workspace.data_ptr() % 256:
+        workspace = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+    y = torch.empty(M, K, dtype=torch.bfloat16, device=x.device)
+    b_up = None if up.bias is None else up.bias.to(torch.bfloat16).contiguous()
+    b_down = None if down.bias is None else down.bias.to(torch.bfloat16).contiguous()
+    status = L.status_word(x.device)
+    with torch.cuda.device(x.device):
+        L.check(lib.qik_fp8_ffn(x2.data_ptr(), M, K, hidden, up.weight.data_ptr(), up.weight_scale.data_ptr(),
+                                L.ptr(b_up), down.weight.data_ptr(), down.weight_scale.data_ptr(), L.ptr(b_down),
+                                y.data_ptr(), workspace.data_ptr(), workspace.numel(), status.data_ptr(),
+                                L.stream_ptr()), "qik_fp8_ffn")
+    return y.reshape(*x.shape[:-1], K)

@@ -36,7 +36,8 @@ def _one():
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 128), (128, 256, 256), (256, 512, 384), (1, 16, 16),
                                    (2, 48, 32), (127, 272, 112), (129, 256, 144), (300, 3072, 3072),
-                                   (4352, 256, 128)])
+                                   (4352, 256, 128), (512, 1024, 12288), (2, 18432, 3072), (256, 3072, 3072),
+                                   (1000, 1040, 2048)])
 def test_gemm_exact_small_ints(fp8, M, N, K):
     """Exact integer products: any layout/descriptor/tail error shows up as a mismatch."""
     a = _e4m3_small_ints(M * 7 + K, (M, K))
@@ -45,6 +46,20 @@ def test_gemm_exact_small_ints(fp8, M, N, K):
     y = fp8.fp8_gemm(a.cuda(), _one(), b.cuda(), _one(), out_dtype=torch.float32)
     torch.cuda.synchronize()
     assert torch.equal(y.cpu(), ref)
+
+
+def test_gemm_deterministic(fp8):
+    """Repeated launches give bitwise-identical results (fixed schedule, no atomics)."""
+    M, N, K = 640, 768, 6144
+    a = _e4m3_small_ints(11, (M, K)).cuda()
+    b = _e4m3_small_ints(12, (N, K)).cuda()
+    x = GI.randn_bf16(13, (M, K)).cuda()
+    xq, sx = fp8.quantize_tensorwise(x)
+    y1 = fp8.fp8_gemm(xq, sx, b, _one())
+    y2 = fp8.fp8_gemm(xq, sx, b, _one())
+    assert torch.equal(y1, y2)
+    assert torch.equal(fp8.fp8_gemm(a, _one(), b, _one(), out_dtype=torch.float32).cpu(),
+                       a.cpu().float() @ b.cpu().float().t())
 
 
 def test_gemm_scales_and_bias(fp8):
