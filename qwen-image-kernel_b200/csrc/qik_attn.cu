@@ -190,9 +190,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       constexpr uint32_t idesc_s = idesc_f32acc(1, 1, 0, 0, kAttnBM, kAttnBN);
       constexpr uint32_t idesc_o = idesc_f32acc(1, 1, 0, 1, kAttnBM, kAttnD);      // bf16 P, bf16 V
       constexpr uint32_t idesc_o16 = idesc_f32acc(0, 0, 0, 1, kAttnBM, kAttnD);    // f16 P, f16 V (fp8 slab)
-      const uint32_t tS[2] = {tmem + 0u, tmem + 128u};
+      // TMEM columns: S_s at 128 s, O at 256, P_s at 384 + 64 s
       const uint32_t tO = tmem + 256u;
-      const uint32_t tP[2] = {tmem + 384u, tmem + 448u};
       bool ok = mbar_wait(q_full, 0, abort_flag, a.status);
       const uint32_t q_addr = smem_u32(sQ);
       auto issue_pv = [&](int t) -> bool {
@@ -206,7 +205,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int k = 0; k < kAttnBN / 16; ++k) {
           // 16 keys per step: V rows [16k, 16k+16) (2048 B); d halves 16 KB apart
           const uint64_t vd = sdesc_sw128(v_addr + k * 2048, 16384, 1024);
-          umma_f16_ts(tO, tP[s] + k * 8, vd, (v_fp8 && t < n_slab) ? idesc_o16 : idesc_o, (t > 0 || k > 0) ? 1u : 0u);
+          umma_f16_ts(tO, tmem + 384u + 64u * s + k * 8, vd, (v_fp8 && t < n_slab) ? idesc_o16 : idesc_o, (t > 0 || k > 0) ? 1u : 0u);
         }
         umma_commit(&pv_done[s]);
         umma_commit(&v_empty[s]);
@@ -226,7 +225,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
           const uint64_t qd = sdesc_sw128(q_addr + off, 16, 1024);
           const uint64_t kd = sdesc_sw128(k_addr + off, 16, 1024);
-          umma_f16_ss(tS[s], qd, kd, idesc_s, k > 0 ? 1u : 0u);
+          umma_f16_ss(tmem + 128u * s, qd, kd, idesc_s, k > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[s]);
         umma_commit(&k_empty[ks]);
@@ -269,9 +268,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int quarter = warp & 3;
     const int row = threadIdx.x - 128;  // == quarter * 32 + lane
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t tS[2] = {tmem + lane_base, tmem + lane_base + 128u};
     const uint32_t tO = tmem + lane_base + 256u;
-    const uint32_t tP[2] = {tmem + lane_base + 384u, tmem + lane_base + 448u};
     const uint8_t* kvb = has_kv ? a.key_valid + static_cast<int64_t>(b) * a.kv_sb : nullptr;
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
@@ -282,10 +279,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int t = 0; t < n_tiles; ++t) {
       const int s = t & 1;
       const uint32_t ph = (t >> 1) & 1;
+      const uint32_t tS = tmem + lane_base + 128u * s;        // this tile's S buffer
+      const uint32_t tP = tmem + lane_base + 384u + 64u * s;  // this tile's P buffer
       if (!mbar_wait(&s_full[s], ph, abort_flag, a.status)) {
         ok = false;
         break;
       }
+      __syncwarp();  // lanes leave the spin loop separately; tcgen05.ld is warp-aligned
       tc_fence_after();
       const bool slab = t < n_slab;
       const int kv0 = slab ? t * kAttnBN : P + (t - n_slab) * kAttnBN;
@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
       for (int c = 0; c < kAttnBN / 32; ++c) {
         uint32_t r[32];
-        tmem_ld32(tS[s] + c * 32, r);
+        tmem_ld32(tS + c * 32, r);
 #pragma unroll
         for (int j = 0; j < 32; ++j) sv[c * 32 + j] = __uint_as_float(r[j]);
       }
@@ -353,12 +353,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         ok = false;
         break;
       }
+      __syncwarp();
+      // O is touched only when some row of the warp rescales (or at the slab
+      // boundary); the whole warp then runs the warp-collective TMEM loads/stores, a
+      // row that keeps its max with factor 1.  pv_done of tile t-1 cannot run two
+      // phases ahead of this thread: P.V_t needs this thread's P_t.
       const bool boundary = !vsc_applied && t == n_slab;  // first fresh tile after the fp8 slab
-      if ((rescale_o || boundary) && t >= 1) {
+      if (t >= 1 && __any_sync(0xffffffffu, rescale_o || boundary)) {
         if (!mbar_wait(&pv_done[(t - 1) & 1], ((t - 1) >> 1) & 1, abort_flag, a.status)) {
           ok = false;
           break;
         }
+        __syncwarp();
         tc_fence_after();
         const float f = (rescale_o ? alpha : 1.0f) * (boundary ? vsc : 1.0f);
 #pragma unroll
@@ -376,7 +382,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         uint32_t r[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) r[j] = pk[c * 32 + j];
-        tmem_st32(tP[s] + c * 32, r);
+        tmem_st32(tP + c * 32, r);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -390,6 +396,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (ok && n_tiles > 0) {
       const int tl = n_tiles - 1;
       if (mbar_wait(&pv_done[tl & 1], (tl >> 1) & 1, abort_flag, a.status)) {
+        __syncwarp();
         tc_fence_after();
 #pragma unroll
         for (int c = 0; c < kAttnD / 32; ++c) {

@@ -236,6 +236,41 @@ def test_fp8_slab_rows_ending_inside_slab(attn):
     _check(out, exact, tag="fp8 slab partial")
 
 
+@pytest.mark.parametrize("slab", [False, True])
+def test_running_max_jumps_in_some_rows(attn, slab):
+    """Rows whose running max grows by far more than 2^8 (log2 units) in a later key
+    tile while their warp neighbours' does not: O is rescaled in TMEM for some rows
+    of a warp only (factor 1 for the others), after the first tile and, with the fp8
+    slab, at the same time as the slab-scale boundary."""
+    from qik.kv_cache import ContiguousKVCache
+    H, S = 2, 640
+    P = 256 if slab else 0
+    q = GI.randn_bf16(81, (1, S, H, 128), 0.3)
+    k = GI.randn_bf16(82, (1, S, H, 128), 0.3)
+    v = GI.randn_bf16(83, (1, S, H, 128), 0.5)
+    rows = torch.arange(0, S, 3)
+    q[0, rows, :, 0] = 4.0
+    k[0, 400, :, 0] = 40.0          # raw score ~160 -> ~20 log2 units above the rest
+    k[0, 130, :, 0] = -40.0
+    L = torch.full((S,), P + S - 1, dtype=torch.int32)
+    L[:200] = torch.arange(P, P + 200, dtype=torch.int32)   # causal head rows see the jump only later
+    if slab:
+        cache = ContiguousKVCache(1, 1, P, H, 128, v_fp8=True, device="cuda")
+        cache.get_layer(0).store(GI.randn_bf16(84, (1, P, H, 128), 0.3).cuda(),
+                                 GI.randn_bf16(85, (1, P, H, 128), 0.5).cuda())
+        ck, cv, vs = cache.get_layer(0).views()
+        out = attn.block_causal_flash_attention(q.cuda(), k.cuda(), v.cuda(), L.cuda(), None, ck, cv, vs)
+        ref32 = O.block_causal_attention(q, k, v, L, None, ck.cpu(), cv.cpu(), vs.cpu(), out_dtype=torch.float32,
+                                         slab_v_bf16=False)
+    else:
+        out = attn.block_causal_flash_attention(q.cuda(), k.cuda(), v.cuda(), L.cuda(), None)
+        ref32 = O.block_causal_attention(q, k, v, L, None, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    _check(out, ref32, tag=f"max jumps slab={slab}")
+    from qik import _lib as QL
+    assert QL.device_status() == 0
+
+
 def test_status_word_clean(attn):
     from qik import _lib as L
     assert L.device_status() == 0
