@@ -206,6 +206,57 @@ int qik_kv_store(const void* k, const void* v, int64_t B, int64_t P, int64_t H, 
                  int64_t pmax, int v_fp8, float* v_scale_layer, void* ws, void* stream);
 
 /*
+ * Per-head RMSNorm + rotary embedding of one of q / k: for every (b, s, h) row of D,
+ * rrms = rsqrt(sum(x^2) / D + eps), n = bf16(x * rrms * weight), then each pair
+ * (n[2i], n[2i+1]) is rotated by (cos[s, i], sin[s, i]); bf16 out.  Replaces
+ * fused_rms_norm_rope + rms_rope_kernel (qwen_image_kernel/triton_fused.py:27-117);
+ * unlike the reference it reads strided q / k views of the fused QKV output directly.
+ *   x: [B, S, H, D] bf16, element strides (x_sb, x_ss, x_sh), unit D stride
+ *   weight: D fp32; cos_tab, sin_tab: [S, D/2] fp32 (rows contiguous)
+ *   out: [B, S, H, D] bf16 with strides (o_sb, o_ss, o_sh)
+ *   D in {64, 128, 256}; pointers 16-byte aligned, strides multiples of 8.
+ */
+int qik_rms_norm_rope(const void* x, int64_t B, int64_t S, int64_t H, int64_t D, int64_t x_sb, int64_t x_ss,
+                      int64_t x_sh, const float* weight, const float* cos_tab, const float* sin_tab, float eps,
+                      void* out, int64_t o_sb, int64_t o_ss, int64_t o_sh, void* stream);
+
+/*
+ * LayerNorm (no affine, fp32 mean and centred variance, bf16 result) times
+ * bf16(1 + scale), the scale row chosen per position: row b where target_mask[s]
+ * is non-zero (or target_mask is NULL), row B + b elsewhere (the t = 0 rows).
+ * Replaces fused_layer_norm_modulate + ln_modulate_kernel and _modulation_row_map
+ * (qwen_image_kernel/triton_fused.py:75-160).
+ *   x, out: [B, S, D] bf16 contiguous; modulation: mod_rows rows of mod_stride bf16
+ *   (at least B rows, 2B with a target_mask), scale at column scale_off;
+ *   target_mask: S bytes or NULL; D % 8 == 0, D <= 4096.
+ *   amax_out: NULL, or a u32 receiving atomicMax of the fp32 bit patterns of |out|
+ *   (the amax of the next linear's dynamic quantization; the caller zeroes it).
+ */
+int qik_layer_norm_modulate(const void* x, int64_t B, int64_t S, int64_t D, const void* modulation,
+                            int64_t mod_rows, int64_t mod_stride, int64_t scale_off, const uint8_t* target_mask,
+                            float eps, void* out, uint32_t* amax_out, void* stream);
+
+/*
+ * Gated residual out = x + bf16(tanh(gate)) * f in bf16 arithmetic, the gate row
+ * chosen per position as in qik_layer_norm_modulate.  Replaces fused_gate_residual
+ * + gate_residual_kernel (qwen_image_kernel/triton_fused.py:168-218).
+ *   x, f, out: [B, S, D] bf16 contiguous, out distinct from x and f; gate at column gate_off.
+ */
+int qik_gate_residual(const void* x, const void* f, int64_t B, int64_t S, int64_t D, const void* modulation,
+                      int64_t mod_rows, int64_t mod_stride, int64_t gate_off, const uint8_t* target_mask, void* out,
+                      void* stream);
+
+/*
+ * SwiGLU out = bf16(bf16(silu(gate)) * up).  Replaces fused_swiglu + swiglu_kernel
+ * (qwen_image_kernel/triton_fused.py:227-262); gate and up may be the two halves of
+ * the fused up-projection output (row pitches ld_*, in elements), read in place.
+ *   [M, N] bf16 each; N and the pitches multiples of 8; amax_out as in
+ *   qik_layer_norm_modulate (for the down projection's quantizer).
+ */
+int qik_swiglu(const void* gate, int64_t ld_gate, const void* up, int64_t ld_up, int64_t M, int64_t N, void* out,
+               int64_t ld_out, uint32_t* amax_out, void* stream);
+
+/*
  * Self-test of the bounded-wait machinery: launches one CTA that waits on an
  * mbarrier nothing will ever complete, with a limit of `wait_ns` nanoseconds, and
  * writes QIK_STATUS_TIMEOUT to *status when the wait gives up.  The GPU context

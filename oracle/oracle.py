@@ -312,3 +312,80 @@ def act_reciprocal(s: float) -> float:
     if sb in _RECIP_TABLE:
         return float(np.uint32(_RECIP_TABLE[sb]).view(np.float32))
     return reciprocal_rn(s)
+
+
+# ---------------------------------------------------------------- fused elementwise ops
+# Restatements of the reference's fused Triton kernels (qwen_image_kernel/triton_fused.py)
+# in fp32 on the CPU with bf16 roundings at the points the kernels round.
+
+def _rb(t: torch.Tensor) -> torch.Tensor:
+    """Round an fp32 tensor to bf16 (nearest-even) and back to fp32."""
+    return t.to(torch.bfloat16).float()
+
+
+def modulation_rows(target_token_mask: torch.Tensor | None, B: int, S: int) -> torch.Tensor:
+    """[B, S] modulation row of each (sample, position): the row map of
+    _modulation_row_map (triton_fused.py:128-139, 0 for target positions, B
+    otherwise) plus the sample index, as the kernels add it (triton_fused.py:111,188)."""
+    if target_token_mask is None:
+        base = torch.zeros(S, dtype=torch.int64)
+    else:
+        base = torch.where(target_token_mask.cpu().to(torch.bool), 0, B).to(torch.int64)
+    return base[None, :] + torch.arange(B, dtype=torch.int64)[:, None]
+
+
+def rms_norm_rope(x: torch.Tensor, weight: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                  eps: float) -> torch.Tensor:
+    """rms_rope_kernel (triton_fused.py:27-67): per (b, s, h) row of D,
+    rrms = rsqrt(sum(x^2) / D + eps); n = bf16((x * rrms) * w) in fp32; the pairs
+    (n[2i], n[2i+1]) rotate by (cos[s, i], sin[s, i]); bf16 out.
+    x: [B, S, H, D] bf16 (any strides); weight: [D]; cos, sin: [S, D/2] fp32."""
+    x = x.cpu().float()
+    D = x.shape[-1]
+    ss = (x * x).sum(-1, keepdim=True)
+    rrms = torch.rsqrt(ss / D + eps)
+    n = _rb((x * rrms) * weight.cpu().float())
+    ne, no = n[..., 0::2], n[..., 1::2]
+    c = cos.cpu().float()[None, :, None, :]
+    s = sin.cpu().float()[None, :, None, :]
+    oe = ne * c - no * s
+    oo = ne * s + no * c
+    return torch.stack([oe, oo], -1).flatten(-2).to(torch.bfloat16)
+
+
+def layer_norm_modulate(x: torch.Tensor, modulation: torch.Tensor, scale_off: int,
+                        target_token_mask: torch.Tensor | None, eps: float) -> torch.Tensor:
+    """ln_modulate_kernel (triton_fused.py:75-108): LayerNorm without affine in fp32
+    (mean, then the centred variance), y = bf16(xc * rsqrt(var + eps)), then
+    bf16(y * bf16(1 + scale)) with scale = modulation[row, scale_off : scale_off + D].
+    x: [B, S, D] bf16; modulation: [R, >= scale_off + D] bf16."""
+    x = x.cpu().float()
+    B, S, D = x.shape
+    mean = x.sum(-1, keepdim=True) / D
+    xc = x - mean
+    var = (xc * xc).sum(-1, keepdim=True) / D
+    y = _rb(xc * torch.rsqrt(var + eps))
+    rows = modulation_rows(target_token_mask, B, S)
+    sc = modulation.cpu()[rows][..., scale_off:scale_off + D].float()
+    return (y * _rb(1.0 + sc)).to(torch.bfloat16)
+
+
+def gate_residual(x: torch.Tensor, f: torch.Tensor, modulation: torch.Tensor, gate_off: int,
+                  target_token_mask: torch.Tensor | None) -> torch.Tensor:
+    """gate_residual_kernel (triton_fused.py:168-196): g = bf16(tanh(gate)) with gate =
+    modulation[row, gate_off : gate_off + D]; y = x + g * f in bf16 arithmetic (the
+    product rounded to bf16, then the sum), as the stock expression rounds."""
+    x = x.cpu().float()
+    B, S, D = x.shape
+    rows = modulation_rows(target_token_mask, B, S)
+    g = _rb(torch.tanh(modulation.cpu()[rows][..., gate_off:gate_off + D].float()))
+    t = _rb(g * f.cpu().float())
+    return (x + t).to(torch.bfloat16)
+
+
+def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """swiglu_kernel (triton_fused.py:227-240): s = bf16(g * sigmoid(g)) in fp32, then
+    bf16(s * up)."""
+    g = gate.cpu().float()
+    s = _rb(g * torch.sigmoid(g))
+    return (s * up.cpu().float()).to(torch.bfloat16)

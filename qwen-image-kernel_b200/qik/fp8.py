@@ -185,6 +185,19 @@ class FP8Linear(nn.Module):
         out = out.reshape(*x.shape[:-1], self.out_features)
         return out.to(x.dtype) if out.dtype != x.dtype else out
 
+    def forward_from_amax(self, x: torch.Tensor, amax: torch.Tensor | None) -> torch.Tensor:
+        """forward(x) when the producer of x already reduced max|x| into ``amax``
+        (int32 [1], fp32 bit pattern; e.g. the amax_out of the fused layer-norm /
+        SwiGLU kernels): the quantizer skips its own amax pass.  Same bytes and
+        scale as forward(x), since the amax is the same number."""
+        if amax is None or self.in_features < 256:
+            return self.forward(x)
+        x2 = x.reshape(-1, x.shape[-1])
+        xq, s_a = quantize_from_amax(x2, amax)
+        out = fp8_gemm(xq, s_a, self.weight, self.weight_scale, self.bias)
+        out = out.reshape(*x.shape[:-1], self.out_features)
+        return out.to(x.dtype) if out.dtype != x.dtype else out
+
     def forward_fp32(self, x: torch.Tensor) -> torch.Tensor:
         """Same computation with the fp32 GEMM output before the bf16 cast (parity mode)."""
         x2 = x.reshape(-1, x.shape[-1])

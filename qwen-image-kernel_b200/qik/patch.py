@@ -7,13 +7,15 @@ the reference package is imported:
     qwen_image_kernel.triton_attention  -> qik.triton_attention
     qwen_image_kernel.kv_cache          -> qik.kv_cache
     qwen_image_kernel.quantize_offline  -> qik.quantize_offline
+    qwen_image_kernel.triton_fused      -> qik.triton_fused
+    qwen_image_kernel.processors        -> qik.processors
 
-The reference's own relative imports (``from .fp8 import FP8Linear`` in runtime.py:33,
-``from .triton_attention import block_causal_flash_attention`` in processors.py:18,
-``from .kv_cache import ContiguousKVCache`` in runtime.py:34) resolve through
-``sys.modules`` and therefore bind the qik implementations; everything else in the
-reference package (runtime, processors, the fused elementwise kernels) loads from
-the checkout as before.
+The reference's own relative imports (``from .fp8 import FP8Linear`` and
+``from .processors import QwenImage21KernelBlock, QwenImage21KernelProcessor`` in
+runtime.py:33-35, ``from .kv_cache import ContiguousKVCache`` in runtime.py:34)
+resolve through ``sys.modules`` and therefore bind the qik implementations;
+everything else in the reference package (the runtime, metrics, the web UI) loads
+from the checkout as before.
 """
 from __future__ import annotations
 
@@ -25,6 +27,8 @@ MODULES = {
     "triton_attention": "qik.triton_attention",
     "kv_cache": "qik.kv_cache",
     "quantize_offline": "qik.quantize_offline",
+    "triton_fused": "qik.triton_fused",
+    "processors": "qik.processors",
 }
 
 

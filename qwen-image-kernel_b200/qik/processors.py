@@ -1,14 +1,34 @@
-"""Prefix-length construction of the block-causal mask.
+"""Attention processor and fused transformer block of Qwen-Image 2.1 on the qik kernels.
 
-``_build_prefix_lengths`` follows qwen_image_kernel/processors.py:22-36: the
-block-causal mask of a joint [prefix ; target] sequence collapses to one inclusive
-key limit per query row -- text rows are causal (L = q), image-block rows see the
-whole prefix up to the end of their block (L = end - 1), target rows see everything
-(L = S - 1).  BASELINE's "causal length" is the exclusive count L + 1.
+Same names and call signatures as ``qwen_image_kernel/processors.py``
+(gomezcojj-coder/qwen-image-kernel):
+
+* ``_build_prefix_lengths`` (processors.py:22-36): the block-causal mask of a joint
+  [prefix ; target] sequence collapses to one inclusive key limit per query row --
+  text rows are causal (L = q), image-block rows see the whole prefix up to the end
+  of their block (L = end - 1), target rows see everything (L = S - 1).  BASELINE's
+  "causal length" is the exclusive count L + 1.
+* ``QwenImage21KernelProcessor`` (processors.py:39-126): fused QKV FP8 GEMM, per-head
+  RMSNorm + RoPE, prefill (block-causal over the joint sequence) or decode (target
+  rows over [cached prefix ; fresh target] without concatenation), output FP8 GEMM.
+* ``QwenImage21KernelBlock`` (processors.py:129-187): LayerNorm + modulation, gated
+  residuals and the SwiGLU MLP around the attention, same submodule names so state
+  dicts load unchanged.
+* ``convert_transformer_to_kernels`` (processors.py:190-211).
+
+Where the data layout allows, tensors stay in place instead of being copied: q / k /
+v are strided views of the fused QKV output, gate / up the two halves of the fused
+up projection, and the slab store reads the key / value views directly.  The fused
+layer-norm and SwiGLU kernels also reduce the amax of their output, which the next
+FP8 linear uses instead of its own amax pass (same bytes and scale).
 """
 from __future__ import annotations
 
 import torch
+
+from .fp8 import FP8Linear
+from .triton_attention import block_causal_flash_attention
+from .triton_fused import fused_gate_residual, fused_layer_norm_modulate, fused_rms_norm_rope, fused_swiglu
 
 
 def _build_prefix_lengths(segments: list[tuple[int, int, bool]], prefix_len: int, seq_len: int,
@@ -20,3 +40,165 @@ def _build_prefix_lengths(segments: list[tuple[int, int, bool]], prefix_len: int
             L[start:end] = end - 1
     L[prefix_len:] = seq_len - 1
     return L
+
+
+def _linear(mod, x: torch.Tensor, amax: torch.Tensor | None) -> torch.Tensor:
+    """mod(x), with the producer's amax of x when mod is an FP8 linear."""
+    if amax is not None and isinstance(mod, FP8Linear):
+        return mod.forward_from_amax(x, amax)
+    return mod(x)
+
+
+def _new_amax(x: torch.Tensor) -> torch.Tensor:
+    return torch.zeros(1, dtype=torch.int32, device=x.device)
+
+
+class QwenImage21KernelProcessor:
+    """Drop-in for ``QwenImage21AttnProcessor``: same call signature (plus the optional
+    ``hidden_states_amax`` the fused block passes), one attention kernel for both the
+    prefill and the decode form."""
+
+    _attention_backend = None
+    _parallel_config = None
+
+    def __call__(
+        self,
+        attn,
+        hidden_states: torch.Tensor,
+        attention_mask=None,
+        rotary_emb=None,
+        layer_cache=None,
+        kv_cache_mode: str | None = None,
+        cache_write_slice=None,
+        segments=None,
+        key_valid=None,
+        hidden_states_amax: torch.Tensor | None = None,
+    ) -> torch.Tensor:
+        B, S, _ = hidden_states.shape
+        H = attn.heads
+        fused_qkv = getattr(attn, "fused_qkv", None)
+        if fused_qkv is not None:
+            # one quantization + one GEMM for Q, K and V; the splits are views
+            D = fused_qkv.out_features // (3 * H)
+            qkv = _linear(fused_qkv, hidden_states, hidden_states_amax)
+            query, key, value = qkv.unflatten(-1, (3 * H, D)).chunk(3, dim=-2)
+        else:
+            D = attn.to_q.out_features // H
+            query = _linear(attn.to_q, hidden_states, hidden_states_amax).unflatten(-1, (H, D))
+            key = _linear(attn.to_k, hidden_states, hidden_states_amax).unflatten(-1, (H, D))
+            value = _linear(attn.to_v, hidden_states, hidden_states_amax).unflatten(-1, (H, D))
+
+        query = fused_rms_norm_rope(query, attn.norm_q.weight, rotary_emb, attn.norm_q.eps)
+        key = fused_rms_norm_rope(key, attn.norm_k.weight, rotary_emb, attn.norm_k.eps)
+
+        if kv_cache_mode == "extract" and layer_cache is not None and cache_write_slice is not None:
+            # the slab store copies (and quantizes V) on the stream: the views suffice
+            layer_cache.store(key[:, cache_write_slice], value[:, cache_write_slice])
+
+        if segments is not None:
+            # prefill over the full joint sequence
+            assert key_valid is None or key_valid.dim() == 2
+            prefix_end = segments[-1][1] if segments else 0
+            L = _build_prefix_lengths(segments, prefix_end, S, query.device)
+            out = block_causal_flash_attention(query, key, value, L, key_valid, cache_k=None, cache_v=None)
+        else:
+            kv_mask = attention_mask
+            if kv_mask is not None:
+                kv_mask = kv_mask.reshape(kv_mask.shape[0], -1)
+            if layer_cache is not None:
+                # decode: target rows over [prefix slab ; fresh target]
+                if hasattr(layer_cache, "views"):
+                    cache_k, cache_v, v_scale = layer_cache.views()
+                else:
+                    cache_k, cache_v = layer_cache.get()
+                    v_scale = None
+                kv_total = cache_k.shape[1] + key.shape[1]
+                L = torch.full((key.shape[1],), kv_total - 1, dtype=torch.int32, device=query.device)
+                out = block_causal_flash_attention(query, key, value, L, kv_mask, cache_k=cache_k, cache_v=cache_v,
+                                                   cache_v_scale=v_scale, uniform_full=kv_mask is None)
+            else:
+                L = torch.full((key.shape[1],), key.shape[1] - 1, dtype=torch.int32, device=query.device)
+                out = block_causal_flash_attention(query, key, value, L, kv_mask, uniform_full=kv_mask is None)
+
+        out = out.flatten(2, 3).type_as(query)
+        out = attn.to_out[0](out)
+        return attn.to_out[1](out)
+
+
+class QwenImage21KernelBlock(torch.nn.Module):
+    """Fused replacement for ``QwenImage21TransformerBlock`` (processors.py:129-187):
+    reuses the original block's submodules, runs the fused norm / modulation / gate /
+    SwiGLU kernels, and sends the attention through the (swapped) processor."""
+
+    def __init__(self, original_block):
+        super().__init__()
+        self.img_norm1 = original_block.img_norm1  # LayerNorm without affine (params unused)
+        self.attn = original_block.attn
+        self.img_norm2 = original_block.img_norm2
+        self.img_mlp = original_block.img_mlp
+        self._eps = self.img_norm1.eps
+
+    def forward(
+        self,
+        hidden_states: torch.Tensor,  # [B, S, D] bf16
+        modulation: torch.Tensor,     # [B (+B), 4 inner]
+        rotary_emb=None,
+        attention_mask=None,
+        target_token_mask=None,
+        layer_cache=None,
+        kv_cache_mode=None,
+        cache_write_slice=None,
+        segments=None,
+        key_valid=None,
+    ) -> torch.Tensor:
+        mod_stride = modulation.stride(0)
+        fused_qkv = getattr(self.attn, "fused_qkv", None)
+        inner = fused_qkv.out_features // 3 if fused_qkv is not None else self.attn.to_q.out_features
+        # mod1.scale @ 0, mod1.gate @ inner, mod2.scale @ 2 inner, mod2.gate @ 3 inner
+        amax1 = _new_amax(hidden_states)
+        img_mod = fused_layer_norm_modulate(hidden_states, modulation, 0, mod_stride, target_token_mask, self._eps,
+                                            amax_out=amax1)
+        attn_kwargs = dict(hidden_states=img_mod, attention_mask=attention_mask, rotary_emb=rotary_emb,
+                           layer_cache=layer_cache, kv_cache_mode=kv_cache_mode, cache_write_slice=cache_write_slice,
+                           segments=segments, key_valid=key_valid)
+        if isinstance(getattr(self.attn, "processor", None), QwenImage21KernelProcessor):
+            attn_kwargs["hidden_states_amax"] = amax1
+        attn_out = self.attn(**attn_kwargs)
+        hidden_states = fused_gate_residual(hidden_states, attn_out, modulation, inner, target_token_mask)
+
+        amax2 = _new_amax(hidden_states)
+        img_mod2 = fused_layer_norm_modulate(hidden_states, modulation, 2 * inner, mod_stride, target_token_mask,
+                                             self._eps, amax_out=amax2)
+        fused_up = getattr(self.img_mlp, "fused_up", None)
+        if fused_up is not None:
+            gate, up = _linear(fused_up, img_mod2, amax2).chunk(2, dim=-1)
+        else:
+            gate = _linear(self.img_mlp.gate_layer, img_mod2, amax2)
+            up = _linear(self.img_mlp.proj, img_mod2, amax2)
+        amax3 = _new_amax(hidden_states)
+        mlp_mid = fused_swiglu(gate, up, amax_out=amax3)
+        mlp_out = _linear(self.img_mlp.out, mlp_mid, amax3)
+        return fused_gate_residual(hidden_states, mlp_out, modulation, 3 * inner, target_token_mask)
+
+
+def convert_transformer_to_kernels(transformer, use_fp8: bool = False) -> int:
+    """Swap the stock blocks for fused kernel blocks; optionally FP8-quantize the block
+    linears (processors.py:190-211).  Returns the number of blocks converted."""
+    new_blocks = []
+    for blk in transformer.transformer_blocks:
+        kb = QwenImage21KernelBlock(blk)
+        if use_fp8:
+            for lin_name in ("to_q", "to_k", "to_v"):
+                lin = getattr(kb.attn, lin_name)
+                if isinstance(lin, torch.nn.Linear):
+                    setattr(kb.attn, lin_name, FP8Linear.from_linear(lin))
+            if isinstance(kb.attn.to_out[0], torch.nn.Linear):
+                kb.attn.to_out[0] = FP8Linear.from_linear(kb.attn.to_out[0])
+            for mlp_name in ("gate_layer", "proj", "out"):
+                lin = getattr(kb.img_mlp, mlp_name, None)
+                if isinstance(lin, torch.nn.Linear):
+                    setattr(kb.img_mlp, mlp_name, FP8Linear.from_linear(lin))
+        kb.attn.set_processor(QwenImage21KernelProcessor())
+        new_blocks.append(kb)
+    transformer.transformer_blocks = torch.nn.ModuleList(new_blocks)
+    return len(new_blocks)
