@@ -309,6 +309,43 @@ def _time_ms(fn, iters: int, flush: torch.Tensor, stream) -> float:
     return sum(a.elapsed_time(b) for a, b in evs) / iters
 
 
+def fused_ops(device: torch.device, flush: torch.Tensor, iters: int, x: torch.Tensor, mod: torch.Tensor) -> dict:
+    """HBM roofline of the four fused elementwise kernels at the t2i block shapes
+    (B = 2, S = 4352, width 3072, 24 heads of 128, MLP 12288).  Algorithmic bytes:
+    every input element read once and every output element written once (bf16), the
+    modulation rows and RoPE tables (L2-resident, shared by all rows) excluded."""
+    from qik.triton_fused import fused_gate_residual, fused_layer_norm_modulate, fused_rms_norm_rope, fused_swiglu
+    stream = torch.cuda.current_stream(device)
+    hbm = peaks()["hbm_gbs"]
+    B, S, K = x.shape
+    H, D = 24, 128
+    g = torch.Generator(device=device).manual_seed(11)
+    qkv = torch.randn(B, S, 3 * H * D, device=device, generator=g).to(torch.bfloat16)
+    q = qkv.unflatten(-1, (3 * H, D)).chunk(3, dim=-2)[0]
+    wn = torch.ones(D, device=device)
+    freqs = torch.polar(torch.ones(S, D // 2, device=device), torch.rand(S, D // 2, device=device, generator=g))
+    f = torch.randn_like(x)
+    gu = torch.randn(B * S, 2 * 12288, device=device, generator=g).to(torch.bfloat16)
+    gate, up = gu.chunk(2, dim=-1)
+    amax = torch.zeros(1, dtype=torch.int32, device=device)
+    n_x = x.numel()
+    cases = {
+        "layer_norm_modulate": (lambda: fused_layer_norm_modulate(x, mod, 0, mod.stride(0), None, 1e-6, amax), 4 * n_x),
+        "rms_norm_rope_q": (lambda: fused_rms_norm_rope(q, wn, freqs, 1e-6), 4 * q.numel()),
+        "gate_residual": (lambda: fused_gate_residual(x, f, mod, K, None), 6 * n_x),
+        "swiglu_12288": (lambda: fused_swiglu(gate, up, amax), 6 * gate.numel()),
+    }
+    res = {}
+    for name, (fn, nbytes) in cases.items():
+        for _ in range(3):
+            fn()
+        ms = _time_ms(fn, iters, flush, stream)
+        gbs = nbytes / ms / 1e6
+        res[name] = {"us": round(ms * 1e3, 1), "gbs": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3),
+                     "bytes": nbytes}
+    return res
+
+
 def extras(device: torch.device, flush: torch.Tensor, iters: int = 10) -> dict:
     """Attention at BASELINE config 4 and the DiT-block time at 1024 px (configs[2] +
     the t2i attention), each on synthetic inputs with the BASELINE shapes."""
@@ -346,11 +383,14 @@ def extras(device: torch.device, flush: torch.Tensor, iters: int = 10) -> dict:
     ms = _time_ms(run, iters, flush, stream)
     out["attention_cfg4_decode_fp8_slab"] = {"ms": round(ms, 4), "tflops": round(fl / ms / 1e9, 1),
                                              "gflop": round(fl / 1e9, 1)}
-    # DiT block @1024 px, CFG batch 2: M = 2 x 4352; QKV, block-causal
-    # attention (256 text causal + 4096 image), out-proj, FFN (GELU-tanh), and the
-    # timestep modulation linear on M = 2.  Elementwise norm/RoPE/modulate/residual
-    # ops are not part of this path and are not timed.
-    M, K = 2 * 4352, 3072
+    # DiT block @1024 px, CFG batch 2: M = 2 x 4352, the whole block --
+    # timestep modulation linear (M = 2), LayerNorm + modulate (its amax feeds the QKV
+    # quantizer), fused QKV, per-head RMSNorm + RoPE of q and k, block-causal attention
+    # (256 text causal + 4096 image), out-proj, gated residual, LayerNorm + modulate,
+    # FFN (GELU-tanh) and the second gated residual.
+    from qik.triton_fused import fused_gate_residual, fused_layer_norm_modulate, fused_rms_norm_rope
+    B2, S2 = 2, 4352
+    M, K = B2 * S2, 3072
     lin = {}
     for name, (n_out, n_in) in {"qkv": (9216, 3072), "out": (3072, 3072), "up": (12288, 3072),
                                 "down": (3072, 12288), "mod": (18432, 3072)}.items():
@@ -359,26 +399,40 @@ def extras(device: torch.device, flush: torch.Tensor, iters: int = 10) -> dict:
         f.weight.copy_(wq)
         f.weight_scale.copy_(sw)
         lin[name] = f
-    x = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
-    temb = torch.randn(2, K, device=device, generator=g).to(torch.bfloat16)
-    Lt = torch.arange(4352, dtype=torch.int32, device=device)
-    Lt[256:] = 4351
+    x = torch.randn(B2, S2, K, device=device, generator=g).to(torch.bfloat16)
+    temb = torch.randn(B2, K, device=device, generator=g).to(torch.bfloat16)
+    wn = torch.ones(D, device=device)
+    inv = 1.0 / (10000 ** (torch.arange(0, D, 2, device=device).float() / D))
+    freqs = torch.polar(torch.ones(S2, D // 2, device=device),
+                        torch.outer(torch.arange(S2, device=device).float(), inv))
+    Lt = torch.arange(S2, dtype=torch.int32, device=device)
+    Lt[256:] = S2 - 1
+    amax = torch.zeros(2, dtype=torch.int32, device=device)
 
     def block():
-        lin["mod"](temb)
-        qkv = lin["qkv"](x).view(2, 4352, 3, H, D)
-        o = attn(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2], Lt, None)
-        h = lin["out"](o.reshape(M, K))
-        return F.fp8_ffn_gelu(h, lin["up"], lin["down"])
+        mod = lin["mod"](temb) * 0.05  # [B, 6 x 3072]: scale / gate rows of the two sub-blocks
+        amax.zero_()
+        hm = fused_layer_norm_modulate(x, mod, 0, mod.stride(0), None, 1e-6, amax_out=amax[0:1])
+        qkv = lin["qkv"].forward_from_amax(hm, amax[0:1]).unflatten(-1, (3 * H, D))
+        q, k, v = qkv.chunk(3, dim=-2)
+        q = fused_rms_norm_rope(q, wn, freqs, 1e-6)
+        k = fused_rms_norm_rope(k, wn, freqs, 1e-6)
+        o = attn(q, k, v, Lt, None)
+        h = fused_gate_residual(x, lin["out"](o.flatten(2, 3)), mod, K, None)
+        hm2 = fused_layer_norm_modulate(h, mod, 2 * K, mod.stride(0), None, 1e-6)
+        f2 = F.fp8_ffn_gelu(hm2.reshape(M, K), lin["up"], lin["down"]).view(B2, S2, K)
+        return fused_gate_residual(h, f2, mod, 3 * K, None)
 
     for _ in range(3):
         block()
     ms = _time_ms(block, iters, flush, stream)
-    lin_fl = 2.0 * M * K * (9216 + 3072 + 12288) + 2.0 * M * 12288 * K + 2.0 * 2 * K * 18432
-    at_fl = 4.0 * D * H * 2 * float((Lt.long() + 1).sum())
+    lin_fl = 2.0 * M * K * (9216 + 3072 + 12288) + 2.0 * M * 12288 * K + 2.0 * B2 * K * 18432
+    at_fl = 4.0 * D * H * B2 * float((Lt.long() + 1).sum())
     out["dit_block_1024px_cfg2"] = {"ms": round(ms, 4), "tflops": round((lin_fl + at_fl) / ms / 1e9, 1),
                                     "linear_gflop": round(lin_fl / 1e9, 1), "attention_gflop": round(at_fl / 1e9, 1),
-                                    "excluded": "elementwise norm/RoPE/modulate/residual ops"}
+                                    "includes": "modulation GEMV, 2x LayerNorm+modulate, RMSNorm+RoPE (q, k), "
+                                                "attention, 4 FP8 linears (GELU FFN), 2x gated residual"}
+    out["fused_ops_t2i"] = fused_ops(device, flush, iters, x, mod=lin["mod"](temb))
     out["device_status"] = L.device_status(device)
     return out
 
@@ -492,6 +546,47 @@ def run_reference(args, rank: int, world: int) -> dict | None:
             "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def sweep(device: torch.device, iters: int = 20) -> list[dict]:
+    """the FP8 linear at K = 3072 over N x M, qik's tcgen05 GEMM
+    next to cuBLASLt (torch._scaled_mm, the reference's call, fp8.py:87-88) on the same
+    e4m3 operands and scales, and the dynamic activation quantizer at each M
+    (3 algorithmic bytes per element).  One JSON line per shape."""
+    from qik import fp8 as F
+    stream = torch.cuda.current_stream(device)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    pk = peaks()
+    g = torch.Generator(device=device).manual_seed(5)
+    K = 3072
+    rows = []
+    for N in (3072, 9216, 12288, 18432):
+        wq, sw = F.quantize_weight_tensorwise(torch.randn(N, K, device=device, generator=g) * 0.02)
+        for M in (256, 1024, 4352, 9472, 16384):
+            x = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
+            xq, sx = F.quantize_tensorwise(x)
+            runs = {"qik": lambda: F.fp8_gemm(xq, sx, wq, sw),
+                    "cublaslt": lambda: torch._scaled_mm(xq, wq.t(), scale_a=sx, scale_b=sw,
+                                                         out_dtype=torch.bfloat16)}
+            row = {"M": M, "N": N, "K": K, "gflop": round(2.0 * M * N * K / 1e9, 2)}
+            for name, fn in runs.items():
+                for _ in range(3):
+                    fn()
+                ms = _time_ms(fn, iters, flush, stream)
+                row[f"{name}_us"] = round(ms * 1e3, 2)
+                row[f"{name}_tflops"] = round(2.0 * M * N * K / ms / 1e9, 1)
+            row["qik_vs_cublaslt"] = round(row["cublaslt_us"] / row["qik_us"], 3)
+            row["qik_frac_fp8_peak"] = round(row["qik_tflops"] / pk["fp8_tflops_burst"], 3)
+            if N == 3072:
+                fn = lambda: F.quantize_tensorwise(x)  # noqa: E731
+                for _ in range(3):
+                    fn()
+                ms = _time_ms(fn, iters, flush, stream)
+                row["quantizer_us"] = round(ms * 1e3, 2)
+                row["quantizer_gbs"] = round(3.0 * M * K / ms / 1e6, 1)
+                row["quantizer_frac_hbm"] = round(row["quantizer_gbs"] / pk["hbm_gbs"], 3)
+            rows.append(row)
+    return rows
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -499,6 +594,8 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["qik", "reference"], default="qik")
     ap.add_argument("--no-extras", action="store_true", help="skip the attention / DiT-block measurements")
+    ap.add_argument("--sweep", action="store_true",
+                    help="print the configs[4] GEMM / quantizer sweep (one JSON line per shape) instead of the bench")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -514,6 +611,10 @@ def main() -> int:
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if args.sweep:
+        for row in sweep(device):
+            print(json.dumps(row), flush=True)
+        return 0
     if world > 1:
         import datetime
         torch.distributed.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))

@@ -37,7 +37,7 @@ __device__ __forceinline__ float4 ldg16f(const float* p) { return __ldg(reinterp
 
 // Block-wide max of u32 values; one atomicMax per CTA into *dst (skipped for 0).
 __device__ __forceinline__ void block_atomic_max(uint32_t v, uint32_t* dst) {
-  __shared__ uint32_t red[kThreads / 32];
+  __shared__ uint32_t red[32];
   v = __reduce_max_sync(0xffffffffu, v);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) red[warp] = v;
@@ -51,7 +51,10 @@ __device__ __forceinline__ void block_atomic_max(uint32_t v, uint32_t* dst) {
 
 // ---------------------------------------------------------------- RMSNorm + RoPE
 // G = D / 8 lanes per (b, s, h) row, 8 consecutive elements (4 rotation pairs) per
-// lane; 32 / G rows per warp.  Sum of squares reduced over the lane group.
+// lane; 32 / G rows per warp and kRopeUnroll row groups per warp iteration, whose
+// loads (x and the RoPE table rows) are all issued before any arithmetic.
+constexpr int kRopeUnroll = 4;
+
 template <int G>
 __global__ void __launch_bounds__(kThreads) rms_rope_kernel(const uint16_t* __restrict__ x, int64_t x_sb,
                                                             int64_t x_ss, int64_t x_sh, uint16_t* __restrict__ out,
@@ -59,7 +62,8 @@ __global__ void __launch_bounds__(kThreads) rms_rope_kernel(const uint16_t* __re
                                                             const float* __restrict__ w, const float* __restrict__ cs,
                                                             const float* __restrict__ sn, int64_t S, int64_t H,
                                                             int64_t nrows, float eps) {
-  constexpr int D = 8 * G, HALF = D / 2, RPW = 32 / G;
+  constexpr int D = 8 * G, HALF = D / 2, RPW = 32 / G, U = kRopeUnroll;
+  const uint32_t S32 = static_cast<uint32_t>(S), H32 = static_cast<uint32_t>(H);
   const int lane = threadIdx.x & 31;
   const int sub = lane / G, gl = lane % G;
   // weights of this lane's 8 columns: loop invariant
@@ -67,41 +71,51 @@ __global__ void __launch_bounds__(kThreads) rms_rope_kernel(const uint16_t* __re
   const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
   const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   const int64_t groups = (nrows + RPW - 1) / RPW;
-  for (int64_t wg = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); wg < groups;
-       wg += warps_total) {
-    const int64_t row = wg * RPW + sub;
-    const bool live = row < nrows;
-    const int64_t r = live ? row : 0;
-    const int64_t h = r % H, bs = r / H;
-    const int64_t s = bs % S, b = bs / S;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (live) v = ldg16(x + b * x_sb + s * x_ss + h * x_sh + gl * 8);
-    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-    float xe[4], xo[4];
-    float ss = 0.0f;
+  for (int64_t wg0 = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) * U; wg0 < groups;
+       wg0 += warps_total * U) {
+    uint4 v[U];
+    float4 c4[U], s4[U];
+    int64_t dst[U];
+    bool live[U];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      xe[i] = bf_lo(u[i]);
-      xo[i] = bf_hi(u[i]);
-      ss = fmaf(xe[i], xe[i], ss);
-      ss = fmaf(xo[i], xo[i], ss);
+    for (int u = 0; u < U; ++u) {
+      const int64_t row = (wg0 + u) * RPW + sub;
+      live[u] = row < nrows;
+      const uint32_t r = live[u] ? static_cast<uint32_t>(row) : 0u;  // nrows < 2^31 (host check)
+      const uint32_t bs = r / H32, h = r - bs * H32;
+      const uint32_t b = bs / S32, s = bs - b * S32;
+      v[u] = live[u] ? ldg16(x + b * x_sb + s * x_ss + h * x_sh + gl * 8) : make_uint4(0u, 0u, 0u, 0u);
+      c4[u] = ldg16f(cs + static_cast<int64_t>(s) * HALF + gl * 4);
+      s4[u] = ldg16f(sn + static_cast<int64_t>(s) * HALF + gl * 4);
+      dst[u] = b * o_sb + s * o_ss + h * o_sh + gl * 8;
     }
 #pragma unroll
-    for (int o = G / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float rrms = rsqrtf(ss / static_cast<float>(D) + eps);
-    const float4 c4 = ldg16f(cs + s * HALF + gl * 4), s4 = ldg16f(sn + s * HALF + gl * 4);
-    const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
-    uint32_t o4[4];
+    for (int u = 0; u < U; ++u) {
+      const uint32_t uu[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      float xe[4], xo[4];
+      float ss = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      // fp32 norm, one rounding to bf16, back to fp32 for the rotation
-      const float ne = round_bf16((xe[i] * rrms) * wv[2 * i]);
-      const float no = round_bf16((xo[i] * rrms) * wv[2 * i + 1]);
-      // (e + i o)(c + i s) = (e c - o s) + i (e s + o c)
-      o4[i] = pack_bf16x2(ne * cv[i] - no * sv[i], ne * sv[i] + no * cv[i]);
+      for (int i = 0; i < 4; ++i) {
+        xe[i] = bf_lo(uu[i]);
+        xo[i] = bf_hi(uu[i]);
+        ss = fmaf(xe[i], xe[i], ss);
+        ss = fmaf(xo[i], xo[i], ss);
+      }
+#pragma unroll
+      for (int o = G / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float rrms = rsqrtf(ss / static_cast<float>(D) + eps);
+      const float cv[4] = {c4[u].x, c4[u].y, c4[u].z, c4[u].w}, sv[4] = {s4[u].x, s4[u].y, s4[u].z, s4[u].w};
+      uint32_t o4[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        // fp32 norm, one rounding to bf16, back to fp32 for the rotation
+        const float ne = round_bf16((xe[i] * rrms) * wv[2 * i]);
+        const float no = round_bf16((xo[i] * rrms) * wv[2 * i + 1]);
+        // (e + i o)(c + i s) = (e c - o s) + i (e s + o c)
+        o4[i] = pack_bf16x2(ne * cv[i] - no * sv[i], ne * sv[i] + no * cv[i]);
+      }
+      if (live[u]) *reinterpret_cast<uint4*>(out + dst[u]) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
     }
-    if (live)
-      *reinterpret_cast<uint4*>(out + b * o_sb + s * o_ss + h * o_sh + gl * 8) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
   }
 }
 
@@ -176,37 +190,88 @@ __global__ void __launch_bounds__(kThreads) ln_modulate_kernel(const uint16_t* _
 }
 
 // ---------------------------------------------------------------- gate + residual
-// 8 elements per thread iteration; rows of D contiguous elements.
-__global__ void __launch_bounds__(kThreads) gate_residual_kernel(const uint16_t* __restrict__ x,
-                                                                 const uint16_t* __restrict__ f,
-                                                                 const uint16_t* __restrict__ mod, int64_t mod_stride,
-                                                                 int64_t gate_off, const uint8_t* __restrict__ tmask,
-                                                                 uint16_t* __restrict__ out, int64_t B, int64_t S,
-                                                                 int64_t D) {
-  const int64_t nvr = D >> 3;
-  const int64_t total = B * S * nvr;
-  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += nthreads) {
-    const int64_t row = i / nvr, v = i - row * nvr;
-    const int64_t b = row / S, s = row % S;
-    const int64_t mrow = (tmask == nullptr || tmask[s] != 0) ? b : B + b;
-    const uint4 g4 = ldg16(mod + mrow * mod_stride + gate_off + v * 8);
-    const uint4 x4 = ldg16(x + i * 8), f4 = ldg16(f + i * 8);
-    const uint32_t gu[4] = {g4.x, g4.y, g4.z, g4.w}, xu[4] = {x4.x, x4.y, x4.z, x4.w},
-                   fu[4] = {f4.x, f4.y, f4.z, f4.w};
-    uint32_t o[4];
+// Thread = one 8-column vector of the width, walking kGateRows consecutive rows
+// (4 at a time, loads first).  bf16(tanh(gate)) depends only on the modulation row
+// (b for target positions, B + b otherwise), so each thread computes it once per
+// distinct row it meets and keeps the two rows of the current sample in registers.
+constexpr int kGateRows = 32;
+constexpr int kGateThreads = 128;
+
+struct GateCache {
+  int64_t row;
+  float t[8];
+};
+
+__device__ __forceinline__ void gate_fill(GateCache& c, int64_t mrow, const uint16_t* __restrict__ mod,
+                                          int64_t mod_stride, int64_t col) {
+  const uint4 g4 = ldg16(mod + mrow * mod_stride + col);
+  const uint32_t gu[4] = {g4.x, g4.y, g4.z, g4.w};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float t0 = round_bf16(round_bf16(tanhf(bf_lo(gu[j]))) * bf_lo(fu[j]));
-      const float t1 = round_bf16(round_bf16(tanhf(bf_hi(gu[j]))) * bf_hi(fu[j]));
-      o[j] = pack_bf16x2(bf_lo(xu[j]) + t0, bf_hi(xu[j]) + t1);
+  for (int j = 0; j < 4; ++j) {
+    c.t[2 * j] = round_bf16(tanhf(bf_lo(gu[j])));
+    c.t[2 * j + 1] = round_bf16(tanhf(bf_hi(gu[j])));
+  }
+  c.row = mrow;
+}
+
+__global__ void __launch_bounds__(kGateThreads, 7) gate_residual_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ f, const uint16_t* __restrict__ mod,
+    int64_t mod_stride, int64_t gate_off, const uint8_t* __restrict__ tmask, uint16_t* __restrict__ out, int64_t B,
+    int64_t S, int64_t D) {
+  const int64_t nvr = D >> 3;
+  const int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (v >= nvr) return;
+  const int64_t rows = B * S;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * kGateRows;
+  const int64_t r1 = min(rows, r0 + kGateRows);
+  const int64_t col = gate_off + v * 8;
+  GateCache ct, cz;  // row b (target positions) and row B + b (t = 0 positions)
+  ct.row = cz.row = -1;
+  for (int64_t rb = r0; rb < r1; rb += 4) {
+    uint4 x4[4], f4[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int64_t r = rb + k;
+      x4[k] = r < r1 ? ldg16(x + r * D + v * 8) : make_uint4(0u, 0u, 0u, 0u);
+      f4[k] = r < r1 ? ldg16(f + r * D + v * 8) : make_uint4(0u, 0u, 0u, 0u);
     }
-    *reinterpret_cast<uint4*>(out + i * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int64_t r = rb + k;
+      if (r >= r1) break;
+      const int64_t b = static_cast<uint32_t>(r) / static_cast<uint32_t>(S);  // rows < 2^31 (host check)
+      const int64_t s = r - b * S;
+      const uint32_t xu[4] = {x4[k].x, x4[k].y, x4[k].z, x4[k].w}, fu[4] = {f4[k].x, f4[k].y, f4[k].z, f4[k].w};
+      uint32_t o[4];
+      auto apply = [&](const GateCache& c) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float t0 = round_bf16(c.t[2 * j] * bf_lo(fu[j]));
+          const float t1 = round_bf16(c.t[2 * j + 1] * bf_hi(fu[j]));
+          o[j] = pack_bf16x2(bf_lo(xu[j]) + t0, bf_hi(xu[j]) + t1);
+        }
+      };
+      if (tmask == nullptr || tmask[s] != 0) {
+        if (ct.row != b) gate_fill(ct, b, mod, mod_stride, col);
+        apply(ct);
+      } else {
+        if (cz.row != B + b) gate_fill(cz, B + b, mod, mod_stride, col);
+        apply(cz);
+      }
+      *reinterpret_cast<uint4*>(out + r * D + v * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
   }
 }
 
 // ---------------------------------------------------------------- SwiGLU
-__device__ __forceinline__ float silu_bf16(float g) { return round_bf16(g / (1.0f + __expf(-g))); }
+// silu(g) = g / (1 + e^-g) with the reciprocal from rcp.approx (an error of about one
+// fp32 ulp, far below the bf16 rounding of the result; 1 / inf = 0 gives
+// silu(-large) = -0).
+__device__ __forceinline__ float silu_bf16(float g) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + __expf(-g)));
+  return round_bf16(g * r);
+}
 
 __global__ void __launch_bounds__(kThreads) swiglu_kernel(const uint16_t* __restrict__ g, int64_t ld_g,
                                                           const uint16_t* __restrict__ p, int64_t ld_p,
@@ -216,17 +281,34 @@ __global__ void __launch_bounds__(kThreads) swiglu_kernel(const uint16_t* __rest
   const int64_t total = M * nvr;
   const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
   uint32_t am2 = 0;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += nthreads) {
-    const int64_t m = i / nvr, c = (i - m * nvr) * 8;
-    const uint4 g4 = ldg16(g + m * ld_g + c), p4 = ldg16(p + m * ld_p + c);
-    const uint32_t gu[4] = {g4.x, g4.y, g4.z, g4.w}, pu[4] = {p4.x, p4.y, p4.z, p4.w};
-    uint32_t o[4];
+  // two vectors per iteration, both loads issued first
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += 2 * nthreads) {
+    uint4 g4[2], p4[2];
+    int64_t off[2][3];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      o[j] = pack_bf16x2(silu_bf16(bf_lo(gu[j])) * bf_lo(pu[j]), silu_bf16(bf_hi(gu[j])) * bf_hi(pu[j]));
-      am2 = absmax_bf16x2(am2, o[j]);
+    for (int k = 0; k < 2; ++k) {
+      const int64_t e = i + k * nthreads;
+      // total < 2^31 (host check): 32-bit division
+      const int64_t m = e < total ? static_cast<uint32_t>(e) / static_cast<uint32_t>(nvr) : 0;
+      const int64_t c = e < total ? (e - m * nvr) * 8 : 0;
+      off[k][0] = m * ld_g + c;
+      off[k][1] = m * ld_p + c;
+      off[k][2] = m * ld_o + c;
+      g4[k] = e < total ? ldg16(g + off[k][0]) : make_uint4(0u, 0u, 0u, 0u);
+      p4[k] = e < total ? ldg16(p + off[k][1]) : make_uint4(0u, 0u, 0u, 0u);
     }
-    *reinterpret_cast<uint4*>(out + m * ld_o + c) = make_uint4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      if (i + k * nthreads >= total) break;
+      const uint32_t gu[4] = {g4[k].x, g4[k].y, g4[k].z, g4[k].w}, pu[4] = {p4[k].x, p4[k].y, p4[k].z, p4[k].w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        o[j] = pack_bf16x2(silu_bf16(bf_lo(gu[j])) * bf_lo(pu[j]), silu_bf16(bf_hi(gu[j])) * bf_hi(pu[j]));
+        am2 = absmax_bf16x2(am2, o[j]);
+      }
+      *reinterpret_cast<uint4*>(out + off[k][2]) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
   }
   if (amax_out) block_atomic_max(max(am2 & 0xFFFFu, am2 >> 16) << 16, amax_out);
 }
@@ -258,11 +340,12 @@ int qik_rms_norm_rope(const void* x, int64_t B, int64_t S, int64_t H, int64_t D,
                      static_cast<long long>(D));
   QIK_REQUIRE(aligned16(x) && aligned16(out) && aligned16(weight) && aligned16(cos_tab) && aligned16(sin_tab),
               "qik_rms_norm_rope: pointers must be 16-byte aligned");
+  QIK_REQUIRE(nrows < (int64_t{1} << 31), "qik_rms_norm_rope: more than 2^31 rows");
   QIK_REQUIRE(aligned_elems(x_sb) && aligned_elems(x_ss) && aligned_elems(x_sh) && aligned_elems(o_sb) &&
                   aligned_elems(o_ss) && aligned_elems(o_sh),
               "qik_rms_norm_rope: strides must be multiples of 8 elements");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int rows_per_cta = (kThreads / 32) * (32 / static_cast<int>(D / 8));
+  const int rows_per_cta = (kThreads / 32) * (32 / static_cast<int>(D / 8)) * kRopeUnroll;
   const int grid = grid_cap((nrows + rows_per_cta - 1) / rows_per_cta, 8);
   const uint16_t* xs = static_cast<const uint16_t*>(x);
   uint16_t* os = static_cast<uint16_t*>(out);
@@ -285,6 +368,7 @@ int qik_layer_norm_modulate(const void* x, int64_t B, int64_t S, int64_t D, cons
   if (B * S == 0) return QIK_OK;
   QIK_REQUIRE(x && modulation && out, "qik_layer_norm_modulate: NULL pointer");
   QIK_REQUIRE(D % 8 == 0 && D <= 4096, "qik_layer_norm_modulate: D must be a multiple of 8 and at most 4096");
+  QIK_REQUIRE(B * S < (int64_t{1} << 31), "qik_layer_norm_modulate: more than 2^31 rows");
   QIK_REQUIRE(aligned16(x) && aligned16(out) && aligned16(modulation),
               "qik_layer_norm_modulate: pointers must be 16-byte aligned");
   QIK_REQUIRE(aligned_elems(mod_stride) && aligned_elems(scale_off) && scale_off >= 0 && scale_off + D <= mod_stride,
@@ -320,14 +404,17 @@ int qik_gate_residual(const void* x, const void* f, int64_t B, int64_t S, int64_
   QIK_REQUIRE(D % 8 == 0, "qik_gate_residual: D must be a multiple of 8");
   QIK_REQUIRE(aligned16(x) && aligned16(f) && aligned16(out) && aligned16(modulation),
               "qik_gate_residual: pointers must be 16-byte aligned");
+  QIK_REQUIRE(B * S < (int64_t{1} << 31), "qik_gate_residual: more than 2^31 rows");
   QIK_REQUIRE(aligned_elems(mod_stride) && aligned_elems(gate_off) && gate_off >= 0 && gate_off + D <= mod_stride,
               "qik_gate_residual: modulation stride/offset must be multiples of 8 with offset + D <= stride");
   QIK_REQUIRE(mod_rows >= (target_mask ? 2 * B : B), "qik_gate_residual: %lld modulation rows; B = %lld needs %s",
               static_cast<long long>(mod_rows), static_cast<long long>(B),
               target_mask ? "2B (rows B..2B-1 are the t = 0 rows)" : "B");
-  const int64_t total = B * S * (D / 8);
-  const int grid = grid_cap((total + kThreads - 1) / kThreads, 8);
-  gate_residual_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+  const dim3 grid(static_cast<unsigned>((D / 8 + kGateThreads - 1) / kGateThreads),
+                  static_cast<unsigned>((B * S + kGateRows - 1) / kGateRows));
+  QIK_REQUIRE((B * S + kGateRows - 1) / kGateRows < 65536, "qik_gate_residual: too many rows (%lld)",
+              static_cast<long long>(B * S));
+  gate_residual_kernel<<<grid, kGateThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(f), static_cast<const uint16_t*>(modulation),
       mod_stride, gate_off, target_mask, static_cast<uint16_t*>(out), B, S, D);
   return check_launch("gate_residual_kernel");
@@ -343,7 +430,8 @@ int qik_swiglu(const void* gate, int64_t ld_gate, const void* up, int64_t ld_up,
   QIK_REQUIRE(ld_gate >= N && ld_up >= N && ld_out >= N, "qik_swiglu: row pitch smaller than N");
   QIK_REQUIRE(aligned16(gate) && aligned16(up) && aligned16(out), "qik_swiglu: pointers must be 16-byte aligned");
   const int64_t total = M * (N / 8);
-  const int grid = grid_cap((total + kThreads - 1) / kThreads, 8);
+  QIK_REQUIRE(total < (int64_t{1} << 31), "qik_swiglu: more than 2^34 elements");
+  const int grid = grid_cap((total + 2 * kThreads - 1) / (2 * kThreads), 8);
   swiglu_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t*>(gate), ld_gate, static_cast<const uint16_t*>(up), ld_up,
       static_cast<uint16_t*>(out), ld_out, M, N, amax_out);
