@@ -195,13 +195,17 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
 
     # ---- per-launch GEMM durations (roofline): the same step launch by launch
     ev_k = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
-    torch.cuda._sleep(int(2e7))
+    torch.cuda._sleep(int(1e8))  # ~50 ms head start: the host queues every split step
     for i in range(args.steps):
         flush.fill_(float(i))
         step_split(x, ev_k[i])
     barrier()
-    t_gemm = [ev[0].elapsed_time(ev[1]) for ev in ev_k] + [ev[2].elapsed_time(ev[3]) for ev in ev_k]
-    gemm_ms = sum(t_gemm) / len(t_gemm)
+    torch.cuda.synchronize(device)
+    # median per GEMM shape, then their mean: one interval that caught a host stall
+    # (the queue running dry) cannot move the roofline
+    t1 = sorted(ev[0].elapsed_time(ev[1]) for ev in ev_k)
+    t2 = sorted(ev[2].elapsed_time(ev[3]) for ev in ev_k)
+    gemm_ms = 0.5 * (t1[len(t1) // 2] + t2[len(t2) // 2])
 
     # ---- end-to-end through the public API with host buffers
     x_host = x_cpu.pin_memory()
@@ -269,7 +273,7 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
         "gpu_launches_note": "qik kernels inside the timed regions (device-resident steps + e2e steps: "
                              "amax, pack, GEMM+GELU+amax, pack, GEMM per step, chained with programmatic "
                              "dependent launch); the L2-flush fills are torch's; GEMM launch times for the "
-                             "roofline come from a second pass that runs the step launch by launch with events",
+                             "roofline come from a second pass that runs the step launch by launch with events (median per GEMM)",
         "device_status": int(status),
         "clocks": clocks,
     }

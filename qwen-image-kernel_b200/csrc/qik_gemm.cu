@@ -3,17 +3,25 @@
 // C[M,N] = epilogue(A[M,K] . B[N,K]^T): the W8A8 per-tensor linear of
 // FP8Linear.forward (qwen_image_kernel/fp8.py:78-90), whose reference computes it
 // with torch._scaled_mm.  Design:
-//   * persistent CTAs (one per SM), tiles of 128 x BN outputs visited round-robin;
-//   * warp 0: TMA producer -- one 128x128 A box and one BNx128 B box per stage,
-//     128-byte swizzle, no cluster multicast (each CTA loads its own tiles; L2
-//     absorbs the cross-CTA reuse);
-//   * warp 1: one thread issues tcgen05.mma.kind::f8f6f4 (M=128, N=BN, K=32 per
-//     instruction) into a double-buffered fp32 accumulator in tensor memory and
-//     releases smem stages / accumulators with tcgen05.commit;
-//   * warps 2-5: epilogue -- tcgen05.ld of one accumulator row per thread, scale by
-//     sa*sb, optional bias and GELU-tanh, bf16/fp32 stores, optional amax of the
-//     bf16 output for the next dynamic quantization.
+//   * persistent CTAs, output tiles visited round-robin, in one of two modes:
+//     - CTA pairs (clusters of 2, the default from M = 512): 256 x 256 tiles computed
+//       by tcgen05.mma.cta_group::2 -- each CTA loads 128 rows of A and 128 rows of B
+//       per stage, so a CTA moves 32 KB instead of 48 KB per 128-deep K step for the
+//       same 128 x 256 share of the output, with 6 pipeline stages;
+//     - single CTAs with 128 x BN tiles (BN = 256, 128 or 64) for skinny M;
+//   * warp 0: TMA producer -- 128-byte swizzle, no cluster multicast (each CTA loads
+//     its own tiles; in a pair both CTAs' loads complete on the leader's barrier);
+//   * warp 1: one thread (of the leader CTA in a pair) issues tcgen05.mma.kind::f8f6f4
+//     (K = 32 per instruction) into a double-buffered fp32 accumulator in tensor
+//     memory and releases smem stages / accumulators with tcgen05.commit (multicast
+//     to both CTAs of a pair);
+//   * warps 2-9: epilogue -- tcgen05.ld of the CTA's own accumulator rows, scale by
+//     sa*sb, optional bias and GELU-tanh, bf16/fp32 via swizzled staging and TMA
+//     stores, optional amax of the bf16 output for the next dynamic quantization.
 // The epilogue of tile i overlaps the MMAs of tile i+1.
+#include <stdlib.h>
+#include <string.h>
+
 #include "qik_device.cuh"
 #include "qik_host.h"
 
@@ -37,10 +45,12 @@ struct GemmParams {
   int* status;
 };
 
-template <int BN, int STAGES>
+// TWO_SM: the CTA is half of a 2-CTA cluster computing 256 x BN tiles with
+// tcgen05.mma.cta_group::2 -- it loads 128 rows of A and BN / 2 rows of B per stage.
+template <int BN, int STAGES, bool TWO_SM = false>
 struct GemmLayout {
   static constexpr int kABytes = kGemmBM * kGemmBK;
-  static constexpr int kBBytes = BN * kGemmBK;
+  static constexpr int kBBytes = (TWO_SM ? BN / 2 : BN) * kGemmBK;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStageOutOffset = STAGES * kStageBytes;  // 8 warps x 2 buffers x 2 KB
   static constexpr int kOutBufBytes = 2048;                      // 32 rows x 64 bytes
@@ -64,11 +74,12 @@ __device__ __forceinline__ float gelu_tanh_f32(float x) {
   return x * r;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool TWO_SM>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
-  using Lay = GemmLayout<BN, STAGES>;
+  using Lay = GemmLayout<BN, STAGES, TWO_SM>;
+  constexpr int kTileM = TWO_SM ? 2 * kGemmBM : kGemmBM;  // output rows per tile
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -83,6 +94,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = TWO_SM ? cluster_ctarank() : 0u;  // 0 = leader (issues the MMAs)
+  // tile index, and the stride over tiles: one per CTA, or one per CTA pair
+  const int tile0 = TWO_SM ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int tile_step = TWO_SM ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -91,7 +106,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], kGemmEpiWarps);
+      // the leader's accumulator is free once the epilogue warps of both CTAs drained it
+      mbar_init(&tempty[a], TWO_SM ? 2 * kGemmEpiWarps : kGemmEpiWarps);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -100,17 +116,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Lay::kTmemCols);
-    tmem_relinquish();
+    if constexpr (TWO_SM) {
+      tmem_alloc_cg2(tmem_slot, Lay::kTmemCols);
+      tmem_relinquish_cg2();
+    } else {
+      tmem_alloc(tmem_slot, Lay::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (TWO_SM) cluster_sync();  // both CTAs' barriers exist before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // the set-up above overlaps the predecessor's tail; operands are read below
   pdl_wait();
 
-  const int num_m = (p.M + kGemmBM - 1) / kGemmBM;
+  const int num_m = (p.M + kTileM - 1) / kTileM;
   const int num_n = (p.N + BN - 1) / BN;
   const int num_k = (p.K + kGemmBK - 1) / kGemmBK;
   const int tiles = num_m * num_n;
@@ -119,13 +141,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+      // TWO_SM: both CTAs' loads complete on the leader's full barrier, which alone
+      // expects the bytes of the pair
+      const uint32_t full_leader = TWO_SM ? mapa_shared(full, 0) : 0u;
+      for (int tile = tile0; tile < tiles; tile += tile_step) {
         const int mb = tile / num_n, nb = tile % num_n;
         for (int kb = 0; kb < num_k; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status)) goto producer_done;
-          mbar_arrive_expect_tx(&full[stage], Lay::kStageBytes);
-          tma_load_2d(sA + stage * Lay::kABytes, &tmA, kb * kGemmBK, mb * kGemmBM, &full[stage]);
-          tma_load_2d(sB + stage * Lay::kBBytes, &tmB, kb * kGemmBK, nb * BN, &full[stage]);
+          if constexpr (TWO_SM) {
+            if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, p.status)) goto producer_done;
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Lay::kStageBytes);
+            const uint32_t bar = full_leader + static_cast<uint32_t>(stage) * 8u;
+            tma_load_2d_cg2(sA + stage * Lay::kABytes, &tmA, kb * kGemmBK,
+                            mb * kTileM + static_cast<int>(rank) * kGemmBM, bar);
+            tma_load_2d_cg2(sB + stage * Lay::kBBytes, &tmB, kb * kGemmBK,
+                            nb * BN + static_cast<int>(rank) * (BN / 2), bar);
+          } else {
+            if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status)) goto producer_done;
+            mbar_arrive_expect_tx(&full[stage], Lay::kStageBytes);
+            tma_load_2d(sA + stage * Lay::kABytes, &tmA, kb * kGemmBK, mb * kGemmBM, &full[stage]);
+            tma_load_2d(sB + stage * Lay::kBBytes, &tmB, kb * kGemmBK, nb * BN, &full[stage]);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -136,20 +171,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     pdl_trigger();
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f32acc(0, 0, 0, 0, kGemmBM, BN);
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_f32acc(0, 0, 0, 0, kTileM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
-      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+      for (int tile = tile0; tile < tiles; tile += tile_step, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.status)) break;
+        const bool got = TWO_SM ? mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, abort_flag, p.status)
+                                : mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.status);
+        if (!got) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         bool ok = true;
         for (int kb = 0; kb < num_k; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, p.status)) {
+          const bool ready = TWO_SM ? mbar_wait_cluster(&full[stage], phase, abort_flag, p.status)
+                                    : mbar_wait(&full[stage], phase, abort_flag, p.status);
+          if (!ready) {
             ok = false;
             break;
           }
@@ -160,16 +199,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int k = 0; k < kGemmBK / 32; ++k) {
             const uint64_t ad = sdesc_sw128(a_addr + k * 32, 16, 1024);
             const uint64_t bd = sdesc_sw128(b_addr + k * 32, 16, 1024);
-            umma_f8f6f4_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            if constexpr (TWO_SM)
+              umma_f8f6f4_ss_cg2(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            else
+              umma_f8f6f4_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
           }
-          umma_commit(&empty[stage]);
+          if constexpr (TWO_SM)
+            umma_commit_cg2(&empty[stage], 0x3);  // the stage of both CTAs is free
+          else
+            umma_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull[acc]);
+        if constexpr (TWO_SM)
+          umma_commit_cg2(&tfull[acc], 0x3);  // both CTAs' halves of the accumulator are ready
+        else
+          umma_commit(&tfull[acc]);
       }
     }
     pdl_trigger();
@@ -186,14 +234,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t amax_local = 0;
     int local = 0;
     int buf = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+    for (int tile = tile0; tile < tiles; tile += tile_step, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status)) break;
+      const bool got = TWO_SM ? mbar_wait_cluster(&tfull[acc], acc_phase, abort_flag, p.status)
+                              : mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status);
+      if (!got) break;
       tc_fence_after();
-      if (tile + static_cast<int>(gridDim.x) >= tiles) pdl_trigger();  // last tile of this CTA
+      if (tile + tile_step >= tiles) pdl_trigger();  // last tile of this CTA
       const int mb = tile / num_n, nb = tile % num_n;
-      const int row0 = mb * kGemmBM + quarter * 32;
+      const int row0 = mb * kTileM + static_cast<int>(rank) * kGemmBM + quarter * 32;
       const bool row_ok = row0 + lane < p.M;
 #pragma unroll 1
       for (int c = half; c < BN / 32; c += 2) {
@@ -278,7 +328,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (lane == 0) {
+        if constexpr (TWO_SM)
+          mbar_arrive_remote(mapa_shared(&tempty[acc], 0));  // the leader's accumulator barrier
+        else
+          mbar_arrive(&tempty[acc]);
+      }
     }
     if (lane == 0) bulk_wait_all();
     if (p.amax_out) {
@@ -287,24 +342,60 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   }
 
+  tc_fence_before();
   __syncthreads();
+  // the leader's MMAs read the peer's shared memory and write its tensor memory: neither
+  // CTA frees either before both are done
+  if constexpr (TWO_SM) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Lay::kTmemCols);
+    if constexpr (TWO_SM)
+      tmem_dealloc_cg2(tmem_base, Lay::kTmemCols);
+    else
+      tmem_dealloc(tmem_base, Lay::kTmemCols);
   }
 }
 
-template <int BN, int STAGES>
+// Tile configurations: CTA pairs with 256 x 256 tiles, or single CTAs with 128 x BN
+// tiles.  QIK_GEMM_CFG = "2sm" | "256" | "128" | "64" in the environment forces one of
+// them for every shape (a comparison switch for measurements; read once per process).
+enum GemmCfg { kCfgAuto = 0, kCfg2Sm, kCfg256, kCfg128, kCfg64 };
+static GemmCfg gemm_cfg_override() {
+  static const GemmCfg cfg = [] {
+    const char* v = getenv("QIK_GEMM_CFG");
+    if (!v) return kCfgAuto;
+    if (!strcmp(v, "2sm")) return kCfg2Sm;
+    if (!strcmp(v, "256")) return kCfg256;
+    if (!strcmp(v, "128")) return kCfg128;
+    if (!strcmp(v, "64")) return kCfg64;
+    return kCfgAuto;
+  }();
+  return cfg;
+}
+
+// Shape -> tile configuration, from the configs[4] sweep (K = 3072) with every
+// configuration forced in turn: CTA pairs win from M = 512 up and at M = 256 once
+// N >= 12288; at M = 256 with a narrower N, 128 x 128 single-CTA tiles (more CTAs on
+// the same work) win; below 128 rows a single 128-row tile spans M and the N tiles
+// spread the weight stream over the SMs.
+static GemmCfg gemm_pick_cfg(int64_t M, int64_t N) {
+  if (M > 2 * kGemmBM) return kCfg2Sm;
+  if (M > kGemmBM) return N >= 12288 ? kCfg2Sm : kCfg128;
+  return (N + 127) / 128 >= sm_count() / 2 ? kCfg128 : kCfg64;
+}
+
+template <int BN, int STAGES, bool TWO_SM>
 static int launch_gemm(const uint8_t* A, const uint8_t* B, const GemmParams& p, int64_t lda, int64_t ldb,
                        cudaStream_t st, bool pdl) {
-  using Lay = GemmLayout<BN, STAGES>;
+  using Lay = GemmLayout<BN, STAGES, TWO_SM>;
+  constexpr int kBRows = TWO_SM ? BN / 2 : BN;  // rows of B each CTA loads per stage
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, static_cast<uint64_t>(p.K),
                         static_cast<uint64_t>(p.M), static_cast<uint64_t>(lda), kGemmBK, kGemmBM,
                         CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.N),
-                    static_cast<uint64_t>(ldb), kGemmBK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+                    static_cast<uint64_t>(ldb), kGemmBK, kBRows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   CUtensorMap tc;
   if (p.out_f32)
@@ -318,14 +409,35 @@ static int launch_gemm(const uint8_t* A, const uint8_t* B, const GemmParams& p, 
   int dev = 0;
   QIK_TRY_CUDA(cudaGetDevice(&dev));
   if (dev < 64 && !attr_set[dev]) {
-    QIK_TRY_CUDA(cudaFuncSetAttribute(fp8_gemm_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      Lay::kSmemBytes));
+    QIK_TRY_CUDA(cudaFuncSetAttribute(fp8_gemm_kernel<BN, STAGES, TWO_SM>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kSmemBytes));
     attr_set[dev] = true;
   }
-  const int tiles = ((p.M + kGemmBM - 1) / kGemmBM) * ((p.N + BN - 1) / BN);
-  const int grid = min(tiles, sm_count());
-  QIK_TRY_CUDA(launch_kernel(fp8_gemm_kernel<BN, STAGES>, dim3(grid), dim3(kGemmThreads), Lay::kSmemBytes, st, pdl,
-                             ta, tb, tc, p));
+  constexpr int kTileM = TWO_SM ? 2 * kGemmBM : kGemmBM;
+  const int tiles = ((p.M + kTileM - 1) / kTileM) * ((p.N + BN - 1) / BN);
+  if constexpr (TWO_SM) {
+    // persistent CTA pairs (clusters of 2), at most one CTA per SM
+    const int pairs = min(tiles, sm_count() / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = Lay::kSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    QIK_TRY_CUDA(cudaLaunchKernelEx(&cfg, fp8_gemm_kernel<BN, STAGES, TWO_SM>, ta, tb, tc, p));
+  } else {
+    const int grid = min(tiles, sm_count());
+    QIK_TRY_CUDA(launch_kernel(fp8_gemm_kernel<BN, STAGES, TWO_SM>, dim3(grid), dim3(kGemmThreads), Lay::kSmemBytes,
+                               st, pdl, ta, tb, tc, p));
+  }
   return check_launch("fp8_gemm_kernel");
 }
 
@@ -361,7 +473,18 @@ int launch_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, in
   p.epilogue = epilogue;
   p.amax_out = amax_out;
   p.status = status;
-  return launch_gemm<256, 4>(A, B, p, lda, ldb, stream, pdl);
+  GemmCfg cfg = gemm_cfg_override();
+  if (cfg == kCfgAuto) cfg = gemm_pick_cfg(M, N);
+  switch (cfg) {
+    case kCfg2Sm:
+      return launch_gemm<256, 6, true>(A, B, p, lda, ldb, stream, pdl);
+    case kCfg128:
+      return launch_gemm<128, 6, false>(A, B, p, lda, ldb, stream, pdl);
+    case kCfg64:
+      return launch_gemm<64, 8, false>(A, B, p, lda, ldb, stream, pdl);
+    default:
+      return launch_gemm<256, 4, false>(A, B, p, lda, ldb, stream, pdl);
+  }
 }
 
 }  // namespace qik
