@@ -109,6 +109,14 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* m
       "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
       : "memory");
 }
+// Untiled bulk copy of `bytes` (multiple of 16; both addresses 16-byte aligned) from
+// global memory into this CTA's shared memory, completing on `bar` (tx bytes).
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
 // 2-D tiled store from this CTA's shared memory (bulk-group completion); elements
 // outside the tensor are not written.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, int32_t x, int32_t y, const void* smem_src) {

@@ -20,7 +20,9 @@ namespace qik {
 
 struct QuantWs {
   uint32_t amax_bits;
-  uint32_t pad[3];
+  uint32_t arrived;  // CTAs past phase 1 of the single-pass quantizer
+  uint32_t go;       // set by the last of them: the amax is complete
+  uint32_t pad;
 };
 
 constexpr int kQuantThreads = 256;
@@ -253,6 +255,183 @@ __global__ void __launch_bounds__(kQuantThreads) kv_store_kernel(
   }
 }
 
+// ---------------------------------------------------------------- single-pass activation quantizer
+// One CTA per SM, launched cooperatively (all CTAs resident at once).  Phase 1: each
+// CTA streams the first kQfSmemBytes of its contiguous slice into shared memory with
+// bulk copies (16 KB chunks, each on its own mbarrier, all issued up front so the
+// copy engine keeps the whole slice in flight), reduces max|x| chunk by chunk as the
+// chunks land, reads any remainder of the slice with plain loads, and folds its
+// maximum into the global amax.  A grid barrier (arrival counter + release flag in
+// the workspace, spin bounded by QIK_WAIT_NS) makes the amax complete.  Phase 2: each
+// CTA packs its slice from shared memory where it was kept, so a tensor up to
+// ~28 MB (148 x 192 KB) is read from HBM exactly once: 2 B read + 1 B written per
+// element.  On a timeout the kernel writes no codes and a NaN scale.
+constexpr int kQfThreads = 512;
+constexpr int kQfChunkVecs = 1024;  // 16 KB per bulk copy
+constexpr int kQfChunks = 12;
+constexpr int kQfSmemVecs = kQfChunkVecs * kQfChunks;
+constexpr int kQfSmemBytes = kQfSmemVecs * 16;
+
+__device__ __forceinline__ uint32_t pack8_e4m3(const uint4 a, float inv, uint32_t& hi_word) {
+  const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+  uint32_t o[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const uint32_t u0 = w[2 * j], u1 = w[2 * j + 1];
+    const uint16_t lo = cvt_e4m3x2(__uint_as_float(u0 << 16) * inv, __uint_as_float(u0 & 0xFFFF0000u) * inv);
+    const uint16_t hi = cvt_e4m3x2(__uint_as_float(u1 << 16) * inv, __uint_as_float(u1 & 0xFFFF0000u) * inv);
+    o[j] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+  }
+  hi_word = o[1];
+  return o[0];
+}
+
+__device__ __forceinline__ uint32_t absmax8(uint32_t m2, const uint4 a) {
+  return __vmaxu2(m2, __vmaxu2(__vmaxu2(a.x & 0x7FFF7FFFu, a.y & 0x7FFF7FFFu),
+                               __vmaxu2(a.z & 0x7FFF7FFFu, a.w & 0x7FFF7FFFu)));
+}
+
+__global__ void __launch_bounds__(kQfThreads, 1) quant_act_single_pass_kernel(const uint16_t* __restrict__ x,
+                                                                              int64_t n, uint8_t* __restrict__ q,
+                                                                              float* __restrict__ scale_out,
+                                                                              QuantWs* __restrict__ ws) {
+  extern __shared__ __align__(16) uint4 stage[];
+  __shared__ __align__(8) uint64_t bars[kQfChunks];
+  __shared__ int abort_cta;
+  const int64_t nvec = n >> 3;
+  const int64_t chunk = (nvec + gridDim.x - 1) / gridDim.x;
+  const int64_t v0 = min(nvec, static_cast<int64_t>(blockIdx.x) * chunk);
+  const int64_t v1 = min(nvec, v0 + chunk);
+  const int64_t cnt = v1 - v0;
+  const int64_t nkeep = min(cnt, static_cast<int64_t>(kQfSmemVecs));
+  const int nch = static_cast<int>((nkeep + kQfChunkVecs - 1) / kQfChunkVecs);
+  const uint4* xv = reinterpret_cast<const uint4*>(x);
+  if (threadIdx.x == 0) {
+    abort_cta = 0;
+    for (int c = 0; c < nch; ++c) mbar_init(&bars[c], 1);
+    fence_mbar_init();
+    for (int c = 0; c < nch; ++c) {
+      const int64_t a = static_cast<int64_t>(c) * kQfChunkVecs;
+      const uint32_t bytes = static_cast<uint32_t>(min(static_cast<int64_t>(kQfChunkVecs), nkeep - a) * 16);
+      mbar_arrive_expect_tx(&bars[c], bytes);
+      bulk_load(stage + a, xv + v0 + a, bytes, &bars[c]);
+    }
+  }
+  __syncthreads();
+  // phase 1: amax of the slice (bf16 |x| as halfword maxima)
+  uint32_t m2 = 0;
+  bool ok = true;
+  for (int c = 0; c < nch && ok; ++c) {
+    ok = mbar_wait(&bars[c], 0, &abort_cta, nullptr);
+    const int64_t a = static_cast<int64_t>(c) * kQfChunkVecs;
+    const int64_t b = min(a + kQfChunkVecs, nkeep);
+    for (int64_t i = a + threadIdx.x; ok && i < b; i += kQfThreads) m2 = absmax8(m2, stage[i]);
+  }
+  // the part of the slice beyond shared memory: 8 loads per thread in flight
+  for (int64_t base = nkeep; ok && base < cnt; base += 8 * kQfThreads) {
+    uint4 r[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int64_t i = base + k * kQfThreads + threadIdx.x;
+      r[k] = i < cnt ? __ldg(xv + v0 + i) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) m2 = absmax8(m2, r[k]);
+  }
+  if (blockIdx.x == 0)  // the n % 8 tail elements
+    for (int64_t i = (nvec << 3) + threadIdx.x; i < n; i += kQfThreads)
+      m2 = __vmaxu2(m2, static_cast<uint32_t>(x[i] & 0x7FFFu));
+  const uint32_t m = block_max_u32(max(m2 & 0xFFFFu, m2 >> 16));
+  if (threadIdx.x == 0) {
+    // release/acquire at GPU scope order the amax update before the arrival and the
+    // arrival before the flag, without full fences
+    if (m != 0u) atomicMax(&ws->amax_bits, m << 16);
+    uint32_t prev;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(&ws->arrived) : "memory");
+    if (prev == gridDim.x - 1) asm volatile("st.release.gpu.global.u32 [%0], 1;" ::"l"(&ws->go) : "memory");
+    // grid barrier: every CTA is resident (cooperative launch); the wait is bounded
+    const uint64_t t0 = globaltimer();
+    for (uint32_t it = 0;; ++it) {
+      uint32_t go;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(go) : "l"(&ws->go) : "memory");
+      if (go) break;
+      if ((it & 255u) == 255u && globaltimer() - t0 > QIK_WAIT_NS) {
+        abort_cta = 1;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (abort_cta) {  // a chunk or the grid barrier gave up
+    if (blockIdx.x == 0 && threadIdx.x == 0) scale_out[0] = __int_as_float(0x7fc00000);
+    return;
+  }
+  // phase 2: scale from the complete amax, codes from smem (or re-read past its capacity)
+  __shared__ uint32_t amax_all;
+  if (threadIdx.x == 0)
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(amax_all) : "l"(&ws->amax_bits) : "memory");
+  __syncthreads();
+  const float s = scale_from_amax_bits(amax_all);
+  const float inv = act_inverse(s);
+  if (blockIdx.x == 0 && threadIdx.x == 0) scale_out[0] = s;
+  uint2* qv = reinterpret_cast<uint2*>(q);
+  for (int64_t base = 0; base < cnt; base += 4 * kQfThreads) {
+    uint4 a[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int64_t i = base + k * kQfThreads + threadIdx.x;
+      a[k] = i < nkeep ? stage[i] : (i < cnt ? __ldg(xv + v0 + i) : make_uint4(0u, 0u, 0u, 0u));
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int64_t i = base + k * kQfThreads + threadIdx.x;
+      if (i < cnt) {
+        uint32_t hi;
+        const uint32_t lo = pack8_e4m3(a[k], inv, hi);
+        qv[v0 + i] = make_uint2(lo, hi);
+      }
+    }
+  }
+  if (blockIdx.x == 0)
+    for (int64_t i = (nvec << 3) + threadIdx.x; i < n; i += kQfThreads) {
+      const float v = __uint_as_float(static_cast<uint32_t>(x[i]) << 16) * inv;
+      q[i] = static_cast<uint8_t>(cvt_e4m3x2(v, 0.0f) & 0xFFu);
+    }
+}
+
+// Cooperative launch of the single-pass quantizer over ws (cleared here, 16 bytes).
+int launch_quant_single_pass(const void* x, int64_t n, uint8_t* q, float* scale_out, QuantWs* ws,
+                             cudaStream_t st) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  QIK_TRY_CUDA(cudaGetDevice(&dev));
+  if (dev < 64 && !attr_set[dev]) {
+    QIK_TRY_CUDA(cudaFuncSetAttribute(quant_act_single_pass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      kQfSmemBytes));
+    attr_set[dev] = true;
+  }
+  const int64_t nvec = n >> 3;
+  int64_t grid = (nvec + 4 * kQfThreads - 1) / (4 * kQfThreads);
+  const int64_t sms = sm_count();
+  grid = grid < 1 ? 1 : (grid > sms ? sms : grid);
+  const int64_t chunk = (nvec + grid - 1) / grid;
+  const size_t smem = static_cast<size_t>(chunk < kQfSmemVecs ? chunk : kQfSmemVecs) * 16;
+  QIK_TRY_CUDA(cudaMemsetAsync(ws, 0, sizeof(QuantWs), st));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kQfThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  QIK_TRY_CUDA(cudaLaunchKernelEx(&cfg, quant_act_single_pass_kernel, static_cast<const uint16_t*>(x), n, q,
+                                  scale_out, ws));
+  return check_launch("quant_act_single_pass_kernel");
+}
+
 static int grid_for(int64_t work_items, int per_thread) {
   const int64_t want = (work_items + static_cast<int64_t>(kQuantThreads) * per_thread - 1) /
                        (static_cast<int64_t>(kQuantThreads) * per_thread);
@@ -323,7 +502,9 @@ int qik_quantize_act(const void* x, int64_t n, uint8_t* q, float* scale_out, voi
   QIK_REQUIRE(n >= 0, "qik_quantize_act: negative n");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   QuantWs* w = static_cast<QuantWs*>(ws);
-  QIK_TRY_CUDA(cudaMemsetAsync(&w->amax_bits, 0, sizeof(uint32_t), st));
+  // one pass over HBM (16-byte aligned operands); otherwise an amax pass then a pack pass
+  if (aligned16(x) && aligned16(q) && aligned16(ws)) return launch_quant_single_pass(x, n, q, scale_out, w, st);
+  QIK_TRY_CUDA(cudaMemsetAsync(w, 0, sizeof(QuantWs), st));
   int rc = launch_amax(x, QIK_DTYPE_BF16, n, &w->amax_bits, st, false);
   if (rc) return rc;
   return qik_quantize_act_from_amax(x, n, &w->amax_bits, q, scale_out, stream);
