@@ -451,47 +451,59 @@ def tp_stack(device: torch.device, rank: int, world: int, flush: torch.Tensor, i
     from qik import parallel as PX
     H, D, K, HID, B, S = 24, 128, 3072, 12288, 2, 4352
     g = torch.Generator(device=device).manual_seed(11)
-    blocks = []
+    fulls = []
     for _ in range(4):
         full = {}
         for name, (n, kk) in {"qkv": (3 * H * D, K), "out": (K, H * D), "up": (HID, K), "down": (K, HID)}.items():
             w = torch.randn(n, kk, device=device, generator=g) * 0.02
             full[name] = (*F.quantize_weight_tensorwise(w), None)
-        blocks.append(PX.TPBlock.from_full(full, H, D, rank, world))
+        fulls.append(full)
     x = torch.randn(B * S, K, device=device, generator=g).to(torch.bfloat16)
     Lt = torch.arange(S, dtype=torch.int32, device=device)
     Lt[256:] = S - 1
 
-    def stack():
-        h = x
-        for blk in blocks:
-            h = blk(h, B, S, Lt)
-        return h
+    def timed(chunks: int) -> float:
+        """Mean ms per 4-block stack (max over ranks) with `chunks` row blocks per
+        row-parallel GEMM / all-reduce (1 = one all-reduce after the whole GEMM)."""
+        blocks = [PX.TPBlock.from_full(full, H, D, rank, world, chunks=chunks) for full in fulls]
 
-    stream = torch.cuda.current_stream(device)
-    for _ in range(2):
-        stack()
-    torch.cuda.synchronize(device)
-    if world > 1:
-        torch.distributed.barrier()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
-    torch.cuda._sleep(int(2e7))
-    for i in range(iters):
-        flush.fill_(float(i))
-        evs[i][0].record(stream)
-        stack()
-        evs[i][1].record(stream)
-    torch.cuda.synchronize(device)
-    ms = torch.tensor([sum(a.elapsed_time(b) for a, b in evs) / iters], dtype=torch.float64, device=device)
-    if world > 1:
-        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
-    ms = float(ms.item())
+        def stack():
+            h = x
+            for blk in blocks:
+                h = blk(h, B, S, Lt)
+            return h
+
+        stream = torch.cuda.current_stream(device)
+        for _ in range(2):
+            stack()
+        torch.cuda.synchronize(device)
+        if world > 1:
+            torch.distributed.barrier()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+        torch.cuda._sleep(int(2e7))
+        for i in range(iters):
+            flush.fill_(float(i))
+            evs[i][0].record(stream)
+            stack()
+            evs[i][1].record(stream)
+        torch.cuda.synchronize(device)
+        t = torch.tensor([sum(a.elapsed_time(b) for a, b in evs) / iters], dtype=torch.float64, device=device)
+        if world > 1:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    ms = timed(1)
+    ms_overlap = timed(4) if world > 1 else ms
     M = B * S
     lin = 2.0 * M * K * (3 * H * D + K + HID) + 2.0 * M * HID * K
     att = 4.0 * D * H * B * float((Lt.long() + 1).sum())
     total = 4 * (lin + att)
     return {"ms": round(ms, 4), "tflops_total": round(total / ms / 1e9, 1),
             "tflops_per_gpu": round(total / ms / 1e9 / world, 1), "n_gpus": world, "scaling": "strong",
+            "ms_overlapped_4_blocks": round(ms_overlap, 4),
+            "overlapped_form": "row-parallel GEMMs in 4 row blocks, each block's all-reduce on a side stream "
+                               "under the next block's GEMM (slower here: NCCL's kernels take SMs from the "
+                               "persistent GEMM)" if world > 1 else "n/a",
             "collectives_per_stack": "8 x all-reduce(SUM) fp32 [8704, 3072] + 8 x all-reduce(MAX) 4 bytes"
             if world > 1 else "none"}
 

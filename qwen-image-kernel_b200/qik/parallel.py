@@ -42,9 +42,11 @@ class QikOps:
         from .fp8 import quantize_from_amax
         return quantize_from_amax(x, amax)
 
-    def gemm(self, xq, sx, wq, sw, bias=None, out_dtype=torch.bfloat16, epilogue=L.EPI_SCALE, amax_out=None):
+    def gemm(self, xq, sx, wq, sw, bias=None, out_dtype=torch.bfloat16, epilogue=L.EPI_SCALE, amax_out=None,
+             out=None):
         from .fp8 import fp8_gemm
-        return fp8_gemm(xq, sx, wq, sw, bias=bias, out_dtype=out_dtype, epilogue=epilogue, amax_out=amax_out)
+        return fp8_gemm(xq, sx, wq, sw, bias=bias, out_dtype=out_dtype, epilogue=epilogue, amax_out=amax_out,
+                        out=out)
 
     def zeros_amax(self, device) -> torch.Tensor:
         return torch.zeros(1, dtype=torch.int32, device=device)
@@ -52,6 +54,19 @@ class QikOps:
     def attention(self, q, k, v, L):
         from .triton_attention import block_causal_flash_attention
         return block_causal_flash_attention(q, k, v, L, None)
+
+
+_comm_streams: dict[int, torch.cuda.Stream] = {}
+
+
+def _comm_stream(device: torch.device) -> torch.cuda.Stream:
+    """One side stream per device for collectives that overlap compute."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    st = _comm_streams.get(idx)
+    if st is None:
+        st = torch.cuda.Stream(device=torch.device("cuda", idx))
+        _comm_streams[idx] = st
+    return st
 
 
 def _world(group) -> tuple[int, int]:
@@ -167,11 +182,19 @@ class RowParallelFP8Linear(nn.Module):
     """y = sum_ranks x_local . W_local^T (+ b): the input holds this rank's slice of the
     input features.  The dynamic scale is global (4-byte all-reduce MAX of the amax
     bits), the fp32 partial products are summed with an all-reduce, and the bias is
-    added once after the sum."""
+    added once after the sum.
+
+    With ``chunks`` > 1 on GPUs (more than one rank) the GEMM runs in row blocks: the
+    all-reduce of block i runs on a side stream while the GEMM of block i + 1 runs.
+    Every rank issues the same collectives in the same order; the sum is the same as
+    one all-reduce of the whole partial product (the reduction is per element).  The
+    default is one block: measured on 2 B200 the overlapped form was slower (the
+    NCCL kernels occupy SMs the persistent GEMM grid counts on)."""
 
     def __init__(self, weight: torch.Tensor, weight_scale: torch.Tensor, bias: torch.Tensor | None, group=None,
-                 ops=None):
+                 ops=None, chunks: int = 1):
         super().__init__()
+        self.chunks = chunks
         self.register_buffer("weight", weight)
         self.register_buffer("weight_scale", weight_scale)
         if bias is not None:
@@ -182,16 +205,40 @@ class RowParallelFP8Linear(nn.Module):
         self.ops = ops or QikOps()
 
     @classmethod
-    def from_full(cls, weight, weight_scale, bias, rank, world, group=None, ops=None):
-        return cls(shard_cols(weight, rank, world), weight_scale.clone(), bias, group, ops)
+    def from_full(cls, weight, weight_scale, bias, rank, world, group=None, ops=None, chunks: int = 1):
+        return cls(shard_cols(weight, rank, world), weight_scale.clone(), bias, group, ops, chunks)
 
     def forward_quantized(self, xq: torch.Tensor, sx: torch.Tensor) -> torch.Tensor:
-        part = self.ops.gemm(xq, sx, self.weight, self.weight_scale, None, out_dtype=torch.float32)
-        if _world(self.group)[1] > 1:
-            dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
+        world = _world(self.group)[1]
+        M = xq.shape[0]
+        if world > 1 and xq.is_cuda and self.chunks > 1 and M >= 2 * self.chunks:
+            part = self._gemm_allreduce_overlapped(xq, sx)
+        else:
+            part = self.ops.gemm(xq, sx, self.weight, self.weight_scale, None, out_dtype=torch.float32)
+            if world > 1:
+                dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
         if self.bias is not None:
             part = part + self.bias.float()
         return part.to(torch.bfloat16)
+
+    def _gemm_allreduce_overlapped(self, xq: torch.Tensor, sx: torch.Tensor) -> torch.Tensor:
+        M = xq.shape[0]
+        N = self.weight.shape[0]
+        part = torch.empty(M, N, dtype=torch.float32, device=xq.device)
+        cur = torch.cuda.current_stream(xq.device)
+        comm = _comm_stream(xq.device)
+        for c in range(self.chunks):
+            lo, hi = row_range(M, c, self.chunks)
+            blk = part[lo:hi]
+            self.ops.gemm(xq[lo:hi], sx, self.weight, self.weight_scale, None, out_dtype=torch.float32, out=blk)
+            done = torch.cuda.Event()
+            done.record(cur)
+            comm.wait_event(done)
+            with torch.cuda.stream(comm):
+                dist.all_reduce(blk, op=dist.ReduceOp.SUM, group=self.group)
+        cur.wait_stream(comm)
+        part.record_stream(comm)
+        return part
 
     def forward(self, x_local: torch.Tensor, amax: torch.Tensor | None = None) -> torch.Tensor:
         x2 = x_local.reshape(-1, x_local.shape[-1])
@@ -225,13 +272,15 @@ class TPBlock(nn.Module):
         self.hl, self.d = heads_local, head_dim
 
     @classmethod
-    def from_full(cls, full: dict, heads: int, head_dim: int, rank: int, world: int, group=None, ops=None):
+    def from_full(cls, full: dict, heads: int, head_dim: int, rank: int, world: int, group=None, ops=None,
+                  chunks: int = 1):
         """full: name -> (weight e4m3 [N, K], weight_scale [1], bias or None) for
-        'qkv', 'out', 'up', 'down' (unsharded, quantized once)."""
+        'qkv', 'out', 'up', 'down' (unsharded, quantized once).  ``chunks``: row blocks of
+        the row-parallel GEMMs whose all-reduce overlaps the next block's GEMM."""
         qkv = ColumnParallelFP8Linear.from_full(*full["qkv"], rank, world, qkv_heads=(heads, head_dim), ops=ops)
-        out = RowParallelFP8Linear.from_full(*full["out"], rank, world, group, ops)
+        out = RowParallelFP8Linear.from_full(*full["out"], rank, world, group, ops, chunks)
         up = ColumnParallelFP8Linear.from_full(*full["up"], rank, world, ops=ops)
-        down = RowParallelFP8Linear.from_full(*full["down"], rank, world, group, ops)
+        down = RowParallelFP8Linear.from_full(*full["down"], rank, world, group, ops, chunks)
         return cls(qkv, out, up, down, heads // world, head_dim)
 
     def forward(self, x: torch.Tensor, batch: int, seq: int, prefix_lengths: torch.Tensor) -> torch.Tensor:

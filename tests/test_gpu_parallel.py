@@ -4,7 +4,8 @@
   the bytes and scale of the single-GPU quantization of the whole tensor;
 * the tensor-parallel DiT block (QKV by heads, attention on local heads, row-parallel
   out / FFN-down with fp32 partial all-reduce) matches the single-GPU block within
-  the BASELINE tolerances.
+  the BASELINE tolerances, in both forms (one all-reduce, or row blocks whose
+  all-reduces run on a side stream).
 """
 import datetime
 import os
@@ -64,6 +65,9 @@ def _worker(rank, world, port, outdir):
         Lp = torch.arange(S, dtype=torch.int32, device=dev)
         Lp[64:] = S - 1
         res["block"] = blk(xb, B, S, Lp).float().cpu().numpy()
+        # row-parallel GEMMs in 4 row blocks, each all-reduce on a side stream
+        blk4 = PX.TPBlock.from_full(full, heads, d, rank, world, chunks=4)
+        res["block4"] = blk4(xb, B, S, Lp).float().cpu().numpy()
         torch.cuda.synchronize()
         with open(os.path.join(outdir, f"r{rank}.pkl"), "wb") as f:
             pickle.dump(res, f)
@@ -98,3 +102,6 @@ def test_sharded_quantization_and_tp_block_on_two_gpus():
     for r in res:
         y = torch.from_numpy(r["block"])
         assert O.relf(y, ref) <= 5e-3
+        # the blocked form: same partial products, summed block by block (its GEMM
+        # blocks may use another tile configuration, so the gate is the tolerance)
+        assert O.relf(torch.from_numpy(r["block4"]), ref) <= 5e-3
