@@ -362,6 +362,30 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ---------------------------------------------------------------- numerics
+// Dynamic activation scale from the fp32 bit pattern of max|x| (fp8.py:24-26 as it
+// evaluates on CUDA: a division by a host scalar is a multiplication by its fp32
+// reciprocal), and the 1/s the activation cast multiplies by.  Shared by every kernel
+// that quantizes activations, so they produce the same bytes.
+__device__ __forceinline__ float scale_from_amax_bits(uint32_t bits) {
+  const float amax = __uint_as_float(bits);
+  float s = amax * (1.0f / 448.0f);
+  if (s < 1e-12f) s = 1e-12f;  // NaN compares false and passes through
+  return s;
+}
+
+// 1/s as the activation cast forms it (fp8.py:39 `1.0 / tl.load(...)`): Triton
+// lowers an fp32 division to PTX div.full.f32; QIK_ACT_RECIP_RN selects the
+// IEEE round-to-nearest reciprocal instead.
+__device__ __forceinline__ float act_inverse(float s) {
+#ifdef QIK_ACT_RECIP_RN
+  return __frcp_rn(s);
+#else
+  float r;
+  asm("div.full.f32 %0, %1, %2;" : "=f"(r) : "f"(1.0f), "f"(s));
+  return r;
+#endif
+}
+
 // fp32 pair -> e4m3 pair, round to nearest even, saturating to +-448 (NaN -> NaN).
 __device__ __forceinline__ uint16_t cvt_e4m3x2(float lo, float hi) {
   uint16_t r;

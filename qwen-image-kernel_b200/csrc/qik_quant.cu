@@ -27,26 +27,6 @@ struct QuantWs {
 
 constexpr int kQuantThreads = 256;
 
-__device__ __forceinline__ float scale_from_amax_bits(uint32_t bits) {
-  const float amax = __uint_as_float(bits);
-  float s = amax * (1.0f / 448.0f);
-  if (s < 1e-12f) s = 1e-12f;  // NaN compares false and passes through
-  return s;
-}
-
-// 1/s as the activation cast forms it (fp8.py:39 `1.0 / tl.load(...)`): Triton
-// lowers an fp32 division to PTX div.full.f32; QIK_ACT_RECIP_RN selects the
-// IEEE round-to-nearest reciprocal instead.
-__device__ __forceinline__ float act_inverse(float s) {
-#ifdef QIK_ACT_RECIP_RN
-  return __frcp_rn(s);
-#else
-  float r;
-  asm("div.full.f32 %0, %1, %2;" : "=f"(r) : "f"(1.0f), "f"(s));
-  return r;
-#endif
-}
-
 __device__ __forceinline__ uint32_t block_max_u32(uint32_t v) {
   __shared__ uint32_t red[32];
   v = __reduce_max_sync(0xffffffffu, v);
