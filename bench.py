@@ -13,8 +13,10 @@ A step is one FFN pair over one batch.  ``value`` = FLOPs (2*M*N*K summed over b
 linears and all ranks) / device time of the K timed steps (CUDA events on the
 launching stream, max over ranks); L2 is flushed (256 MiB write) between steps,
 outside the timed events.  ``e2e`` is the same metric through the public API
-with the step's input copied from pinned host memory and its output copied back
-inside the timed region.  ``roofline`` covers the dominant kernel (the tcgen05 FP8
+with every step's input copied from pinned host memory and its output copied back
+inside the timed region: the serving form (qik.host_pipeline.HostPipeline, the copies
+of neighbouring steps overlapping this step's kernels) as the value, the form with
+copy in, kernels and copy out back to back beside it as ``e2e.serial``.  ``roofline`` covers the dominant kernel (the tcgen05 FP8
 GEMM): algorithmic FLOPs per launch / its average CUDA-event duration.
 
 Multi-GPU: token-row shards, one process per GPU, no collective on the data path
@@ -208,12 +210,30 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
     gemm_ms = 0.5 * (t1[len(t1) // 2] + t2[len(t2) // 2])
 
     # ---- end-to-end through the public API with host buffers
+    # (a) serving form: qik.host_pipeline.HostPipeline, the next batch's host->device copy
+    # and the previous batch's device->host copy overlap this batch's kernels; timed from
+    # before the first copy in to the end of the last copy out, every step's copies inside
+    from qik.host_pipeline import HostPipeline
     x_host = x_cpu.pin_memory()
-    y_host = torch.empty(M_ROWS, K_IN, dtype=torch.bfloat16).pin_memory()
-    for _ in range(2):
-        y_host.copy_(F.fp8_ffn_gelu(x_host.to(device, non_blocking=True), up, down, workspace=ws),
-                     non_blocking=True)
+    y_hosts = [torch.empty(M_ROWS, K_IN, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    pipe = HostPipeline(lambda xd, yd: F.fp8_ffn_gelu(xd, up, down, workspace=ws, out=yd),
+                        (M_ROWS, K_IN), (M_ROWS, K_IN), device=device, depth=2)
+    for i in range(3):
+        pipe.submit(x_host, y_hosts[i % 2])
+    pipe.synchronize()
     barrier()
+    e2e_start = torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(int(2e7))
+    e2e_start.record(stream)
+    pipe.h2d_stream.wait_event(e2e_start)
+    for i in range(args.steps):
+        flush.fill_(float(i))  # L2 flush on the compute stream, inside the timed span
+        e2e_end = pipe.submit(x_host, y_hosts[i % 2])
+    pipe.synchronize()
+    barrier()
+    t_e2e = e2e_start.elapsed_time(e2e_end) / 1e3
+    # (b) one batch at a time on one stream: copy in, kernels, copy out (events around each)
+    y_host = y_hosts[0]
     e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(args.steps)]
     torch.cuda._sleep(int(2e7))
@@ -224,15 +244,15 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
         y_host.copy_(F.fp8_ffn_gelu(xd, up, down, workspace=ws), non_blocking=True)
         e2e_ev[i][1].record(stream)
     barrier()
-    t_e2e = sum(a.elapsed_time(b) for a, b in e2e_ev) / 1e3
+    t_e2e_serial = sum(a.elapsed_time(b) for a, b in e2e_ev) / 1e3
 
     ext = extras(device, flush) if (rank == 0 and not args.no_extras) else None
     tp = tp_stack(device, rank, world, flush) if not args.no_extras else None
     status = L.device_status(device)
-    t = torch.tensor([t_steps, t_e2e, gemm_ms, float(status)], dtype=torch.float64, device=device)
+    t = torch.tensor([t_steps, t_e2e, t_e2e_serial, gemm_ms, float(status)], dtype=torch.float64, device=device)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    t_steps, t_e2e, gemm_ms, status = t.tolist()
+    t_steps, t_e2e, t_e2e_serial, gemm_ms, status = t.tolist()
     if rank != 0:
         return None
 
@@ -263,14 +283,21 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
         "pct_nominal_fp8_4500": round(100.0 * value / world / NOMINAL_FP8_TFLOPS, 1),
         "e2e": {"value": round(total_flops / t_e2e / 1e12, 2), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": M_ROWS * K_IN * 2, "d2h_bytes_per_step": M_ROWS * K_IN * 2,
-                "ms_per_step": round(t_e2e / args.steps * 1e3, 4)},
+                "ms_per_step": round(t_e2e / args.steps * 1e3, 4),
+                "api": "qik.host_pipeline.HostPipeline over qik.fp8.fp8_ffn_gelu (C ABI qik_fp8_ffn): pinned "
+                       "host input copied in and bf16 result copied out every step, the copies of "
+                       "neighbouring steps overlapping this step's kernels (depth 2); timed from before "
+                       "the first copy in to the end of the last copy out",
+                "serial": {"value": round(total_flops / t_e2e_serial / 1e12, 2),
+                           "ms_per_step": round(t_e2e_serial / args.steps * 1e3, 4),
+                           "form": "copy in, kernels, copy out back to back on one stream"}},
         "roofline": {"kernel": "qik::fp8_gemm_kernel (tcgen05 kind::f8f6f4)", "bound": "tensor",
                      "achieved": round(achieved, 1), "peak": round(pk["fp8_tflops"], 1), "unit": "TFLOP/s",
                      "frac": round(achieved / pk["fp8_tflops"], 3), "traffic": traffic_from_profile(),
                      "peak_source": pk["source"], "avg_launch_ms": round(gemm_ms, 4),
                      "flops_per_launch": FLOPS_PER_LINEAR},
-        "gpu_launches": launches_per_step * args.steps * 2,
-        "gpu_launches_note": "qik kernels inside the timed regions (device-resident steps + e2e steps: "
+        "gpu_launches": launches_per_step * args.steps * 3,
+        "gpu_launches_note": "qik kernels inside the timed regions (device-resident steps + pipelined and serial e2e steps: "
                              "amax, pack, GEMM+GELU+amax, pack, GEMM per step, chained with programmatic "
                              "dependent launch); the L2-flush fills are torch's; GEMM launch times for the "
                              "roofline come from a second pass that runs the step launch by launch with events (median per GEMM)",

@@ -242,8 +242,8 @@ def fp8_state_dict(model: nn.Module) -> dict[str, torch.Tensor]:
     return {k: v for k, v in model.state_dict().items()}
 
 
-def fp8_ffn_gelu(x: torch.Tensor, up: FP8Linear, down: FP8Linear, workspace: torch.Tensor | None = None
-                 ) -> torch.Tensor:
+def fp8_ffn_gelu(x: torch.Tensor, up: FP8Linear, down: FP8Linear, workspace: torch.Tensor | None = None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
     """DiT FFN pair: down(gelu_tanh(up(x))) with both linears FP8 per-tensor and the
     hidden activation re-quantized dynamically between them (qik_fp8_ffn: one chain
     of five kernels with programmatic dependent launches).
@@ -251,7 +251,8 @@ def fp8_ffn_gelu(x: torch.Tensor, up: FP8Linear, down: FP8Linear, workspace: tor
     The up-projection epilogue applies GELU-tanh to the bf16 linear output and
     accumulates max|h| on the fly, so the hidden tensor is quantized with one pack
     pass.  ``workspace`` (uint8, >= qik_fp8_ffn_workspace_bytes) may be passed to
-    avoid an allocation per call."""
+    avoid an allocation per call, ``out`` (contiguous bf16, x's shape) to write the
+    result into a buffer the caller owns."""
     _require_cuda(x, "x")
     if x.dtype != torch.bfloat16:
         raise TypeError("qik.fp8_ffn_gelu: bf16 activations only")
@@ -265,7 +266,13 @@ def fp8_ffn_gelu(x: torch.Tensor, up: FP8Linear, down: FP8Linear, workspace: tor
     nbytes = lib.qik_fp8_ffn_workspace_bytes(M, K, hidden)
     if workspace is None or workspace.numel() < nbytes or workspace.data_ptr() % 256:
         workspace = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
-    y = torch.empty(M, K, dtype=torch.bfloat16, device=x.device)
+    if out is None:
+        y = torch.empty(M, K, dtype=torch.bfloat16, device=x.device)
+    else:
+        if (out.dtype != torch.bfloat16 or out.device != x.device or not out.is_contiguous()
+                or out.numel() != M * K):
+            raise ValueError("qik.fp8_ffn_gelu: out must be a contiguous bf16 tensor of x's shape on x's device")
+        y = out.view(M, K)
     b_up = None if up.bias is None else up.bias.to(torch.bfloat16).contiguous()
     b_down = None if down.bias is None else down.bias.to(torch.bfloat16).contiguous()
     status = L.status_word(x.device)
