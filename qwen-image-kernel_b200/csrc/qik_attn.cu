@@ -14,41 +14,59 @@
 // product fl32(v8) * scale; the difference to the reference kernel's bf16 rounding
 // of each dequantized V element is below half a bf16 ulp of V.
 //
-// One CTA per (128-query tile, b, h):
-//   warp 0     TMA producer: Q once (two 64-column halves, 128-byte swizzle), then
-//              K tiles into a 3-stage ring (freed as soon as S = Q K^T completes)
-//              and V tiles (bf16, or e4m3 raw for the fp8 slab) into a 2-stage ring
-//              (freed after P.V), V lagging K by one tile so K runs ahead;
-//   warp 1     MMA issuer (one thread): S_t = Q K_t^T (kind::f16, M=N=128, K=16 x 8)
-//              into a double-buffered TMEM S, then O += P_t V_t with P_t read from
-//              TMEM (A operand) and V_t from shared memory (MN-major B operand);
-//   warps 2-3  e4m3 -> f16 V converters for slab tiles when V is fp8 (exact);
-//   warps 4-7  softmax: thread = query row; reads S_t from TMEM, masks, online
-//              max/sum (the accumulator O is rescaled in TMEM only when the running
-//              max grows by more than 2^8, which leaves the final O/l unchanged),
-//              writes bf16 P_t to TMEM; finally O / l -> bf16 -> global.
-// TMEM columns: S0 [0,128) S1 [128,256) O [256,384) P0 [384,448) P1 [448,512).
+// One CTA per (256-query block, b, h): two 128-row query tiles, A and B, share every
+// K/V tile, and each has its own softmax warpgroup, so the tensor core computes one
+// tile's S and P.V while the other tile's softmax runs (and two softmax warps share
+// each SM sub-partition, hiding each other's latencies).
+//   warp 0      TMA producer: Q_A and Q_B once (64-column halves, 128-byte swizzle),
+//               K tiles into a 2-stage ring (freed once S_A and S_B are computed), V
+//               tiles (bf16, or e4m3 raw for the fp8 slab) into a 2-stage ring (freed
+//               after P_B.V), V lagging K by one tile;
+//   warp 1      MMA issuer (one thread), per key tile t:
+//                 O_A += P_A(t) V_t ; S_A(t+1) = Q_A K_{t+1}^T ;
+//                 O_B += P_B(t) V_t ; S_B(t+1) = Q_B K_{t+1}^T
+//               tcgen05.mma runs in issue order and tcgen05.commit tracks every
+//               earlier MMA of the thread, so when S_g(t+1) is complete, P_g(t).V has
+//               been consumed: P_g(t+1) can overwrite S_g's columns and O_g can be
+//               rescaled without another barrier;
+//   warps 2-3   e4m3 -> f16 V converters for slab tiles when V is fp8 (exact);
+//   warps 4-7   softmax of tile A, warps 8-11 softmax of tile B: thread = query row;
+//               reads S_g(t) from TMEM, masks, online max/sum (O_g is rescaled in
+//               TMEM only when the running max grows by more than 2^8, which leaves
+//               the final O/l unchanged), writes P_g(t) as bf16 over S_g's first 64
+//               columns; finally O_g / l -> bf16 -> global.
+// TMEM columns: S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512); P_g over S_g.
+// CTAs are numbered heaviest-first (the last query blocks, which see the most keys
+// under a block-causal mask, start first) so the short blocks fill the tail.
 #include "qik_device.cuh"
 #include "qik_host.h"
 
 namespace qik {
 
-constexpr int kAttnBM = 128;
+constexpr int kAttnBM = 128;                        // query rows per tile (one TMEM lane each)
+constexpr int kAttnTiles = 2;                       // query tiles per CTA
+constexpr int kAttnRows = kAttnBM * kAttnTiles;     // query rows per CTA
 constexpr int kAttnBN = 128;
 constexpr int kAttnD = 128;
-constexpr int kAttnThreads = 256;
+constexpr int kAttnThreads = 128 + 128 * kAttnTiles;  // producer, MMA, 2 converters, softmax warpgroups
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when the max grows by > 2^8
+// Softmax exponentials: pairs j >= kPolyFromPair of a row (on tiles where every key
+// is allowed) use the FMA-pipe 2^x, the others MUFU ex2.  The FMA-pipe pairs come
+// last, where most scores of the row are consumed and its constants fit the 168
+// registers of a 384-thread CTA.
+constexpr int kPolyFromPair = 46;
 
 struct AttnSmem {
-  static constexpr int kQ = 0;                    // 32 KB: two 16 KB halves (d 0-63, d 64-127)
-  static constexpr int kKStages = 3;
+  static constexpr int kQ = 0;                          // per tile 32 KB: two 16 KB halves (d 0-63, 64-127)
+  static constexpr int kKStages = 2;
   static constexpr int kVStages = 2;
-  static constexpr int kK0 = 32768;               // K ring: 3 x 32 KB
-  static constexpr int kV0 = kK0 + kKStages * 32768;   // V ring: 2 x 32 KB (bf16)
-  static constexpr int kV80 = kV0 + kVStages * 32768;  // raw e4m3 V: 2 x 16 KB
+  static constexpr int kK0 = kAttnTiles * 32768;        // K ring: 2 x 32 KB
+  static constexpr int kV0 = kK0 + kKStages * 32768;    // V ring: 2 x 32 KB (bf16)
+  static constexpr int kV80 = kV0 + kVStages * 32768;   // raw e4m3 V: 2 x 16 KB
   static constexpr int kBar = kV80 + kVStages * 16384;
-  static constexpr int kBytes = kBar + 256 + 1024;  // barriers + alignment slack
+  static constexpr int kBytes = kBar + 256 + 1024;      // barriers + alignment slack
 };
+static_assert(AttnSmem::kBytes <= 232448, "attention shared memory above the 227 KB per-CTA limit");
 
 struct AttnDev {
   const int32_t* L;
@@ -69,6 +87,40 @@ __device__ __forceinline__ void load_bf16_tile(const CUtensorMap* tm, void* dst,
   tma_load_4d(static_cast<uint8_t*>(dst) + 16384, tm, 64, key0, h, b, bar);
 }
 
+// P row of one 128-key tile: p = 2^(s * scale - m) computed in pairs (f32x2), packed
+// (f16 for fp8-slab tiles, else bf16) and written to TMEM at tP; returns the fp32
+// row sum.  kPoly (tiles where every key of the row is allowed): pairs
+// j >= kPolyFromPair take 2^x on the FMA pipe (exp2_poly2), the rest MUFU ex2, so
+// the two pipes share the 128 exponentials of the row.
+template <bool kPoly, bool kF16>
+__device__ __forceinline__ float softmax_row(const float (&sv)[kAttnBN], float scale, float neg_m, uint32_t tP) {
+  const uint64_t sc2 = f2_pack(scale, scale), nm2 = f2_pack(neg_m, neg_m);
+  uint64_t acc[2] = {0ull, 0ull};  // (0.f, 0.f) pairs
+  uint32_t pk[kAttnBN / 2];
+#pragma unroll
+  for (int j = 0; j < kAttnBN / 2; ++j) {
+    const uint64_t x2 = ffma2(f2_pack(sv[2 * j], sv[2 * j + 1]), sc2, nm2);
+    uint64_t p2;
+    if (kPoly && j >= kPolyFromPair) {
+      p2 = exp2_poly2(x2);
+    } else {
+      float x0, x1;
+      f2_unpack(x2, x0, x1);
+      p2 = f2_pack(ex2(x0), ex2(x1));
+    }
+    acc[j & 1] = fadd2(acc[j & 1], p2);
+    float p0, p1;
+    f2_unpack(p2, p0, p1);
+    pk[j] = kF16 ? pack_f16x2(p0, p1) : pack_bf16x2(p0, p1);
+  }
+  __syncwarp();
+  tmem_st64(tP, pk);
+  float a0, a1, b0, b1;
+  f2_unpack(acc[0], a0, a1);
+  f2_unpack(acc[1], b0, b1);
+  return (a0 + a1) + (b0 + b1);
+}
+
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_ck,
@@ -78,22 +130,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + AttnSmem::kBar);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;    // [3]
-  uint64_t* k_empty = bars + 4;   // [3] K stage free (after S = Q K^T)
-  uint64_t* v_full = bars + 7;    // [2] V bf16 ready (TMA or converters)
-  uint64_t* v8_full = bars + 9;   // [2] raw e4m3 V landed
-  uint64_t* v_empty = bars + 11;  // [2] V stage free (after P.V)
-  uint64_t* s_full = bars + 13;   // [2]
-  uint64_t* p_full = bars + 15;   // [2]
-  uint64_t* pv_done = bars + 17;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* k_empty = bars + 3;   // [2] K stage free (after S_A and S_B)
+  uint64_t* v_full = bars + 5;    // [2] V bf16 ready (TMA or converters)
+  uint64_t* v8_full = bars + 7;   // [2] raw e4m3 V landed
+  uint64_t* v_empty = bars + 9;   // [2] V stage free (after P_B.V)
+  uint64_t* s_full = bars + 11;   // [tile] S_g(t) computed (and everything before it)
+  uint64_t* p_full = bars + 13;   // [tile] P_g(t) written (4 softmax warps)
+  uint64_t* o_full = bars + 15;   // [tile] last P_g.V done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* lmax_slot = reinterpret_cast<int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kAttnBM;
-  const int bh = blockIdx.y;
+  const int m0 = (gridDim.y - 1 - blockIdx.y) * kAttnRows;  // heaviest-first
+  const int bh = blockIdx.x;
   const int b = bh / a.H, h = bh % a.H;
   const bool has_cache = (a.flags & QIK_ATTN_HAS_CACHE) && a.P > 0;
   const bool uniform = (a.flags & QIK_ATTN_UNIFORM) != 0;
@@ -104,17 +156,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < AttnSmem::kKStages; ++s) {
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
-    }
-    for (int s = 0; s < 2; ++s) {
       mbar_init(&v_full[s], 1);
       mbar_init(&v8_full[s], 1);
       mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&p_full[s], 4);
-      mbar_init(&pv_done[s], 1);
+      mbar_init(&o_full[s], 1);
     }
     *abort_flag = 0;
     *lmax_slot = -1;
@@ -124,7 +174,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
-  // per-row limits; the largest L of the tile decides how many key tiles exist
+  // per-row limits; the largest L of the block decides how many key tiles exist
   int my_L = -1;
   if (warp >= 4) {
     const int r = m0 + (threadIdx.x - 128);
@@ -154,13 +204,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0 && n_tiles > 0) {
       tma_prefetch_desc(&tm_q);
-      mbar_arrive_expect_tx(q_full, 32768);
-      load_bf16_tile(&tm_q, sQ, m0, h, b, q_full);
+      mbar_arrive_expect_tx(q_full, 32768 * kAttnTiles);
+      for (int g = 0; g < kAttnTiles; ++g) load_bf16_tile(&tm_q, sQ + g * 32768, m0 + g * kAttnBM, h, b, q_full);
       // step u: K of tile u, then V of tile u - 1
       for (int u = 0; u <= n_tiles; ++u) {
         if (u < n_tiles) {
-          const int ks = u % AttnSmem::kKStages;
-          const uint32_t kph = (u / AttnSmem::kKStages) & 1;
+          const int ks = u & 1;
+          const uint32_t kph = (u >> 1) & 1;
           if (!mbar_wait(&k_empty[ks], kph ^ 1u, abort_flag, a.status)) break;
           const bool slab = u < n_slab;
           const int key0 = slab ? u * kAttnBN : (u - n_slab) * kAttnBN;
@@ -190,51 +240,60 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       constexpr uint32_t idesc_s = idesc_f32acc(1, 1, 0, 0, kAttnBM, kAttnBN);
       constexpr uint32_t idesc_o = idesc_f32acc(1, 1, 0, 1, kAttnBM, kAttnD);      // bf16 P, bf16 V
       constexpr uint32_t idesc_o16 = idesc_f32acc(0, 0, 0, 1, kAttnBM, kAttnD);    // f16 P, f16 V (fp8 slab)
-      // TMEM columns: S_s at 128 s, O at 256, P_s at 384 + 64 s
-      const uint32_t tO = tmem + 256u;
+      // S_g at column 128 g (P_g over its first 64 columns), O_g at 256 + 128 g
       bool ok = mbar_wait(q_full, 0, abort_flag, a.status);
       const uint32_t q_addr = smem_u32(sQ);
-      auto issue_pv = [&](int t) -> bool {
-        const int s = t & 1;
-        const uint32_t ph = (t >> 1) & 1;
-        if (!mbar_wait(&p_full[s], ph, abort_flag, a.status)) return false;
-        if (!mbar_wait(&v_full[s], ph, abort_flag, a.status)) return false;
+      auto issue_s = [&](int g, int t) {  // K_t resident (k_full waited)
+        const uint32_t k_addr = smem_u32(k_ptr(t & 1));
+#pragma unroll
+        for (int k = 0; k < kAttnD / 16; ++k) {
+          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+          const uint64_t qd = sdesc_sw128(q_addr + g * 32768 + off, 16, 1024);
+          const uint64_t kd = sdesc_sw128(k_addr + off, 16, 1024);
+          umma_f16_ss(tmem + 128u * g, qd, kd, idesc_s, k > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[g]);
+      };
+      auto wait_k = [&](int t) -> bool {
+        if (!mbar_wait(&k_full[t & 1], (t >> 1) & 1, abort_flag, a.status)) return false;
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(v_ptr(s));
+        return true;
+      };
+      auto issue_pv = [&](int g, int t) -> bool {
+        const int vs = t & 1;
+        if (!mbar_wait(&p_full[g], t & 1, abort_flag, a.status)) return false;
+        if (g == 0 && !mbar_wait(&v_full[vs], (t >> 1) & 1, abort_flag, a.status)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(v_ptr(vs));
+        const uint32_t idesc = (v_fp8 && t < n_slab) ? idesc_o16 : idesc_o;
 #pragma unroll
         for (int k = 0; k < kAttnBN / 16; ++k) {
           // 16 keys per step: V rows [16k, 16k+16) (2048 B); d halves 16 KB apart
           const uint64_t vd = sdesc_sw128(v_addr + k * 2048, 16384, 1024);
-          umma_f16_ts(tO, tmem + 384u + 64u * s + k * 8, vd, (v_fp8 && t < n_slab) ? idesc_o16 : idesc_o, (t > 0 || k > 0) ? 1u : 0u);
+          umma_f16_ts(tmem + 256u + 128u * g, tmem + 128u * g + k * 8, vd, idesc, (t > 0 || k > 0) ? 1u : 0u);
         }
-        umma_commit(&pv_done[s]);
-        umma_commit(&v_empty[s]);
+        if (t == n_tiles - 1) umma_commit(&o_full[g]);
+        if (g == kAttnTiles - 1) umma_commit(&v_empty[vs]);
         return true;
       };
-      for (int t = 0; ok && t < n_tiles; ++t) {
-        const int s = t & 1;
-        const int ks = t % AttnSmem::kKStages;
-        if (!mbar_wait(&k_full[ks], (t / AttnSmem::kKStages) & 1, abort_flag, a.status)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(k_ptr(ks));
-#pragma unroll
-        for (int k = 0; k < kAttnD / 16; ++k) {
-          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-          const uint64_t qd = sdesc_sw128(q_addr + off, 16, 1024);
-          const uint64_t kd = sdesc_sw128(k_addr + off, 16, 1024);
-          umma_f16_ss(tmem + 128u * s, qd, kd, idesc_s, k > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[s]);
-        umma_commit(&k_empty[ks]);
-        if (t > 0 && !issue_pv(t - 1)) {
-          ok = false;
-          break;
+      if (ok && wait_k(0)) {
+        issue_s(0, 0);
+        issue_s(1, 0);
+        umma_commit(&k_empty[0]);
+        for (int t = 0; t < n_tiles; ++t) {
+          const bool next = t + 1 < n_tiles;
+          if (!issue_pv(0, t)) break;
+          if (next) {
+            if (!wait_k(t + 1)) break;
+            issue_s(0, t + 1);
+          }
+          if (!issue_pv(1, t)) break;
+          if (next) {
+            issue_s(1, t + 1);
+            umma_commit(&k_empty[(t + 1) & 1]);
+          }
         }
       }
-      if (ok) issue_pv(n_tiles - 1);
     }
   } else if (warp < 4) {
     // ------------------------------------------------------------ V converters
@@ -264,11 +323,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax
-    const int quarter = warp & 3;
-    const int row = threadIdx.x - 128;  // == quarter * 32 + lane
+    // ------------------------------------------------------------ softmax (tile g)
+    const int g = (warp - 4) >> 2;
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t tO = tmem + lane_base + 256u;
+    const uint32_t tS = tmem + lane_base + 128u * g;  // S_g; P_g over its first 64 columns
+    const uint32_t tO = tmem + lane_base + 256u + 128u * g;
     const uint8_t* kvb = has_kv ? a.key_valid + static_cast<int64_t>(b) * a.kv_sb : nullptr;
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
@@ -277,15 +338,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const float vsc = slab_f16 ? __ldg(a.v_scale + static_cast<int64_t>(b) * a.H + h) : 1.0f;
     bool vsc_applied = !slab_f16;
     for (int t = 0; t < n_tiles; ++t) {
-      const int s = t & 1;
-      const uint32_t ph = (t >> 1) & 1;
-      const uint32_t tS = tmem + lane_base + 128u * s;        // this tile's S buffer
-      const uint32_t tP = tmem + lane_base + 384u + 64u * s;  // this tile's P buffer
-      if (!mbar_wait(&s_full[s], ph, abort_flag, a.status)) {
+      // the warp leaves together (tcgen05.ld/st are warp-collective), also on a timeout
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[g], t & 1, abort_flag, a.status))) {
         ok = false;
         break;
       }
-      __syncwarp();  // lanes leave the spin loop separately; tcgen05.ld is warp-aligned
       tc_fence_after();
       const bool slab = t < n_slab;
       const int kv0 = slab ? t * kAttnBN : P + (t - n_slab) * kAttnBN;
@@ -302,30 +359,36 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       }
       float sv[kAttnBN];
+      {
+        uint32_t r[kAttnBN];
+        tmem_ld128(tS, r);
 #pragma unroll
-      for (int c = 0; c < kAttnBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tS + c * 32, r);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) sv[c * 32 + j] = __uint_as_float(r[j]);
+        for (int j = 0; j < kAttnBN; ++j) sv[j] = __uint_as_float(r[j]);
       }
       // raw scores stay unscaled; the scale is folded into the exponent below
-      float mx[8];
+      // every key of the tile allowed for every row of the warp (warp-uniform: the
+      // branches below end in warp-collective TMEM stores)
+      const bool full = __all_sync(0xffffffffu, lim_rel >= kAttnBN - 1 && !has_kv);
+      float mx[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
-      if (lim_rel >= kAttnBN - 1 && !has_kv) {
+      for (int i = 0; i < 4; ++i) mx[i] = -INFINITY;
+      if (full) {
 #pragma unroll
-        for (int c = 0; c < kAttnBN; ++c) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
+        for (int c = 0; c < kAttnBN; c += 8) {
+          mx[0] = fmax3(mx[0], sv[c], sv[c + 1]);
+          mx[1] = fmax3(mx[1], sv[c + 2], sv[c + 3]);
+          mx[2] = fmax3(mx[2], sv[c + 4], sv[c + 5]);
+          mx[3] = fmax3(mx[3], sv[c + 6], sv[c + 7]);
+        }
       } else {
 #pragma unroll
         for (int c = 0; c < kAttnBN; ++c) {
           const bool allowed = (c <= lim_rel) && ((kvm[c >> 5] >> (c & 31)) & 1u);
           sv[c] = allowed ? sv[c] : -INFINITY;
-          mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
+          mx[c & 3] = fmaxf(mx[c & 3], sv[c]);
         }
       }
-      const float raw_max = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                  fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      const float raw_max = fmax3(mx[0], mx[1], fmaxf(mx[2], mx[3]));
       const float tmax = raw_max * a.qk_scale_log2;  // scale > 0: max commutes with it
       // the running max moves (and O, l are rescaled) only when it grows by > 2^8
       float alpha = 1.0f;
@@ -336,36 +399,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         m_run = tmax;
       }
       const float neg_m = (m_run == -INFINITY) ? 0.0f : -m_run;
-      float ps[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      uint32_t pk[kAttnBN / 2];
-#pragma unroll
-      for (int c = 0; c < kAttnBN; c += 2) {
-        const float p0 = ex2(fmaf(sv[c], a.qk_scale_log2, neg_m));
-        const float p1 = ex2(fmaf(sv[c + 1], a.qk_scale_log2, neg_m));
-        ps[(c >> 1) & 3] += p0 + p1;
-        pk[c / 2] = (slab_f16 && slab) ? pack_f16x2(p0, p1) : pack_bf16x2(p0, p1);
-      }
-      const float psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
+      // S_g(t) is in registers: P_g(t) overwrites its first 64 columns
+      const bool f16p = slab_f16 && slab;
+      float psum;
+      if (full)
+        psum = f16p ? softmax_row<true, true>(sv, a.qk_scale_log2, neg_m, tS)
+                    : softmax_row<true, false>(sv, a.qk_scale_log2, neg_m, tS);
+      else
+        psum = f16p ? softmax_row<false, true>(sv, a.qk_scale_log2, neg_m, tS)
+                    : softmax_row<false, false>(sv, a.qk_scale_log2, neg_m, tS);
       l_run = l_run * alpha + psum;
-      // P buffer s is free once P.V of tile t-2 finished; O may be rescaled once
-      // P.V of tile t-1 finished.
-      if (t >= 2 && !mbar_wait(&pv_done[s], ((t - 2) >> 1) & 1, abort_flag, a.status)) {
-        ok = false;
-        break;
-      }
-      __syncwarp();
-      // O is touched only when some row of the warp rescales (or at the slab
-      // boundary); the whole warp then runs the warp-collective TMEM loads/stores, a
-      // row that keeps its max with factor 1.  pv_done of tile t-1 cannot run two
-      // phases ahead of this thread: P.V_t needs this thread's P_t.
+      // O_g holds the sum up to tile t-1 (P_g(t-1).V completed before S_g(t)): it is
+      // touched only when some row of the warp rescales (or at the slab boundary);
+      // the whole warp then runs the warp-collective TMEM loads/stores, a row that
+      // keeps its max with factor 1.
       const bool boundary = !vsc_applied && t == n_slab;  // first fresh tile after the fp8 slab
       if (t >= 1 && __any_sync(0xffffffffu, rescale_o || boundary)) {
-        if (!mbar_wait(&pv_done[(t - 1) & 1], ((t - 1) >> 1) & 1, abort_flag, a.status)) {
-          ok = false;
-          break;
-        }
-        __syncwarp();
-        tc_fence_after();
         const float f = (rescale_o ? alpha : 1.0f) * (boundary ? vsc : 1.0f);
 #pragma unroll
         for (int c = 0; c < kAttnD / 32; ++c) {
@@ -377,36 +426,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         if (boundary) vsc_applied = true;
       }
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t r[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) r[j] = pk[c * 32 + j];
-        tmem_st32(tP + c * 32, r);
-      }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[s]);
+      if (lane == 0) mbar_arrive(&p_full[g]);
     }
     // epilogue: O / l -> bf16
-    const int grow = m0 + row;
+    const int grow = m0 + g * kAttnBM + row;
     float o[kAttnD];
     bool have_o = false;
-    if (ok && n_tiles > 0) {
-      const int tl = n_tiles - 1;
-      if (mbar_wait(&pv_done[tl & 1], (tl >> 1) & 1, abort_flag, a.status)) {
-        __syncwarp();
-        tc_fence_after();
+    const bool o_ready = ok && n_tiles > 0 && mbar_wait(&o_full[g], 0, abort_flag, a.status);
+    if (__all_sync(0xffffffffu, o_ready)) {  // warp-uniform: tcgen05.ld is warp-collective
+      tc_fence_after();
+      uint32_t r[kAttnD];
+      tmem_ld128(tO, r);
 #pragma unroll
-        for (int c = 0; c < kAttnD / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tO + c * 32, r);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) o[c * 32 + j] = __uint_as_float(r[j]);
-        }
-        have_o = true;
-      }
+      for (int j = 0; j < kAttnD; ++j) o[j] = __uint_as_float(r[j]);
+      have_o = true;
     }
     if (grow < a.SQ) {
       const bool nz = have_o && l_run > 0.0f;
@@ -454,7 +490,7 @@ extern "C" int qik_block_causal_attention(const qik_attn_args* args, int* status
   QIK_REQUIRE(A.B >= 0 && A.SQ >= 0 && A.SN >= 0 && A.P >= 0 && A.H > 0, "qik_block_causal_attention: bad sizes");
   if (A.B == 0 || A.SQ == 0) return QIK_OK;
   QIK_REQUIRE(A.SN > 0, "qik_block_causal_attention: no fresh keys (SN == 0)");
-  QIK_REQUIRE(A.B * A.H <= 65535 && A.SQ <= (1ll << 30) && A.SN + A.P <= (1ll << 30),
+  QIK_REQUIRE(A.B * A.H <= 65535 && (A.SQ + kAttnRows - 1) / kAttnRows <= 65535 && A.SN + A.P <= (1ll << 30),
               "qik_block_causal_attention: size out of range");
   QIK_REQUIRE(A.q && A.k && A.v && A.out, "qik_block_causal_attention: NULL q/k/v/out");
   const bool has_cache = (A.flags & QIK_ATTN_HAS_CACHE) && A.P > 0;
@@ -525,7 +561,8 @@ extern "C" int qik_block_causal_attention(const qik_attn_args* args, int* status
     QIK_TRY_CUDA(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem::kBytes));
     attr_set[dev] = true;
   }
-  dim3 grid(static_cast<unsigned>((A.SQ + kAttnBM - 1) / kAttnBM), static_cast<unsigned>(A.B * A.H));
+  // x = (b, h), y = query block (numbered from the last block: heaviest first)
+  dim3 grid(static_cast<unsigned>(A.B * A.H), static_cast<unsigned>((A.SQ + kAttnRows - 1) / kAttnRows));
   attn_fwd_kernel<<<grid, kAttnThreads, AttnSmem::kBytes, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, tck, tcv,
                                                                                                   d);
   return check_launch("attn_fwd_kernel");

@@ -6,10 +6,18 @@ The modules are stand-ins with the attribute names the reference's processor and
 block read (processors.py:50-126, 137-187): ``attn.heads``, ``attn.fused_qkv``,
 ``attn.norm_q/norm_k`` (weight, eps), ``attn.to_out[0/1]``, ``img_norm1/2`` (eps),
 ``img_mlp.fused_up/out``; the reference's own block test needs diffusers, which is
-not installed.  Each stage of the oracle composition re-quantizes the previous
-stage's bf16 output, so the end-to-end gate is a relative Frobenius error (1e-2 for
-the processor, 2e-2 for the whole block); a wiring mistake (an offset, a view, a row
-map) gives errors of order 1.
+not installed.
+
+Gates.  Every FP8 linear re-quantizes its bf16 input with a dynamic per-tensor scale,
+so a last-bit difference in the largest element of an intermediate (a different but
+equally exact summation order) moves the scale and re-rounds about half of the e4m3
+codes: ~2% relative Frobenius error end to end with no error in any stage.  The
+processor is therefore checked stage by stage on its own intermediates, captured at
+the attention call: attention on the q / k / v the processor passed (relF <= 5e-3),
+and the out-projection on the processor's own attention output (relF <= 5e-3, the
+quantizer being bit-exact).  End to end against the oracle composition from the
+hidden states the gate is 5e-2: it catches wiring mistakes (an offset, a view, a row
+map), which give errors of order 1.
 """
 import numpy as np
 import pytest
@@ -117,8 +125,43 @@ def o_attention_part(attn, x, fr, L, cache=None):
     return o_linear(o.flatten(2, 3), attn.to_out[0]), k, v
 
 
+E2E_GATE = 5e-2    # end to end through re-quantizing FP8 linears (wiring check)
+STAGE_GATE = 5e-3  # one stage on the product's own inputs
+
+
+@pytest.fixture
+def capture(monkeypatch):
+    """Records each attention call the processor makes (inputs, options, output)."""
+    import qik.processors as PR
+    calls = []
+    real = PR.block_causal_flash_attention
+
+    def wrap(q, k, v, L, key_valid, **kw):
+        out = real(q, k, v, L, key_valid, **kw)
+        cpu = lambda t: None if t is None else t.detach().cpu()  # noqa: E731
+        calls.append({"q": cpu(q), "k": cpu(k), "v": cpu(v), "L": cpu(L), "key_valid": cpu(key_valid),
+                      "cache_k": cpu(kw.get("cache_k")), "cache_v": cpu(kw.get("cache_v")),
+                      "cache_v_scale": cpu(kw.get("cache_v_scale")), "out": cpu(out)})
+        return out
+
+    monkeypatch.setattr(PR, "block_causal_flash_attention", wrap)
+    return calls
+
+
+def check_stages(attn, call, out, tag):
+    """Attention on the processor's own q / k / v, and the out-projection on its own
+    attention output."""
+    ref_att = O.block_causal_attention(call["q"], call["k"], call["v"], call["L"], call["key_valid"],
+                                       call["cache_k"], call["cache_v"], call["cache_v_scale"],
+                                       out_dtype=torch.float32)
+    r_att = O.relf(call["out"], ref_att)
+    r_out = O.relf(out.cpu(), o_linear(call["out"].flatten(2, 3), attn.to_out[0]))
+    print(f"{tag}: attention stage relF {r_att:.2e}, out-projection stage relF {r_out:.2e}")
+    assert r_att <= STAGE_GATE and r_out <= STAGE_GATE
+
+
 # ---------------------------------------------------------------- processor
-def test_processor_prefill_block_causal():
+def test_processor_prefill_block_causal(capture):
     """Prefill over text + two image blocks + target rows (processors.py:88-97)."""
     blk = _block()
     S = 384
@@ -127,14 +170,16 @@ def test_processor_prefill_block_causal():
     fr = _freqs(S, HD)
     out = blk.attn(hidden_states=x.cuda(), rotary_emb=fr.cuda(), segments=segments)
     torch.cuda.synchronize()
+    check_stages(blk.attn, capture[-1], out, "prefill")
     L = O.build_prefix_lengths(segments, 256, S)
+    assert torch.equal(capture[-1]["L"].long(), L.long())
     ref, _, _ = o_attention_part(blk.attn, x, fr, L)
     r = O.relf(out.cpu(), ref)
-    print("processor prefill relF", r)
-    assert r <= 1e-2
+    print("processor prefill end-to-end relF", r)
+    assert r <= E2E_GATE
 
 
-def test_processor_extract_then_decode_through_fp8_slab():
+def test_processor_extract_then_decode_through_fp8_slab(capture):
     """Step 1 stores the prefix K/V in the slab (kv_cache_mode="extract",
     processors.py:84-85); later steps attend target rows over [slab ; fresh]
     (processors.py:99-111)."""
@@ -154,6 +199,7 @@ def test_processor_extract_then_decode_through_fp8_slab():
     fr_t = fr[P:].contiguous()
     out = blk.attn(hidden_states=xt.cuda(), rotary_emb=fr_t.cuda(), layer_cache=layer)
     torch.cuda.synchronize()
+    check_stages(blk.attn, capture[-1], out, "decode")
     ck, cv, vs = layer.views()
     # the slab holds the prefix keys / values of step 1
     _, k1, v1 = o_attention_part(blk.attn, x, fr, O.build_prefix_lengths(segments, P, S))
@@ -162,23 +208,26 @@ def test_processor_extract_then_decode_through_fp8_slab():
     L = torch.full((T,), P + T - 1, dtype=torch.int32)
     ref, _, _ = o_attention_part(blk.attn, xt, fr_t, L, cache=(ck.cpu(), cv.cpu(), vs.cpu()))
     r = O.relf(out.cpu(), ref)
-    print("processor decode relF", r)
-    assert r <= 1e-2
+    print("processor decode end-to-end relF", r)
+    assert r <= E2E_GATE
 
 
-def test_processor_without_cache_is_full_attention():
+def test_processor_without_cache_is_full_attention(capture):
     blk = _block()
     S = 200
     x = GI.randn_bf16(513, (2, S, DIM))
     fr = _freqs(S, HD)
     out = blk.attn(hidden_states=x.cuda(), rotary_emb=fr.cuda())
     torch.cuda.synchronize()
+    check_stages(blk.attn, capture[-1], out, "no cache")
     ref, _, _ = o_attention_part(blk.attn, x, fr, torch.full((S,), S - 1, dtype=torch.int32))
-    assert O.relf(out.cpu(), ref) <= 1e-2
+    r = O.relf(out.cpu(), ref)
+    print("processor without cache end-to-end relF", r)
+    assert r <= E2E_GATE
 
 
 # ---------------------------------------------------------------- block
-def test_fused_block_matches_oracle_composition():
+def test_fused_block_matches_oracle_composition(capture):
     """QwenImage21KernelBlock.forward (processors.py:145-187): B=2 with a target mask
     (prefix positions use the t = 0 modulation rows B..2B-1)."""
     from qik.processors import QwenImage21KernelBlock
@@ -192,6 +241,11 @@ def test_fused_block_matches_oracle_composition():
     fr = _freqs(S, HD)
     out = blk(x.cuda(), mod.cuda(), rotary_emb=fr.cuda(), target_token_mask=tmask.cuda())
     torch.cuda.synchronize()
+    c = capture[-1]
+    r_att = O.relf(c["out"], O.block_causal_attention(c["q"], c["k"], c["v"], c["L"], c["key_valid"],
+                                                     out_dtype=torch.float32))
+    print("block attention stage relF", r_att)
+    assert r_att <= STAGE_GATE
 
     a = blk.attn
     img_mod = O.layer_norm_modulate(x, mod, 0, tmask, 1e-6)
@@ -202,8 +256,8 @@ def test_fused_block_matches_oracle_composition():
     mlp_out = o_linear(O.swiglu(gate, up), blk.img_mlp.out)
     ref = O.gate_residual(h, mlp_out, mod, 3 * DIM, tmask)
     r = O.relf(out.cpu(), ref)
-    print("block relF", r, "max-abs", (out.cpu().float() - ref.float()).abs().max().item())
-    assert r <= 2e-2
+    print("block end-to-end relF", r, "max-abs", (out.cpu().float() - ref.float()).abs().max().item())
+    assert r <= E2E_GATE
 
 
 def test_convert_transformer_to_kernels_swaps_blocks_and_processor():
