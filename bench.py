@@ -377,29 +377,20 @@ def fused_ops(device: torch.device, flush: torch.Tensor, iters: int, x: torch.Te
     return res
 
 
-def extras(device: torch.device, flush: torch.Tensor, iters: int = 10) -> dict:
-    """Attention at BASELINE config 4 and the DiT-block time at 1024 px (configs[2] +
-    the t2i attention), each on synthetic inputs with the BASELINE shapes."""
-    from qik import fp8 as F
-    from qik import _lib as L
+def attention_cfg4_cases(device: torch.device, g: torch.Generator) -> dict:
+    """BASELINE config 4 attention, synthetic inputs: the prefill form (256 text rows
+    with L = q, 2304 cond rows with L = 2559, 4096 target rows with L = 6655) and the
+    decode form (4096 target queries over the e4m3-V slab of 2560 keys + 4096 fresh).
+    Returns {name: (callable, flops)}."""
     from qik.kv_cache import ContiguousKVCache
     from qik.triton_attention import block_causal_flash_attention as attn
-    stream = torch.cuda.current_stream(device)
-    g = torch.Generator(device=device).manual_seed(7)
     H, D = 24, 128
-    out = {}
-    # config 4, prefill form: 256 text (L = q) + 2304 cond (L = 2559) + 4096 target (L = 6655)
     S = 6656
     q, k, v = (torch.randn(1, S, H, D, device=device, generator=g, dtype=torch.bfloat16) for _ in range(3))
     Lp = torch.arange(S, dtype=torch.int32, device=device)
     Lp[256:2560] = 2559
     Lp[2560:] = S - 1
-    fl = 4.0 * D * H * float((Lp.long() + 1).sum())
-    for _ in range(3):
-        attn(q, k, v, Lp, None)
-    ms = _time_ms(lambda: attn(q, k, v, Lp, None), iters, flush, stream)
-    out["attention_cfg4_prefill"] = {"ms": round(ms, 4), "tflops": round(fl / ms / 1e9, 1), "gflop": round(fl / 1e9, 1)}
-    # config 4, decode form: 4096 target queries over the e4m3-V slab (2560) + 4096 fresh
+    fl_p = 4.0 * D * H * float((Lp.long() + 1).sum())
     P, T = 2560, 4096
     kp, vp = (torch.randn(1, P, H, D, device=device, generator=g, dtype=torch.bfloat16) for _ in range(2))
     cache = ContiguousKVCache(1, 1, P, H, D, v_fp8=True, device=device)
@@ -407,19 +398,23 @@ def extras(device: torch.device, flush: torch.Tensor, iters: int = 10) -> dict:
     ck, cv, vs = cache.get_layer(0).views()
     qd, kn, vn = (torch.randn(1, T, H, D, device=device, generator=g, dtype=torch.bfloat16) for _ in range(3))
     Ld = torch.full((T,), P + T - 1, dtype=torch.int32, device=device)
-    fl = 4.0 * D * H * T * (P + T)
-    run = lambda: attn(qd, kn, vn, Ld, None, ck, cv, vs, uniform_full=True)  # noqa: E731
-    for _ in range(3):
-        run()
-    ms = _time_ms(run, iters, flush, stream)
-    out["attention_cfg4_decode_fp8_slab"] = {"ms": round(ms, 4), "tflops": round(fl / ms / 1e9, 1),
-                                             "gflop": round(fl / 1e9, 1)}
-    # DiT block @1024 px, CFG batch 2: M = 2 x 4352, the whole block --
-    # timestep modulation linear (M = 2), LayerNorm + modulate (its amax feeds the QKV
-    # quantizer), fused QKV, per-head RMSNorm + RoPE of q and k, block-causal attention
-    # (256 text causal + 4096 image), out-proj, gated residual, LayerNorm + modulate,
-    # FFN (GELU-tanh) and the second gated residual.
+    fl_d = 4.0 * D * H * T * (P + T)
+    return {"attention_cfg4_prefill": (lambda: attn(q, k, v, Lp, None), fl_p),
+            "attention_cfg4_decode_fp8_slab": (lambda: attn(qd, kn, vn, Ld, None, ck, cv, vs, uniform_full=True),
+                                               fl_d)}
+
+
+def dit_block_case(device: torch.device, g: torch.Generator) -> dict:
+    """DiT block @1024 px, CFG batch 2: M = 2 x 4352, the whole block --
+    timestep modulation linear (M = 2), LayerNorm + modulate (its amax feeds the QKV
+    quantizer), fused QKV, per-head RMSNorm + RoPE of q and k, block-causal attention
+    (256 text causal + 4096 image), out-proj, gated residual, LayerNorm + modulate,
+    FFN (GELU-tanh) and the second gated residual; random-init
+    FP8 weights, synthetic activations."""
+    from qik import fp8 as F
+    from qik.triton_attention import block_causal_flash_attention as attn
     from qik.triton_fused import fused_gate_residual, fused_layer_norm_modulate, fused_rms_norm_rope
+    H, D = 24, 128
     B2, S2 = 2, 4352
     M, K = B2 * S2, 3072
     lin = {}
@@ -454,16 +449,49 @@ def extras(device: torch.device, flush: torch.Tensor, iters: int = 10) -> dict:
         f2 = F.fp8_ffn_gelu(hm2.reshape(M, K), lin["up"], lin["down"]).view(B2, S2, K)
         return fused_gate_residual(h, f2, mod, 3 * K, None)
 
+    lin_fl = 2.0 * M * K * (9216 + 3072 + 12288) + 2.0 * M * 12288 * K + 2.0 * B2 * K * 18432
+    at_fl = 4.0 * D * H * B2 * float((Lt.long() + 1).sum())
+    return {"block": block, "linear_flops": lin_fl, "attention_flops": at_fl, "x": x,
+            "mod": lambda: lin["mod"](temb)}
+
+
+PROFILE_CASES = ("attention_cfg4_prefill", "attention_cfg4_decode_fp8_slab", "dit_block_1024px_cfg2")
+
+
+def profile_case(device: torch.device, name: str) -> None:
+    """Runs one workload three times (the launches an ncu capture selects from)."""
+    g = torch.Generator(device=device).manual_seed(7)
+    fn = dit_block_case(device, g)["block"] if name == "dit_block_1024px_cfg2" else attention_cfg4_cases(device, g)[name][0]
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize(device)
+    from qik import _lib as L
+    print(json.dumps({"profile_case": name, "runs": 3, "device_status": L.device_status(device)}), flush=True)
+
+
+def extras(device: torch.device, flush: torch.Tensor, iters: int = 10) -> dict:
+    """Attention at BASELINE config 4 and the DiT-block time at 1024 px (configs[2] +
+    the t2i attention), each on synthetic inputs with the BASELINE shapes."""
+    from qik import _lib as L
+    stream = torch.cuda.current_stream(device)
+    g = torch.Generator(device=device).manual_seed(7)
+    out = {}
+    for name, (fn, fl) in attention_cfg4_cases(device, g).items():
+        for _ in range(3):
+            fn()
+        ms = _time_ms(fn, iters, flush, stream)
+        out[name] = {"ms": round(ms, 4), "tflops": round(fl / ms / 1e9, 1), "gflop": round(fl / 1e9, 1)}
+    case = dit_block_case(device, g)
+    block = case["block"]
     for _ in range(3):
         block()
     ms = _time_ms(block, iters, flush, stream)
-    lin_fl = 2.0 * M * K * (9216 + 3072 + 12288) + 2.0 * M * 12288 * K + 2.0 * B2 * K * 18432
-    at_fl = 4.0 * D * H * B2 * float((Lt.long() + 1).sum())
+    lin_fl, at_fl = case["linear_flops"], case["attention_flops"]
     out["dit_block_1024px_cfg2"] = {"ms": round(ms, 4), "tflops": round((lin_fl + at_fl) / ms / 1e9, 1),
                                     "linear_gflop": round(lin_fl / 1e9, 1), "attention_gflop": round(at_fl / 1e9, 1),
                                     "includes": "modulation GEMV, 2x LayerNorm+modulate, RMSNorm+RoPE (q, k), "
                                                 "attention, 4 FP8 linears (GELU FFN), 2x gated residual"}
-    out["fused_ops_t2i"] = fused_ops(device, flush, iters, x, mod=lin["mod"](temb))
+    out["fused_ops_t2i"] = fused_ops(device, flush, iters, case["x"], mod=case["mod"]())
     out["device_status"] = L.device_status(device)
     return out
 
@@ -639,6 +667,8 @@ def main() -> int:
     ap.add_argument("--no-extras", action="store_true", help="skip the attention / DiT-block measurements")
     ap.add_argument("--sweep", action="store_true",
                     help="print the configs[4] GEMM / quantizer sweep (one JSON line per shape) instead of the bench")
+    ap.add_argument("--profile-case", choices=PROFILE_CASES,
+                    help="run one extras workload three times and exit (the launches an ncu capture selects from)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -654,6 +684,9 @@ def main() -> int:
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if args.profile_case:
+        profile_case(device, args.profile_case)
+        return 0
     if args.sweep:
         for row in sweep(device):
             print(json.dumps(row), flush=True)
