@@ -500,8 +500,9 @@ def tp_stack(device: torch.device, rank: int, world: int, flush: torch.Tensor, i
     """BASELINE configs[4]'s layer-stack case: 4 DiT blocks at 1024 px, CFG batch 2
     (M = 8704), tensor parallel over `world` GPUs -- QKV by heads and FFN-up column-
     parallel, attention on local heads, out-proj and FFN-down row-parallel with a
-    4-byte amax all-reduce(MAX) and an fp32 NCCL all-reduce(SUM) of the partial
-    products.  Strong scaling: the total work is fixed.  Time = max over ranks."""
+    4-byte amax all-reduce(MAX) and the partial products summed over NVLink peer
+    memory by the GEMM's own epilogue (the fp32 NCCL all-reduce(SUM) form is timed
+    beside it).  Strong scaling: the total work is fixed.  Time = max over ranks."""
     from qik import fp8 as F
     from qik import parallel as PX
     H, D, K, HID, B, S = 24, 128, 3072, 12288, 2, 4352
@@ -517,10 +518,11 @@ def tp_stack(device: torch.device, rank: int, world: int, flush: torch.Tensor, i
     Lt = torch.arange(S, dtype=torch.int32, device=device)
     Lt[256:] = S - 1
 
-    def timed(chunks: int) -> float:
+    def timed(chunks: int, comm: str = "nccl") -> float:
         """Mean ms per 4-block stack (max over ranks) with `chunks` row blocks per
-        row-parallel GEMM / all-reduce (1 = one all-reduce after the whole GEMM)."""
-        blocks = [PX.TPBlock.from_full(full, H, D, rank, world, chunks=chunks) for full in fulls]
+        row-parallel GEMM / all-reduce (1 = one all-reduce after the whole GEMM), or with
+        the row-parallel sums over NVLink peer memory fused with the GEMM (comm="peer")."""
+        blocks = [PX.TPBlock.from_full(full, H, D, rank, world, chunks=chunks, comm=comm) for full in fulls]
 
         def stack():
             h = x
@@ -545,22 +547,33 @@ def tp_stack(device: torch.device, rank: int, world: int, flush: torch.Tensor, i
         t = torch.tensor([sum(a.elapsed_time(b) for a, b in evs) / iters], dtype=torch.float64, device=device)
         if world > 1:
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            torch.distributed.barrier()  # no rank still writes into a peer's workspace
+        for blk in blocks:
+            for lin in (blk.out, blk.down):
+                for red in lin._peer.values():
+                    red.close()
         return float(t.item())
 
-    ms = timed(1)
-    ms_overlap = timed(4) if world > 1 else ms
+    ms_peer = timed(1, "peer")
+    ms_nccl = timed(1, "nccl") if world > 1 else ms_peer
+    ms_overlap = timed(4, "nccl") if world > 1 else ms_peer
+    ms = ms_peer
     M = B * S
     lin = 2.0 * M * K * (3 * H * D + K + HID) + 2.0 * M * HID * K
     att = 4.0 * D * H * B * float((Lt.long() + 1).sum())
     total = 4 * (lin + att)
     return {"ms": round(ms, 4), "tflops_total": round(total / ms / 1e9, 1),
             "tflops_per_gpu": round(total / ms / 1e9 / world, 1), "n_gpus": world, "scaling": "strong",
-            "ms_overlapped_4_blocks": round(ms_overlap, 4),
+            "form": "row-parallel GEMM epilogue stores fp32 tiles into the owner rank's memory over NVLink "
+                    "(CUDA IPC), owner sums its rows and stores bf16 rows into every rank "
+                    "(qik_fp8_gemm_scatter + qik_tp_reduce_gather + qik_tp_wait)" if world > 1 else "one GPU",
+            "ms_nccl_allreduce": round(ms_nccl, 4),
+            "ms_nccl_overlapped_4_blocks": round(ms_overlap, 4),
             "overlapped_form": "row-parallel GEMMs in 4 row blocks, each block's all-reduce on a side stream "
                                "under the next block's GEMM (slower here: NCCL's kernels take SMs from the "
                                "persistent GEMM)" if world > 1 else "n/a",
-            "collectives_per_stack": "8 x all-reduce(SUM) fp32 [8704, 3072] + 8 x all-reduce(MAX) 4 bytes"
-            if world > 1 else "none"}
+            "collectives_per_stack": "8 x peer-memory row reductions of fp32 [8704, 3072] partial products "
+                                     "+ 8 x all-reduce(MAX) 4 bytes (NCCL)" if world > 1 else "none"}
 
 
 # ------------------------------------------------------------------------------ CPU arm

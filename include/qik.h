@@ -113,6 +113,7 @@ int qik_quantize_weight(const void* w, int dtype, int64_t n, uint8_t* q, float* 
 /* Epilogue selectors for qik_fp8_gemm. */
 #define QIK_EPI_SCALE 0      /* y = acc * sa * sb (+ bias) */
 #define QIK_EPI_GELU_TANH 1  /* y = gelu_tanh(bf16(acc * sa * sb (+ bias))) */
+#define QIK_EPI_SCATTER 2    /* fp32 acc * sa * sb rows to their owner rank (qik_fp8_gemm_scatter) */
 
 /*
  * FP8 GEMM on tcgen05: C[M,N] = epilogue(A[M,K] . B[N,K]^T), e4m3 x e4m3 with
@@ -255,6 +256,73 @@ int qik_gate_residual(const void* x, const void* f, int64_t B, int64_t S, int64_
  */
 int qik_swiglu(const void* gate, int64_t ld_gate, const void* up, int64_t ld_up, int64_t M, int64_t N, void* out,
                int64_t ld_out, uint32_t* amax_out, void* stream);
+
+/* ---------------------------------------------------------------- tensor parallel
+ * Row-parallel FP8 linear with the reduction over peer memory, replacing the
+ * fp32 partial product + NCCL all-reduce of the tensor-parallel block stack
+ * (4-block TP; the reference itself is single-GPU: its
+ * FP8Linear.forward is qwen_image_kernel/fp8.py:78-90).  One process per GPU; every
+ * rank maps its peers' workspaces (CUDA IPC) and calls, in the same order:
+ *   qik_fp8_gemm_scatter   (its GEMM's fp32 rows stored straight into the owner
+ *                           rank's receive slot over NVLink, tile by tile, each tile
+ *                           counted at the owner with a system-scope atomic),
+ *   qik_tp_reduce_gather   (the owner sums its rows over the ranks in rank order,
+ *                           adds the bias, stores bf16 rows into every rank's output
+ *                           and counts them there),
+ *   qik_tp_wait            (this rank waits until every owner's rows arrived).
+ * Rank o owns rows [o R, min((o + 1) R, M)), R a multiple of 256.  Counters only grow:
+ * call number e waits for e x the per-call count (uint32 arithmetic modulo 2^32), and
+ * the receive slots alternate with the parity of e.  Every wait is bounded (status
+ * QIK_STATUS_TIMEOUT); no multicast is used.
+ */
+#define QIK_TP_MAX_WORLD 8
+
+/* Bytes of a CUDA IPC memory handle (cudaIpcMemHandle_t). */
+size_t qik_ipc_handle_bytes(void);
+
+/*
+ * Export the allocation holding `ptr`: writes its IPC handle (qik_ipc_handle_bytes()
+ * bytes) and the offset of `ptr` from the allocation's base.
+ */
+int qik_ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out);
+
+/*
+ * Map a peer's exported allocation into this process: *base_out is the mapped base
+ * (to pass to qik_ipc_close), the exported pointer is *base_out + offset.
+ */
+int qik_ipc_open(const void* handle, void** base_out);
+int qik_ipc_close(void* base);
+
+/*
+ * Arrivals qik_fp8_gemm_scatter produces per call at owner `owner` from one rank
+ * (tiles whose first row the owner holds x tiles across N x CTAs per tile).
+ */
+int64_t qik_fp8_gemm_scatter_signals(int64_t M, int64_t N, int64_t rows_per_owner, int owner);
+
+/*
+ * Partial product of a row-parallel linear: P = A . B^T * sa * sb (fp32, no bias),
+ * row r stored at dst[r / R] + (r mod R) * N and, after each tile, one
+ * atomicAdd (system scope) of 1 at cnt[owner].
+ *   A [M, K] e4m3 (this rank's K slice), B [N, K] e4m3; dst / cnt: host arrays of
+ *   `world` device pointers (peer memory for other owners); status as qik_fp8_gemm.
+ */
+int qik_fp8_gemm_scatter(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda,
+                         int64_t ldb, const float* scale_a, const float* scale_b, int world, int64_t rows_per_owner,
+                         float* const* dst, uint32_t* const* cnt, int* status, void* stream);
+
+/*
+ * Owner step: waits until cnt_in[s] reached cnt_target (as signed 32-bit distance) for
+ * every rank s, then out_p[row, :] = bf16(sum_{s = 0..world-1} recv[s][row - o R, :]
+ * (+ bias)) for its rows, into every rank p's output out[p] ([M, N] bf16), and one
+ * atomicAdd (system scope) of 1 per CTA at gcnt[p]; `ctas` CTAs (the per-call count).
+ *   recv: world slots of R x N fp32, slot s at recv + s R N.
+ */
+int qik_tp_reduce_gather(const float* recv, const uint32_t* cnt_in, uint32_t cnt_target, int world, int owner,
+                         int64_t M, int64_t N, int64_t rows_per_owner, const void* bias, void* const* out,
+                         uint32_t* const* gcnt, int ctas, int* status, void* stream);
+
+/* Waits until gcnt[o] reached target for every owner o (this rank's counters). */
+int qik_tp_wait(const uint32_t* gcnt, uint32_t target, int world, int* status, void* stream);
 
 /*
  * Self-test of the bounded-wait machinery: launches one CTA that waits on an

@@ -17,7 +17,9 @@
 //     to both CTAs of a pair);
 //   * warps 2-9: epilogue -- tcgen05.ld of the CTA's own accumulator rows, scale by
 //     sa*sb, optional bias and GELU-tanh, bf16/fp32 via swizzled staging and TMA
-//     stores, optional amax of the bf16 output for the next dynamic quantization.
+//     stores, optional amax of the bf16 output for the next dynamic quantization;
+//     or (QIK_EPI_SCATTER) fp32 rows stored from the staging buffer straight into the
+//     owner rank's receive slot in peer memory, each finished tile counted there.
 // The epilogue of tile i overlaps the MMAs of tile i+1.
 #include <stdlib.h>
 #include <string.h>
@@ -43,6 +45,12 @@ struct GemmParams {
   int epilogue;
   uint32_t* amax_out;
   int* status;
+  // QIK_EPI_SCATTER (row-parallel partial products reduced over peer memory): row r
+  // of the fp32 result goes to scat_dst[r / scat_rows] + (r % scat_rows) * N, and each
+  // CTA counts every finished tile at scat_cnt[owner] (system-scope atomic).
+  float* scat_dst[QIK_TP_MAX_WORLD];
+  uint32_t* scat_cnt[QIK_TP_MAX_WORLD];
+  int scat_rows;
 };
 
 // TWO_SM: the CTA is half of a 2-CTA cluster computing 256 x BN tiles with
@@ -282,11 +290,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               *reinterpret_cast<float4*>(sb + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) =
                   make_float4(v[hb * 16 + 4 * q], v[hb * 16 + 4 * q + 1], v[hb * 16 + 4 * q + 2],
                               v[hb * 16 + 4 * q + 3]);
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0 && row0 < p.M) {
-              tma_store_2d(&tmC, col0 + hb * 16, row0, sb);
-              bulk_commit_group();
+            if (p.epilogue == QIK_EPI_SCATTER) {
+              // 32 rows x 64 bytes: lane l stores 16-byte chunk (l & 3) of rows
+              // (l >> 2) + 8 i, i.e. 8 contiguous 64-byte row pieces per store
+              __syncwarp();
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int rr = (lane >> 2) + 8 * i, q = lane & 3;
+                const int grow = row0 + rr;
+                const float4 val =
+                    *reinterpret_cast<const float4*>(sb + rr * 64 + ((q ^ ((rr >> 1) & 3)) << 4));
+                if (grow < p.M) {
+                  const int o = grow / p.scat_rows;
+                  float* dst = p.scat_dst[o] + static_cast<int64_t>(grow - o * p.scat_rows) * p.N + col0 + hb * 16 + 4 * q;
+                  *reinterpret_cast<float4*>(dst) = val;
+                }
+              }
+              __syncwarp();
+            } else {
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0 && row0 < p.M) {
+                tma_store_2d(&tmC, col0 + hb * 16, row0, sb);
+                bulk_commit_group();
+              }
             }
             buf ^= 1;
           }
@@ -333,6 +360,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           mbar_arrive_remote(mapa_shared(&tempty[acc], 0));  // the leader's accumulator barrier
         else
           mbar_arrive(&tempty[acc]);
+      }
+      if (p.epilogue == QIK_EPI_SCATTER) {
+        // the tile's rows of this CTA are stored by all epilogue warps; then one thread
+        // releases them at system scope (cumulative over the barrier) and counts the
+        // tile at the owner of the tile's rows (tiles never straddle owners)
+        named_bar_sync(1, 32 * kGemmEpiWarps);
+        if (warp == 2 && lane == 0) {
+          __threadfence_system();
+          atomicAdd_system(p.scat_cnt[(mb * kTileM) / p.scat_rows], 1u);
+        }
       }
     }
     if (lane == 0) bulk_wait_all();
@@ -441,9 +478,10 @@ static int launch_gemm(const uint8_t* A, const uint8_t* B, const GemmParams& p, 
   return check_launch("fp8_gemm_kernel");
 }
 
-int launch_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
-                    const float* scale_a, const float* scale_b, const void* bias, void* C, int64_t ldc, int out_dtype,
-                    int epilogue, uint32_t* amax_out, int* status, cudaStream_t stream, bool pdl) {
+int launch_fp8_gemm_ex(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                       const float* scale_a, const float* scale_b, const void* bias, void* C, int64_t ldc,
+                       int out_dtype, int epilogue, uint32_t* amax_out, int* status, cudaStream_t stream, bool pdl,
+                       const GemmParams* scatter) {
   QIK_REQUIRE(M >= 0 && N >= 0 && K >= 0, "qik_fp8_gemm: negative size");
   if (M == 0 || N == 0) return QIK_OK;
   QIK_REQUIRE(K > 0, "qik_fp8_gemm: K must be positive");
@@ -456,11 +494,17 @@ int launch_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, in
   QIK_REQUIRE(N % 16 == 0, "qik_fp8_gemm: N=%lld must be a multiple of 16", (long long)N);
   QIK_REQUIRE(ldc >= N && ldc % 8 == 0, "qik_fp8_gemm: ldc must be >= N and a multiple of 8");
   QIK_REQUIRE(out_dtype == QIK_DTYPE_BF16 || out_dtype == QIK_DTYPE_F32, "qik_fp8_gemm: out_dtype must be BF16/F32");
-  QIK_REQUIRE(epilogue == QIK_EPI_SCALE || epilogue == QIK_EPI_GELU_TANH, "qik_fp8_gemm: unknown epilogue");
-  QIK_REQUIRE(!(out_dtype == QIK_DTYPE_F32 && (epilogue != QIK_EPI_SCALE || amax_out)),
+  QIK_REQUIRE(epilogue == QIK_EPI_SCALE || epilogue == QIK_EPI_GELU_TANH ||
+                  (epilogue == QIK_EPI_SCATTER && scatter && out_dtype == QIK_DTYPE_F32 && !bias),
+              "qik_fp8_gemm: unknown epilogue");
+  QIK_REQUIRE(!(out_dtype == QIK_DTYPE_F32 && ((epilogue != QIK_EPI_SCALE && epilogue != QIK_EPI_SCATTER) || amax_out)),
               "qik_fp8_gemm: GELU and amax need BF16 output");
   QIK_REQUIRE(!bias || aligned16(bias), "qik_fp8_gemm: bias must be 16-byte aligned");
   GemmParams p;
+  if (scatter)
+    p = *scatter;
+  else
+    memset(&p, 0, sizeof(p));
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
@@ -487,7 +531,63 @@ int launch_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, in
   }
 }
 
+int launch_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                    const float* scale_a, const float* scale_b, const void* bias, void* C, int64_t ldc, int out_dtype,
+                    int epilogue, uint32_t* amax_out, int* status, cudaStream_t stream, bool pdl) {
+  return launch_fp8_gemm_ex(A, B, M, N, K, lda, ldb, scale_a, scale_b, bias, C, ldc, out_dtype, epilogue, amax_out,
+                            status, stream, pdl, nullptr);
+}
+
 }  // namespace qik
+
+namespace qik {
+// Tile height and width of the configuration launch_fp8_gemm picks for (M, N).
+static void gemm_tile_shape(int64_t M, int64_t N, int* tile_m, int* tile_n, int* ctas_per_tile) {
+  GemmCfg cfg = gemm_cfg_override();
+  if (cfg == kCfgAuto) cfg = gemm_pick_cfg(M, N);
+  *tile_m = cfg == kCfg2Sm ? 2 * kGemmBM : kGemmBM;
+  *tile_n = (cfg == kCfg2Sm || cfg == kCfg256) ? 256 : (cfg == kCfg128 ? 128 : 64);
+  *ctas_per_tile = cfg == kCfg2Sm ? 2 : 1;
+}
+}  // namespace qik
+
+extern "C" int64_t qik_fp8_gemm_scatter_signals(int64_t M, int64_t N, int64_t rows_per_owner, int owner) {
+  if (M <= 0 || N <= 0 || rows_per_owner <= 0 || owner < 0) return 0;
+  int tm, tn, cpt;
+  qik::gemm_tile_shape(M, N, &tm, &tn, &cpt);
+  const int64_t lo = static_cast<int64_t>(owner) * rows_per_owner;
+  const int64_t hi = lo + rows_per_owner < M ? lo + rows_per_owner : M;
+  if (hi <= lo) return 0;
+  // tiles whose first row lies in [lo, hi): rows_per_owner is a multiple of the tile height
+  const int64_t tiles_m = (hi - lo + tm - 1) / tm;
+  return tiles_m * ((N + tn - 1) / tn) * cpt;
+}
+
+extern "C" int qik_fp8_gemm_scatter(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda,
+                                    int64_t ldb, const float* scale_a, const float* scale_b, int world,
+                                    int64_t rows_per_owner, float* const* dst, uint32_t* const* cnt, int* status,
+                                    void* stream) {
+  using namespace qik;
+  QIK_REQUIRE(world >= 1 && world <= QIK_TP_MAX_WORLD, "qik_fp8_gemm_scatter: world %d outside 1..%d", world,
+              QIK_TP_MAX_WORLD);
+  QIK_REQUIRE(dst && cnt, "qik_fp8_gemm_scatter: NULL dst / cnt array");
+  QIK_REQUIRE(rows_per_owner > 0 && rows_per_owner % (2 * kGemmBM) == 0 && rows_per_owner * world >= M,
+              "qik_fp8_gemm_scatter: rows per owner must be a positive multiple of %d covering M", 2 * kGemmBM);
+  QIK_REQUIRE(M <= (1ll << 31) - 1 && N <= (1ll << 31) - 1, "qik_fp8_gemm_scatter: size above 2^31");
+  for (int o = 0; o < world; ++o)
+    QIK_REQUIRE(dst[o] && cnt[o] && aligned16(dst[o]), "qik_fp8_gemm_scatter: dst[%d] / cnt[%d] NULL or unaligned",
+                o, o);
+  // the rest of the checks and the launch are qik_fp8_gemm's, with fp32 output
+  GemmParams extra;
+  memset(&extra, 0, sizeof(extra));
+  for (int o = 0; o < world; ++o) {
+    extra.scat_dst[o] = dst[o];
+    extra.scat_cnt[o] = cnt[o];
+  }
+  extra.scat_rows = static_cast<int>(rows_per_owner);
+  return launch_fp8_gemm_ex(A, B, M, N, K, lda, ldb, scale_a, scale_b, nullptr, dst[0], N, QIK_DTYPE_F32,
+                            QIK_EPI_SCATTER, nullptr, status, static_cast<cudaStream_t>(stream), false, &extra);
+}
 
 extern "C" int qik_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda,
                             int64_t ldb, const float* scale_a, const float* scale_b, const void* bias, void* C,

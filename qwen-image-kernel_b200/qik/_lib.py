@@ -16,7 +16,8 @@ LIB_PATH = Path(__file__).resolve().parent / "libqik.so"
 
 QIK_OK = 0
 DTYPE_BF16, DTYPE_F32, DTYPE_E4M3 = 0, 1, 2
-EPI_SCALE, EPI_GELU_TANH = 0, 1
+EPI_SCALE, EPI_GELU_TANH, EPI_SCATTER = 0, 1, 2
+TP_MAX_WORLD = 8
 ATTN_HAS_CACHE, ATTN_HAS_KEY_VALID, ATTN_UNIFORM, ATTN_V_FP8 = 1, 2, 4, 8
 STATUS_OK, STATUS_TIMEOUT = 0, 1
 
@@ -67,6 +68,16 @@ SIGNATURES = {
     "qik_gate_residual": (_i32, [_vp, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _vp]),
     "qik_swiglu": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),
     "qik_selftest_wait_timeout": (_i32, [_vp, _u64, _vp]),
+    "qik_ipc_handle_bytes": (ctypes.c_size_t, []),
+    "qik_ipc_export": (_i32, [_vp, _vp, ctypes.POINTER(_u64)]),
+    "qik_ipc_open": (_i32, [_vp, ctypes.POINTER(_vp)]),
+    "qik_ipc_close": (_i32, [_vp]),
+    "qik_fp8_gemm_scatter_signals": (_i64, [_i64, _i64, _i64, _i32]),
+    "qik_fp8_gemm_scatter": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _i32, _i64, _vp, _vp, _vp,
+                                    _vp]),
+    "qik_tp_reduce_gather": (_i32, [_vp, _vp, ctypes.c_uint32, _i32, _i32, _i64, _i64, _i64, _vp, _vp, _vp, _i32,
+                                    _vp, _vp]),
+    "qik_tp_wait": (_i32, [_vp, ctypes.c_uint32, _i32, _vp, _vp]),
 }
 
 _lock = threading.Lock()

@@ -189,11 +189,23 @@ class RowParallelFP8Linear(nn.Module):
     Every rank issues the same collectives in the same order; the sum is the same as
     one all-reduce of the whole partial product (the reduction is per element).  The
     default is one block: measured on 2 B200 the overlapped form was slower (the
-    NCCL kernels occupy SMs the persistent GEMM grid counts on)."""
+    NCCL kernels occupy SMs the persistent GEMM grid counts on).
+
+    With ``comm="peer"`` (the default; GPUs, more than one rank) the sum runs over NVLink peer
+    memory instead (``qik.tp_comm.PeerRowReduce``): the GEMM's epilogue stores each
+    finished fp32 tile into the receive slot of the rank owning those rows while the
+    GEMM goes on, the owner sums its rows in rank order, adds the bias and stores bf16
+    rows into every rank's output.  Its workspace is set up collectively at the first
+    call with a given row count; the output stays valid until this module's
+    second-next call."""
 
     def __init__(self, weight: torch.Tensor, weight_scale: torch.Tensor, bias: torch.Tensor | None, group=None,
-                 ops=None, chunks: int = 1):
+                 ops=None, chunks: int = 1, comm: str = "peer"):
         super().__init__()
+        if comm not in ("nccl", "peer"):
+            raise ValueError(f"RowParallelFP8Linear: comm must be 'nccl' or 'peer', not {comm!r}")
+        self.comm = comm
+        self._peer: dict = {}
         self.chunks = chunks
         self.register_buffer("weight", weight)
         self.register_buffer("weight_scale", weight_scale)
@@ -205,12 +217,20 @@ class RowParallelFP8Linear(nn.Module):
         self.ops = ops or QikOps()
 
     @classmethod
-    def from_full(cls, weight, weight_scale, bias, rank, world, group=None, ops=None, chunks: int = 1):
-        return cls(shard_cols(weight, rank, world), weight_scale.clone(), bias, group, ops, chunks)
+    def from_full(cls, weight, weight_scale, bias, rank, world, group=None, ops=None, chunks: int = 1,
+                  comm: str = "peer"):
+        return cls(shard_cols(weight, rank, world), weight_scale.clone(), bias, group, ops, chunks, comm)
 
     def forward_quantized(self, xq: torch.Tensor, sx: torch.Tensor) -> torch.Tensor:
         world = _world(self.group)[1]
         M = xq.shape[0]
+        if world > 1 and xq.is_cuda and self.comm == "peer" and self.chunks == 1:
+            red = self._peer.get(M)
+            if red is None:
+                from .tp_comm import PeerRowReduce
+                red = PeerRowReduce(M, self.weight.shape[0], self.group, xq.device)
+                self._peer[M] = red
+            return red(xq, sx, self.weight, self.weight_scale, self.bias)
         if world > 1 and xq.is_cuda and self.chunks > 1 and M >= 2 * self.chunks:
             part = self._gemm_allreduce_overlapped(xq, sx)
         else:
@@ -273,14 +293,16 @@ class TPBlock(nn.Module):
 
     @classmethod
     def from_full(cls, full: dict, heads: int, head_dim: int, rank: int, world: int, group=None, ops=None,
-                  chunks: int = 1):
+                  chunks: int = 1, comm: str = "peer"):
         """full: name -> (weight e4m3 [N, K], weight_scale [1], bias or None) for
         'qkv', 'out', 'up', 'down' (unsharded, quantized once).  ``chunks``: row blocks of
-        the row-parallel GEMMs whose all-reduce overlaps the next block's GEMM."""
+        the row-parallel GEMMs whose all-reduce overlaps the next block's GEMM;
+        ``comm``: "peer" (the default: reduction over NVLink peer memory fused with the
+        GEMM, RowParallelFP8Linear) or "nccl" (all-reduce)."""
         qkv = ColumnParallelFP8Linear.from_full(*full["qkv"], rank, world, qkv_heads=(heads, head_dim), ops=ops)
-        out = RowParallelFP8Linear.from_full(*full["out"], rank, world, group, ops, chunks)
+        out = RowParallelFP8Linear.from_full(*full["out"], rank, world, group, ops, chunks, comm)
         up = ColumnParallelFP8Linear.from_full(*full["up"], rank, world, ops=ops)
-        down = RowParallelFP8Linear.from_full(*full["down"], rank, world, group, ops, chunks)
+        down = RowParallelFP8Linear.from_full(*full["down"], rank, world, group, ops, chunks, comm)
         return cls(qkv, out, up, down, heads // world, head_dim)
 
     def forward(self, x: torch.Tensor, batch: int, seq: int, prefix_lengths: torch.Tensor) -> torch.Tensor:

@@ -5,7 +5,14 @@
 * the tensor-parallel DiT block (QKV by heads, attention on local heads, row-parallel
   out / FFN-down with fp32 partial all-reduce) matches the single-GPU block within
   the BASELINE tolerances, in both forms (one all-reduce, or row blocks whose
-  all-reduces run on a side stream).
+  all-reduces run on a side stream);
+* with the row-parallel sums over NVLink peer memory (qik.tp_comm.PeerRowReduce:
+  GEMM epilogue stores into the owner's memory, owner reduce + bf16 gather) the block
+  is bit-identical to the all-reduce form (same fp32 partial products; for two ranks
+  the fp32 sum of two terms does not depend on the order), over three successive calls
+  (receive slots and counters alternate / grow with the call number), and a direct
+  reduction with ragged ownership (M = 1000: owner 1 holds 488 rows) equals the
+  partial product + all-reduce + bias of the same operands.
 """
 import datetime
 import os
@@ -44,7 +51,7 @@ def _block_weights(dev, heads=24, d=128, k=3072, hidden=12288):
 
 
 def _worker(rank, world, port, outdir):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     dev = torch.device("cuda", rank)
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
@@ -60,15 +67,40 @@ def _worker(rank, world, port, outdir):
         res["s"] = float(s.item())
         B, S, heads, d = 2, 512, 24, 128
         full = _block_weights(dev)
-        blk = PX.TPBlock.from_full(full, heads, d, rank, world)
+        blk = PX.TPBlock.from_full(full, heads, d, rank, world, comm="nccl")
         xb = GI.randn_bf16(220, (B * S, 3072)).to(dev)
         Lp = torch.arange(S, dtype=torch.int32, device=dev)
         Lp[64:] = S - 1
         res["block"] = blk(xb, B, S, Lp).float().cpu().numpy()
         # row-parallel GEMMs in 4 row blocks, each all-reduce on a side stream
-        blk4 = PX.TPBlock.from_full(full, heads, d, rank, world, chunks=4)
+        blk4 = PX.TPBlock.from_full(full, heads, d, rank, world, chunks=4, comm="nccl")
         res["block4"] = blk4(xb, B, S, Lp).float().cpu().numpy()
+        # row-parallel sums over peer memory, three calls
+        blkp = PX.TPBlock.from_full(full, heads, d, rank, world, comm="peer")
+        res["block_peer"] = [blkp(xb, B, S, Lp).float().cpu().numpy() for _ in range(3)]
+        # direct reduction, ragged ownership, bias
+        from qik import _lib as L
+        from qik import fp8 as F
+        from qik.tp_comm import PeerRowReduce
+        M, N, K = 1000, 512, 256
+        a = GI.randn_bf16(230 + rank, (M, K)).to(dev)
+        w = GI.randn_bf16(232 + rank, (N, K), 0.05).to(dev)
+        bias = GI.randn_bf16(234, (N,), 0.1).to(dev)
+        aq, sa = F.quantize_tensorwise(a)
+        wq, sw = F.quantize_weight_tensorwise(w)
+        red = PeerRowReduce(M, N, device=dev)
+        got = [red(aq, sa, wq, sw, bias).clone() for _ in range(3)]
+        part = F.fp8_gemm(aq, sa, wq, sw, out_dtype=torch.float32)
+        dist.all_reduce(part)
+        want = (part + bias.float()).to(torch.bfloat16)
+        res["direct_equal"] = [bool(torch.equal(g, want)) for g in got]
+        res["status"] = L.device_status(dev)
         torch.cuda.synchronize()
+        dist.barrier()
+        red.close()
+        for lin in (blkp.out, blkp.down):
+            for r in lin._peer.values():
+                r.close()
         with open(os.path.join(outdir, f"r{rank}.pkl"), "wb") as f:
             pickle.dump(res, f)
     finally:
@@ -105,3 +137,6 @@ def test_sharded_quantization_and_tp_block_on_two_gpus():
         # the blocked form: same partial products, summed block by block (its GEMM
         # blocks may use another tile configuration, so the gate is the tolerance)
         assert O.relf(torch.from_numpy(r["block4"]), ref) <= 5e-3
+        assert r["status"] == 0
+        assert all(np.array_equal(yp, r["block"]) for yp in r["block_peer"])
+        assert r["direct_equal"] == [True, True, True]
