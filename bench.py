@@ -408,8 +408,9 @@ def dit_block_case(device: torch.device, g: torch.Generator) -> dict:
     """DiT block @1024 px, CFG batch 2: M = 2 x 4352, the whole block --
     timestep modulation linear (M = 2), LayerNorm + modulate (its amax feeds the QKV
     quantizer), fused QKV, per-head RMSNorm + RoPE of q and k, block-causal attention
-    (256 text causal + 4096 image), out-proj, gated residual, LayerNorm + modulate,
-    FFN (GELU-tanh) and the second gated residual; random-init
+    (256 text causal + 4096 image), out-proj, gated residual, LayerNorm + modulate (its
+    amax feeds the FFN's quantizer), FFN (GELU-tanh) and the second
+    gated residual; random-init
     FP8 weights, synthetic activations."""
     from qik import fp8 as F
     from qik.triton_attention import block_causal_flash_attention as attn
@@ -445,8 +446,8 @@ def dit_block_case(device: torch.device, g: torch.Generator) -> dict:
         k = fused_rms_norm_rope(k, wn, freqs, 1e-6)
         o = attn(q, k, v, Lt, None)
         h = fused_gate_residual(x, lin["out"](o.flatten(2, 3)), mod, K, None)
-        hm2 = fused_layer_norm_modulate(h, mod, 2 * K, mod.stride(0), None, 1e-6)
-        f2 = F.fp8_ffn_gelu(hm2.reshape(M, K), lin["up"], lin["down"]).view(B2, S2, K)
+        hm2 = fused_layer_norm_modulate(h, mod, 2 * K, mod.stride(0), None, 1e-6, amax_out=amax[1:2])
+        f2 = F.fp8_ffn_gelu(hm2.reshape(M, K), lin["up"], lin["down"], x_amax=amax[1:2]).view(B2, S2, K)
         return fused_gate_residual(h, f2, mod, 3 * K, None)
 
     lin_fl = 2.0 * M * K * (9216 + 3072 + 12288) + 2.0 * M * 12288 * K + 2.0 * B2 * K * 18432

@@ -154,6 +154,16 @@ int qik_fp8_ffn(const void* x, int64_t M, int64_t K, int64_t hidden, const uint8
                 const void* b_up, const uint8_t* w_down, const float* s_down, const void* b_down, void* y, void* ws,
                 size_t ws_bytes, int* status, void* stream);
 
+/*
+ * qik_fp8_ffn with max|x| supplied: x_amax_bits holds the fp32 bits of max|x| (as the
+ * amax outputs of qik_layer_norm_modulate / qik_swiglu accumulate it), so the chain
+ * starts at the pack of x.  Same result as qik_fp8_ffn on the same x.
+ */
+int qik_fp8_ffn_from_amax(const void* x, const uint32_t* x_amax_bits, int64_t M, int64_t K, int64_t hidden,
+                          const uint8_t* w_up, const float* s_up, const void* b_up, const uint8_t* w_down,
+                          const float* s_down, const void* b_down, void* y, void* ws, size_t ws_bytes, int* status,
+                          void* stream);
+
 /* Attention flags. */
 #define QIK_ATTN_HAS_CACHE 1     /* keys/values = virtual concat [cache ; fresh] */
 #define QIK_ATTN_HAS_KEY_VALID 2 /* per-(batch, key) validity bytes */

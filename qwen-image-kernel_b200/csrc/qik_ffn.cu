@@ -6,6 +6,7 @@
 // projection, processors.py:180-187), the hidden activation re-quantized
 // dynamically.  Five kernels in one stream:
 //   amax(x) -> pack(x) -> GEMM1 (+GELU, amax(h)) -> pack(h) -> GEMM2
+// (qik_fp8_ffn_from_amax starts at pack(x) with max|x| from x's producer).
 // Every kernel after the first is launched as a programmatic dependent of its
 // predecessor, so its launch and set-up (TMEM allocation, barrier init, descriptor
 // prefetch) overlap the predecessor's tail; each waits for the predecessor's
@@ -34,9 +35,12 @@ extern "C" size_t qik_fp8_ffn_workspace_bytes(int64_t M, int64_t K, int64_t hidd
          align_up(static_cast<size_t>(M) * hidden);
 }
 
-extern "C" int qik_fp8_ffn(const void* x, int64_t M, int64_t K, int64_t hidden, const uint8_t* w_up,
-                           const float* s_up, const void* b_up, const uint8_t* w_down, const float* s_down,
-                           const void* b_down, void* y, void* ws, size_t ws_bytes, int* status, void* stream) {
+// x_amax: NULL (the chain computes max|x| itself) or the fp32 bits of max|x| already
+// accumulated by x's producer (a layer norm's or SwiGLU's amax output).
+static int fp8_ffn_chain(const void* x, const uint32_t* x_amax, int64_t M, int64_t K, int64_t hidden,
+                         const uint8_t* w_up, const float* s_up, const void* b_up, const uint8_t* w_down,
+                         const float* s_down, const void* b_down, void* y, void* ws, size_t ws_bytes, int* status,
+                         void* stream) {
   QIK_REQUIRE(M >= 0 && K > 0 && hidden > 0, "qik_fp8_ffn: bad sizes");
   if (M == 0) return QIK_OK;
   QIK_REQUIRE(x && w_up && s_up && w_down && s_down && y && ws, "qik_fp8_ffn: NULL pointer");
@@ -51,8 +55,13 @@ extern "C" int qik_fp8_ffn(const void* x, int64_t M, int64_t K, int64_t hidden, 
   uint8_t* hq = static_cast<uint8_t*>(h) + align_up(static_cast<size_t>(M) * hidden * 2);
 
   QIK_TRY_CUDA(cudaMemsetAsync(hdr, 0, 2 * sizeof(uint32_t), st));
-  int rc = launch_amax(x, QIK_DTYPE_BF16, M * K, &hdr->amax_x, st, false);
-  if (!rc) rc = launch_pack_act(x, M * K, &hdr->amax_x, xq, &hdr->sx, st, true);
+  int rc = QIK_OK;
+  if (x_amax) {
+    rc = launch_pack_act(x, M * K, x_amax, xq, &hdr->sx, st, false);
+  } else {
+    rc = launch_amax(x, QIK_DTYPE_BF16, M * K, &hdr->amax_x, st, false);
+    if (!rc) rc = launch_pack_act(x, M * K, &hdr->amax_x, xq, &hdr->sx, st, true);
+  }
   if (!rc)
     rc = launch_fp8_gemm(xq, w_up, M, hidden, K, K, K, &hdr->sx, s_up, b_up, h, hidden, QIK_DTYPE_BF16,
                          QIK_EPI_GELU_TANH, &hdr->amax_h, status, st, true);
@@ -61,4 +70,20 @@ extern "C" int qik_fp8_ffn(const void* x, int64_t M, int64_t K, int64_t hidden, 
     rc = launch_fp8_gemm(hq, w_down, M, K, hidden, hidden, hidden, &hdr->sh, s_down, b_down, y, K, QIK_DTYPE_BF16,
                          QIK_EPI_SCALE, nullptr, status, st, true);
   return rc;
+}
+
+extern "C" int qik_fp8_ffn(const void* x, int64_t M, int64_t K, int64_t hidden, const uint8_t* w_up,
+                           const float* s_up, const void* b_up, const uint8_t* w_down, const float* s_down,
+                           const void* b_down, void* y, void* ws, size_t ws_bytes, int* status, void* stream) {
+  return fp8_ffn_chain(x, nullptr, M, K, hidden, w_up, s_up, b_up, w_down, s_down, b_down, y, ws, ws_bytes, status,
+                       stream);
+}
+
+extern "C" int qik_fp8_ffn_from_amax(const void* x, const uint32_t* x_amax_bits, int64_t M, int64_t K, int64_t hidden,
+                                     const uint8_t* w_up, const float* s_up, const void* b_up, const uint8_t* w_down,
+                                     const float* s_down, const void* b_down, void* y, void* ws, size_t ws_bytes,
+                                     int* status, void* stream) {
+  QIK_REQUIRE(x_amax_bits, "qik_fp8_ffn_from_amax: NULL amax");
+  return fp8_ffn_chain(x, x_amax_bits, M, K, hidden, w_up, s_up, b_up, w_down, s_down, b_down, y, ws, ws_bytes, status,
+                       stream);
 }

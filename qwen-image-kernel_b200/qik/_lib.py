@@ -58,6 +58,8 @@ SIGNATURES = {
     "qik_fp8_ffn_workspace_bytes": (ctypes.c_size_t, [_i64, _i64, _i64]),
     "qik_fp8_ffn": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp,
                            _vp]),
+    "qik_fp8_ffn_from_amax": (_i32, [_vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                     ctypes.c_size_t, _vp, _vp]),
     "qik_block_causal_attention": (_i32, [ctypes.POINTER(AttnArgs), _vp, _vp]),
     "qik_kv_store": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _i64,
                             _i32, _vp, _vp, _vp]),

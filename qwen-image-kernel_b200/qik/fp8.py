@@ -243,7 +243,7 @@ def fp8_state_dict(model: nn.Module) -> dict[str, torch.Tensor]:
 
 
 def fp8_ffn_gelu(x: torch.Tensor, up: FP8Linear, down: FP8Linear, workspace: torch.Tensor | None = None,
-                 out: torch.Tensor | None = None) -> torch.Tensor:
+                 out: torch.Tensor | None = None, x_amax: torch.Tensor | None = None) -> torch.Tensor:
     """DiT FFN pair: down(gelu_tanh(up(x))) with both linears FP8 per-tensor and the
     hidden activation re-quantized dynamically between them (qik_fp8_ffn: one chain
     of five kernels with programmatic dependent launches).
@@ -252,7 +252,9 @@ def fp8_ffn_gelu(x: torch.Tensor, up: FP8Linear, down: FP8Linear, workspace: tor
     accumulates max|h| on the fly, so the hidden tensor is quantized with one pack
     pass.  ``workspace`` (uint8, >= qik_fp8_ffn_workspace_bytes) may be passed to
     avoid an allocation per call, ``out`` (contiguous bf16, x's shape) to write the
-    result into a buffer the caller owns."""
+    result into a buffer the caller owns, ``x_amax`` (int32 [1] on x's device: the
+    fp32 bits of max|x|, as fused_layer_norm_modulate's ``amax_out`` accumulates them)
+    to skip the chain's own max pass."""
     _require_cuda(x, "x")
     if x.dtype != torch.bfloat16:
         raise TypeError("qik.fp8_ffn_gelu: bf16 activations only")
@@ -277,8 +279,17 @@ def fp8_ffn_gelu(x: torch.Tensor, up: FP8Linear, down: FP8Linear, workspace: tor
     b_down = None if down.bias is None else down.bias.to(torch.bfloat16).contiguous()
     status = L.status_word(x.device)
     with torch.cuda.device(x.device):
-        L.check(lib.qik_fp8_ffn(x2.data_ptr(), M, K, hidden, up.weight.data_ptr(), up.weight_scale.data_ptr(),
-                                L.ptr(b_up), down.weight.data_ptr(), down.weight_scale.data_ptr(), L.ptr(b_down),
-                                y.data_ptr(), workspace.data_ptr(), workspace.numel(), status.data_ptr(),
-                                L.stream_ptr()), "qik_fp8_ffn")
+        if x_amax is None:
+            L.check(lib.qik_fp8_ffn(x2.data_ptr(), M, K, hidden, up.weight.data_ptr(), up.weight_scale.data_ptr(),
+                                    L.ptr(b_up), down.weight.data_ptr(), down.weight_scale.data_ptr(), L.ptr(b_down),
+                                    y.data_ptr(), workspace.data_ptr(), workspace.numel(), status.data_ptr(),
+                                    L.stream_ptr()), "qik_fp8_ffn")
+        else:
+            if x_amax.dtype != torch.int32 or x_amax.device != x.device or x_amax.numel() < 1:
+                raise ValueError("qik.fp8_ffn_gelu: x_amax must be an int32 tensor on x's device")
+            L.check(lib.qik_fp8_ffn_from_amax(x2.data_ptr(), x_amax.data_ptr(), M, K, hidden, up.weight.data_ptr(),
+                                              up.weight_scale.data_ptr(), L.ptr(b_up), down.weight.data_ptr(),
+                                              down.weight_scale.data_ptr(), L.ptr(b_down), y.data_ptr(),
+                                              workspace.data_ptr(), workspace.numel(), status.data_ptr(),
+                                              L.stream_ptr()), "qik_fp8_ffn_from_amax")
     return y.reshape(*x.shape[:-1], K)

@@ -185,6 +185,35 @@ def test_ffn_pair_parity(fp8):
     ref = O.fp8_linear(hq, sh, down.weight.cpu(), float(down.weight_scale.item()))
     assert (y.cpu().float() - ref).abs().max().item() <= 5 * MAX_ABS
     assert O.relf(y.cpu(), ref) <= RELF
+    # max|x| supplied by x's producer (qik_fp8_ffn_from_amax): the chain starts at the
+    # pack of x and gives the same bytes
+    xd = x.cuda()
+    amax = torch.tensor([int(np.array([xd.float().abs().max().item()], np.float32).view(np.int32)[0])],
+                        dtype=torch.int32, device="cuda")
+    y2 = fp8.fp8_ffn_gelu(xd, up, down, x_amax=amax)
+    torch.cuda.synchronize()
+    assert torch.equal(y2, y)
+
+
+def test_ffn_pair_from_layer_norm_amax(fp8):
+    """The DiT block's second half: LayerNorm + modulate accumulating max|out|, fed to
+    the FFN chain as its input amax -- identical to the chain computing it itself."""
+    from qik.triton_fused import fused_layer_norm_modulate
+    M, K, Hd = 384, 3072, 12288
+    h = GI.randn_bf16(95, (1, M, K)).cuda()
+    mod = GI.randn_bf16(96, (1, 4 * K), 0.2).cuda()
+    up = fp8.FP8Linear(K, Hd).cuda()
+    down = fp8.FP8Linear(Hd, K).cuda()
+    for lin, seed in ((up, 97), (down, 98)):
+        wq, sw = fp8.quantize_weight_tensorwise(GI.randn_bf16(seed, (lin.out_features, lin.in_features), 0.02).cuda())
+        lin.weight.copy_(wq)
+        lin.weight_scale.copy_(sw)
+    amax = torch.zeros(1, dtype=torch.int32, device="cuda")
+    hm = fused_layer_norm_modulate(h, mod, 2 * K, 4 * K, None, 1e-6, amax_out=amax)
+    y_fused = fp8.fp8_ffn_gelu(hm.reshape(M, K), up, down, x_amax=amax)
+    y_plain = fp8.fp8_ffn_gelu(hm.reshape(M, K), up, down)
+    torch.cuda.synchronize()
+    assert torch.equal(y_fused, y_plain)
 
 
 def test_gemm_rejects_bad_shapes(fp8):
