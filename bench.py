@@ -340,14 +340,13 @@ def _time_ms(fn, iters: int, flush: torch.Tensor, stream) -> float:
     return sum(a.elapsed_time(b) for a, b in evs) / iters
 
 
-def fused_ops(device: torch.device, flush: torch.Tensor, iters: int, x: torch.Tensor, mod: torch.Tensor) -> dict:
-    """HBM roofline of the four fused elementwise kernels at the t2i block shapes
-    (B = 2, S = 4352, width 3072, 24 heads of 128, MLP 12288).  Algorithmic bytes:
-    every input element read once and every output element written once (bf16), the
-    modulation rows and RoPE tables (L2-resident, shared by all rows) excluded."""
+def fused_ops_cases(device: torch.device, x: torch.Tensor, mod: torch.Tensor) -> dict:
+    """The four fused elementwise ops at the t2i block shapes (B = 2, S = 4352, width
+    3072, 24 heads of 128, MLP 12288): {name: (callable, algorithmic bytes)}.
+    Algorithmic bytes: every input element read once and every output element written
+    once (bf16), the modulation rows and RoPE tables (L2-resident, shared by all rows)
+    excluded."""
     from qik.triton_fused import fused_gate_residual, fused_layer_norm_modulate, fused_rms_norm_rope, fused_swiglu
-    stream = torch.cuda.current_stream(device)
-    hbm = peaks()["hbm_gbs"]
     B, S, K = x.shape
     H, D = 24, 128
     g = torch.Generator(device=device).manual_seed(11)
@@ -360,14 +359,21 @@ def fused_ops(device: torch.device, flush: torch.Tensor, iters: int, x: torch.Te
     gate, up = gu.chunk(2, dim=-1)
     amax = torch.zeros(1, dtype=torch.int32, device=device)
     n_x = x.numel()
-    cases = {
+    return {
         "layer_norm_modulate": (lambda: fused_layer_norm_modulate(x, mod, 0, mod.stride(0), None, 1e-6, amax), 4 * n_x),
         "rms_norm_rope_q": (lambda: fused_rms_norm_rope(q, wn, freqs, 1e-6), 4 * q.numel()),
         "gate_residual": (lambda: fused_gate_residual(x, f, mod, K, None), 6 * n_x),
         "swiglu_12288": (lambda: fused_swiglu(gate, up, amax), 6 * gate.numel()),
     }
+
+
+def fused_ops(device: torch.device, flush: torch.Tensor, iters: int, x: torch.Tensor, mod: torch.Tensor) -> dict:
+    """HBM roofline of the four fused elementwise kernels at the t2i block shapes
+    (fused_ops_cases), L2 flushed between launches."""
+    stream = torch.cuda.current_stream(device)
+    hbm = peaks()["hbm_gbs"]
     res = {}
-    for name, (fn, nbytes) in cases.items():
+    for name, (fn, nbytes) in fused_ops_cases(device, x, mod).items():
         for _ in range(3):
             fn()
         ms = _time_ms(fn, iters, flush, stream)
@@ -456,15 +462,27 @@ def dit_block_case(device: torch.device, g: torch.Generator) -> dict:
             "mod": lambda: lin["mod"](temb)}
 
 
-PROFILE_CASES = ("attention_cfg4_prefill", "attention_cfg4_decode_fp8_slab", "dit_block_1024px_cfg2")
+PROFILE_CASES = ("attention_cfg4_prefill", "attention_cfg4_decode_fp8_slab", "dit_block_1024px_cfg2", "fused_ops_t2i")
 
 
 def profile_case(device: torch.device, name: str) -> None:
-    """Runs one workload three times (the launches an ncu capture selects from)."""
+    """Runs one workload three times (the launches an ncu capture selects from); for
+    fused_ops_t2i each of the four ops three times, a 256 MiB write before every launch
+    (cold L2)."""
     g = torch.Generator(device=device).manual_seed(7)
-    fn = dit_block_case(device, g)["block"] if name == "dit_block_1024px_cfg2" else attention_cfg4_cases(device, g)[name][0]
-    for _ in range(3):
-        fn()
+    if name == "fused_ops_t2i":
+        x = torch.randn(2, 4352, 3072, device=device, generator=g).to(torch.bfloat16)
+        mod = (torch.randn(2, 6 * 3072, device=device, generator=g) * 0.05).to(torch.bfloat16)
+        flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)
+        for i, (fn, _) in enumerate(fused_ops_cases(device, x, mod).values()):
+            for r in range(3):
+                flush.fill_(float(3 * i + r))
+                fn()
+    else:
+        fn = (dit_block_case(device, g)["block"] if name == "dit_block_1024px_cfg2"
+              else attention_cfg4_cases(device, g)[name][0])
+        for _ in range(3):
+            fn()
     torch.cuda.synchronize(device)
     from qik import _lib as L
     print(json.dumps({"profile_case": name, "runs": 3, "device_status": L.device_status(device)}), flush=True)
