@@ -570,7 +570,8 @@ def tp_stack(device: torch.device, rank: int, world: int, flush: torch.Tensor, i
         for blk in blocks:
             for lin in (blk.out, blk.down):
                 for red in lin._peer.values():
-                    red.close()
+                    if red:
+                        red.close()
         return float(t.item())
 
     ms_peer = timed(1, "peer")

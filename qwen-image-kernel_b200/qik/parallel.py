@@ -24,6 +24,8 @@ default and the only product path) or a test double with the same methods.
 """
 from __future__ import annotations
 
+import warnings
+
 import torch
 import torch.distributed as dist
 import torch.nn as nn
@@ -227,10 +229,17 @@ class RowParallelFP8Linear(nn.Module):
         if world > 1 and xq.is_cuda and self.comm == "peer" and self.chunks == 1:
             red = self._peer.get(M)
             if red is None:
-                from .tp_comm import PeerRowReduce
-                red = PeerRowReduce(M, self.weight.shape[0], self.group, xq.device)
+                from .tp_comm import PeerMappingUnavailable, PeerRowReduce
+                try:
+                    red = PeerRowReduce(M, self.weight.shape[0], self.group, xq.device)
+                except PeerMappingUnavailable as e:
+                    # collective decision: every rank falls back to the all-reduce
+                    warnings.warn(f"RowParallelFP8Linear: peer-memory reduction unavailable ({e}); "
+                                  "using the NCCL all-reduce")
+                    red = False
                 self._peer[M] = red
-            return red(xq, sx, self.weight, self.weight_scale, self.bias)
+            if red is not False:
+                return red(xq, sx, self.weight, self.weight_scale, self.bias)
         if world > 1 and xq.is_cuda and self.chunks > 1 and M >= 2 * self.chunks:
             part = self._gemm_allreduce_overlapped(xq, sx)
         else:

@@ -39,6 +39,12 @@ _ALIGN = 256      # byte alignment of the workspace regions
 _MASK32 = 0xFFFFFFFF
 
 
+class PeerMappingUnavailable(RuntimeError):
+    """Raised on every rank when some rank could not map its peers' workspaces (no
+    CUDA IPC / peer access between the GPUs); the decision is collective, so all ranks
+    take the same fallback."""
+
+
 def rows_per_owner(M: int, world: int) -> int:
     """Rows each rank owns: ceil(M / world) rounded up to a multiple of 256."""
     per = -(-M // world)
@@ -103,15 +109,26 @@ class PeerRowReduce:
         dist.all_gather_object(every, mine, group=group)
         self._opened: list[int] = []
         self.base: list[int] = []
+        err = ""
         with torch.cuda.device(self.device):
             for p, (h, o) in enumerate(every):
                 if p == self.rank:
                     self.base.append(self.buf.data_ptr())
                     continue
                 b = ctypes.c_void_p()
-                L.check(self.lib.qik_ipc_open(ctypes.create_string_buffer(h, hb), ctypes.byref(b)), "qik_ipc_open")
+                rc = self.lib.qik_ipc_open(ctypes.create_string_buffer(h, hb), ctypes.byref(b))
+                if rc != L.QIK_OK:
+                    msg = self.lib.qik_last_error()
+                    err = f"rank {self.rank} cannot map rank {p}: {msg.decode() if msg else rc}"
+                    break
                 self._opened.append(b.value)
                 self.base.append(b.value + o)
+        # every rank learns whether all mappings exist before any kernel writes to a peer
+        ok = torch.tensor([0 if err else 1], dtype=torch.int32, device=self.device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if int(ok.item()) == 0:
+            self.close()
+            raise PeerMappingUnavailable(err or "a peer rank could not map the workspaces")
         dist.barrier(group=group)
         self.calls = 0
         self.signals = self.lib.qik_fp8_gemm_scatter_signals(M, N, self.lay["R"], self.rank)

@@ -100,6 +100,7 @@ def _worker(rank, world, port, outdir):
         red.close()
         for lin in (blkp.out, blkp.down):
             for r in lin._peer.values():
+                assert r, "peer-memory reduction fell back to NCCL"
                 r.close()
         with open(os.path.join(outdir, f"r{rank}.pkl"), "wb") as f:
             pickle.dump(res, f)
