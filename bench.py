@@ -519,9 +519,10 @@ def tp_stack(device: torch.device, rank: int, world: int, flush: torch.Tensor, i
     """BASELINE configs[4]'s layer-stack case: 4 DiT blocks at 1024 px, CFG batch 2
     (M = 8704), tensor parallel over `world` GPUs -- QKV by heads and FFN-up column-
     parallel, attention on local heads, out-proj and FFN-down row-parallel with a
-    4-byte amax all-reduce(MAX) and the partial products summed over NVLink peer
-    memory by the GEMM's own epilogue (the fp32 NCCL all-reduce(SUM) form is timed
-    beside it).  Strong scaling: the total work is fixed.  Time = max over ranks."""
+    4-byte amax all-reduce(MAX) and the partial products summed as the library's
+    comm="auto" does: over NVLink peer memory by the GEMM's own epilogue on 2 ranks, by
+    an fp32 NCCL all-reduce(SUM) on more (both forms timed beside it).  Strong scaling:
+    the total work is fixed.  Time = max over ranks."""
     from qik import fp8 as F
     from qik import parallel as PX
     H, D, K, HID, B, S = 24, 128, 3072, 12288, 2, 4352
@@ -577,22 +578,26 @@ def tp_stack(device: torch.device, rank: int, world: int, flush: torch.Tensor, i
     ms_peer = timed(1, "peer")
     ms_nccl = timed(1, "nccl") if world > 1 else ms_peer
     ms_overlap = timed(4, "nccl") if world > 1 else ms_peer
-    ms = ms_peer
+    ms = ms_peer if world <= 2 else ms_nccl  # comm="auto", the library default
     M = B * S
     lin = 2.0 * M * K * (3 * H * D + K + HID) + 2.0 * M * HID * K
     att = 4.0 * D * H * B * float((Lt.long() + 1).sum())
     total = 4 * (lin + att)
     return {"ms": round(ms, 4), "tflops_total": round(total / ms / 1e9, 1),
             "tflops_per_gpu": round(total / ms / 1e9 / world, 1), "n_gpus": world, "scaling": "strong",
-            "form": "row-parallel GEMM epilogue stores fp32 tiles into the owner rank's memory over NVLink "
-                    "(CUDA IPC), owner sums its rows and stores bf16 rows into every rank "
-                    "(qik_fp8_gemm_scatter + qik_tp_reduce_gather + qik_tp_wait)" if world > 1 else "one GPU",
+            "form": ("one GPU" if world == 1 else
+                     "comm='auto' = peer: row-parallel GEMM epilogue stores fp32 tiles into the owner rank's "
+                     "memory over NVLink (CUDA IPC), owner sums its rows and stores bf16 rows into every rank "
+                     "(qik_fp8_gemm_scatter + qik_tp_reduce_gather + qik_tp_wait)" if world == 2 else
+                     "comm='auto' = nccl: fp32 all-reduce(SUM) of the partial products (faster than the "
+                     "peer-memory form from 4 ranks)"),
+            "ms_peer_reduction": round(ms_peer, 4),
             "ms_nccl_allreduce": round(ms_nccl, 4),
             "ms_nccl_overlapped_4_blocks": round(ms_overlap, 4),
             "overlapped_form": "row-parallel GEMMs in 4 row blocks, each block's all-reduce on a side stream "
                                "under the next block's GEMM (slower here: NCCL's kernels take SMs from the "
                                "persistent GEMM)" if world > 1 else "n/a",
-            "collectives_per_stack": "8 x peer-memory row reductions of fp32 [8704, 3072] partial products "
+            "collectives_per_stack": "8 x row reductions of fp32 [8704, 3072] partial products "
                                      "+ 8 x all-reduce(MAX) 4 bytes (NCCL)" if world > 1 else "none"}
 
 

@@ -193,19 +193,23 @@ class RowParallelFP8Linear(nn.Module):
     default is one block: measured on 2 B200 the overlapped form was slower (the
     NCCL kernels occupy SMs the persistent GEMM grid counts on).
 
-    With ``comm="peer"`` (the default; GPUs, more than one rank) the sum runs over NVLink peer
+    With ``comm="peer"`` (GPUs, more than one rank) the sum runs over NVLink peer
     memory instead (``qik.tp_comm.PeerRowReduce``): the GEMM's epilogue stores each
     finished fp32 tile into the receive slot of the rank owning those rows while the
     GEMM goes on, the owner sums its rows in rank order, adds the bias and stores bf16
     rows into every rank's output.  Its workspace is set up collectively at the first
     call with a given row count; the output stays valid until this module's
-    second-next call."""
+    second-next call.  ``comm="auto"`` (the default) takes the peer-memory sum for two
+    ranks and the NCCL all-reduce for more: measured on B200 for the 4-block TP stack,
+    4.29 ms (peer) against 4.99 ms (NCCL) on 2 GPUs, but 5.19 ms against 4.53 ms on 4,
+    where each rank ships three quarters of its fp32 partial product and NCCL reduces in
+    the NVSwitch."""
 
     def __init__(self, weight: torch.Tensor, weight_scale: torch.Tensor, bias: torch.Tensor | None, group=None,
-                 ops=None, chunks: int = 1, comm: str = "peer"):
+                 ops=None, chunks: int = 1, comm: str = "auto"):
         super().__init__()
-        if comm not in ("nccl", "peer"):
-            raise ValueError(f"RowParallelFP8Linear: comm must be 'nccl' or 'peer', not {comm!r}")
+        if comm not in ("auto", "nccl", "peer"):
+            raise ValueError(f"RowParallelFP8Linear: comm must be 'auto', 'nccl' or 'peer', not {comm!r}")
         self.comm = comm
         self._peer: dict = {}
         self.chunks = chunks
@@ -220,13 +224,14 @@ class RowParallelFP8Linear(nn.Module):
 
     @classmethod
     def from_full(cls, weight, weight_scale, bias, rank, world, group=None, ops=None, chunks: int = 1,
-                  comm: str = "peer"):
+                  comm: str = "auto"):
         return cls(shard_cols(weight, rank, world), weight_scale.clone(), bias, group, ops, chunks, comm)
 
     def forward_quantized(self, xq: torch.Tensor, sx: torch.Tensor) -> torch.Tensor:
         world = _world(self.group)[1]
         M = xq.shape[0]
-        if world > 1 and xq.is_cuda and self.comm == "peer" and self.chunks == 1:
+        peer = self.comm == "peer" or (self.comm == "auto" and world == 2)
+        if world > 1 and xq.is_cuda and peer and self.chunks == 1:
             red = self._peer.get(M)
             if red is None:
                 from .tp_comm import PeerMappingUnavailable, PeerRowReduce
@@ -302,12 +307,13 @@ class TPBlock(nn.Module):
 
     @classmethod
     def from_full(cls, full: dict, heads: int, head_dim: int, rank: int, world: int, group=None, ops=None,
-                  chunks: int = 1, comm: str = "peer"):
+                  chunks: int = 1, comm: str = "auto"):
         """full: name -> (weight e4m3 [N, K], weight_scale [1], bias or None) for
         'qkv', 'out', 'up', 'down' (unsharded, quantized once).  ``chunks``: row blocks of
         the row-parallel GEMMs whose all-reduce overlaps the next block's GEMM;
-        ``comm``: "peer" (the default: reduction over NVLink peer memory fused with the
-        GEMM, RowParallelFP8Linear) or "nccl" (all-reduce)."""
+        ``comm``: "peer" (reduction over NVLink peer memory fused with the GEMM,
+        RowParallelFP8Linear), "nccl" (all-reduce) or "auto" (the default: "peer" for two
+        ranks, "nccl" for more)."""
         qkv = ColumnParallelFP8Linear.from_full(*full["qkv"], rank, world, qkv_heads=(heads, head_dim), ops=ops)
         out = RowParallelFP8Linear.from_full(*full["out"], rank, world, group, ops, chunks, comm)
         up = ColumnParallelFP8Linear.from_full(*full["up"], rank, world, ops=ops)
