@@ -149,7 +149,7 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
     ws = torch.empty(lib.qik_fp8_ffn_workspace_bytes(M_ROWS, K_IN, HIDDEN), dtype=torch.uint8, device=device)
 
     def step(xin: torch.Tensor):
-        # the public FP8 FFN path: one chain of five kernels (qik_fp8_ffn)
+        # the public FP8 FFN path: one chain of four kernels (qik_fp8_ffn)
         return F.fp8_ffn_gelu(xin, up, down, workspace=ws)
 
     def step_split(xin: torch.Tensor, ev):
@@ -166,7 +166,7 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
         ev[3].record(stream)
         return y
 
-    launches_per_step = 5  # amax, pack, gemm (GELU+amax), pack, gemm
+    launches_per_step = 4  # single-pass quantizer, gemm (GELU+amax), pack, gemm
     clk = ClockSampler(device.index if device.index is not None else 0).__enter__()
     for _ in range(args.warmup):
         step(x)
@@ -298,8 +298,9 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
                      "flops_per_launch": FLOPS_PER_LINEAR},
         "gpu_launches": launches_per_step * args.steps * 3,
         "gpu_launches_note": "qik kernels inside the timed regions (device-resident steps + pipelined and serial e2e steps: "
-                             "amax, pack, GEMM+GELU+amax, pack, GEMM per step, chained with programmatic "
-                             "dependent launch); the L2-flush fills are torch's; GEMM launch times for the "
+                             "single-pass quantizer of x, GEMM+GELU+amax, pack, GEMM per step, the last three "
+                             "chained with programmatic dependent launch; a 80-byte memset clears the chain's "
+                             "counters); the L2-flush fills are torch's; GEMM launch times for the "
                              "roofline come from a second pass that runs the step launch by launch with events (median per GEMM)",
         "device_status": int(status),
         "clocks": clocks,

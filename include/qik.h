@@ -143,8 +143,9 @@ size_t qik_fp8_ffn_workspace_bytes(int64_t M, int64_t K, int64_t hidden);
  * DiT FFN pair y = down(gelu_tanh(up(x))), both linears FP8 per-tensor with the
  * hidden activation re-quantized dynamically: two FP8Linear.forward calls
  * (qwen_image_kernel/fp8.py:78-90) with GELU-tanh between them, run as one chain
- * of five kernels (amax, pack, GEMM+GELU+amax, pack, GEMM) with programmatic
- * dependent launches.
+ * of four kernels (single-pass quantizer of x, GEMM+GELU+amax, pack, GEMM; amax and
+ * pack of x instead of the single pass when x is not 16-byte aligned) with
+ * programmatic dependent launches.
  *   x: [M, K] bf16 row-major; w_up: [hidden, K] e4m3, s_up: 1 fp32, b_up: hidden bf16
  *   or NULL; w_down: [K, hidden] e4m3, s_down, b_down likewise; y: [M, K] bf16.
  *   ws: qik_fp8_ffn_workspace_bytes(M, K, hidden) bytes, 256-byte aligned (holds the

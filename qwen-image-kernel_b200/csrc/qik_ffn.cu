@@ -4,10 +4,12 @@
 // FP8Linear.forward (qwen_image_kernel/fp8.py:78-90) with GELU-tanh between them
 // (the reference block uses SwiGLU through a fused up
 // projection, processors.py:180-187), the hidden activation re-quantized
-// dynamically.  Five kernels in one stream:
-//   amax(x) -> pack(x) -> GEMM1 (+GELU, amax(h)) -> pack(h) -> GEMM2
-// (qik_fp8_ffn_from_amax starts at pack(x) with max|x| from x's producer).
-// Every kernel after the first is launched as a programmatic dependent of its
+// dynamically.  Four kernels in one stream (five without the single pass):
+//   quantize(x) -> GEMM1 (+GELU, amax(h)) -> pack(h) -> GEMM2
+// where quantize(x) is the single-pass cooperative quantizer (x 16-byte aligned) or
+// amax(x) -> pack(x) (qik_fp8_ffn_from_amax: pack(x) alone, with max|x| from x's
+// producer).
+// Every kernel after the quantizer is launched as a programmatic dependent of its
 // predecessor, so its launch and set-up (TMEM allocation, barrier init, descriptor
 // prefetch) overlap the predecessor's tail; each waits for the predecessor's
 // results before reading them.  The intermediates live in the caller's workspace.
@@ -23,6 +25,8 @@ struct FfnHeader {
   float sh;
 };
 constexpr size_t kAlign = 256;
+constexpr size_t kQuantWsOffset = 64;  // inside the 256-byte header
+constexpr size_t kQuantWsBytes = 16;
 size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 }  // namespace
 }  // namespace qik
@@ -54,10 +58,15 @@ static int fp8_ffn_chain(const void* x, const uint32_t* x_amax, int64_t M, int64
   void* h = xq + align_up(static_cast<size_t>(M) * K);
   uint8_t* hq = static_cast<uint8_t*>(h) + align_up(static_cast<size_t>(M) * hidden * 2);
 
-  QIK_TRY_CUDA(cudaMemsetAsync(hdr, 0, 2 * sizeof(uint32_t), st));
+  // header words and the single-pass quantizer's counter block, cleared by one memset
+  QuantWs* qws = reinterpret_cast<QuantWs*>(base + kQuantWsOffset);
+  QIK_TRY_CUDA(cudaMemsetAsync(base, 0, kQuantWsOffset + kQuantWsBytes, st));
   int rc = QIK_OK;
   if (x_amax) {
     rc = launch_pack_act(x, M * K, x_amax, xq, &hdr->sx, st, false);
+  } else if (aligned16(x)) {
+    // one kernel: x read from HBM once (it fits the SMs' shared memory up to ~28 MB)
+    rc = launch_quant_single_pass(x, M * K, xq, &hdr->sx, qws, st, true);
   } else {
     rc = launch_amax(x, QIK_DTYPE_BF16, M * K, &hdr->amax_x, st, false);
     if (!rc) rc = launch_pack_act(x, M * K, &hdr->amax_x, xq, &hdr->sx, st, true);

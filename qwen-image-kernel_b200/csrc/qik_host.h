@@ -73,6 +73,12 @@ cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
 int launch_amax(const void* x, int dtype, int64_t n, uint32_t* amax_bits, cudaStream_t st, bool pdl);
 int launch_pack_act(const void* x, int64_t n, const uint32_t* amax_bits, uint8_t* q, float* scale_out,
                     cudaStream_t st, bool pdl);
+// Single-pass activation quantizer (one cooperative kernel; x, q and ws 16-byte aligned):
+// ws is its 16-byte counter block, which must be zero when the kernel starts -- cleared
+// here on the stream unless the caller already did (ws_zeroed).
+struct QuantWs;
+int launch_quant_single_pass(const void* x, int64_t n, uint8_t* q, float* scale_out, QuantWs* ws, cudaStream_t st,
+                             bool ws_zeroed);
 int launch_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
                     const float* scale_a, const float* scale_b, const void* bias, void* C, int64_t ldc, int out_dtype,
                     int epilogue, uint32_t* amax_out, int* status, cudaStream_t st, bool pdl);

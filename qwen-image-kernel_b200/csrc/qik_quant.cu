@@ -381,7 +381,7 @@ __global__ void __launch_bounds__(kQfThreads, 1) quant_act_single_pass_kernel(co
 
 // Cooperative launch of the single-pass quantizer over ws (cleared here, 16 bytes).
 int launch_quant_single_pass(const void* x, int64_t n, uint8_t* q, float* scale_out, QuantWs* ws,
-                             cudaStream_t st) {
+                             cudaStream_t st, bool ws_zeroed) {
   static bool attr_set[64] = {false};
   int dev = 0;
   QIK_TRY_CUDA(cudaGetDevice(&dev));
@@ -396,7 +396,7 @@ int launch_quant_single_pass(const void* x, int64_t n, uint8_t* q, float* scale_
   grid = grid < 1 ? 1 : (grid > sms ? sms : grid);
   const int64_t chunk = (nvec + grid - 1) / grid;
   const size_t smem = static_cast<size_t>(chunk < kQfSmemVecs ? chunk : kQfSmemVecs) * 16;
-  QIK_TRY_CUDA(cudaMemsetAsync(ws, 0, sizeof(QuantWs), st));
+  if (!ws_zeroed) QIK_TRY_CUDA(cudaMemsetAsync(ws, 0, sizeof(QuantWs), st));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(kQfThreads);
@@ -483,7 +483,7 @@ int qik_quantize_act(const void* x, int64_t n, uint8_t* q, float* scale_out, voi
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   QuantWs* w = static_cast<QuantWs*>(ws);
   // one pass over HBM (16-byte aligned operands); otherwise an amax pass then a pack pass
-  if (aligned16(x) && aligned16(q) && aligned16(ws)) return launch_quant_single_pass(x, n, q, scale_out, w, st);
+  if (aligned16(x) && aligned16(q) && aligned16(ws)) return launch_quant_single_pass(x, n, q, scale_out, w, st, false);
   QIK_TRY_CUDA(cudaMemsetAsync(w, 0, sizeof(QuantWs), st));
   int rc = launch_amax(x, QIK_DTYPE_BF16, n, &w->amax_bits, st, false);
   if (rc) return rc;

@@ -246,7 +246,7 @@ def fp8_ffn_gelu(x: torch.Tensor, up: FP8Linear, down: FP8Linear, workspace: tor
                  out: torch.Tensor | None = None, x_amax: torch.Tensor | None = None) -> torch.Tensor:
     """DiT FFN pair: down(gelu_tanh(up(x))) with both linears FP8 per-tensor and the
     hidden activation re-quantized dynamically between them (qik_fp8_ffn: one chain
-    of five kernels with programmatic dependent launches).
+    of four kernels with programmatic dependent launches).
 
     The up-projection epilogue applies GELU-tanh to the bf16 linear output and
     accumulates max|h| on the fly, so the hidden tensor is quantized with one pack
