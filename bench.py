@@ -415,7 +415,8 @@ def dit_block_case(device: torch.device, g: torch.Generator) -> dict:
     """DiT block @1024 px, CFG batch 2: M = 2 x 4352, the whole block --
     timestep modulation linear (M = 2), LayerNorm + modulate (its amax feeds the QKV
     quantizer), fused QKV, per-head RMSNorm + RoPE of q and k, block-causal attention
-    (256 text causal + 4096 image), out-proj, gated residual, LayerNorm + modulate (its
+    (256 text causal + 4096 image; its amax feeds the out-proj quantizer), out-proj, gated
+    residual, LayerNorm + modulate (its
     amax feeds the FFN's quantizer), FFN (GELU-tanh) and the second
     gated residual; random-init
     FP8 weights, synthetic activations."""
@@ -441,7 +442,7 @@ def dit_block_case(device: torch.device, g: torch.Generator) -> dict:
                         torch.outer(torch.arange(S2, device=device).float(), inv))
     Lt = torch.arange(S2, dtype=torch.int32, device=device)
     Lt[256:] = S2 - 1
-    amax = torch.zeros(2, dtype=torch.int32, device=device)
+    amax = torch.zeros(3, dtype=torch.int32, device=device)
 
     def block():
         mod = lin["mod"](temb) * 0.05  # [B, 6 x 3072]: scale / gate rows of the two sub-blocks
@@ -451,8 +452,8 @@ def dit_block_case(device: torch.device, g: torch.Generator) -> dict:
         q, k, v = qkv.chunk(3, dim=-2)
         q = fused_rms_norm_rope(q, wn, freqs, 1e-6)
         k = fused_rms_norm_rope(k, wn, freqs, 1e-6)
-        o = attn(q, k, v, Lt, None)
-        h = fused_gate_residual(x, lin["out"](o.flatten(2, 3)), mod, K, None)
+        o = attn(q, k, v, Lt, None, amax_out=amax[2:3])
+        h = fused_gate_residual(x, lin["out"].forward_from_amax(o.flatten(2, 3), amax[2:3]), mod, K, None)
         hm2 = fused_layer_norm_modulate(h, mod, 2 * K, mod.stride(0), None, 1e-6, amax_out=amax[1:2])
         f2 = F.fp8_ffn_gelu(hm2.reshape(M, K), lin["up"], lin["down"], x_amax=amax[1:2]).view(B2, S2, K)
         return fused_gate_residual(h, f2, mod, 3 * K, None)

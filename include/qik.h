@@ -192,6 +192,9 @@ typedef struct qik_attn_args {
   int64_t kv_sb;       /* key_valid batch stride */
   float sm_scale;      /* softmax scale, D^-0.5 in the reference */
   int flags;           /* QIK_ATTN_* */
+  uint32_t* amax_out;  /* NULL, or one device word that receives (atomic max) the fp32 bits of
+                          max|out| over the rows written: the dynamic scale of the FP8
+                          out-projection that consumes out, without a pass over out */
 } qik_attn_args;
 
 /*

@@ -78,6 +78,7 @@ struct AttnDev {
   float qk_scale_log2;
   int flags;
   int* status;
+  uint32_t* amax_out;
 };
 
 // Two boxes of 64 d-columns x 128 keys (rows) of one (b, h).
@@ -444,6 +445,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int j = 0; j < kAttnD; ++j) o[j] = __uint_as_float(r[j]);
       have_o = true;
     }
+    uint32_t am2 = 0;  // two running bf16 |out| maxima (amax_out)
     if (grow < a.SQ) {
       const bool nz = have_o && l_run > 0.0f;
       const float inv = nz ? (vsc_applied ? 1.0f : vsc) / l_run : 0.0f;
@@ -455,8 +457,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (nz)
           w = make_uint4(pack_bf16x2(o[c] * inv, o[c + 1] * inv), pack_bf16x2(o[c + 2] * inv, o[c + 3] * inv),
                          pack_bf16x2(o[c + 4] * inv, o[c + 5] * inv), pack_bf16x2(o[c + 6] * inv, o[c + 7] * inv));
+        am2 = __vmaxu2(am2, __vmaxu2(__vmaxu2(w.x & 0x7FFF7FFFu, w.y & 0x7FFF7FFFu),
+                                     __vmaxu2(w.z & 0x7FFF7FFFu, w.w & 0x7FFF7FFFu)));
         *reinterpret_cast<uint4*>(dst + c) = w;
       }
+    }
+    if (a.amax_out) {  // CTA-uniform: the whole warp reduces
+      const uint32_t m = __reduce_max_sync(0xffffffffu, max(am2 & 0xFFFFu, am2 >> 16));
+      if (lane == 0 && m != 0u) atomicMax(a.amax_out, m << 16);
     }
   }
 
@@ -554,6 +562,7 @@ extern "C" int qik_block_causal_attention(const qik_attn_args* args, int* status
   d.qk_scale_log2 = A.sm_scale * 1.4426950408889634f;
   d.flags = A.flags;
   d.status = status;
+  d.amax_out = A.amax_out;
   static bool attr_set[64] = {false};
   int dev = 0;
   QIK_TRY_CUDA(cudaGetDevice(&dev));

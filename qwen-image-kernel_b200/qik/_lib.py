@@ -39,6 +39,7 @@ class AttnArgs(ctypes.Structure):
         ("kv_sb", _i64),
         ("sm_scale", _f32),
         ("flags", _i32),
+        ("amax_out", _vp),
     ]
 
 

@@ -95,12 +95,15 @@ class QwenImage21KernelProcessor:
             # the slab store copies (and quantizes V) on the stream: the views suffice
             layer_cache.store(key[:, cache_write_slice], value[:, cache_write_slice])
 
+        # max|attention output| for the FP8 out-projection, accumulated by the kernel
+        out_amax = _new_amax(query) if isinstance(attn.to_out[0], FP8Linear) else None
         if segments is not None:
             # prefill over the full joint sequence
             assert key_valid is None or key_valid.dim() == 2
             prefix_end = segments[-1][1] if segments else 0
             L = _build_prefix_lengths(segments, prefix_end, S, query.device)
-            out = block_causal_flash_attention(query, key, value, L, key_valid, cache_k=None, cache_v=None)
+            out = block_causal_flash_attention(query, key, value, L, key_valid, cache_k=None, cache_v=None,
+                                               amax_out=out_amax)
         else:
             kv_mask = attention_mask
             if kv_mask is not None:
@@ -115,13 +118,17 @@ class QwenImage21KernelProcessor:
                 kv_total = cache_k.shape[1] + key.shape[1]
                 L = torch.full((key.shape[1],), kv_total - 1, dtype=torch.int32, device=query.device)
                 out = block_causal_flash_attention(query, key, value, L, kv_mask, cache_k=cache_k, cache_v=cache_v,
-                                                   cache_v_scale=v_scale, uniform_full=kv_mask is None)
+                                                   cache_v_scale=v_scale, uniform_full=kv_mask is None,
+                                                   amax_out=out_amax)
             else:
                 L = torch.full((key.shape[1],), key.shape[1] - 1, dtype=torch.int32, device=query.device)
-                out = block_causal_flash_attention(query, key, value, L, kv_mask, uniform_full=kv_mask is None)
+                out = block_causal_flash_attention(query, key, value, L, kv_mask, uniform_full=kv_mask is None,
+                                                   amax_out=out_amax)
 
         out = out.flatten(2, 3).type_as(query)
-        out = attn.to_out[0](out)
+        # the attention epilogue accumulated max|out|: the out-projection's quantizer
+        # skips its own max pass
+        out = _linear(attn.to_out[0], out, out_amax)
         return attn.to_out[1](out)
 
 

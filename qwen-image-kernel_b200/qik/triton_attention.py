@@ -29,6 +29,7 @@ def block_causal_flash_attention(
     cache_v: torch.Tensor | None = None,
     cache_v_scale: torch.Tensor | None = None,  # [B, H] fp32, only with fp8 cache V
     uniform_full: bool = False,  # caller guarantee: L == KV_TOTAL-1 for every row
+    amax_out: torch.Tensor | None = None,  # int32 [1]: atomic max of the fp32 bits of max|out|
 ) -> torch.Tensor:
     """Exact block-causal attention via per-row prefix lengths.
 
@@ -37,6 +38,9 @@ def block_causal_flash_attention(
     ``prefix_lengths``/``key_valid`` are indexed in absolute (cache-aware) space.
     Rows with ``L = -1`` attend to nothing and produce zeros.  When
     ``cache_v_scale`` is given the cache V is fp8e4m3 dequantized per head.
+    ``amax_out`` (int32 [1] on the query's device) receives, by atomic max, the fp32
+    bits of max|out|: the dynamic scale of the FP8 out-projection that follows
+    (``FP8Linear.forward_from_amax``) without another pass over ``out``.
     """
     assert query.dtype in (torch.bfloat16, torch.float16), "fp16/bf16 only"
     if query.dtype != torch.bfloat16:
@@ -88,6 +92,10 @@ def block_causal_flash_attention(
     a.o_sb, a.o_ss, a.o_sh = out.stride(0), out.stride(1), out.stride(2)
     a.sm_scale = D ** -0.5
     a.flags = flags
+    if amax_out is not None:
+        if amax_out.dtype != torch.int32 or amax_out.device != query.device:
+            raise ValueError("block_causal_flash_attention: amax_out must be int32 on the query's device")
+        a.amax_out = amax_out.data_ptr()
     lib = L.load()
     status = L.status_word(query.device)
     with torch.cuda.device(query.device):

@@ -274,3 +274,32 @@ def test_running_max_jumps_in_some_rows(attn, slab):
 def test_status_word_clean(attn):
     from qik import _lib as L
     assert L.device_status() == 0
+
+
+def test_amax_out_is_max_abs_of_the_output():
+    """amax_out (the FP8 out-projection's dynamic scale input) holds the fp32 bits of
+    max|out| exactly, for a block-causal prefill and for a decode over the e4m3 slab
+    (rows with no allowed key give 0 and do not count)."""
+    from qik.kv_cache import ContiguousKVCache
+    from qik.triton_attention import block_causal_flash_attention as attn
+    B, S, H, D = 2, 300, 3, 128
+    q, k, v = (GI.randn_bf16(700 + i, (B, S, H, D), 1.0 + i).cuda() for i in range(3))
+    L = torch.arange(S, dtype=torch.int32)
+    L[40:] = S - 1
+    L[5] = -1
+    amax = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = attn(q, k, v, L.cuda(), None, amax_out=amax)
+    torch.cuda.synchronize()
+    want = np.array([out.float().abs().max().item()], np.float32).view(np.int32)[0]
+    assert int(amax.item()) == int(want)
+    P, T = 256, 128
+    cache = ContiguousKVCache(1, B, P, H, D, v_fp8=True, device="cuda")
+    cache.get_layer(0).store(GI.randn_bf16(710, (B, P, H, D)).cuda(), GI.randn_bf16(711, (B, P, H, D), 3.0).cuda())
+    ck, cv, vs = cache.get_layer(0).views()
+    amax.zero_()
+    Ld = torch.full((T,), P + T - 1, dtype=torch.int32, device="cuda")
+    out = attn(q[:, :T].contiguous(), k[:, :T].contiguous(), v[:, :T].contiguous(), Ld, None, ck, cv, vs,
+               uniform_full=True, amax_out=amax)
+    torch.cuda.synchronize()
+    want = np.array([out.float().abs().max().item()], np.float32).view(np.int32)[0]
+    assert int(amax.item()) == int(want)
