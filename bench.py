@@ -464,15 +464,25 @@ def dit_block_case(device: torch.device, g: torch.Generator) -> dict:
             "mod": lambda: lin["mod"](temb)}
 
 
-PROFILE_CASES = ("attention_cfg4_prefill", "attention_cfg4_decode_fp8_slab", "dit_block_1024px_cfg2", "fused_ops_t2i")
+PROFILE_CASES = ("attention_cfg4_prefill", "attention_cfg4_decode_fp8_slab", "dit_block_1024px_cfg2", "fused_ops_t2i",
+                 "modulation_linear")
 
 
 def profile_case(device: torch.device, name: str) -> None:
     """Runs one workload three times (the launches an ncu capture selects from); for
-    fused_ops_t2i each of the four ops three times, a 256 MiB write before every launch
-    (cold L2)."""
+    fused_ops_t2i each of the four ops three times and for modulation_linear the FP8
+    linear three times, a 256 MiB write before every launch (cold L2)."""
     g = torch.Generator(device=device).manual_seed(7)
-    if name == "fused_ops_t2i":
+    if name == "modulation_linear":
+        # the DiT block's timestep-modulation FP8 linear: M = 2 (CFG batch) x 3072 -> 18432
+        from qik import fp8 as F
+        wq, sw = F.quantize_weight_tensorwise(torch.randn(18432, 3072, device=device, generator=g) * 0.02)
+        xq, sx = F.quantize_tensorwise(torch.randn(2, 3072, device=device, generator=g).to(torch.bfloat16))
+        flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)
+        for r in range(3):
+            flush.fill_(float(r))
+            F.fp8_gemm(xq, sx, wq, sw)
+    elif name == "fused_ops_t2i":
         x = torch.randn(2, 4352, 3072, device=device, generator=g).to(torch.bfloat16)
         mod = (torch.randn(2, 6 * 3072, device=device, generator=g) * 0.05).to(torch.bfloat16)
         flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)
