@@ -207,33 +207,45 @@ class FP8Linear(nn.Module):
 
     @staticmethod
     def from_linear(linear: nn.Linear) -> "FP8Linear":
-        """Convert a loaded bf16 nn.Linear (weights on CPU or GPU; quantized on the GPU)."""
-        mod = FP8Linear(linear.in_features, linear.out_features, bias=linear.bias is not None)
-        wq, s = quantize_weight_tensorwise(linear.weight.data.float())
-        mod.weight = wq.to(linear.weight.device)
-        mod.weight_scale = s.to(linear.weight.device)
+        """An FP8Linear holding ``linear``'s weight quantized per tensor (on the GPU, from
+        its fp32 values, as fp8.py:92-101 does) and its bias in bf16, on the linear's
+        device.  The shell is made on the meta device, so no zero buffers are allocated
+        before the quantized tensors are assigned."""
+        dev = linear.weight.device
+        wq, scale = quantize_weight_tensorwise(linear.weight.detach().float())
+        with torch.device("meta"):
+            mod = FP8Linear(linear.in_features, linear.out_features, bias=linear.bias is not None)
+        mod.weight = wq.to(dev)
+        mod.weight_scale = scale.to(dev)
         if linear.bias is not None:
-            mod.bias = linear.bias.data.to(torch.bfloat16).clone()
-        return mod.to(linear.weight.device)
+            mod.bias = linear.bias.detach().to(device=dev, dtype=torch.bfloat16).clone()
+        return mod
 
     def extra_repr(self) -> str:
         return f"in_features={self.in_features}, out_features={self.out_features}, bias={self.bias is not None}"
 
 
 def convert_linears_fp8(module: nn.Module, skip_patterns: tuple[str, ...] = (), prefix: str = "") -> list[str]:
-    """Recursively replace nn.Linear submodules with FP8Linear (in place); returns the
-    converted fully-qualified names.  Names containing any of ``skip_patterns`` are
-    left alone."""
-    converted = []
-    for name, child in list(module.named_children()):
-        full = f"{prefix}.{name}" if prefix else name
-        if any(p in full for p in skip_patterns):
-            continue
-        if isinstance(child, nn.Linear):
-            setattr(module, name, FP8Linear.from_linear(child))
-            converted.append(full)
-        else:
-            converted.extend(convert_linears_fp8(child, skip_patterns, full))
+    """Swap every nn.Linear under ``module`` for ``FP8Linear.from_linear`` of it, in
+    place (fp8.py:104-120).  A submodule whose qualified name (``prefix`` + the path)
+    contains one of ``skip_patterns`` is left alone with everything below it.  Returns
+    the qualified names converted, parents before children and siblings in
+    registration order."""
+    converted: list[str] = []
+    pending = [(prefix, module)]
+    while pending:
+        path, mod = pending.pop()
+        below = []
+        for name, child in mod.named_children():
+            full = f"{path}.{name}" if path else name
+            if any(p in full for p in skip_patterns):
+                continue
+            if isinstance(child, nn.Linear):
+                setattr(mod, name, FP8Linear.from_linear(child))
+                converted.append(full)
+            else:
+                below.append((full, child))
+        pending.extend(reversed(below))
     return converted
 
 

@@ -115,23 +115,19 @@ def reference_block_causal_attention(
     cache_k: torch.Tensor | None = None,
     cache_v: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """Plain-PyTorch statement of the same semantics, kept for API compatibility with
-    the reference module (triton_attention.py:266-293), which exports it for its unit
-    tests.  block_causal_flash_attention never calls it."""
-    B, SQ, H, D = query.shape
-    k_all = key if cache_k is None else torch.cat([cache_k, key], dim=1)
-    v_all = value if cache_v is None else torch.cat([cache_v, value], dim=1)
-    KV = k_all.shape[1]
-    idx = torch.arange(KV, device=query.device)
-    allowed = idx[None, None, None, :] <= prefix_lengths[None, None, :, None]
-    allowed = allowed.expand(B, -1, -1, -1) if allowed.shape[0] == 1 else allowed
+    """fp32 PyTorch statement of the attention semantics, exported because the
+    reference module exports a function of this name and signature for its unit
+    tests (triton_attention.py:266-293).  ``block_causal_flash_attention`` never calls
+    it.  Keys and values are the concatenation [cache ; fresh]; query row r sees key j
+    when j <= prefix_lengths[r] and, with ``key_valid`` [B, KV], key j of its sample
+    is valid.  As in the reference, a row that sees no key comes out NaN (a softmax
+    over an empty set), where the kernel writes zeros."""
+    keys = key if cache_k is None else torch.cat((cache_k, key), dim=1)
+    vals = value if cache_v is None else torch.cat((cache_v, value), dim=1)
+    j = torch.arange(keys.shape[1], device=query.device)
+    visible = j.view(1, 1, -1) <= prefix_lengths.to(query.device).view(1, -1, 1)       # [1, SQ, KV]
     if key_valid is not None:
-        allowed = allowed & key_valid[:, None, None, :].to(torch.bool)
-    q = query.transpose(1, 2).float()
-    k = k_all.transpose(1, 2).float()
-    v = v_all.transpose(1, 2).float()
-    scores = q @ k.transpose(-1, -2) * (D ** -0.5)
-    scores = scores.masked_fill(~allowed, float("-inf"))
-    attn = torch.softmax(scores, dim=-1)
-    out = attn.to(v.dtype) @ v
-    return out.transpose(1, 2).to(query.dtype)
+        visible = visible & key_valid.to(torch.bool).view(key_valid.shape[0], 1, -1)   # [B, SQ, KV]
+    logits = torch.einsum("bqhd,bkhd->bhqk", query.float(), keys.float()) * query.shape[-1] ** -0.5
+    weights = logits.masked_fill(~visible.unsqueeze(1), float("-inf")).softmax(dim=-1)
+    return torch.einsum("bhqk,bkhd->bqhd", weights, vals.float()).to(query.dtype)

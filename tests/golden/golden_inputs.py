@@ -120,3 +120,60 @@ def attention_cases():
     decode("decode_bf16_slab", 70, 130, 140)
     decode("decode_fp8_slab", 200, 96, 150, fp8=True)
     return cases
+
+
+def standin_dit(d: int = 64, hidden: int = 96, n_blocks: int = 2, fill: bool = True) -> torch.nn.Module:
+    """A small module tree with the attribute names of the Qwen-Image DiT that the e4m3
+    cache format depends on: ``transformer_blocks.{i}`` with ``attn.to_q/to_k/to_v``
+    (biased), ``attn.norm_q/norm_k`` (RMSNorm weights), ``attn.to_out.0`` and
+    ``img_mlp.gate_layer/proj/out``; outside the blocks ``img_in`` (K < 256),
+    ``norm_out.linear``, ``proj_out``, a persistent ``time_embed.freqs`` buffer (which
+    the writer drops) and a buffer that is a view of another (which it must copy
+    out).  ``fill=False`` leaves the tensors as allocated (use under a meta device
+    context to get the skeleton a cache loads into); otherwise every tensor is drawn
+    from ``randn_bf16`` with a fixed seed, so the tree rebuilds bit-identically."""
+    nn = torch.nn
+    seed = iter(range(1000, 2000))
+
+    def linear(k, n, bias):
+        lin = nn.Linear(k, n, bias=bias, dtype=torch.bfloat16)
+        if fill:
+            with torch.no_grad():
+                lin.weight.copy_(randn_bf16(next(seed), (n, k), 0.02))
+                if bias:
+                    lin.bias.copy_(randn_bf16(next(seed), (n,), 0.1))
+        return lin
+
+    def block():
+        b = nn.Module()
+        b.img_norm1 = nn.LayerNorm(d, elementwise_affine=False, eps=1e-6)
+        b.attn = nn.Module()
+        for name in ("to_q", "to_k", "to_v"):
+            setattr(b.attn, name, linear(d, d, True))
+        b.attn.norm_q = nn.RMSNorm(32, eps=1e-6, dtype=torch.bfloat16)
+        b.attn.norm_k = nn.RMSNorm(32, eps=1e-6, dtype=torch.bfloat16)
+        b.attn.to_out = nn.ModuleList([linear(d, d, True), nn.Dropout(0.0)])
+        b.img_norm2 = nn.LayerNorm(d, elementwise_affine=False, eps=1e-6)
+        b.img_mlp = nn.Module()
+        b.img_mlp.gate_layer = linear(d, hidden, False)
+        b.img_mlp.proj = linear(d, hidden, False)
+        b.img_mlp.out = linear(hidden, d, False)
+        if fill:
+            with torch.no_grad():
+                b.attn.norm_q.weight.copy_(randn_bf16(next(seed), (32,), 0.5))
+                b.attn.norm_k.weight.copy_(randn_bf16(next(seed), (32,), 0.5))
+        return b
+
+    m = nn.Module()
+    m.img_in = linear(16, d, True)
+    m.time_embed = nn.Module()
+    m.time_embed.register_buffer("freqs", torch.arange(8, dtype=torch.float32))
+    m.time_embed.linear_1 = linear(32, d, True)
+    table = torch.zeros(12, 4, dtype=torch.float32) if not fill else randn_bf16(next(seed), (12, 4)).float()
+    m.register_buffer("pos_table", table)
+    m.register_buffer("pos_table_head", table[:3])
+    m.transformer_blocks = nn.ModuleList([block() for _ in range(n_blocks)])
+    m.norm_out = nn.Module()
+    m.norm_out.linear = linear(d, 2 * d, True)
+    m.proj_out = linear(d, 16, True)
+    return m

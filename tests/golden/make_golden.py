@@ -3,7 +3,10 @@
 Run once in a container where the reference checkout is present (it does not
 travel to GPU boxes):
 
-    python tests/golden/make_golden.py /path/to/qwen-image-kernel
+    python tests/golden/make_golden.py /path/to/qwen-image-kernel [section ...]
+
+Sections: ``vectors`` (items 1-5 below, into the .npz files) and ``fp8_cache`` (item
+6, into fp8_cache_ref.safetensors); the default is both.
 
 The reference package cannot be imported as a whole (its ``__init__`` pulls in the
 diffusers/accelerate runtime), so its leaf modules are loaded by file path under a
@@ -14,6 +17,9 @@ synthetic package.  Functions exercised (all run on CPU tensors):
   qwen_image_kernel/kv_cache.py:23-95     ContiguousKVCache / _LayerView.store/get/views
   qwen_image_kernel/triton_attention.py:266-293  reference_block_causal_attention
   qwen_image_kernel/processors.py:22-36   _build_prefix_lengths
+  qwen_image_kernel/quantize_offline.py:29-104  _fuse_block_linears, _convert_module_fp8,
+                                          _sd_for_save (+ safetensors save_file): the e4m3
+                                          cache of golden_inputs.standin_dit()
 
 Inputs are drawn from numpy's PCG64 (stable across versions) so the tests can
 regenerate them; only outputs (and input checksums) are stored.  CPU evaluation
@@ -43,7 +49,7 @@ def load_reference(root: Path):
     pkg.__path__ = [str(pkg_dir)]
     sys.modules["qwen_image_kernel"] = pkg
     mods = {}
-    for name in ("fp8", "triton_attention", "kv_cache", "triton_fused", "processors"):
+    for name in ("fp8", "triton_attention", "kv_cache", "triton_fused", "processors", "quantize_offline"):
         spec = importlib.util.spec_from_file_location(f"qwen_image_kernel.{name}", pkg_dir / f"{name}.py")
         m = importlib.util.module_from_spec(spec)
         sys.modules[f"qwen_image_kernel.{name}"] = m
@@ -60,10 +66,33 @@ def digest(t: torch.Tensor) -> str:
     return hashlib.sha256(t.contiguous().view(torch.uint8).numpy().tobytes()).hexdigest()[:16]
 
 
-def main(ref_root: str) -> None:
+def fp8_cache(R) -> None:
+    """The reference's offline writer, exactly as build_transformer_fp8_cache drives it
+    (quantize_offline.py:121-131), over the stand-in tree: fuse each block's groups,
+    convert the remaining linears, drop ``.freqs``, save.  On a CPU-only machine the
+    reference quantizes on the CPU (quantize_offline.py:16), i.e. with the true-division
+    scale (the oracle's SCALE_CPU form)."""
+    from safetensors.torch import save_file
+    qo = R["quantize_offline"]
+    model = GI.standin_dit()
+    for blk in model.transformer_blocks:
+        qo._fuse_block_linears(blk)
+    qo._convert_module_fp8(model)
+    save_file(qo._sd_for_save(model, drop_patterns=(".freqs",)), str(HERE / "fp8_cache_ref.safetensors"))
+
+
+def main(ref_root: str, sections: list[str]) -> None:
     R = load_reference(Path(ref_root))
-    fp8, attn, kvc, proc = R["fp8"], R["triton_attention"], R["kv_cache"], R["processors"]
     torch.set_num_threads(8)
+    if "fp8_cache" in sections:
+        fp8_cache(R)
+    if "vectors" in sections:
+        vectors(R)
+    print("golden files written to", HERE)
+
+
+def vectors(R) -> None:
+    fp8, attn, kvc, proc = R["fp8"], R["triton_attention"], R["kv_cache"], R["processors"]
 
     # ---- 1. compute_scale over every positive finite bf16 amax (CPU form) ----
     amax_bits = np.arange(1, 0x7F80, dtype=np.uint16)              # +min subnormal .. max finite
@@ -132,8 +161,9 @@ def main(ref_root: str) -> None:
         at_out[f"{name}__out"] = bits16(out)
         at_out[f"{name}__in"] = np.array(digest(q) + digest(k) + digest(v))
     np.savez_compressed(HERE / "attention.npz", **at_out)
-    print("golden vectors written to", HERE)
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py <reference checkout> [vectors] [fp8_cache]")
+    main(sys.argv[1], sys.argv[2:] or ["vectors", "fp8_cache"])

@@ -1,100 +1,118 @@
-"""CPU tests of the e4m3 cache format (qik.quantize_offline) and the drop-in
-installer (qik.patch).  The weight quantizer is the oracle here (the library's GPU
-quantizer is checked byte for byte against it in test_gpu_quant.py)."""
+"""CPU tests of the e4m3 cache format (qik.quantize_offline) against a file the
+reference's own writer produced (tests/golden/fp8_cache_ref.safetensors), and of the
+drop-in installer (qik.patch).  The weight quantizer is the oracle here (the library's
+GPU quantizer is checked byte for byte against it in test_gpu_quant.py)."""
 import importlib
 import sys
 import textwrap
 
+import pytest
 import torch
 
 from oracle import oracle as O
 
 
-def _oracle_quant(w):
-    q, s = O.quantize_weight(w.cpu(), O.SCALE_CUDA)
-    return torch.from_numpy(q).view(torch.float8_e4m3fn), torch.tensor([s], dtype=torch.float32)
+GOLDEN_CACHE = "fp8_cache_ref.safetensors"
 
 
-class _Attn(torch.nn.Module):
-    def __init__(self, d, bias):
-        super().__init__()
-        self.to_q = torch.nn.Linear(d, d, bias=bias, dtype=torch.bfloat16)
-        self.to_k = torch.nn.Linear(d, d, bias=bias, dtype=torch.bfloat16)
-        self.to_v = torch.nn.Linear(d, d, bias=bias, dtype=torch.bfloat16)
-        self.to_out = torch.nn.ModuleList([torch.nn.Linear(d, d, bias=True, dtype=torch.bfloat16),
-                                           torch.nn.Dropout(0.0)])
+def _oracle_quant(mode):
+    def quant(w):
+        q, s = O.quantize_weight(w.cpu(), mode)
+        return torch.from_numpy(q).view(torch.float8_e4m3fn), torch.tensor([s], dtype=torch.float32)
+    return quant
 
 
-class _Mlp(torch.nn.Module):
-    def __init__(self, d, h):
-        super().__init__()
-        self.gate_layer = torch.nn.Linear(d, h, bias=False, dtype=torch.bfloat16)
-        self.proj = torch.nn.Linear(d, h, bias=False, dtype=torch.bfloat16)
-        self.out = torch.nn.Linear(h, d, bias=False, dtype=torch.bfloat16)
+def test_writer_reproduces_reference_cache_bytes(tmp_path, golden_dir):
+    """The reference's writer (quantize_offline.py:29-131, run on CPU by
+    tests/golden/make_golden.py over golden_inputs.standin_dit) and this writer, fed
+    the same tree and the same (CPU-form) weight quantizer, produce the same file
+    byte for byte."""
+    import golden_inputs as GI
+    from qik import quantize_offline as QO
+    m = GI.standin_dit()
+    QO.convert_model_fp8(m, quantize=_oracle_quant(O.SCALE_CPU))
+    path = tmp_path / "fp8_cache" / "transformer_fused_fp8.safetensors"
+    n = QO.write_fp8_cache(m, str(path))
+    mine, ref = path.read_bytes(), (golden_dir / GOLDEN_CACHE).read_bytes()
+    assert len(mine) == len(ref) and mine == ref
+    assert n == 38
 
 
-class _Block(torch.nn.Module):
-    def __init__(self, d=64, h=128, bias=True):
-        super().__init__()
-        self.attn = _Attn(d, bias)
-        self.img_mlp = _Mlp(d, h)
-        self.register_buffer("freqs", torch.ones(4))
+def test_reference_cache_layout(golden_dir):
+    """Key schema of the reference-written file: fused groups with one scale, the
+    members absent, ``.freqs`` dropped, e4m3 / f32 / bf16 dtypes."""
+    import golden_inputs as GI
+    from safetensors.torch import load_file
+    sd = load_file(str(golden_dir / GOLDEN_CACHE))
+    assert not any(".freqs" in k for k in sd)
+    assert not any(f".{m}." in k for k in sd for m in ("to_q", "to_k", "to_v", "gate_layer", "proj"))
+    for i in range(2):
+        w = sd[f"transformer_blocks.{i}.attn.fused_qkv.weight"]
+        assert w.dtype == torch.float8_e4m3fn and tuple(w.shape) == (192, 64)
+        assert sd[f"transformer_blocks.{i}.attn.fused_qkv.weight_scale"].shape == (1,)
+        assert sd[f"transformer_blocks.{i}.attn.fused_qkv.bias"].dtype == torch.bfloat16
+        assert tuple(sd[f"transformer_blocks.{i}.img_mlp.fused_up.weight"].shape) == (192, 64)
+        assert f"transformer_blocks.{i}.img_mlp.fused_up.bias" not in sd
+    assert sd["pos_table_head"].shape == (3, 4)
+    # one scale over the concatenated Q/K/V weights of block 0, in the oracle's CPU form
+    src = GI.standin_dit()
+    a = src.transformer_blocks[0].attn
+    q_exp, s_exp = _oracle_quant(O.SCALE_CPU)(torch.cat([a.to_q.weight, a.to_k.weight, a.to_v.weight]).detach())
+    assert torch.equal(sd["transformer_blocks.0.attn.fused_qkv.weight"].view(torch.uint8), q_exp.view(torch.uint8))
+    assert sd["transformer_blocks.0.attn.fused_qkv.weight_scale"].item() == s_exp.item()
 
 
-def _model():
-    torch.manual_seed(0)
-    m = torch.nn.Module()
-    m.transformer_blocks = torch.nn.ModuleList([_Block(), _Block()])
-    m.proj_out = torch.nn.Linear(64, 32, bias=True, dtype=torch.bfloat16)
-    return m
-
-
-def test_fused_cache_keys_layout_and_roundtrip(tmp_path):
-    from safetensors import safe_open
+def test_reader_loads_reference_cache(golden_dir):
+    """A skeleton built on the meta device takes the reference-written file through the
+    shells (runtime.py:76-123,196-200): no missing or unexpected key, nothing left on
+    the meta device, fused shells where the file has fused keys."""
+    import golden_inputs as GI
+    from safetensors.torch import load_file
     from qik import quantize_offline as QO
     from qik.fp8 import FP8Linear
-    m = _model()
-    wq_ref = torch.cat([m.transformer_blocks[0].attn.to_q.weight, m.transformer_blocks[0].attn.to_k.weight,
-                        m.transformer_blocks[0].attn.to_v.weight], 0).detach().clone()
-    for blk in m.transformer_blocks:
-        QO._fuse_block_linears(blk, quantize=_oracle_quant)
-    QO._convert_module_fp8(m, quantize=_oracle_quant)
-    path = tmp_path / "fp8_cache" / "transformer_fused_fp8.safetensors"
-    n = QO.save_fp8_cache(m, str(path))
-    with safe_open(str(path), framework="pt") as f:
-        keys = set(f.keys())
-        w = f.get_tensor("transformer_blocks.0.attn.fused_qkv.weight")
-        s = f.get_tensor("transformer_blocks.0.attn.fused_qkv.weight_scale")
-        assert w.dtype == torch.float8_e4m3fn and tuple(w.shape) == (192, 64)
-        assert s.dtype == torch.float32 and tuple(s.shape) == (1,)
-        assert f.get_tensor("transformer_blocks.0.attn.fused_qkv.bias").dtype == torch.bfloat16
-    assert len(keys) == n
-    assert not any(".freqs" in k for k in keys)
-    assert not any("to_q" in k or "gate_layer" in k for k in keys)
-    for must in ("transformer_blocks.1.img_mlp.fused_up.weight", "transformer_blocks.1.img_mlp.out.weight_scale",
-                 "transformer_blocks.0.attn.to_out.0.weight", "proj_out.bias"):
-        assert must in keys
-    # one scale over the concatenated Q/K/V weight, bytes = the oracle's quantization of the cat
-    q_exp, s_exp = _oracle_quant(wq_ref)
-    assert torch.equal(w.view(torch.uint8), q_exp.view(torch.uint8)) and float(s) == float(s_exp)
-    # loads into FP8Linear shells with assign=True (runtime.py:196-200)
-    shell = FP8Linear(64, 192, bias=True)
+    with torch.device("meta"):
+        m = GI.standin_dit(fill=False)
+    QO.load_fp8_cache(m, str(golden_dir / GOLDEN_CACHE))
+    sd = load_file(str(golden_dir / GOLDEN_CACHE))
+    blk = m.transformer_blocks[1]
+    assert isinstance(blk.attn.fused_qkv, FP8Linear) and isinstance(blk.attn.to_q, torch.nn.Identity)
+    assert isinstance(blk.img_mlp.fused_up, FP8Linear) and blk.img_mlp.fused_up.bias is None
+    assert isinstance(m.img_in, FP8Linear) and isinstance(blk.attn.to_out[0], FP8Linear)
+    got = m.state_dict()
+    for k, t in sd.items():
+        assert torch.equal(got[k].view(torch.uint8), t.view(torch.uint8)), k
+
+
+def test_reader_rejects_mismatched_cache(golden_dir):
+    import golden_inputs as GI
     from safetensors.torch import load_file
-    sd = load_file(str(path))
-    missing, unexpected = shell.load_state_dict(
-        {k.split("attn.fused_qkv.")[1]: v for k, v in sd.items() if k.startswith("transformer_blocks.0.attn.fused_qkv.")},
-        strict=True, assign=True)
-    assert not missing and not unexpected
+    from qik import quantize_offline as QO
+    sd = load_file(str(golden_dir / GOLDEN_CACHE))
+    broken = dict(sd)
+    del broken["proj_out.weight_scale"]
+    with torch.device("meta"):
+        m = GI.standin_dit(fill=False)
+    with pytest.raises(ValueError, match="missing"):
+        QO.load_fp8_cache(m, broken)
+    extra = dict(sd)
+    extra["proj_out.stray"] = torch.zeros(1)
+    with torch.device("meta"):
+        m = GI.standin_dit(fill=False)
+    with pytest.raises(ValueError, match="unexpected"):
+        QO.load_fp8_cache(m, extra)
 
 
-def test_sd_for_save_dealiases():
+def test_cache_state_dict_copies_out_shared_storage():
     from qik import quantize_offline as QO
     m = torch.nn.Module()
     base = torch.arange(8, dtype=torch.float32)
     m.register_buffer("a", base)
     m.register_buffer("b", base[:4])
-    sd = QO._sd_for_save(m)
+    m.register_buffer("c", torch.ones(3))
+    sd = QO.cache_state_dict(m)
     assert sd["a"].untyped_storage().data_ptr() != sd["b"].untyped_storage().data_ptr()
+    assert sd["c"].data_ptr() == m.c.data_ptr()          # sole owner of a whole storage: not copied
+    assert torch.equal(sd["b"], base[:4])
 
 
 def test_patch_install_binds_qik_modules(tmp_path):

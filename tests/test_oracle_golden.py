@@ -138,3 +138,18 @@ def test_fp8_linear_oracle_reference_bound():
     y = O.fp8_linear(xq, sx, wq, sw)
     ref = x.float() @ w.float().t()
     assert O.relf(y, ref) < 0.06
+
+
+def test_exported_reference_attention_matches_golden(golden_dir):
+    """qik.triton_attention.reference_block_causal_attention (the compatibility export
+    of triton_attention.py:266-293) reproduces the reference function's outputs."""
+    from qik.triton_attention import reference_block_causal_attention
+    g = np.load(golden_dir / "attention.npz")
+    for name, c in GI.attention_cases().items():
+        if c.get("slab_fp8"):
+            continue
+        out = reference_block_causal_attention(c["q"], c["k"], c["v"], c["L"], c["key_valid"], c["cache_k"],
+                                               c["cache_v"])
+        ref = torch.from_numpy(g[f"{name}__out"].view(np.int16)).view(torch.bfloat16).reshape(out.shape)
+        assert (out.float() - ref.float()).abs().max().item() <= 2e-3, name
+        assert O.relf(out, ref) < 1e-3, name
