@@ -11,8 +11,9 @@ N(0,1) with 8 outlier channels x20 (synthetic; no dataset is involved).
 
 A step is one FFN pair over one batch.  ``value`` = FLOPs (2*M*N*K summed over both
 linears and all ranks) / device time of the K timed steps (CUDA events on the
-launching stream, max over ranks); L2 is flushed (256 MiB write) between steps,
-outside the timed events.  ``e2e`` is the same metric through the public API
+launching stream, max over ranks); L2 is flushed between steps, outside the timed
+events: a 256 MiB write, then a 256 MiB read of a second buffer, so the write's dirty
+lines are written back during the flush and not during the next timed kernel.  ``e2e`` is the same metric through the public API
 with every step's input copied from pinned host memory and its output copied back
 inside the timed region: the serving form (qik.host_pipeline.HostPipeline, the copies
 of neighbouring steps overlapping this step's kernels) as the value, the form with
@@ -56,9 +57,71 @@ def peaks() -> dict:
         d = json.loads(p.read_text())
         return {"fp8_tflops": 2.0 * float(d["bf16_tflops_sustained"]),
                 "fp8_tflops_burst": 2.0 * float(d["bf16_tflops"]), "hbm_gbs": float(d["hbm_gbs"]),
-                "source": "measured (MEASURED_PEAKS.json): FP8 dense = 2 x measured bf16 cuBLAS, sustained"}
+                "source": "measured (MEASURED_PEAKS.json)"}
     return {"fp8_tflops": 2.0 * 1400.0, "fp8_tflops_burst": 2.0 * 1590.0, "hbm_gbs": 6650.0,
-            "source": "fallback: 2 x 1.40 PFLOP/s sustained bf16, 6.65 TB/s"}
+            "source": "fallback: 2 x 1.40 PFLOP/s sustained bf16, 2 x 1.59 burst, 6.65 TB/s"}
+
+
+def fp8_peak_cublaslt(device: torch.device, iters: int = 10) -> float:
+    """Dense FP8 tensor-core peak measured on this GPU: the best of `iters` back-to-back
+    torch._scaled_mm (cuBLASLt, the reference's call, fp8.py:87) at 8192^3 in e4m3,
+    bf16 out, per-tensor scales (a burst figure: each launch timed alone)."""
+    n = 8192
+    g = torch.Generator(device=device).manual_seed(3)
+    a = torch.randn(n, n, device=device, generator=g).to(torch.float8_e4m3fn)
+    b = torch.randn(n, n, device=device, generator=g).to(torch.float8_e4m3fn)
+    one = torch.ones((), device=device)
+    fn = lambda: torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16)  # noqa: E731
+    for _ in range(3):
+        fn()
+    stream = torch.cuda.current_stream(device)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    torch.cuda._sleep(int(2e7))
+    for e0, e1 in evs:
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+    torch.cuda.synchronize(device)
+    best = min(e0.elapsed_time(e1) for e0, e1 in evs)
+    return 2.0 * n ** 3 / (best / 1e3) / 1e12
+
+
+class L2Flush:
+    """The cache flush between timed launches: a 256 MiB write (more than the 126 MB L2,
+    so nothing of the previous launch stays cached) followed by a 256 MiB read of a
+    second buffer, which writes the first buffer's dirty lines back to HBM here rather
+    than during the next timed kernel's reads."""
+
+    def __init__(self, device: torch.device):
+        n = 256 * 1024 * 1024 // 4
+        self.w = torch.empty(n, dtype=torch.float32, device=device)
+        self.r = torch.zeros(n, dtype=torch.float32, device=device)
+        self.sink = torch.empty((), dtype=torch.float32, device=device)
+
+    def __call__(self, i: int = 0) -> None:
+        self.w.fill_(float(i))
+        torch.sum(self.r, dim=0, out=self.sink)
+
+
+# DRAM traffic of the FP8 GEMM inside the FFN step: dram__bytes_read.sum +
+# dram__bytes_write.sum per launch, the mean of GEMM1 and GEMM2 of one configs[1]
+# step, from `ncu --set full --clock-control none -k regex:fp8_gemm -s 2 -c 2
+# python bench.py --steps 3 --warmup 3 --no-extras` (the algorithmic bytes are 158.1 MB
+# for GEMM1 and 117.9 MB for GEMM2).
+GEMM_DRAM_BYTES_PER_LAUNCH = 136778496
+GEMM_TRAFFIC_SOURCE = ("ncu capture (dram__bytes_read.sum + dram__bytes_write.sum, mean of the step's two GEMM "
+                       "launches): ncu --set full --clock-control none -k regex:fp8_gemm -s 2 -c 2 "
+                       "python bench.py --steps 3 --warmup 3 --no-extras")
+
+
+def bench_config(world: int) -> dict:
+    """The workload both arms run (identical for the qik and the reference arm)."""
+    return {"workload": "configs[1] DiT FFN pair: M=4352 x 3072 -> 12288 (GELU-tanh) -> 3072, FP8 per-tensor, "
+                        "dynamic activation re-quantization, bf16 out",
+            "rows_per_gpu": M_ROWS, "global_rows": M_ROWS * world,
+            "l2": "flushed between timed steps, outside the timed events: 256 MiB write, then a 256 MiB read of "
+                  "a second buffer (the write's dirty lines go back to HBM during the flush)",
+            "parallelism": f"dp{world}: token-row shards, no data-path collective"}
 
 
 # ------------------------------------------------------------------------------ inputs
@@ -142,7 +205,7 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
         lin.weight.copy_(wq)
         lin.weight_scale.copy_(sw)
     x = x_cpu.to(device)
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    flush = L2Flush(device)
     stream = torch.cuda.current_stream(device)
 
     lib = L.load()
@@ -185,7 +248,7 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
     # no host launch latency appears inside the device-timed events
     torch.cuda._sleep(int(2e7))
     for i in range(args.steps):
-        flush.fill_(float(i))
+        flush(i)
         ev_step[i][0].record(stream)
         step(x)
         ev_step[i][1].record(stream)
@@ -199,7 +262,7 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
     ev_k = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     torch.cuda._sleep(int(1e8))  # ~50 ms head start: the host queues every split step
     for i in range(args.steps):
-        flush.fill_(float(i))
+        flush(i)
         step_split(x, ev_k[i])
     barrier()
     torch.cuda.synchronize(device)
@@ -227,7 +290,7 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
     e2e_start.record(stream)
     pipe.h2d_stream.wait_event(e2e_start)
     for i in range(args.steps):
-        flush.fill_(float(i))  # L2 flush on the compute stream, inside the timed span
+        flush(i)  # L2 flush on the compute stream, inside the timed span
         e2e_end = pipe.submit(x_host, y_hosts[i % 2])
     pipe.synchronize()
     barrier()
@@ -238,7 +301,7 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
               for _ in range(args.steps)]
     torch.cuda._sleep(int(2e7))
     for i in range(args.steps):
-        flush.fill_(float(i))
+        flush(i)
         e2e_ev[i][0].record(stream)
         xd = x_host.to(device, non_blocking=True)
         y_host.copy_(F.fp8_ffn_gelu(xd, up, down, workspace=ws), non_blocking=True)
@@ -246,8 +309,11 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
     barrier()
     t_e2e_serial = sum(a.elapsed_time(b) for a, b in e2e_ev) / 1e3
 
+    parity = ffn_parity(x_cpu, up, down, step(x)) if rank == 0 else {}
     ext = extras(device, flush) if (rank == 0 and not args.no_extras) else None
     tp = tp_stack(device, rank, world, flush) if not args.no_extras else None
+    sweep_n = row_shard_sweep(device, rank, world, flush) if not args.no_extras else None
+    fp8_peak = fp8_peak_cublaslt(device)
     status = L.device_status(device)
     t = torch.tensor([t_steps, t_e2e, t_e2e_serial, gemm_ms, float(status)], dtype=torch.float64, device=device)
     if world > 1:
@@ -257,6 +323,12 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
         return None
 
     pk = peaks()
+    # the GEMM is timed launch by launch (a burst), so the roofline compares it with burst
+    # peaks: the larger of cuBLASLt's own FP8 GEMM measured above and 2 x the measured
+    # burst bf16 rate
+    peak = max(fp8_peak, pk["fp8_tflops_burst"])
+    peak_source = (f"max of cuBLASLt FP8 8192^3 measured in this run ({fp8_peak:.1f} TF/s, burst) and 2 x "
+                   f"bf16 burst from {pk['source']} ({pk['fp8_tflops_burst']:.1f} TF/s)")
     total_flops = FLOPS_PER_STEP * args.steps * world
     value = total_flops / t_steps / 1e12
     achieved = FLOPS_PER_LINEAR / (gemm_ms / 1e3) / 1e12
@@ -273,13 +345,9 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
         "vs_baseline": None,
         "dtype": "e4m3 x e4m3 -> fp32 accumulate, bf16 out",
         "data": "synthetic: N(0,1) activations with 8 outlier channels x20, N(0,0.02) random-init weights",
-        "config": {"workload": "configs[1] DiT FFN pair: M=4352 x 3072 -> 12288 (GELU-tanh) -> 3072, FP8 "
-                               "per-tensor, dynamic activation re-quantization, bf16 out",
-                   "rows_per_gpu": M_ROWS, "global_rows": M_ROWS * world,
-                   "l2": "flushed between timed steps (256 MiB write outside the timed events)",
-                   "parallelism": f"dp{world}: token-row shards, no data-path collective"},
+        "config": bench_config(world),
         "per_gpu_tflops": round(value / world, 2),
-        "pct_dense_fp8_peak": round(100.0 * value / world / pk["fp8_tflops"], 1),
+        "pct_dense_fp8_peak": round(100.0 * value / world / peak, 1),
         "pct_nominal_fp8_4500": round(100.0 * value / world / NOMINAL_FP8_TFLOPS, 1),
         "e2e": {"value": round(total_flops / t_e2e / 1e12, 2), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": M_ROWS * K_IN * 2, "d2h_bytes_per_step": M_ROWS * K_IN * 2,
@@ -292,15 +360,19 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
                            "ms_per_step": round(t_e2e_serial / args.steps * 1e3, 4),
                            "form": "copy in, kernels, copy out back to back on one stream"}},
         "roofline": {"kernel": "qik::fp8_gemm_kernel (tcgen05 kind::f8f6f4)", "bound": "tensor",
-                     "achieved": round(achieved, 1), "peak": round(pk["fp8_tflops"], 1), "unit": "TFLOP/s",
-                     "frac": round(achieved / pk["fp8_tflops"], 3), "traffic": traffic_from_profile(),
-                     "peak_source": pk["source"], "avg_launch_ms": round(gemm_ms, 4),
-                     "flops_per_launch": FLOPS_PER_LINEAR},
+                     "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 3), "traffic": GEMM_DRAM_BYTES_PER_LAUNCH,
+                     "traffic_source": GEMM_TRAFFIC_SOURCE, "peak_source": peak_source,
+                     "frac_vs_2x_bf16_burst": round(achieved / pk["fp8_tflops_burst"], 3),
+                     "frac_vs_cublaslt_fp8": round(achieved / fp8_peak, 3),
+                     "avg_launch_ms": round(gemm_ms, 4), "flops_per_launch": FLOPS_PER_LINEAR},
+        "parity": parity,
         "gpu_launches": launches_per_step * args.steps * 3,
         "gpu_launches_note": "qik kernels inside the timed regions (device-resident steps + pipelined and serial e2e steps: "
                              "single-pass quantizer of x, GEMM+GELU+amax, pack, GEMM per step, the last three "
-                             "chained with programmatic dependent launch; a 80-byte memset clears the chain's "
-                             "counters); the L2-flush fills are torch's; GEMM launch times for the "
+                             "chained with programmatic dependent launch; one 1040-byte memset per step clears the "
+                             "quantizer's barrier word and the chain's counters); the L2 flush (fill + sum) is "
+                             "torch's; GEMM launch times for the "
                              "roofline come from a second pass that runs the step launch by launch with events (median per GEMM)",
         "device_status": int(status),
         "clocks": clocks,
@@ -309,31 +381,21 @@ def run_qik(args, rank: int, world: int, device: torch.device) -> dict | None:
         out["extras"] = ext
     if tp is not None:
         out.setdefault("extras", {})["tp_stack_4block_1024px"] = tp
+        if "parity" in tp:
+            out["parity"]["tp_peer_vs_nccl"] = tp.pop("parity")
+    if sweep_n is not None:
+        out.setdefault("extras", {})["cfg5_row_shard_sweep"] = sweep_n
     if world == 1:
         out["cpu_baseline"] = cpu_baseline(args)
     return out
 
 
-def traffic_from_profile():
-    """DRAM bytes per GEMM launch (read + write, averaged over the FFN's two GEMM
-    launches) from the committed ncu summary, if present."""
-    p = ROOT / "profiles" / "fp8_gemm_ffn_cfg2.md"
-    if p.exists():
-        for line in p.read_text().splitlines():
-            if line.strip().startswith("dram_bytes_per_launch_avg"):
-                try:
-                    return int(line.split("=")[1].strip().split()[0])
-                except (IndexError, ValueError):
-                    return None
-    return None
-
-
 # ------------------------------------------------------------------------------ extras
-def _time_ms(fn, iters: int, flush: torch.Tensor, stream) -> float:
+def _time_ms(fn, iters: int, flush: L2Flush, stream) -> float:
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
     torch.cuda._sleep(int(2e7))
     for i in range(iters):
-        flush.fill_(float(i))
+        flush(i)
         evs[i][0].record(stream)
         fn()
         evs[i][1].record(stream)
@@ -368,7 +430,7 @@ def fused_ops_cases(device: torch.device, x: torch.Tensor, mod: torch.Tensor) ->
     }
 
 
-def fused_ops(device: torch.device, flush: torch.Tensor, iters: int, x: torch.Tensor, mod: torch.Tensor) -> dict:
+def fused_ops(device: torch.device, flush: L2Flush, iters: int, x: torch.Tensor, mod: torch.Tensor) -> dict:
     """HBM roofline of the four fused elementwise kernels at the t2i block shapes
     (fused_ops_cases), L2 flushed between launches."""
     stream = torch.cuda.current_stream(device)
@@ -464,8 +526,83 @@ def dit_block_case(device: torch.device, g: torch.Generator) -> dict:
             "mod": lambda: lin["mod"](temb)}
 
 
-PROFILE_CASES = ("attention_cfg4_prefill", "attention_cfg4_decode_fp8_slab", "dit_block_1024px_cfg2", "fused_ops_t2i",
-                 "modulation_linear")
+class _Attention(torch.nn.Module):
+    """Stand-in for the diffusers attention module with the attributes the processor
+    reads (processors.py:50-126): heads, fused_qkv, norm_q / norm_k (weight, eps),
+    to_out[0 / 1], and the processor call."""
+
+    def __init__(self, heads, fused_qkv, to_out, wq, wk):
+        super().__init__()
+        self.heads = heads
+        self.fused_qkv = fused_qkv
+        self.norm_q = torch.nn.RMSNorm(wq.numel(), eps=1e-6, device=wq.device)
+        self.norm_k = torch.nn.RMSNorm(wk.numel(), eps=1e-6, device=wk.device)
+        with torch.no_grad():
+            self.norm_q.weight.copy_(wq)
+            self.norm_k.weight.copy_(wk)
+        self.to_out = torch.nn.ModuleList([to_out, torch.nn.Identity()])
+        self.processor = None
+
+    def set_processor(self, p):
+        self.processor = p
+
+    def forward(self, hidden_states, **kw):
+        return self.processor(self, hidden_states, **kw)
+
+
+def dit_block_product_case(device: torch.device, g: torch.Generator) -> dict:
+    """The DiT block @1024 px, CFG batch 2 (M = 2 x 4352), through the product API:
+    qik.processors.QwenImage21KernelBlock.forward over stand-in submodules with the
+    reference's names -- fused QKV 3072 -> 9216, 24 heads of 128 with RMSNorm + RoPE,
+    block-causal prefill attention (256 causal text rows + 4096 image rows), out-proj
+    3072 -> 3072, the SwiGLU MLP of the reference block (processors.py:180-187) with its
+    fused up projection at BASELINE's 3072 -> 12288 (gate and up halves of 6144) and
+    6144 -> 3072 down, the two LayerNorm + modulate and gated residuals -- preceded by the
+    timestep-modulation FP8 linear (M = 2, 3072 -> 18432) whose first 4 x 3072 columns
+    are the block's modulation rows.  Random-init FP8 weights, synthetic activations."""
+    from qik import fp8 as F
+    from qik.processors import QwenImage21KernelBlock, QwenImage21KernelProcessor
+    H, D, K, B2, S2, HALF = 24, 128, 3072, 2, 4352, 6144
+
+    def lin(n_out, n_in):
+        f = F.FP8Linear(n_in, n_out).to(device)
+        wq, sw = F.quantize_weight_tensorwise(torch.randn(n_out, n_in, device=device, generator=g) * 0.02)
+        f.weight.copy_(wq)
+        f.weight_scale.copy_(sw)
+        return f
+
+    attn = _Attention(H, lin(3 * K, K), lin(K, K), torch.ones(D, device=device), torch.ones(D, device=device))
+    attn.set_processor(QwenImage21KernelProcessor())
+    shell = torch.nn.Module()
+    shell.img_norm1 = torch.nn.LayerNorm(K, elementwise_affine=False, eps=1e-6)
+    shell.img_norm2 = torch.nn.LayerNorm(K, elementwise_affine=False, eps=1e-6)
+    shell.attn = attn
+    shell.img_mlp = torch.nn.Module()
+    shell.img_mlp.fused_up = lin(2 * HALF, K)
+    shell.img_mlp.out = lin(K, HALF)
+    block = QwenImage21KernelBlock(shell)
+    mod_lin = lin(6 * K, K)
+    x = torch.randn(B2, S2, K, device=device, generator=g).to(torch.bfloat16)
+    temb = torch.randn(B2, K, device=device, generator=g).to(torch.bfloat16)
+    inv = 1.0 / (10000 ** (torch.arange(0, D, 2, device=device).float() / D))
+    freqs = torch.polar(torch.ones(S2, D // 2, device=device),
+                        torch.outer(torch.arange(S2, device=device).float(), inv))
+    segments = [(0, 256, True)]
+
+    def run():
+        mod = mod_lin(temb)[:, :4 * K]
+        return block(x, mod, rotary_emb=freqs, segments=segments)
+
+    M = B2 * S2
+    Lt = torch.arange(S2, dtype=torch.int64)
+    Lt[256:] = S2 - 1
+    lin_fl = 2.0 * M * K * (3 * K + K + 2 * HALF) + 2.0 * M * HALF * K + 2.0 * B2 * K * 6 * K
+    at_fl = 4.0 * D * H * B2 * float((Lt + 1).sum())
+    return {"block": run, "linear_flops": lin_fl, "attention_flops": at_fl}
+
+
+PROFILE_CASES = ("attention_cfg4_prefill", "attention_cfg4_decode_fp8_slab", "dit_block_1024px_cfg2",
+                 "dit_block_1024px_cfg2_gelu_ffn", "fused_ops_t2i", "modulation_linear")
 
 
 def profile_case(device: torch.device, name: str) -> None:
@@ -478,21 +615,25 @@ def profile_case(device: torch.device, name: str) -> None:
         from qik import fp8 as F
         wq, sw = F.quantize_weight_tensorwise(torch.randn(18432, 3072, device=device, generator=g) * 0.02)
         xq, sx = F.quantize_tensorwise(torch.randn(2, 3072, device=device, generator=g).to(torch.bfloat16))
-        flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)
+        flush = L2Flush(device)
         for r in range(3):
-            flush.fill_(float(r))
+            flush(r)
             F.fp8_gemm(xq, sx, wq, sw)
     elif name == "fused_ops_t2i":
         x = torch.randn(2, 4352, 3072, device=device, generator=g).to(torch.bfloat16)
         mod = (torch.randn(2, 6 * 3072, device=device, generator=g) * 0.05).to(torch.bfloat16)
-        flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)
+        flush = L2Flush(device)
         for i, (fn, _) in enumerate(fused_ops_cases(device, x, mod).values()):
             for r in range(3):
-                flush.fill_(float(3 * i + r))
+                flush(3 * i + r)
                 fn()
     else:
-        fn = (dit_block_case(device, g)["block"] if name == "dit_block_1024px_cfg2"
-              else attention_cfg4_cases(device, g)[name][0])
+        if name == "dit_block_1024px_cfg2":
+            fn = dit_block_product_case(device, g)["block"]
+        elif name == "dit_block_1024px_cfg2_gelu_ffn":
+            fn = dit_block_case(device, g)["block"]
+        else:
+            fn = attention_cfg4_cases(device, g)[name][0]
         for _ in range(3):
             fn()
     torch.cuda.synchronize(device)
@@ -500,7 +641,7 @@ def profile_case(device: torch.device, name: str) -> None:
     print(json.dumps({"profile_case": name, "runs": 3, "device_status": L.device_status(device)}), flush=True)
 
 
-def extras(device: torch.device, flush: torch.Tensor, iters: int = 10) -> dict:
+def extras(device: torch.device, flush: L2Flush, iters: int = 10) -> dict:
     """Attention at BASELINE config 4 and the DiT-block time at 1024 px (configs[2] +
     the t2i attention), each on synthetic inputs with the BASELINE shapes."""
     from qik import _lib as L
@@ -512,22 +653,37 @@ def extras(device: torch.device, flush: torch.Tensor, iters: int = 10) -> dict:
             fn()
         ms = _time_ms(fn, iters, flush, stream)
         out[name] = {"ms": round(ms, 4), "tflops": round(fl / ms / 1e9, 1), "gflop": round(fl / 1e9, 1)}
+    prod = dit_block_product_case(device, g)
+    for _ in range(3):
+        prod["block"]()
+    ms = _time_ms(prod["block"], iters, flush, stream)
+    lin_fl, at_fl = prod["linear_flops"], prod["attention_flops"]
+    out["dit_block_1024px_cfg2"] = {
+        "ms": round(ms, 4), "tflops": round((lin_fl + at_fl) / ms / 1e9, 1),
+        "linear_gflop": round(lin_fl / 1e9, 1), "attention_gflop": round(at_fl / 1e9, 1),
+        "api": "qik.processors.QwenImage21KernelBlock.forward (+ the timestep-modulation FP8Linear)",
+        "includes": "modulation GEMV (M=2, 3072->18432), 2x LayerNorm+modulate, fused QKV 3072->9216, "
+                    "RMSNorm+RoPE (q, k), block-causal attention, out-proj, SwiGLU MLP (fused up 3072->12288, "
+                    "down 6144->3072), 2x gated residual"}
     case = dit_block_case(device, g)
     block = case["block"]
     for _ in range(3):
         block()
     ms = _time_ms(block, iters, flush, stream)
     lin_fl, at_fl = case["linear_flops"], case["attention_flops"]
-    out["dit_block_1024px_cfg2"] = {"ms": round(ms, 4), "tflops": round((lin_fl + at_fl) / ms / 1e9, 1),
-                                    "linear_gflop": round(lin_fl / 1e9, 1), "attention_gflop": round(at_fl / 1e9, 1),
-                                    "includes": "modulation GEMV, 2x LayerNorm+modulate, RMSNorm+RoPE (q, k), "
-                                                "attention, 4 FP8 linears (GELU FFN), 2x gated residual"}
+    out["dit_block_1024px_cfg2_gelu_ffn"] = {
+        "ms": round(ms, 4), "tflops": round((lin_fl + at_fl) / ms / 1e9, 1),
+        "linear_gflop": round(lin_fl / 1e9, 1), "attention_gflop": round(at_fl / 1e9, 1),
+        "api": "the same kernels composed by hand with BASELINE configs[2]'s FFN (3072->12288 GELU-tanh->3072, "
+               "qik.fp8.fp8_ffn_gelu)",
+        "includes": "modulation GEMV, 2x LayerNorm+modulate, RMSNorm+RoPE (q, k), attention, 4 FP8 linears "
+                    "(GELU FFN), 2x gated residual"}
     out["fused_ops_t2i"] = fused_ops(device, flush, iters, case["x"], mod=case["mod"]())
     out["device_status"] = L.device_status(device)
     return out
 
 
-def tp_stack(device: torch.device, rank: int, world: int, flush: torch.Tensor, iters: int = 5) -> dict:
+def tp_stack(device: torch.device, rank: int, world: int, flush: L2Flush, iters: int = 5) -> dict:
     """BASELINE configs[4]'s layer-stack case: 4 DiT blocks at 1024 px, CFG batch 2
     (M = 8704), tensor parallel over `world` GPUs -- QKV by heads and FFN-up column-
     parallel, attention on local heads, out-proj and FFN-down row-parallel with a
@@ -571,7 +727,7 @@ def tp_stack(device: torch.device, rank: int, world: int, flush: torch.Tensor, i
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
         torch.cuda._sleep(int(2e7))
         for i in range(iters):
-            flush.fill_(float(i))
+            flush(i)
             evs[i][0].record(stream)
             stack()
             evs[i][1].record(stream)
@@ -587,6 +743,35 @@ def tp_stack(device: torch.device, rank: int, world: int, flush: torch.Tensor, i
                         red.close()
         return float(t.item())
 
+    def stack_output(comm: str) -> torch.Tensor:
+        blocks = [PX.TPBlock.from_full(full, H, D, rank, world, chunks=1, comm=comm) for full in fulls]
+        h = x
+        for blk in blocks:
+            h = blk(h, B, S, Lt)
+        h = h.clone()
+        torch.cuda.synchronize(device)
+        if world > 1:
+            torch.distributed.barrier()
+        for blk in blocks:
+            for lin in (blk.out, blk.down):
+                for red in lin._peer.values():
+                    if red:
+                        red.close()
+        return h
+
+    parity = None
+    if world > 1:
+        # the same stack with the row-parallel sums over peer memory and by NCCL's
+        # all-reduce: on 2 ranks both add two fp32 terms, so they must agree bit for bit
+        y_peer, y_nccl = stack_output("peer"), stack_output("nccl")
+        same = torch.tensor([1.0 if torch.equal(y_peer, y_nccl) else 0.0,
+                             (y_peer.float() - y_nccl.float()).abs().max().item()], dtype=torch.float64,
+                            device=device)
+        torch.distributed.all_reduce(same[0:1], op=torch.distributed.ReduceOp.MIN)
+        torch.distributed.all_reduce(same[1:2], op=torch.distributed.ReduceOp.MAX)
+        parity = {"bit_identical_all_ranks": bool(same[0].item() == 1.0), "max_abs_diff": float(same[1].item()),
+                  "expected": "bit-identical on 2 ranks (two-term fp32 sums commute); NCCL's summation order "
+                              "may differ from the rank-order sum on more ranks"}
     ms_peer = timed(1, "peer")
     ms_nccl = timed(1, "nccl") if world > 1 else ms_peer
     ms_overlap = timed(4, "nccl") if world > 1 else ms_peer
@@ -595,7 +780,7 @@ def tp_stack(device: torch.device, rank: int, world: int, flush: torch.Tensor, i
     lin = 2.0 * M * K * (3 * H * D + K + HID) + 2.0 * M * HID * K
     att = 4.0 * D * H * B * float((Lt.long() + 1).sum())
     total = 4 * (lin + att)
-    return {"ms": round(ms, 4), "tflops_total": round(total / ms / 1e9, 1),
+    res = {"ms": round(ms, 4), "tflops_total": round(total / ms / 1e9, 1),
             "tflops_per_gpu": round(total / ms / 1e9 / world, 1), "n_gpus": world, "scaling": "strong",
             "form": ("one GPU" if world == 1 else
                      "comm='auto' = peer: row-parallel GEMM epilogue stores fp32 tiles into the owner rank's "
@@ -611,6 +796,39 @@ def tp_stack(device: torch.device, rank: int, world: int, flush: torch.Tensor, i
                                "persistent GEMM)" if world > 1 else "n/a",
             "collectives_per_stack": "8 x row reductions of fp32 [8704, 3072] partial products "
                                      "+ 8 x all-reduce(MAX) 4 bytes (NCCL)" if world > 1 else "none"}
+    if parity is not None:
+        res["parity"] = parity
+    return res
+
+
+def row_shard_sweep(device: torch.device, rank: int, world: int, flush: L2Flush, iters: int = 10) -> list:
+    """BASELINE configs[4] at this world size: the FP8 linear at K = 3072 for N in
+    {3072, 9216, 12288, 18432} and M in {256, 1024, 4352, 9472, 16384}, the M token rows
+    split across the ranks (rank r takes M // world rows, one more for r < M % world;
+    strong scaling), no collective on the data path: each rank quantizes its rows and
+    runs the GEMM.  Time per shape = max over ranks of the mean CUDA-event time of one
+    launch; TFLOP/s = 2 M N K / that time."""
+    from qik import fp8 as F
+    stream = torch.cuda.current_stream(device)
+    g = torch.Generator(device=device).manual_seed(5 + rank)
+    K = 3072
+    rows = []
+    for N in (3072, 9216, 12288, 18432):
+        wq, sw = F.quantize_weight_tensorwise(torch.randn(N, K, device=device, generator=g) * 0.02)
+        for M in (256, 1024, 4352, 9472, 16384):
+            m_r = M // world + (1 if rank < M % world else 0)
+            x = torch.randn(m_r, K, device=device, generator=g).to(torch.bfloat16)
+            xq, sx = F.quantize_tensorwise(x)
+            fn = lambda: F.fp8_gemm(xq, sx, wq, sw)  # noqa: E731
+            for _ in range(3):
+                fn()
+            t = torch.tensor([_time_ms(fn, iters, flush, stream)], dtype=torch.float64, device=device)
+            if world > 1:
+                torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+            rows.append({"M": M, "N": N, "rows_per_rank": M // world, "ms": round(ms, 4),
+                         "tflops_total": round(2.0 * M * N * K / ms / 1e9, 1)})
+    return rows
 
 
 # ------------------------------------------------------------------------------ CPU arm
@@ -629,42 +847,102 @@ def cpu_ffn_reference(x: torch.Tensor, w1q, s1, w2q, s2) -> torch.Tensor:
     return ((hq.float() * sh) @ (w2q.float() * s2).t()).to(torch.bfloat16)
 
 
-def cpu_baseline(args, budget_s: float = 12.0, rows: int = 512) -> dict:
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
+def _cpu_weights():
     x, w1, w2 = make_inputs(4321, torch.device("cpu"))
-    xs = x[:rows].contiguous()
 
     def wquant(w):
         s = (w.abs().amax().float() / 448.0).clamp_min(1e-12)
         return (w.float() / s).clamp(-448, 448).to(torch.float8_e4m3fn), s
 
-    w1q, s1 = wquant(w1)
-    w2q, s2 = wquant(w2)
-    cpu_ffn_reference(xs[:64], w1q, s1, w2q, s2)                         # warm-up
+    return x, wquant(w1), wquant(w2)
+
+
+def cpu_baseline(args, budget_s: float = 12.0) -> dict:
+    """The reference's arithmetic timed on the host cores (all of them) on the whole
+    configs[1] workload: FFN pair over all 4352 rows per repetition, as many repetitions
+    as fit in `budget_s` (at least one)."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    x, (w1q, s1), (w2q, s2) = _cpu_weights()
+    cpu_ffn_reference(x[:64], w1q, s1, w2q, s2)                          # warm-up
     reps, t0 = 0, time.perf_counter()
     while True:
-        cpu_ffn_reference(xs, w1q, s1, w2q, s2)
+        cpu_ffn_reference(x, w1q, s1, w2q, s2)
         reps += 1
         el = time.perf_counter() - t0
         if el >= budget_s or reps >= 50:
             break
-    flops = 2 * (2.0 * rows * K_IN * HIDDEN) * reps
+    flops = FLOPS_PER_STEP * reps
     return {"value": round(flops / el / 1e12, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"{reps} x FFN pair on {rows} of the {M_ROWS} rows (same shapes/weights), "
-                      f"{el:.1f} s wall, PyTorch CPU fp32 dequant matmuls"}
+            "sample": f"{reps} x FFN pair on all {M_ROWS} rows (configs[1], same shapes and weights), {el:.1f} s "
+                      f"wall, PyTorch CPU fp32 dequant matmuls"}
+
+
+def ffn_parity(x_cpu: torch.Tensor, up, down, y_chain: torch.Tensor) -> dict:
+    """The checker leg: this rank's configs[1] step checked stage by stage against the
+    CPU oracle (oracle/, the tests' checker) on the step's own intermediates -- the input
+    quantizer (bytes and scale bit-exact), GEMM1 + GELU-tanh on the product's e4m3 x
+    (relF), the hidden activation's pack (bit-exact), GEMM2 on the product's e4m3 h
+    (relF) -- and the fused chain's output against the same step launched stage by stage
+    (bit-identical)."""
+    import numpy as np
+    from oracle import oracle as O
+    from qik import _lib as L
+    from qik import fp8 as F
+    dev = y_chain.device
+    x = x_cpu.to(dev)
+    xq, sx = F.quantize_tensorwise(x)
+    amax = torch.zeros(1, dtype=torch.int32, device=dev)
+    h = F.fp8_gemm(xq, sx, up.weight, up.weight_scale, up.bias, epilogue=L.EPI_GELU_TANH, amax_out=amax)
+    hq, sh = F.quantize_from_amax(h, amax)
+    y = F.fp8_gemm(hq, sh, down.weight, down.weight_scale, down.bias)
+    torch.cuda.synchronize(dev)
+    torch.set_num_threads(os.cpu_count() or 1)
+    q_ref, s_ref = O.quantize_act(x_cpu, O.SCALE_CUDA)
+    x_exact = bool(np.array_equal(xq.cpu().view(torch.uint8).numpy(), q_ref)
+                   and np.float32(s_ref) == np.float32(sx.item()))
+    h_ref = O.gelu_tanh(O.fp8_linear(xq.cpu(), float(sx.item()), up.weight.cpu(),
+                                     float(up.weight_scale.item())).to(torch.bfloat16))
+    r1 = O.relf(h.cpu(), h_ref)
+    hq_ref, sh_ref = O.quantize_act(h.cpu(), O.SCALE_CUDA)
+    h_exact = bool(np.array_equal(hq.cpu().view(torch.uint8).numpy(), hq_ref)
+                   and np.float32(sh_ref) == np.float32(sh.item()))
+    y_ref = O.fp8_linear(hq.cpu(), float(sh.item()), down.weight.cpu(), float(down.weight_scale.item()))
+    r2 = O.relf(y.cpu(), y_ref)
+    ident = bool(torch.equal(y, y_chain))
+    ok = x_exact and h_exact and r1 <= 5e-3 and r2 <= 5e-3 and ident
+    return {"x_quant_bit_exact": x_exact, "gemm1_gelu_relF": float(f"{r1:.3e}"), "h_pack_bit_exact": h_exact,
+            "gemm2_relF": float(f"{r2:.3e}"), "chain_vs_stages_bit_identical": ident,
+            "rows_checked": int(x_cpu.shape[0]), "gate": "quantizers bit-exact, relF <= 5e-3 per GEMM stage",
+            "pass": ok}
 
 
 def run_reference(args, rank: int, world: int) -> dict | None:
+    """--impl reference: the reference's arithmetic (cpu_ffn_reference) on the host cores,
+    every step one FFN pair over the whole configs[1] workload (all 4352 rows), W untimed
+    warm-up steps then K timed ones; rank 0 alone runs it."""
     if rank != 0:
         return None
-    cb = cpu_baseline(args, budget_s=max(5.0, min(60.0, 2.0 * (args.steps + args.warmup))))
-    return {"metric": METRIC, "value": cb["value"], "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "e4m3 quantize + fp32 dequant matmul (CPU)", "data": "synthetic",
-            "config": {"workload": "configs[1] DiT FFN pair (row sample)", "rows_per_gpu": M_ROWS},
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    x, (w1q, s1), (w2q, s2) = _cpu_weights()
+    for _ in range(args.warmup):
+        cpu_ffn_reference(x, w1q, s1, w2q, s2)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_ffn_reference(x, w1q, s1, w2q, s2)
+    el = time.perf_counter() - t0
+    value = round(FLOPS_PER_STEP * args.steps / el / 1e12, 4)
+    cb = {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+          "sample": f"{args.steps} timed x FFN pair on all {M_ROWS} rows after {args.warmup} warm-up steps, "
+                    f"{el:.1f} s wall, PyTorch CPU fp32 dequant matmuls"}
+    return {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 quantize + fp32 dequant matmul (CPU)",
+            "data": "synthetic: N(0,1) activations with 8 outlier channels x20, N(0,0.02) random-init weights",
+            "config": bench_config(world),
             "impl": "reference", "cpu_baseline": cb,
-            "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def sweep(device: torch.device, iters: int = 20) -> list[dict]:
@@ -674,7 +952,7 @@ def sweep(device: torch.device, iters: int = 20) -> list[dict]:
     (3 algorithmic bytes per element).  One JSON line per shape."""
     from qik import fp8 as F
     stream = torch.cuda.current_stream(device)
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    flush = L2Flush(device)
     pk = peaks()
     g = torch.Generator(device=device).manual_seed(5)
     K = 3072

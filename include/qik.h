@@ -42,7 +42,7 @@ int qik_version(void);
 /* Message for the last non-zero status returned on this thread. */
 const char* qik_last_error(void);
 
-/* Bytes of scratch `ws` the quantizer entry points need (16-byte aligned). */
+/* Bytes of scratch `ws` the quantizer entry points need (16-byte aligned; 1024). */
 size_t qik_quant_workspace_bytes(void);
 
 /*
@@ -68,6 +68,14 @@ int qik_amax(const void* x, int dtype, int64_t n, uint32_t* amax_bits, void* str
  * q[i] = e4m3_rn_satfinite(fl32(x[i]) * (1/scale)).  Replaces quantize_tensorwise
  * + _scale_cast_fp8_kernel (qwen_image_kernel/fp8.py:29-53).
  *   x: n bf16, contiguous; q: n bytes; scale_out: 1 fp32 (device).
+ *   ws: qik_quant_workspace_bytes() bytes that carry a grid-barrier state from one
+ *       call to the next: zero them once before the first call, then keep passing
+ *       the same workspace (every completed call leaves it ready for the next, so
+ *       the call is a single kernel launch with no clearing).  Calls sharing one
+ *       workspace must be ordered (one stream); give each stream its own.  When a
+ *       call fails (non-zero return, or a NaN *scale_out: a bounded wait inside the
+ *       kernel gave up), zero the workspace again before reusing it.  With x, q or
+ *       ws not 16-byte aligned the call takes a two-pass form that keeps no state.
  */
 int qik_quantize_act(const void* x, int64_t n, uint8_t* q, float* scale_out, void* ws, void* stream);
 
@@ -84,12 +92,15 @@ int qik_quantize_act(const void* x, int64_t n, uint8_t* q, float* scale_out, voi
  * the process exits; this entry point needs qik_quant_workspace_bytes() of it for
  * any n and returns QIK_ERR_INVALID if that ever exceeds the array.  The first
  * call on a device looks up the array's device address (cudaGetSymbolAddress);
- * make that first call before any stream capture.  All calls share the array and
- * its amax word is cleared on the stream at the start of each call, so calls
- * that overlap on the GPU (different streams, or different host threads on one
- * device) race; serialize them.
+ * make that first call before any stream capture.  The address is cached per
+ * device ordinal for the life of the process, which assumes the device's primary
+ * context is never reset (cudaDeviceReset) while the library is loaded.  All calls
+ * share the array; each call clears the array's barrier word on the stream before
+ * its kernel runs (the rest of the array needs no clearing), so calls that overlap
+ * on the GPU (different streams, or different host threads on one device) race;
+ * serialize them.
  */
-#define QIK_NOALLOC_SCRATCH_BYTES 256
+#define QIK_NOALLOC_SCRATCH_BYTES 1024
 int qik_quantize_act_noalloc(const void* x, int64_t n, uint8_t* q, float* scale_out, void* stream);
 
 /*

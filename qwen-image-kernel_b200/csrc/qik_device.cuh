@@ -468,7 +468,7 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 }
 // 2^x for a pair of x <= 2^7 on the FMA pipe (no MUFU): x = n + f with n = round(x)
 // (the 1.5 * 2^23 shifter), 2^f by a cubic in f on [-1/2, 1/2] (coefficients
-// fitted for least relative error by csrc/exp2_poly.py: max relative error
+// fitted for least relative error by tests/exp2_poly.py: max relative error
 // 7.5e-5 = 2^-13.7), 2^n added to the exponent bits.  x is clamped to >= -125, so
 // inputs below give 2^-125 (not 0): callers use it only where every x belongs to an
 // allowed key of a row with a finite running max.

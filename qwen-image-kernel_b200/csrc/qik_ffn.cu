@@ -25,8 +25,12 @@ struct FfnHeader {
   float sh;
 };
 constexpr size_t kAlign = 256;
-constexpr size_t kQuantWsOffset = 64;  // inside the 256-byte header
-constexpr size_t kQuantWsBytes = 16;
+// workspace head: the single-pass quantizer's workspace (1 KB), then the chain's
+// header words; one memset per call clears both (the quantizer's barrier state and
+// amax_h, which GEMM1's epilogue accumulates into)
+constexpr size_t kQuantWsBytes = 1024;
+constexpr size_t kHeaderOffset = kQuantWsBytes;
+constexpr size_t kHeadBytes = 1280;
 size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 }  // namespace
 }  // namespace qik
@@ -34,8 +38,8 @@ size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 using namespace qik;
 
 extern "C" size_t qik_fp8_ffn_workspace_bytes(int64_t M, int64_t K, int64_t hidden) {
-  if (M <= 0 || K <= 0 || hidden <= 0) return kAlign;
-  return kAlign + align_up(static_cast<size_t>(M) * K) + align_up(static_cast<size_t>(M) * hidden * 2) +
+  if (M <= 0 || K <= 0 || hidden <= 0) return kHeadBytes;
+  return kHeadBytes + align_up(static_cast<size_t>(M) * K) + align_up(static_cast<size_t>(M) * hidden * 2) +
          align_up(static_cast<size_t>(M) * hidden);
 }
 
@@ -53,20 +57,19 @@ static int fp8_ffn_chain(const void* x, const uint32_t* x_amax, int64_t M, int64
   QIK_REQUIRE((reinterpret_cast<uintptr_t>(ws) & (kAlign - 1)) == 0, "qik_fp8_ffn: workspace must be 256-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t* base = static_cast<uint8_t*>(ws);
-  FfnHeader* hdr = reinterpret_cast<FfnHeader*>(base);
-  uint8_t* xq = base + kAlign;
+  QuantWs* qws = reinterpret_cast<QuantWs*>(base);
+  FfnHeader* hdr = reinterpret_cast<FfnHeader*>(base + kHeaderOffset);
+  uint8_t* xq = base + kHeadBytes;
   void* h = xq + align_up(static_cast<size_t>(M) * K);
   uint8_t* hq = static_cast<uint8_t*>(h) + align_up(static_cast<size_t>(M) * hidden * 2);
 
-  // header words and the single-pass quantizer's counter block, cleared by one memset
-  QuantWs* qws = reinterpret_cast<QuantWs*>(base + kQuantWsOffset);
-  QIK_TRY_CUDA(cudaMemsetAsync(base, 0, kQuantWsOffset + kQuantWsBytes, st));
+  QIK_TRY_CUDA(cudaMemsetAsync(base, 0, kHeaderOffset + sizeof(FfnHeader), st));
   int rc = QIK_OK;
   if (x_amax) {
     rc = launch_pack_act(x, M * K, x_amax, xq, &hdr->sx, st, false);
   } else if (aligned16(x)) {
     // one kernel: x read from HBM once (it fits the SMs' shared memory up to ~28 MB)
-    rc = launch_quant_single_pass(x, M * K, xq, &hdr->sx, qws, st, true);
+    rc = launch_quant_single_pass(x, M * K, xq, &hdr->sx, qws, st, false);
   } else {
     rc = launch_amax(x, QIK_DTYPE_BF16, M * K, &hdr->amax_x, st, false);
     if (!rc) rc = launch_pack_act(x, M * K, &hdr->amax_x, xq, &hdr->sx, st, true);

@@ -74,11 +74,12 @@ int launch_amax(const void* x, int dtype, int64_t n, uint32_t* amax_bits, cudaSt
 int launch_pack_act(const void* x, int64_t n, const uint32_t* amax_bits, uint8_t* q, float* scale_out,
                     cudaStream_t st, bool pdl);
 // Single-pass activation quantizer (one cooperative kernel; x, q and ws 16-byte aligned):
-// ws is its 16-byte counter block, which must be zero when the kernel starts -- cleared
-// here on the stream unless the caller already did (ws_zeroed).
+// ws is its 1 KB workspace (qik_quant_workspace_bytes), whose barrier word must be
+// zero before the first call and is left ready for the next call by each call that
+// completes; clear_bar zeroes that word on the stream first.
 struct QuantWs;
 int launch_quant_single_pass(const void* x, int64_t n, uint8_t* q, float* scale_out, QuantWs* ws, cudaStream_t st,
-                             bool ws_zeroed);
+                             bool clear_bar);
 int launch_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
                     const float* scale_a, const float* scale_b, const void* bias, void* C, int64_t ldc, int out_dtype,
                     int epilogue, uint32_t* amax_out, int* status, cudaStream_t st, bool pdl);

@@ -18,12 +18,23 @@
 
 namespace qik {
 
+// Workspace of the activation quantizers.  `bar` is the single-pass kernel's grid
+// barrier: a generation in the high 32 bits and the arrivals of the running call in
+// the low 32.  The last CTA to arrive returns the arrivals to 0 and advances the
+// generation in one atomic add, so a workspace that was zeroed once serves any number
+// of calls in stream order without being cleared again.  partial[i] holds CTA i's
+// max|x| bits for the running call: written before the CTA arrives, read by every CTA
+// after the barrier, so stale contents never matter.  amax_bits belongs to the
+// two-pass form (amax kernel, then pack), which clears it itself.
+constexpr int kQuantMaxCtas = 252;
 struct QuantWs {
+  unsigned long long bar;
   uint32_t amax_bits;
-  uint32_t arrived;  // CTAs past phase 1 of the single-pass quantizer
-  uint32_t go;       // set by the last of them: the amax is complete
   uint32_t pad;
+  uint32_t partial[kQuantMaxCtas];
 };
+static_assert(sizeof(QuantWs) == 1024, "QuantWs layout");
+constexpr uint32_t kQuantAbortMark = 0xFFFFFFFFu;  // a partial above every |x| bit pattern: a CTA gave up
 
 constexpr int kQuantThreads = 256;
 
@@ -239,18 +250,52 @@ __global__ void __launch_bounds__(kQuantThreads) kv_store_kernel(
 // One CTA per SM, launched cooperatively (all CTAs resident at once).  Phase 1: each
 // CTA streams the first kQfSmemBytes of its contiguous slice into shared memory with
 // bulk copies (16 KB chunks, each on its own mbarrier, all issued up front so the
-// copy engine keeps the whole slice in flight), reduces max|x| chunk by chunk as the
-// chunks land, reads any remainder of the slice with plain loads, and folds its
-// maximum into the global amax.  A grid barrier (arrival counter + release flag in
-// the workspace, spin bounded by QIK_WAIT_NS) makes the amax complete.  Phase 2: each
-// CTA packs its slice from shared memory where it was kept, so a tensor up to
-// ~28 MB (148 x 192 KB) is read from HBM exactly once: 2 B read + 1 B written per
-// element.  On a timeout the kernel writes no codes and a NaN scale.
+// copy engine keeps the whole slice in flight) while its threads read any remainder of
+// the slice with plain loads (8 per thread in flight), then reduces max|x| over the
+// chunks as they land.  Its maximum goes to its slot of the workspace, and a grid
+// barrier (one 64-bit atomic per CTA; the waits bounded by QIK_WAIT_NS) makes every
+// slot visible.  Phase 2: each CTA reduces the slots to the global amax and packs its
+// slice, from shared memory where it was kept, so a tensor up to ~33 MB (148 x 224 KB)
+// is read from HBM exactly once: 2 B read + 1 B written per element.  A remainder is
+// read with an L2 evict-last policy in phase 1 and re-read (from L2 while it stays
+// there) with evict-first in phase 2; while a remainder exists the codes are stored
+// with evict-first too, so they do not push it out of L2.
+// If any CTA's copy or barrier wait gives up, every CTA that sees it writes no codes
+// and CTA 0 writes a NaN scale; the workspace must then be zeroed again before reuse.
 constexpr int kQfThreads = 512;
 constexpr int kQfChunkVecs = 1024;  // 16 KB per bulk copy
-constexpr int kQfChunks = 12;
+constexpr int kQfChunks = 14;
 constexpr int kQfSmemVecs = kQfChunkVecs * kQfChunks;
 constexpr int kQfSmemBytes = kQfSmemVecs * 16;
+
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint4 ld_nc_hint(const uint4* p, uint64_t pol) {
+  uint4 r;
+  asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p), "l"(pol));
+  return r;
+}
+__device__ __forceinline__ void st_v2_hint(void* p, uint32_t a, uint32_t b, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.v2.b32 [%0], {%1, %2}, %3;" ::"l"(p), "r"(a), "r"(b), "l"(pol) : "memory");
+}
+__device__ __forceinline__ void bulk_load_hint(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar,
+                                               uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
 
 __device__ __forceinline__ uint32_t pack8_e4m3(const uint4 a, float inv, uint32_t& hi_word) {
   const uint32_t w[4] = {a.x, a.y, a.z, a.w};
@@ -278,14 +323,17 @@ __global__ void __launch_bounds__(kQfThreads, 1) quant_act_single_pass_kernel(co
   extern __shared__ __align__(16) uint4 stage[];
   __shared__ __align__(8) uint64_t bars[kQfChunks];
   __shared__ int abort_cta;
+  __shared__ uint32_t amax_all;
   const int64_t nvec = n >> 3;
   const int64_t chunk = (nvec + gridDim.x - 1) / gridDim.x;
   const int64_t v0 = min(nvec, static_cast<int64_t>(blockIdx.x) * chunk);
   const int64_t v1 = min(nvec, v0 + chunk);
   const int64_t cnt = v1 - v0;
   const int64_t nkeep = min(cnt, static_cast<int64_t>(kQfSmemVecs));
+  const bool has_rem = cnt > nkeep;
   const int nch = static_cast<int>((nkeep + kQfChunkVecs - 1) / kQfChunkVecs);
-  const uint4* xv = reinterpret_cast<const uint4*>(x);
+  const uint4* xv = reinterpret_cast<const uint4*>(x) + v0;
+  const uint64_t pol_once = l2_evict_first_policy();
   if (threadIdx.x == 0) {
     abort_cta = 0;
     for (int c = 0; c < nch; ++c) mbar_init(&bars[c], 1);
@@ -294,12 +342,26 @@ __global__ void __launch_bounds__(kQfThreads, 1) quant_act_single_pass_kernel(co
       const int64_t a = static_cast<int64_t>(c) * kQfChunkVecs;
       const uint32_t bytes = static_cast<uint32_t>(min(static_cast<int64_t>(kQfChunkVecs), nkeep - a) * 16);
       mbar_arrive_expect_tx(&bars[c], bytes);
-      bulk_load(stage + a, xv + v0 + a, bytes, &bars[c]);
+      bulk_load_hint(stage + a, xv + a, bytes, &bars[c], pol_once);
     }
   }
   __syncthreads();
-  // phase 1: amax of the slice (bf16 |x| as halfword maxima)
+  // phase 1: amax of the slice (bf16 |x| as halfword maxima); the remainder beyond
+  // shared memory first, so its loads overlap the bulk copies in flight
   uint32_t m2 = 0;
+  if (has_rem) {
+    const uint64_t pol_keep = l2_evict_last_policy();
+    for (int64_t base = nkeep; base < cnt; base += 8 * kQfThreads) {
+      uint4 r[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int64_t i = base + k * kQfThreads + threadIdx.x;
+        r[k] = i < cnt ? ld_nc_hint(xv + i, pol_keep) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m2 = absmax8(m2, r[k]);
+    }
+  }
   bool ok = true;
   for (int c = 0; c < nch && ok; ++c) {
     ok = mbar_wait(&bars[c], 0, &abort_cta, nullptr);
@@ -307,69 +369,85 @@ __global__ void __launch_bounds__(kQfThreads, 1) quant_act_single_pass_kernel(co
     const int64_t b = min(a + kQfChunkVecs, nkeep);
     for (int64_t i = a + threadIdx.x; ok && i < b; i += kQfThreads) m2 = absmax8(m2, stage[i]);
   }
-  // the part of the slice beyond shared memory: 8 loads per thread in flight
-  for (int64_t base = nkeep; ok && base < cnt; base += 8 * kQfThreads) {
-    uint4 r[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int64_t i = base + k * kQfThreads + threadIdx.x;
-      r[k] = i < cnt ? __ldg(xv + v0 + i) : make_uint4(0u, 0u, 0u, 0u);
-    }
-#pragma unroll
-    for (int k = 0; k < 8; ++k) m2 = absmax8(m2, r[k]);
-  }
   if (blockIdx.x == 0)  // the n % 8 tail elements
     for (int64_t i = (nvec << 3) + threadIdx.x; i < n; i += kQfThreads)
       m2 = __vmaxu2(m2, static_cast<uint32_t>(x[i] & 0x7FFFu));
-  const uint32_t m = block_max_u32(max(m2 & 0xFFFFu, m2 >> 16));
+  uint32_t m = block_max_u32(max(m2 & 0xFFFFu, m2 >> 16)) << 16;
   if (threadIdx.x == 0) {
-    // release/acquire at GPU scope order the amax update before the arrival and the
-    // arrival before the flag, without full fences
-    if (m != 0u) atomicMax(&ws->amax_bits, m << 16);
-    uint32_t prev;
-    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(&ws->arrived) : "memory");
-    if (prev == gridDim.x - 1) asm volatile("st.release.gpu.global.u32 [%0], 1;" ::"l"(&ws->go) : "memory");
-    // grid barrier: every CTA is resident (cooperative launch); the wait is bounded
-    const uint64_t t0 = globaltimer();
-    for (uint32_t it = 0;; ++it) {
-      uint32_t go;
-      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(go) : "l"(&ws->go) : "memory");
-      if (go) break;
-      if ((it & 255u) == 255u && globaltimer() - t0 > QIK_WAIT_NS) {
-        abort_cta = 1;
-        break;
+    if (abort_cta) m = kQuantAbortMark;  // a chunk never landed: poison the amax
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(&ws->partial[blockIdx.x]), "r"(m) : "memory");
+    // the arrival releases the slot write; the last arrival acquires every earlier one
+    // (they form one release sequence) and publishes the next generation
+    unsigned long long old;
+    asm volatile("atom.add.acq_rel.gpu.global.u64 %0, [%1], 1;" : "=l"(old) : "l"(&ws->bar) : "memory");
+    const uint32_t gen = static_cast<uint32_t>(old >> 32);
+    if (static_cast<uint32_t>(old) == gridDim.x - 1) {
+      const unsigned long long step = (1ull << 32) - gridDim.x;  // generation + 1, arrivals back to 0
+      asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(&ws->bar), "l"(step) : "memory");
+    } else {
+      // grid barrier: every CTA is resident (cooperative launch); the wait is bounded
+      const uint64_t t0 = globaltimer();
+      for (uint32_t it = 0;; ++it) {
+        unsigned long long cur;
+        asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(cur) : "l"(&ws->bar) : "memory");
+        if (static_cast<uint32_t>(cur >> 32) != gen) break;
+        if ((it & 255u) == 255u && globaltimer() - t0 > QIK_WAIT_NS) {
+          abort_cta = 1;
+          break;
+        }
       }
     }
   }
   __syncthreads();
-  if (abort_cta) {  // a chunk or the grid barrier gave up
+  if (threadIdx.x < 32) {  // the global amax from every CTA's slot
+    uint32_t g = 0;
+    for (uint32_t i = threadIdx.x; i < gridDim.x; i += 32) {
+      uint32_t v;
+      asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(&ws->partial[i]) : "memory");
+      g = max(g, v);
+    }
+    g = __reduce_max_sync(0xffffffffu, g);
+    if (threadIdx.x == 0) amax_all = abort_cta ? kQuantAbortMark : g;
+  }
+  __syncthreads();
+  if (amax_all == kQuantAbortMark) {  // some CTA's copy or barrier wait gave up
     if (blockIdx.x == 0 && threadIdx.x == 0) scale_out[0] = __int_as_float(0x7fc00000);
     return;
   }
-  // phase 2: scale from the complete amax, codes from smem (or re-read past its capacity)
-  __shared__ uint32_t amax_all;
-  if (threadIdx.x == 0)
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(amax_all) : "l"(&ws->amax_bits) : "memory");
-  __syncthreads();
+  // phase 2: scale from the complete amax, codes from shared memory (the remainder
+  // re-read, from L2 while it is there)
   const float s = scale_from_amax_bits(amax_all);
   const float inv = act_inverse(s);
   if (blockIdx.x == 0 && threadIdx.x == 0) scale_out[0] = s;
-  uint2* qv = reinterpret_cast<uint2*>(q);
-  for (int64_t base = 0; base < cnt; base += 4 * kQfThreads) {
-    uint4 a[4];
+  uint2* qv = reinterpret_cast<uint2*>(q) + v0;
+  if (has_rem) {
+    for (int64_t base = nkeep; base < cnt; base += 8 * kQfThreads) {
+      uint4 r[8];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int64_t i = base + k * kQfThreads + threadIdx.x;
-      a[k] = i < nkeep ? stage[i] : (i < cnt ? __ldg(xv + v0 + i) : make_uint4(0u, 0u, 0u, 0u));
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int64_t i = base + k * kQfThreads + threadIdx.x;
-      if (i < cnt) {
-        uint32_t hi;
-        const uint32_t lo = pack8_e4m3(a[k], inv, hi);
-        qv[v0 + i] = make_uint2(lo, hi);
+      for (int k = 0; k < 8; ++k) {
+        const int64_t i = base + k * kQfThreads + threadIdx.x;
+        r[k] = i < cnt ? ld_nc_hint(xv + i, pol_once) : make_uint4(0u, 0u, 0u, 0u);
       }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int64_t i = base + k * kQfThreads + threadIdx.x;
+        if (i < cnt) {
+          uint32_t hi;
+          const uint32_t lo = pack8_e4m3(r[k], inv, hi);
+          st_v2_hint(qv + i, lo, hi, pol_once);
+        }
+      }
+    }
+    for (int64_t i = threadIdx.x; i < nkeep; i += kQfThreads) {
+      uint32_t hi;
+      const uint32_t lo = pack8_e4m3(stage[i], inv, hi);
+      st_v2_hint(qv + i, lo, hi, pol_once);
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < nkeep; i += kQfThreads) {
+      uint32_t hi;
+      const uint32_t lo = pack8_e4m3(stage[i], inv, hi);
+      qv[i] = make_uint2(lo, hi);
     }
   }
   if (blockIdx.x == 0)
@@ -379,24 +457,28 @@ __global__ void __launch_bounds__(kQfThreads, 1) quant_act_single_pass_kernel(co
     }
 }
 
-// Cooperative launch of the single-pass quantizer over ws (cleared here, 16 bytes).
+// Cooperative launch of the single-pass quantizer.  ws->bar must hold a consistent
+// barrier state (zero once, then as each call leaves it); clear_bar zeroes it on the
+// stream first (for callers that cannot keep the workspace between calls).
 int launch_quant_single_pass(const void* x, int64_t n, uint8_t* q, float* scale_out, QuantWs* ws,
-                             cudaStream_t st, bool ws_zeroed) {
-  static bool attr_set[64] = {false};
+                             cudaStream_t st, bool clear_bar) {
+  static std::once_flag attr_once[64];
   int dev = 0;
   QIK_TRY_CUDA(cudaGetDevice(&dev));
-  if (dev < 64 && !attr_set[dev]) {
-    QIK_TRY_CUDA(cudaFuncSetAttribute(quant_act_single_pass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      kQfSmemBytes));
-    attr_set[dev] = true;
-  }
+  QIK_REQUIRE(dev >= 0 && dev < 64, "qik_quantize_act: device ordinal %d out of range", dev);
+  cudaError_t attr_rc = cudaSuccess;
+  std::call_once(attr_once[dev], [&] {
+    attr_rc = cudaFuncSetAttribute(quant_act_single_pass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   kQfSmemBytes);
+  });
+  QIK_TRY_CUDA(attr_rc);
   const int64_t nvec = n >> 3;
   int64_t grid = (nvec + 4 * kQfThreads - 1) / (4 * kQfThreads);
-  const int64_t sms = sm_count();
+  const int64_t sms = min(static_cast<int64_t>(sm_count()), static_cast<int64_t>(kQuantMaxCtas));
   grid = grid < 1 ? 1 : (grid > sms ? sms : grid);
   const int64_t chunk = (nvec + grid - 1) / grid;
   const size_t smem = static_cast<size_t>(chunk < kQfSmemVecs ? chunk : kQfSmemVecs) * 16;
-  if (!ws_zeroed) QIK_TRY_CUDA(cudaMemsetAsync(ws, 0, sizeof(QuantWs), st));
+  if (clear_bar) QIK_TRY_CUDA(cudaMemsetAsync(&ws->bar, 0, sizeof(ws->bar), st));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(kQfThreads);
@@ -476,18 +558,22 @@ int qik_quantize_act_from_amax(const void* x, int64_t n, const uint32_t* amax_bi
   return launch_pack_act(x, n, amax_bits, q, scale_out, static_cast<cudaStream_t>(stream), false);
 }
 
+static int quantize_act_impl(const void* x, int64_t n, uint8_t* q, float* scale_out, void* ws, cudaStream_t st,
+                             bool clear_bar) {
+  QuantWs* w = static_cast<QuantWs*>(ws);
+  // one pass over HBM (16-byte aligned operands); otherwise an amax pass then a pack pass
+  if (aligned16(x) && aligned16(q) && aligned16(ws)) return launch_quant_single_pass(x, n, q, scale_out, w, st, clear_bar);
+  QIK_TRY_CUDA(cudaMemsetAsync(&w->amax_bits, 0, sizeof(uint32_t), st));
+  int rc = launch_amax(x, QIK_DTYPE_BF16, n, &w->amax_bits, st, false);
+  if (rc) return rc;
+  return launch_pack_act(x, n, &w->amax_bits, q, scale_out, st, false);
+}
+
 int qik_quantize_act(const void* x, int64_t n, uint8_t* q, float* scale_out, void* ws, void* stream) {
   QIK_REQUIRE(ws && scale_out, "qik_quantize_act: ws/scale_out is NULL");
   QIK_REQUIRE((x && q) || n == 0, "qik_quantize_act: x/q is NULL");
   QIK_REQUIRE(n >= 0, "qik_quantize_act: negative n");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  QuantWs* w = static_cast<QuantWs*>(ws);
-  // one pass over HBM (16-byte aligned operands); otherwise an amax pass then a pack pass
-  if (aligned16(x) && aligned16(q) && aligned16(ws)) return launch_quant_single_pass(x, n, q, scale_out, w, st, false);
-  QIK_TRY_CUDA(cudaMemsetAsync(w, 0, sizeof(QuantWs), st));
-  int rc = launch_amax(x, QIK_DTYPE_BF16, n, &w->amax_bits, st, false);
-  if (rc) return rc;
-  return qik_quantize_act_from_amax(x, n, &w->amax_bits, q, scale_out, stream);
+  return quantize_act_impl(x, n, q, scale_out, ws, static_cast<cudaStream_t>(stream), false);
 }
 
 int qik_quantize_weight(const void* w, int dtype, int64_t n, uint8_t* q, float* scale_out, void* ws, void* stream) {
@@ -581,6 +667,7 @@ extern "C" int qik_quantize_act_noalloc(const void* x, int64_t n, uint8_t* q, fl
   void* ws = nullptr;
   const int rc = qik::noalloc_scratch_ptr(&ws);
   if (rc) return rc;
-  // qik_quantize_act clears the amax word on the stream before accumulating.
-  return qik_quantize_act(x, n, q, scale_out, ws, stream);
+  // The barrier word is cleared on the stream at the start of every call, so a call
+  // that failed earlier leaves nothing behind; the per-CTA slots need no clearing.
+  return quantize_act_impl(x, n, q, scale_out, ws, static_cast<cudaStream_t>(stream), true);
 }

@@ -150,3 +150,25 @@ def device_status(device: torch.device | None = None) -> int:
     """Read (synchronizing) the device status word; 0 means no kernel gave up a wait."""
     dev = device or torch.device("cuda", torch.cuda.current_device())
     return int(status_word(dev)[0].item())
+
+
+_quant_state: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def quant_state(device: torch.device, stream: int | None = None) -> torch.Tensor:
+    """The workspace qik_quantize_act keeps between calls, one per (device, stream):
+    zeroed when first made, then passed to every call on that stream (each completed
+    call leaves its grid-barrier state ready for the next, so no call clears it)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx, stream_ptr(torch.device("cuda", idx)) if stream is None else stream)
+    t = _quant_state.get(key)
+    if t is None:
+        t = torch.zeros(load().qik_quant_workspace_bytes(), dtype=torch.uint8, device=torch.device("cuda", idx))
+        _quant_state[key] = t
+    return t
+
+
+def reset_quant_state() -> None:
+    """Zero every cached quantizer workspace (needed after a call that failed)."""
+    for t in _quant_state.values():
+        t.zero_()

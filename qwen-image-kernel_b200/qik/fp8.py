@@ -25,7 +25,9 @@ FP8_E4M3_MAX = 448.0
 
 
 def _ws(device: torch.device) -> torch.Tensor:
-    return torch.empty(16, dtype=torch.uint8, device=device)
+    """Scratch for the calls that clear what they use on every call (compute_scale,
+    quantize_weight_tensorwise)."""
+    return torch.empty(L.load().qik_quant_workspace_bytes(), dtype=torch.uint8, device=device)
 
 
 def _dtype_code(t: torch.Tensor) -> int:
@@ -65,8 +67,9 @@ def quantize_tensorwise(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     q = torch.empty(x.shape, dtype=torch.float8_e4m3fn, device=x.device)
     s = torch.empty(1, dtype=torch.float32, device=x.device)
     with torch.cuda.device(x.device):
+        stream = L.stream_ptr()
         L.check(lib.qik_quantize_act(xc.data_ptr(), xc.numel(), q.data_ptr(), s.data_ptr(),
-                                     _ws(x.device).data_ptr(), L.stream_ptr()), "qik_quantize_act")
+                                     L.quant_state(x.device, stream).data_ptr(), stream), "qik_quantize_act")
     return q, s
 
 

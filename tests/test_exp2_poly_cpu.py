@@ -1,6 +1,6 @@
 """The FMA-pipe 2^x of the attention softmax (exp2_poly2 in csrc/qik_device.cuh).
 
-* Its cubic's coefficients are the ones csrc/exp2_poly.py fits (float32 literals).
+* Its cubic's coefficients are the ones tests/exp2_poly.py fits (float32 literals).
 * Its steps, restated in float32 numpy (round-to-nearest shifter, exact reduction,
   Horner with fused multiply-adds, integer exponent add), stay within 7.6e-5
   relative of 2^x on [-125, 8] -- below half a bf16 ulp (2^-9) of P.
@@ -19,7 +19,7 @@ CSRC = ROOT / "qwen-image-kernel_b200" / "csrc"
 
 
 def _fit_module():
-    spec = importlib.util.spec_from_file_location("exp2_poly", CSRC / "exp2_poly.py")
+    spec = importlib.util.spec_from_file_location("exp2_poly", Path(__file__).resolve().parent / "exp2_poly.py")
     m = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(m)
     return m

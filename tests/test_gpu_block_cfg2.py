@@ -1,0 +1,174 @@
+"""BASELINE configs[2] at full size: the DiT block at 1024 px with CFG batch 2
+(M = 2 x 4352 token rows, width 3072, 24 heads of 128) through the product API
+(qik.processors.QwenImage21KernelBlock.forward), checked stage by stage against the
+CPU oracle on the product's own intermediates.
+
+Every kernel call the block makes is recorded (inputs and output) by wrapping the
+module-level functions qik.processors calls; each recorded stage is then recomputed by
+the oracle from the recorded inputs:
+
+* fused LayerNorm + modulate, RMSNorm + RoPE, gated residual, SwiGLU: the fused-op
+  gate of test_gpu_fused.py (<= 0.5% of outputs differ, none by more than 2^-6 of the
+  largest output, relF <= 1e-3), and each amax output equal to the max |output|;
+* every FP8 linear: its bf16 output within max-abs 2e-2 + half a bf16 ulp and relF
+  <= 5e-3 of the fp32 dequant oracle on the same input, quantized by the oracle
+  (bit-exact with the product's quantizer, tested elsewhere) with the amax the
+  product's producer handed over;
+* the attention: max-abs <= 2e-2 and relF <= 5e-3 against the fp32 oracle on the q /
+  k / v the processor passed, all 48 (sample, head) pairs.
+
+The structure is the reference block's (processors.py:129-187): fused QKV 3072 -> 9216,
+out-projection 3072 -> 3072, SwiGLU MLP with its fused up projection at BASELINE's
+3072 -> 12288 and 6144 -> 3072 down.
+"""
+import numpy as np
+import pytest
+import torch
+import torch.nn as nn
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+H, D, K, HALF, B, S = 24, 128, 3072, 6144, 2, 4352
+LIN_MAX_ABS, LIN_RELF = 2e-2, 5e-3
+
+
+class _Attn(nn.Module):
+    def __init__(self, fused_qkv, to_out, wq, wk):
+        super().__init__()
+        self.heads = H
+        self.fused_qkv = fused_qkv
+        self.norm_q = nn.RMSNorm(D, eps=1e-6)
+        self.norm_k = nn.RMSNorm(D, eps=1e-6)
+        with torch.no_grad():
+            self.norm_q.weight.copy_(wq)
+            self.norm_k.weight.copy_(wk)
+        self.to_out = nn.ModuleList([to_out, nn.Identity()])
+        self.processor = None
+
+    def set_processor(self, p):
+        self.processor = p
+
+    def forward(self, hidden_states, **kw):
+        return self.processor(self, hidden_states, **kw)
+
+
+def _lin(g, n_out, n_in, bias):
+    from qik.fp8 import FP8Linear, quantize_weight_tensorwise
+    f = FP8Linear(n_in, n_out, bias=bias).cuda()
+    wq, sw = quantize_weight_tensorwise(torch.randn(n_out, n_in, device="cuda", generator=g) * 0.02)
+    f.weight.copy_(wq)
+    f.weight_scale.copy_(sw)
+    if bias:
+        f.bias.copy_((torch.randn(n_out, device="cuda", generator=g) * 0.05).to(torch.bfloat16))
+    return f
+
+
+@pytest.fixture
+def recorder(monkeypatch):
+    """Wraps the kernels qik.processors calls and records (name, inputs, output)."""
+    import qik.processors as PR
+    calls = []
+    cpu = lambda t: t.detach().cpu() if isinstance(t, torch.Tensor) else t  # noqa: E731
+
+    def wrap(name, fn):
+        def inner(*a, **kw):
+            out = fn(*a, **kw)
+            rec = {"name": name, "args": [cpu(x) for x in a], "kw": {k: cpu(v) for k, v in kw.items()}}
+            if name == "linear":
+                rec["mod"] = a[0]
+            torch.cuda.synchronize()
+            rec["out"] = cpu(out)
+            for k in ("amax_out",):
+                if isinstance(kw.get(k), torch.Tensor):
+                    rec["kw"][k] = kw[k].detach().cpu()
+            calls.append(rec)
+            return out
+        return inner
+
+    for name, attr in (("ln_mod", "fused_layer_norm_modulate"), ("rms_rope", "fused_rms_norm_rope"),
+                       ("gate_res", "fused_gate_residual"), ("swiglu", "fused_swiglu"),
+                       ("attention", "block_causal_flash_attention"), ("linear", "_linear")):
+        monkeypatch.setattr(PR, attr, wrap(name, getattr(PR, attr)))
+    return calls
+
+
+def _fused_gate(out, ref, tag):
+    o, r = out.float(), ref.float()
+    diff = (o - r).abs()
+    frac = (diff > 0).float().mean().item()
+    top = r.abs().max().item()
+    relf = O.relf(o, r)
+    print(f"{tag}: mismatch {frac:.2e} max-abs {diff.max().item():.3e} relF {relf:.2e}")
+    assert frac <= 5e-3 and diff.max().item() <= top * 2.0 ** -6 and relf <= 1e-3, tag
+
+
+def _amax_bits_of(t):
+    return int(np.array([t.float().abs().max().item()], np.float32).view(np.int32)[0])
+
+
+def test_dit_block_cfg2_full_size_stage_by_stage(recorder):
+    from qik.processors import QwenImage21KernelBlock, QwenImage21KernelProcessor
+    torch.backends.cuda.matmul.allow_tf32 = False
+    g = torch.Generator(device="cuda").manual_seed(2024)
+    attn = _Attn(_lin(g, 3 * K, K, True), _lin(g, K, K, True),
+                 1.0 + 0.2 * torch.randn(D, device="cuda", generator=g),
+                 1.0 + 0.2 * torch.randn(D, device="cuda", generator=g))
+    attn.set_processor(QwenImage21KernelProcessor())
+    shell = nn.Module()
+    shell.img_norm1 = nn.LayerNorm(K, elementwise_affine=False, eps=1e-6)
+    shell.img_norm2 = nn.LayerNorm(K, elementwise_affine=False, eps=1e-6)
+    shell.attn = attn
+    shell.img_mlp = nn.Module()
+    shell.img_mlp.fused_up = _lin(g, 2 * HALF, K, False)
+    shell.img_mlp.out = _lin(g, K, HALF, False)
+    block = QwenImage21KernelBlock(shell)
+    x = torch.randn(B, S, K, device="cuda", generator=g).to(torch.bfloat16)
+    mod = (torch.randn(B, 4 * K, device="cuda", generator=g) * 0.3).to(torch.bfloat16)
+    inv = 1.0 / (10000 ** (torch.arange(0, D, 2, device="cuda").float() / D))
+    freqs = torch.polar(torch.ones(S, D // 2, device="cuda"), torch.outer(torch.arange(S, device="cuda").float(), inv))
+    out = block(x, mod, rotary_emb=freqs, segments=[(0, 256, True)])
+    torch.cuda.synchronize()
+    names = [c["name"] for c in recorder]
+    assert names == ["ln_mod", "linear", "rms_rope", "rms_rope", "attention", "linear", "gate_res", "ln_mod",
+                     "linear", "swiglu", "linear", "gate_res"], names
+    assert recorder[-1]["out"].shape == (B, S, K) and torch.equal(recorder[-1]["out"], out.cpu())
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    cos, sin = freqs.real.float().cpu(), freqs.imag.float().cpu()
+    for i, c in enumerate(recorder):
+        a, kw, o = c["args"], c["kw"], c["out"]
+        tag = f"stage {i} {c['name']}"
+        if c["name"] == "ln_mod":
+            xin, m, off = a[0], a[1], a[2]
+            _fused_gate(o, O.layer_norm_modulate(xin, m, off, a[4], a[5]), tag)
+            assert int(kw["amax_out"][0]) == _amax_bits_of(o), tag
+        elif c["name"] == "rms_rope":
+            _fused_gate(o, O.rms_norm_rope(a[0], a[1], cos, sin, a[3]), tag)
+        elif c["name"] == "gate_res":
+            _fused_gate(o, O.gate_residual(a[0], a[1], a[2], a[3], a[4]), tag)
+        elif c["name"] == "swiglu":
+            _fused_gate(o, O.swiglu(a[0], a[1]), tag)
+            assert int(kw["amax_out"][0]) == _amax_bits_of(o), tag
+        elif c["name"] == "linear":
+            lin, xin, amax = c["mod"], a[1], a[2]
+            x2 = xin.reshape(-1, xin.shape[-1]).contiguous()
+            if amax is not None:  # the producer's amax is max|x| itself
+                assert int(amax[0]) == _amax_bits_of(x2), tag
+            q, s = O.quantize_act(x2)
+            ref = O.fp8_linear(q, s, lin.weight.cpu(), float(lin.weight_scale.item()),
+                               None if lin.bias is None else lin.bias.cpu())
+            y = o.reshape(-1, o.shape[-1]).float()
+            d = ((y - ref).abs() - 0.5 * O.bf16_ulp(ref)).max().item()
+            r = O.relf(y, ref)
+            print(f"{tag}: {tuple(x2.shape)} -> {y.shape[-1]}: max-abs over half an ulp {d:.3e} relF {r:.3e}")
+            assert d <= LIN_MAX_ABS and r <= LIN_RELF, tag
+        elif c["name"] == "attention":
+            q, k, v, L, kv = a[0], a[1], a[2], a[3], a[4]
+            ref = O.block_causal_attention(q, k, v, L, kv, out_dtype=torch.float32)
+            d = (o.float() - ref).abs().max().item()
+            r = O.relf(o, ref)
+            print(f"{tag}: max-abs {d:.3e} relF {r:.3e}")
+            assert d <= 2e-2 and r <= 5e-3, tag
+            if isinstance(kw.get("amax_out"), torch.Tensor):
+                assert int(kw["amax_out"][0]) == _amax_bits_of(o), tag

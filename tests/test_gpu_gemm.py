@@ -113,6 +113,38 @@ def test_fp8_linear_parity(fp8, M, N, K):
     assert O.relf(y16.cpu(), x.float() @ w.float().t()) < 0.06
 
 
+CFG5_SHAPES = [(M, N) for N in (3072, 9216, 12288, 18432) for M in (256, 1024, 4352, 9472, 16384)]
+
+
+@pytest.mark.parametrize("M,N", CFG5_SHAPES)
+def test_gemm_cfg5_all_shapes(fp8, M, N):
+    """Every configs[4] shape (K = 3072): the fp32 (pre-cast) GEMM output of the
+    product's own e4m3 operands against the fp32 dequant product computed by plain
+    PyTorch on the GPU (TF32 off: an fp32 reference of the same op), max-abs <= 2e-2 and
+    relF <= 5e-3; the bf16 output is the kernel's fp32 result rounded.  The CPU oracle
+    pins the same computation at the configs[1] shape above."""
+    K = 3072
+    g = torch.Generator(device="cuda").manual_seed(M * 31 + N)
+    x = torch.randn(M, K, device="cuda", generator=g)
+    x[:, :8] *= 20.0
+    w = torch.randn(N, K, device="cuda", generator=g) * 0.02
+    xq, sx = fp8.quantize_tensorwise(x.to(torch.bfloat16))
+    wq, sw = fp8.quantize_weight_tensorwise(w.to(torch.bfloat16))
+    y32 = fp8.fp8_gemm(xq, sx, wq, sw, out_dtype=torch.float32)
+    y16 = fp8.fp8_gemm(xq, sx, wq, sw)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        ref = (xq.float() * sx) @ (wq.float() * sw).t()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    d = (y32 - ref).abs().max().item()
+    r = ((y32 - ref).norm() / ref.norm()).item()
+    print(f"M={M} N={N}: fp32 max-abs {d:.3e} relF {r:.3e}")
+    assert d <= MAX_ABS and r <= RELF
+    assert torch.equal(y16, y32.to(torch.bfloat16))
+
+
 def test_fp8_linear_bias_and_leading_dims(fp8):
     x = GI.randn_bf16(70, (2, 37, 512))
     w = GI.randn_bf16(71, (384, 512), 0.02)

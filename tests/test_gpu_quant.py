@@ -51,6 +51,24 @@ def test_quantize_act_ffn_hidden_size(fp8):
     _check_act(fp8, x)
 
 
+@pytest.mark.parametrize("M", [9472, 16384])
+def test_quantize_act_cfg5_rows(fp8, M):
+    """configs[4] row counts whose slices exceed shared memory: the remainder is read
+    twice (L2 hints), the bytes must not change."""
+    x = GI.outlier_activations(40 + M % 7, M, 3072)
+    _check_act(fp8, x)
+
+
+def test_quantize_act_state_reused_across_sizes(fp8):
+    """One cached workspace serves calls with different grid sizes in a row: each
+    call must leave the barrier ready for the next (no clearing between calls)."""
+    shapes = [(256, 3072), (16384, 3072), (1,), (4352, 3072), (33, 97), (1024, 3072)]
+    xs = [GI.randn_bf16(60 + i, sh, 0.5 + i) for i, sh in enumerate(shapes)]
+    for _ in range(2):
+        for x in xs:
+            _check_act(fp8, x)
+
+
 def test_quantize_act_zero_and_edge_values(fp8):
     _check_act(fp8, torch.zeros(1000, dtype=torch.bfloat16))         # amax 0 -> scale 1e-12
     x = GI.randn_bf16(9, (4096,))

@@ -3,7 +3,8 @@ cannot allocate device memory (plugin hosts and serving runtimes that give a ker
 only its inputs and outputs, or launch paths where cudaMalloc is not allowed).
 
 It is called through the C ABI (ctypes) twice in a row and compared with the
-ordinary entry point qik_quantize_act, which takes a caller-allocated workspace.
+ordinary entry point qik_quantize_act, which takes a caller-allocated workspace
+(zeroed before its first use, as that entry point requires).
 The quantizer's tolerance is exact: bytes and scale bits must be equal.  The second
 call uses an input with a much smaller amax than the first, so a scratch amax word
 left over from the first call would show up as a wrong scale.
@@ -25,7 +26,7 @@ pytestmark = pytest.mark.gpu
 def _reference_call(lib, x):
     q = torch.empty(x.shape, dtype=torch.float8_e4m3fn, device=x.device)
     s = torch.empty(1, dtype=torch.float32, device=x.device)
-    ws = torch.empty(lib.qik_quant_workspace_bytes(), dtype=torch.uint8, device=x.device)
+    ws = torch.zeros(lib.qik_quant_workspace_bytes(), dtype=torch.uint8, device=x.device)
     rc = lib.qik_quantize_act(ctypes.c_void_p(x.data_ptr()), x.numel(), ctypes.c_void_p(q.data_ptr()),
                               ctypes.c_void_p(s.data_ptr()), ctypes.c_void_p(ws.data_ptr()),
                               ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
