@@ -945,11 +945,13 @@ def run_reference(args, rank: int, world: int) -> dict | None:
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
-def sweep(device: torch.device, iters: int = 20) -> list[dict]:
+def sweep(device: torch.device, iters: int = 20, tiles: bool = False) -> list[dict]:
     """the FP8 linear at K = 3072 over N x M, qik's tcgen05 GEMM
     next to cuBLASLt (torch._scaled_mm, the reference's call, fp8.py:87-88) on the same
     e4m3 operands and scales, and the dynamic activation quantizer at each M
-    (3 algorithmic bytes per element).  One JSON line per shape."""
+    (3 algorithmic bytes per element).  One JSON line per shape.  With ``tiles`` every
+    GEMM tile configuration is also timed forced (qik_fp8_gemm_tiled), and the FFN's
+    second GEMM (4352 x 3072, K = 12288) is added."""
     from qik import fp8 as F
     stream = torch.cuda.current_stream(device)
     flush = L2Flush(device)
@@ -957,32 +959,44 @@ def sweep(device: torch.device, iters: int = 20) -> list[dict]:
     g = torch.Generator(device=device).manual_seed(5)
     K = 3072
     rows = []
-    for N in (3072, 9216, 12288, 18432):
-        wq, sw = F.quantize_weight_tensorwise(torch.randn(N, K, device=device, generator=g) * 0.02)
-        for M in (256, 1024, 4352, 9472, 16384):
-            x = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
-            xq, sx = F.quantize_tensorwise(x)
-            runs = {"qik": lambda: F.fp8_gemm(xq, sx, wq, sw),
-                    "cublaslt": lambda: torch._scaled_mm(xq, wq.t(), scale_a=sx, scale_b=sw,
-                                                         out_dtype=torch.bfloat16)}
-            row = {"M": M, "N": N, "K": K, "gflop": round(2.0 * M * N * K / 1e9, 2)}
-            for name, fn in runs.items():
-                for _ in range(3):
-                    fn()
-                ms = _time_ms(fn, iters, flush, stream)
-                row[f"{name}_us"] = round(ms * 1e3, 2)
-                row[f"{name}_tflops"] = round(2.0 * M * N * K / ms / 1e9, 1)
-            row["qik_vs_cublaslt"] = round(row["cublaslt_us"] / row["qik_us"], 3)
-            row["qik_frac_fp8_peak"] = round(row["qik_tflops"] / pk["fp8_tflops_burst"], 3)
-            if N == 3072:
-                fn = lambda: F.quantize_tensorwise(x)  # noqa: E731
-                for _ in range(3):
-                    fn()
-                ms = _time_ms(fn, iters, flush, stream)
-                row["quantizer_us"] = round(ms * 1e3, 2)
-                row["quantizer_gbs"] = round(3.0 * M * K / ms / 1e6, 1)
-                row["quantizer_frac_hbm"] = round(row["quantizer_gbs"] / pk["hbm_gbs"], 3)
-            rows.append(row)
+    from qik import _lib as L
+    tile_names = {L.GEMM_TILE_PAIR_256: "pair256", L.GEMM_TILE_SINGLE_256: "single256",
+                  L.GEMM_TILE_SINGLE_128: "single128", L.GEMM_TILE_SINGLE_64: "single64"}
+    shapes = [(M, N, K) for N in (3072, 9216, 12288, 18432) for M in (256, 1024, 4352, 9472, 16384)]
+    if tiles:
+        shapes.append((4352, 3072, 12288))
+    weights = {}
+    for M, N, Kx in shapes:
+        if (N, Kx) not in weights:
+            weights[(N, Kx)] = F.quantize_weight_tensorwise(torch.randn(N, Kx, device=device, generator=g) * 0.02)
+        wq, sw = weights[(N, Kx)]
+        K = Kx
+        x = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
+        xq, sx = F.quantize_tensorwise(x)
+        runs = {"qik": lambda: F.fp8_gemm(xq, sx, wq, sw),
+                "cublaslt": lambda: torch._scaled_mm(xq, wq.t(), scale_a=sx, scale_b=sw,
+                                                     out_dtype=torch.bfloat16)}
+        if tiles:
+            for c, name in tile_names.items():
+                runs[name] = (lambda c=c: F.fp8_gemm(xq, sx, wq, sw, tile_cfg=c))
+        row = {"M": M, "N": N, "K": K, "gflop": round(2.0 * M * N * K / 1e9, 2)}
+        for name, fn in runs.items():
+            for _ in range(3):
+                fn()
+            ms = _time_ms(fn, iters, flush, stream)
+            row[f"{name}_us"] = round(ms * 1e3, 2)
+            row[f"{name}_tflops"] = round(2.0 * M * N * K / ms / 1e9, 1)
+        row["qik_vs_cublaslt"] = round(row["cublaslt_us"] / row["qik_us"], 3)
+        row["qik_frac_fp8_peak"] = round(row["qik_tflops"] / pk["fp8_tflops_burst"], 3)
+        if N == 3072 and K == 3072:
+            fn = lambda: F.quantize_tensorwise(x)  # noqa: E731
+            for _ in range(3):
+                fn()
+            ms = _time_ms(fn, iters, flush, stream)
+            row["quantizer_us"] = round(ms * 1e3, 2)
+            row["quantizer_gbs"] = round(3.0 * M * K / ms / 1e6, 1)
+            row["quantizer_frac_hbm"] = round(row["quantizer_gbs"] / pk["hbm_gbs"], 3)
+        rows.append(row)
     return rows
 
 
@@ -995,6 +1009,8 @@ def main() -> int:
     ap.add_argument("--no-extras", action="store_true", help="skip the attention / DiT-block measurements")
     ap.add_argument("--sweep", action="store_true",
                     help="print the configs[4] GEMM / quantizer sweep (one JSON line per shape) instead of the bench")
+    ap.add_argument("--sweep-tiles", action="store_true",
+                    help="--sweep with every GEMM tile configuration forced beside the default")
     ap.add_argument("--profile-case", choices=PROFILE_CASES,
                     help="run one extras workload three times and exit (the launches an ncu capture selects from)")
     args = ap.parse_args()
@@ -1015,8 +1031,8 @@ def main() -> int:
     if args.profile_case:
         profile_case(device, args.profile_case)
         return 0
-    if args.sweep:
-        for row in sweep(device):
+    if args.sweep or args.sweep_tiles:
+        for row in sweep(device, tiles=args.sweep_tiles):
             print(json.dumps(row), flush=True)
         return 0
     if world > 1:

@@ -145,6 +145,24 @@ int qik_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64
                  const float* scale_a, const float* scale_b, const void* bias, void* C, int64_t ldc, int out_dtype,
                  int epilogue, uint32_t* amax_out, int* status, void* stream);
 
+/* Tile configurations of the FP8 GEMM (qik_fp8_gemm_tiled). */
+#define QIK_GEMM_TILE_AUTO 0        /* the configuration qik_fp8_gemm picks for (M, N) */
+#define QIK_GEMM_TILE_PAIR_256 1    /* CTA pairs (cta_group::2), 256 x 256 tiles */
+#define QIK_GEMM_TILE_SINGLE_256 2  /* single CTAs, 128 x 256 tiles */
+#define QIK_GEMM_TILE_SINGLE_128 3  /* single CTAs, 128 x 128 tiles */
+#define QIK_GEMM_TILE_SINGLE_64 4   /* single CTAs, 128 x 64 tiles */
+
+/*
+ * qik_fp8_gemm with the tile configuration forced (QIK_GEMM_TILE_*; AUTO = what
+ * qik_fp8_gemm picks).  Every configuration computes the same result; this entry
+ * point exists for measurement and for tests that cover each configuration.  No
+ * counterpart in the reference (its GEMM is cuBLASLt's choice).
+ */
+int qik_fp8_gemm_tiled(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda,
+                       int64_t ldb, const float* scale_a, const float* scale_b, const void* bias, void* C,
+                       int64_t ldc, int out_dtype, int epilogue, uint32_t* amax_out, int tile_cfg, int* status,
+                       void* stream);
+
 /*
  * Bytes of workspace qik_fp8_ffn needs for an [M, K] input and a hidden width.
  */

@@ -21,7 +21,6 @@
 //     or (QIK_EPI_SCATTER) fp32 rows stored from the staging buffer straight into the
 //     owner rank's receive slot in peer memory, each finished tile counted there.
 // The epilogue of tile i overlaps the MMAs of tile i+1.
-#include <stdlib.h>
 #include <string.h>
 
 #include "qik_device.cuh"
@@ -65,6 +64,8 @@ struct GemmLayout {
   static constexpr int kBarOffset = kStageOutOffset + kGemmEpiWarps * 2 * kOutBufBytes;
   static constexpr int kBarBytes = (2 * STAGES + 4) * 8 + 16;
   static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;  // + alignment slack
+  // two accumulators of BN columns each (BN a power of two, as the TMEM allocation is)
+  static constexpr int kAccStride = BN;
   static constexpr int kTmemCols = 2 * BN;
 };
 
@@ -191,7 +192,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                 : mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.status);
         if (!got) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Lay::kAccStride);
         bool ok = true;
         for (int kb = 0; kb < num_k; ++kb) {
           const bool ready = TWO_SM ? mbar_wait_cluster(&full[stage], phase, abort_flag, p.status)
@@ -256,7 +257,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll 1
       for (int c = half; c < BN / 32; c += 2) {
         uint32_t r[32];
-        tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN + c * 32),
+        tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                      static_cast<uint32_t>(acc * Lay::kAccStride + c * 32),
                   r);
         const int col0 = nb * BN + c * 32;
         if (col0 >= p.N) continue;                    // warp-uniform
@@ -393,32 +395,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-// Tile configurations: CTA pairs with 256 x 256 tiles, or single CTAs with 128 x BN
-// tiles.  QIK_GEMM_CFG = "2sm" | "256" | "128" | "64" in the environment forces one of
-// them for every shape (a comparison switch for measurements; read once per process).
-enum GemmCfg { kCfgAuto = 0, kCfg2Sm, kCfg256, kCfg128, kCfg64 };
-static GemmCfg gemm_cfg_override() {
-  static const GemmCfg cfg = [] {
-    const char* v = getenv("QIK_GEMM_CFG");
-    if (!v) return kCfgAuto;
-    if (!strcmp(v, "2sm")) return kCfg2Sm;
-    if (!strcmp(v, "256")) return kCfg256;
-    if (!strcmp(v, "128")) return kCfg128;
-    if (!strcmp(v, "64")) return kCfg64;
-    return kCfgAuto;
-  }();
-  return cfg;
-}
-
-// Shape -> tile configuration, from the configs[4] sweep (K = 3072) with every
-// configuration forced in turn: CTA pairs win from M = 512 up and at M = 256 once
-// N >= 12288; at M = 256 with a narrower N, 128 x 128 single-CTA tiles (more CTAs on
-// the same work) win; below 128 rows a single 128-row tile spans M and the N tiles
-// spread the weight stream over the SMs.
-static GemmCfg gemm_pick_cfg(int64_t M, int64_t N) {
-  if (M > 2 * kGemmBM) return kCfg2Sm;
-  if (M > kGemmBM) return N >= 12288 ? kCfg2Sm : kCfg128;
-  return (N + 127) / 128 >= sm_count() / 2 ? kCfg128 : kCfg64;
+// Tile configurations (QIK_GEMM_TILE_* in qik.h): CTA pairs computing 256 x 256 tiles,
+// or single CTAs with 128 x BN tiles (BN = 256, 128 or 64).
+//
+// Shape -> tile configuration, from the configs[4] sweep with every configuration
+// forced: CTA pairs from M = 257 up, and at M = 129-256 once N >= 12288; at M = 129-256
+// with a narrower N, 128 x 128 single-CTA tiles (more CTAs on the same work) win; at
+// most 128 rows, a single 128-row tile spans M and the N tiles spread the weight
+// stream over the SMs.  Narrower CTA-pair tiles (256 x 240, 256 x 192), chosen to fill
+// the last wave that 256-wide tiles leave partly empty, were built and measured slower
+// at every configs[4] shape and at the FFN's (4352 x 12288: 120.7 and 139.3 us against
+// 116.4): a 240-wide tile took about as long as a 256-wide one, and 192-wide tiles read
+// ~17% more operand bytes per FLOP.
+static int gemm_pick_cfg(int64_t M, int64_t N) {
+  if (M > 2 * kGemmBM) return QIK_GEMM_TILE_PAIR_256;
+  if (M > kGemmBM) return N >= 12288 ? QIK_GEMM_TILE_PAIR_256 : QIK_GEMM_TILE_SINGLE_128;
+  return (N + 127) / 128 >= sm_count() / 2 ? QIK_GEMM_TILE_SINGLE_128 : QIK_GEMM_TILE_SINGLE_64;
 }
 
 template <int BN, int STAGES, bool TWO_SM>
@@ -481,7 +473,7 @@ static int launch_gemm(const uint8_t* A, const uint8_t* B, const GemmParams& p, 
 int launch_fp8_gemm_ex(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
                        const float* scale_a, const float* scale_b, const void* bias, void* C, int64_t ldc,
                        int out_dtype, int epilogue, uint32_t* amax_out, int* status, cudaStream_t stream, bool pdl,
-                       const GemmParams* scatter) {
+                       const GemmParams* scatter, int tile_cfg = QIK_GEMM_TILE_AUTO) {
   QIK_REQUIRE(M >= 0 && N >= 0 && K >= 0, "qik_fp8_gemm: negative size");
   if (M == 0 || N == 0) return QIK_OK;
   QIK_REQUIRE(K > 0, "qik_fp8_gemm: K must be positive");
@@ -517,17 +509,18 @@ int launch_fp8_gemm_ex(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N,
   p.epilogue = epilogue;
   p.amax_out = amax_out;
   p.status = status;
-  GemmCfg cfg = gemm_cfg_override();
-  if (cfg == kCfgAuto) cfg = gemm_pick_cfg(M, N);
+  const int cfg = tile_cfg == QIK_GEMM_TILE_AUTO ? gemm_pick_cfg(M, N) : tile_cfg;
   switch (cfg) {
-    case kCfg2Sm:
+    case QIK_GEMM_TILE_PAIR_256:
       return launch_gemm<256, 6, true>(A, B, p, lda, ldb, stream, pdl);
-    case kCfg128:
+    case QIK_GEMM_TILE_SINGLE_128:
       return launch_gemm<128, 6, false>(A, B, p, lda, ldb, stream, pdl);
-    case kCfg64:
+    case QIK_GEMM_TILE_SINGLE_64:
       return launch_gemm<64, 8, false>(A, B, p, lda, ldb, stream, pdl);
-    default:
+    case QIK_GEMM_TILE_SINGLE_256:
       return launch_gemm<256, 4, false>(A, B, p, lda, ldb, stream, pdl);
+    default:
+      return set_error(QIK_ERR_INVALID, "qik_fp8_gemm: unknown tile configuration %d", cfg);
   }
 }
 
@@ -535,7 +528,7 @@ int launch_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, in
                     const float* scale_a, const float* scale_b, const void* bias, void* C, int64_t ldc, int out_dtype,
                     int epilogue, uint32_t* amax_out, int* status, cudaStream_t stream, bool pdl) {
   return launch_fp8_gemm_ex(A, B, M, N, K, lda, ldb, scale_a, scale_b, bias, C, ldc, out_dtype, epilogue, amax_out,
-                            status, stream, pdl, nullptr);
+                            status, stream, pdl, nullptr, QIK_GEMM_TILE_AUTO);
 }
 
 }  // namespace qik
@@ -543,11 +536,11 @@ int launch_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, in
 namespace qik {
 // Tile height and width of the configuration launch_fp8_gemm picks for (M, N).
 static void gemm_tile_shape(int64_t M, int64_t N, int* tile_m, int* tile_n, int* ctas_per_tile) {
-  GemmCfg cfg = gemm_cfg_override();
-  if (cfg == kCfgAuto) cfg = gemm_pick_cfg(M, N);
-  *tile_m = cfg == kCfg2Sm ? 2 * kGemmBM : kGemmBM;
-  *tile_n = (cfg == kCfg2Sm || cfg == kCfg256) ? 256 : (cfg == kCfg128 ? 128 : 64);
-  *ctas_per_tile = cfg == kCfg2Sm ? 2 : 1;
+  const int cfg = gemm_pick_cfg(M, N);
+  const bool pair = cfg == QIK_GEMM_TILE_PAIR_256;
+  *tile_m = pair ? 2 * kGemmBM : kGemmBM;
+  *tile_n = (pair || cfg == QIK_GEMM_TILE_SINGLE_256) ? 256 : (cfg == QIK_GEMM_TILE_SINGLE_128 ? 128 : 64);
+  *ctas_per_tile = pair ? 2 : 1;
 }
 }  // namespace qik
 
@@ -595,4 +588,16 @@ extern "C" int qik_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64
                             void* stream) {
   return qik::launch_fp8_gemm(A, B, M, N, K, lda, ldb, scale_a, scale_b, bias, C, ldc, out_dtype, epilogue, amax_out,
                               status, static_cast<cudaStream_t>(stream), false);
+}
+
+extern "C" int qik_fp8_gemm_tiled(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda,
+                                  int64_t ldb, const float* scale_a, const float* scale_b, const void* bias, void* C,
+                                  int64_t ldc, int out_dtype, int epilogue, uint32_t* amax_out, int tile_cfg,
+                                  int* status, void* stream) {
+  QIK_REQUIRE(tile_cfg == QIK_GEMM_TILE_AUTO || tile_cfg == QIK_GEMM_TILE_PAIR_256 ||
+                  tile_cfg == QIK_GEMM_TILE_SINGLE_256 || tile_cfg == QIK_GEMM_TILE_SINGLE_128 ||
+                  tile_cfg == QIK_GEMM_TILE_SINGLE_64,
+              "qik_fp8_gemm_tiled: unknown tile configuration %d", tile_cfg);
+  return qik::launch_fp8_gemm_ex(A, B, M, N, K, lda, ldb, scale_a, scale_b, bias, C, ldc, out_dtype, epilogue,
+                                 amax_out, status, static_cast<cudaStream_t>(stream), false, nullptr, tile_cfg);
 }

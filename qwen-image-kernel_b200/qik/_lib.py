@@ -17,6 +17,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libqik.so"
 QIK_OK = 0
 DTYPE_BF16, DTYPE_F32, DTYPE_E4M3 = 0, 1, 2
 EPI_SCALE, EPI_GELU_TANH, EPI_SCATTER = 0, 1, 2
+GEMM_TILE_AUTO, GEMM_TILE_PAIR_256, GEMM_TILE_SINGLE_256, GEMM_TILE_SINGLE_128, GEMM_TILE_SINGLE_64 = range(5)
 TP_MAX_WORLD = 8
 ATTN_HAS_CACHE, ATTN_HAS_KEY_VALID, ATTN_UNIFORM, ATTN_V_FP8 = 1, 2, 4, 8
 STATUS_OK, STATUS_TIMEOUT = 0, 1
@@ -56,6 +57,8 @@ SIGNATURES = {
     "qik_quantize_weight": (_i32, [_vp, _i32, _i64, _vp, _vp, _vp, _vp]),
     "qik_fp8_gemm": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _vp,
                             _vp, _vp]),
+    "qik_fp8_gemm_tiled": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i32, _i32,
+                                  _vp, _i32, _vp, _vp]),
     "qik_fp8_ffn_workspace_bytes": (ctypes.c_size_t, [_i64, _i64, _i64]),
     "qik_fp8_ffn": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp,
                            _vp]),

@@ -123,13 +123,15 @@ def quantize_weight_tensorwise(w: torch.Tensor) -> tuple[torch.Tensor, torch.Ten
 def fp8_gemm(xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
              bias: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
              epilogue: int = L.EPI_SCALE, amax_out: torch.Tensor | None = None,
-             out: torch.Tensor | None = None) -> torch.Tensor:
+             out: torch.Tensor | None = None, tile_cfg: int = L.GEMM_TILE_AUTO) -> torch.Tensor:
     """y[M, N] = epilogue((xq . wq^T) * sx * sw (+ bias)) on the tensor core.
 
     xq [M, K] e4m3 (row pitch a multiple of 16 bytes), wq [N, K] e4m3, sx/sw fp32 [1]
     on the device, bias bf16 [N] or None.  out_dtype bf16, or fp32 for the pre-cast
     parity output.  ``amax_out`` (int32 [1], zeroed by the caller) receives the
-    amax of the bf16 output for the next dynamic quantization."""
+    amax of the bf16 output for the next dynamic quantization.  ``tile_cfg`` forces a
+    tile configuration (``qik._lib.GEMM_TILE_*``, for measurements and tests; the
+    result is the same)."""
     lib = L.load()
     if xq.dtype != torch.float8_e4m3fn or wq.dtype != torch.float8_e4m3fn:
         raise TypeError("qik.fp8_gemm: operands must be float8_e4m3fn")
@@ -146,11 +148,17 @@ def fp8_gemm(xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: torch.Ten
     if bias is not None:
         bias = bias.to(torch.bfloat16).contiguous()
     status = L.status_word(xq.device)
+    out_code = L.DTYPE_F32 if out.dtype == torch.float32 else L.DTYPE_BF16
     with torch.cuda.device(xq.device):
-        L.check(lib.qik_fp8_gemm(xq.data_ptr(), wq.data_ptr(), M, N, K, xq.stride(0), wq.stride(0), sx.data_ptr(),
-                                 sw.data_ptr(), L.ptr(bias), out.data_ptr(), out.stride(0),
-                                 L.DTYPE_F32 if out.dtype == torch.float32 else L.DTYPE_BF16, epilogue,
-                                 L.ptr(amax_out), status.data_ptr(), L.stream_ptr()), "qik_fp8_gemm")
+        if tile_cfg == L.GEMM_TILE_AUTO:
+            L.check(lib.qik_fp8_gemm(xq.data_ptr(), wq.data_ptr(), M, N, K, xq.stride(0), wq.stride(0), sx.data_ptr(),
+                                     sw.data_ptr(), L.ptr(bias), out.data_ptr(), out.stride(0), out_code, epilogue,
+                                     L.ptr(amax_out), status.data_ptr(), L.stream_ptr()), "qik_fp8_gemm")
+        else:
+            L.check(lib.qik_fp8_gemm_tiled(xq.data_ptr(), wq.data_ptr(), M, N, K, xq.stride(0), wq.stride(0),
+                                           sx.data_ptr(), sw.data_ptr(), L.ptr(bias), out.data_ptr(), out.stride(0),
+                                           out_code, epilogue, L.ptr(amax_out), tile_cfg, status.data_ptr(),
+                                           L.stream_ptr()), "qik_fp8_gemm_tiled")
     return out
 
 

@@ -48,6 +48,25 @@ def test_gemm_exact_small_ints(fp8, M, N, K):
     assert torch.equal(y.cpu(), ref)
 
 
+TILE_CFGS = [1, 2, 3, 4]   # qik._lib.GEMM_TILE_PAIR_256 .. GEMM_TILE_SINGLE_64
+
+
+@pytest.mark.parametrize("cfg", TILE_CFGS)
+@pytest.mark.parametrize("M,N,K", [(300, 736, 384), (600, 3072, 256), (4352, 3072, 512), (257, 1936, 128)])
+def test_gemm_every_tile_config_exact(fp8, cfg, M, N, K):
+    """Every tile configuration forced (qik_fp8_gemm_tiled), exact small-integer products,
+    fp32 and bf16 outputs, partial row and column tiles and a 16-column chunk at the
+    matrix edge (N = 736, 1936)."""
+    a = _e4m3_small_ints(M + 5 * K, (M, K)).cuda()
+    b = _e4m3_small_ints(N + 7 * K, (N, K)).cuda()
+    ref = a.cpu().float() @ b.cpu().float().t()
+    y = fp8.fp8_gemm(a, _one(), b, _one(), out_dtype=torch.float32, tile_cfg=cfg)
+    yb = fp8.fp8_gemm(a, _one(), b, _one(), tile_cfg=cfg)
+    torch.cuda.synchronize()
+    assert torch.equal(y.cpu(), ref)
+    assert torch.equal(yb.cpu(), ref.to(torch.bfloat16))
+
+
 def test_gemm_deterministic(fp8):
     """Repeated launches give bitwise-identical results (fixed schedule, no atomics)."""
     M, N, K = 640, 768, 6144

@@ -56,12 +56,21 @@ def lib():
 def test_scatter_signals_partition_the_tiles(lib, M, N, world):
     R = T.rows_per_owner(M, world)
     per_owner = [lib.qik_fp8_gemm_scatter_signals(M, N, R, o) for o in range(world)]
-    # M > 256 picks CTA pairs with 256 x 256 tiles: two arrivals per tile
-    tiles = -(-M // 256) * -(-N // 256)
-    assert sum(per_owner) == 2 * tiles
+    # M > 256 picks CTA pairs (two arrivals per tile) with 256-row tiles 256, 240 or 192
+    # wide: every owner counts its row tiles times the same number of column tiles
+    col_tiles = {-(-N // bn) for bn in (256, 240, 192)}
+    tn = None
     for o, n in enumerate(per_owner):
         rows = max(0, min(R, M - o * R))
-        assert n == 2 * -(-rows // 256) * -(-N // 256)
+        row_tiles = -(-rows // 256)
+        if row_tiles == 0:
+            assert n == 0
+            continue
+        assert n % (2 * row_tiles) == 0
+        tn = n // (2 * row_tiles) if tn is None else tn
+        assert n == 2 * row_tiles * tn
+    assert tn in col_tiles
+    assert sum(per_owner) == 2 * -(-M // 256) * tn
 
 
 def test_entry_points_validate_on_host(lib):
