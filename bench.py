@@ -602,15 +602,25 @@ def dit_block_product_case(device: torch.device, g: torch.Generator) -> dict:
 
 
 PROFILE_CASES = ("attention_cfg4_prefill", "attention_cfg4_decode_fp8_slab", "dit_block_1024px_cfg2",
-                 "dit_block_1024px_cfg2_gelu_ffn", "fused_ops_t2i", "modulation_linear")
+                 "dit_block_1024px_cfg2_gelu_ffn", "fused_ops_t2i", "modulation_linear", "quantizer_4352",
+                 "quantizer_9472", "quantizer_16384")
 
 
 def profile_case(device: torch.device, name: str) -> None:
     """Runs one workload three times (the launches an ncu capture selects from); for
-    fused_ops_t2i each of the four ops three times and for modulation_linear the FP8
-    linear three times, a 256 MiB write before every launch (cold L2)."""
+    fused_ops_t2i each of the four ops three times, for modulation_linear the FP8 linear
+    and for quantizer_<M> the activation quantizer three times, an L2 flush before every
+    launch."""
     g = torch.Generator(device=device).manual_seed(7)
-    if name == "modulation_linear":
+    if name.startswith("quantizer_"):
+        # the dynamic activation quantizer (qik_quantize_act) on M x 3072 bf16 rows
+        from qik import fp8 as F
+        x = torch.randn(int(name.split("_")[1]), 3072, device=device, generator=g).to(torch.bfloat16)
+        flush = L2Flush(device)
+        for r in range(3):
+            flush(r)
+            F.quantize_tensorwise(x)
+    elif name == "modulation_linear":
         # the DiT block's timestep-modulation FP8 linear: M = 2 (CFG batch) x 3072 -> 18432
         from qik import fp8 as F
         wq, sw = F.quantize_weight_tensorwise(torch.randn(18432, 3072, device=device, generator=g) * 0.02)

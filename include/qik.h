@@ -199,18 +199,19 @@ int qik_fp8_ffn_from_amax(const void* x, const uint32_t* x_amax_bits, int64_t M,
 #define QIK_ATTN_HAS_KEY_VALID 2 /* per-(batch, key) validity bytes */
 #define QIK_ATTN_UNIFORM 4       /* every row attends to [0, P+SN): L unused */
 #define QIK_ATTN_V_FP8 8         /* cache V is e4m3 with per-(batch, head) scales */
+#define QIK_ATTN_F16 16          /* q / k / v / cache K (and a 16-bit cache V) / out are fp16, not bf16 */
 
 /* Strides are in elements of the tensor they describe. */
 typedef struct qik_attn_args {
-  const void* q;       /* [B, SQ, H, D] bf16 */
-  const void* k;       /* [B, SN, H, D] bf16 fresh keys */
-  const void* v;       /* [B, SN, H, D] bf16 fresh values */
-  const void* cache_k; /* [B, P, H, D] bf16, or NULL */
-  const void* cache_v; /* [B, P, H, D] bf16 or e4m3, or NULL */
+  const void* q;       /* [B, SQ, H, D] bf16 (fp16 with QIK_ATTN_F16) */
+  const void* k;       /* [B, SN, H, D] fresh keys, q's type */
+  const void* v;       /* [B, SN, H, D] fresh values, q's type */
+  const void* cache_k; /* [B, P, H, D] q's type, or NULL */
+  const void* cache_v; /* [B, P, H, D] q's type or e4m3, or NULL */
   const float* cache_v_scale; /* [B, H] fp32 (V_FP8 only) */
   const int32_t* L;    /* [SQ]: row attends kv iff 0 <= kv <= L[row]; -1 -> no key */
   const uint8_t* key_valid; /* [B, P + SN] bytes, non-zero = valid (HAS_KEY_VALID) */
-  void* out;           /* [B, SQ, H, D] bf16 */
+  void* out;           /* [B, SQ, H, D] q's type */
   int64_t B, SQ, SN, P, H, D;
   int64_t q_sb, q_ss, q_sh;
   int64_t k_sb, k_ss, k_sh;
@@ -230,7 +231,10 @@ typedef struct qik_attn_args {
  * Block-causal flash attention over [prefix slab ; fresh K/V] with per-row
  * prefix lengths, optional key validity and an e4m3 slab V dequantized in the
  * loop as bf16(fl32(v8) * scale[b, h]).  Replaces block_causal_flash_attention
- * + _qwen21_attn_fwd (qwen_image_kernel/triton_attention.py:35-260).
+ * + _qwen21_attn_fwd (qwen_image_kernel/triton_attention.py:35-260), for bf16 or
+ * (QIK_ATTN_F16) fp16 tensors as the reference accepts both
+ * (triton_attention.py:190): P is rounded to the tensors' type before P.V
+ * (triton_attention.py:162-163), fp32 accumulation.
  * Requires D == 128 and unit stride along D; rows with no allowed key give 0.
  */
 int qik_block_causal_attention(const qik_attn_args* args, int* status, void* stream);

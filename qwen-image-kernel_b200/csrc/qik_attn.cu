@@ -6,7 +6,8 @@
 // the keys kv of the virtual concatenation [cache (P keys) ; fresh (SN keys)] with
 // kv <= L[r] (all keys when UNIFORM) and key_valid[b, kv] != 0 (when given);
 // softmax in base 2 with the scores scaled by sm_scale * log2(e); P is rounded to
-// bf16 before P.V; fp32 accumulation; rows with no allowed key are 0.
+// the tensors' type (bf16, or fp16 under QIK_ATTN_F16) before P.V; fp32
+// accumulation; rows with no allowed key are 0.
 // e4m3 slab V (triton_attention.py:154-159, which rounds fl32(v8) * scale[b, h] to
 // bf16 per element): here the slab tiles multiply e4m3-exact f16 V by f16 P (a
 // finer rounding of P than bf16) and the per-(b, h) scale multiplies the fp32
@@ -38,6 +39,8 @@
 // TMEM columns: S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512); P_g over S_g.
 // CTAs are numbered heaviest-first (the last query blocks, which see the most keys
 // under a block-causal mask, start first) so the short blocks fill the tail.
+#include <mutex>
+
 #include "qik_device.cuh"
 #include "qik_host.h"
 
@@ -72,7 +75,7 @@ struct AttnDev {
   const int32_t* L;
   const uint8_t* key_valid;
   const float* v_scale;
-  __nv_bfloat16* out;
+  uint16_t* out;  // bf16 or fp16 bits
   int64_t o_sb, o_ss, o_sh, kv_sb;
   int SQ, SN, P, H;
   float qk_scale_log2;
@@ -152,6 +155,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const bool uniform = (a.flags & QIK_ATTN_UNIFORM) != 0;
   const bool v_fp8 = has_cache && (a.flags & QIK_ATTN_V_FP8);
   const bool has_kv = (a.flags & QIK_ATTN_HAS_KEY_VALID) != 0;
+  const bool f16 = (a.flags & QIK_ATTN_F16) != 0;  // fp16 tensors: f16 MMAs, P and output
   const int P = has_cache ? a.P : 0;
   const int kv_total = P + a.SN;
 
@@ -238,9 +242,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_tiles > 0) {
-      constexpr uint32_t idesc_s = idesc_f32acc(1, 1, 0, 0, kAttnBM, kAttnBN);
-      constexpr uint32_t idesc_o = idesc_f32acc(1, 1, 0, 1, kAttnBM, kAttnD);      // bf16 P, bf16 V
-      constexpr uint32_t idesc_o16 = idesc_f32acc(0, 0, 0, 1, kAttnBM, kAttnD);    // f16 P, f16 V (fp8 slab)
+      constexpr uint32_t idesc_s_bf16 = idesc_f32acc(1, 1, 0, 0, kAttnBM, kAttnBN);
+      constexpr uint32_t idesc_s_f16 = idesc_f32acc(0, 0, 0, 0, kAttnBM, kAttnBN);
+      constexpr uint32_t idesc_o_bf16 = idesc_f32acc(1, 1, 0, 1, kAttnBM, kAttnD);  // bf16 P, bf16 V
+      constexpr uint32_t idesc_o16 = idesc_f32acc(0, 0, 0, 1, kAttnBM, kAttnD);     // f16 P, f16 V
+      const uint32_t idesc_s = f16 ? idesc_s_f16 : idesc_s_bf16;
+      const uint32_t idesc_o = f16 ? idesc_o16 : idesc_o_bf16;
       // S_g at column 128 g (P_g over its first 64 columns), O_g at 256 + 128 g
       bool ok = mbar_wait(q_full, 0, abort_flag, a.status);
       const uint32_t q_addr = smem_u32(sQ);
@@ -401,7 +408,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       const float neg_m = (m_run == -INFINITY) ? 0.0f : -m_run;
       // S_g(t) is in registers: P_g(t) overwrites its first 64 columns
-      const bool f16p = slab_f16 && slab;
+      const bool f16p = f16 || (slab_f16 && slab);
       float psum;
       if (full)
         psum = f16p ? softmax_row<true, true>(sv, a.qk_scale_log2, neg_m, tS)
@@ -449,12 +456,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (grow < a.SQ) {
       const bool nz = have_o && l_run > 0.0f;
       const float inv = nz ? (vsc_applied ? 1.0f : vsc) / l_run : 0.0f;
-      __nv_bfloat16* dst = a.out + static_cast<int64_t>(b) * a.o_sb + static_cast<int64_t>(grow) * a.o_ss +
-                           static_cast<int64_t>(h) * a.o_sh;
+      uint16_t* dst = a.out + static_cast<int64_t>(b) * a.o_sb + static_cast<int64_t>(grow) * a.o_ss +
+                      static_cast<int64_t>(h) * a.o_sh;
 #pragma unroll
       for (int c = 0; c < kAttnD; c += 8) {
         uint4 w = make_uint4(0u, 0u, 0u, 0u);
-        if (nz)
+        if (nz && f16)
+          w = make_uint4(pack_f16x2(o[c] * inv, o[c + 1] * inv), pack_f16x2(o[c + 2] * inv, o[c + 3] * inv),
+                         pack_f16x2(o[c + 4] * inv, o[c + 5] * inv), pack_f16x2(o[c + 6] * inv, o[c + 7] * inv));
+        else if (nz)
           w = make_uint4(pack_bf16x2(o[c] * inv, o[c + 1] * inv), pack_bf16x2(o[c + 2] * inv, o[c + 3] * inv),
                          pack_bf16x2(o[c + 4] * inv, o[c + 5] * inv), pack_bf16x2(o[c + 6] * inv, o[c + 7] * inv));
         am2 = __vmaxu2(am2, __vmaxu2(__vmaxu2(w.x & 0x7FFF7FFFu, w.y & 0x7FFF7FFFu),
@@ -463,8 +473,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
     }
     if (a.amax_out) {  // CTA-uniform: the whole warp reduces
+      // |out| bit patterns order like the values for either 16-bit type; the largest one
+      // is widened to fp32 bits (bf16: the top half; fp16: an exact conversion)
       const uint32_t m = __reduce_max_sync(0xffffffffu, max(am2 & 0xFFFFu, am2 >> 16));
-      if (lane == 0 && m != 0u) atomicMax(a.amax_out, m << 16);
+      const uint32_t bits =
+          f16 ? __float_as_uint(__half2float(__ushort_as_half(static_cast<unsigned short>(m)))) : m << 16;
+      if (lane == 0 && m != 0u) atomicMax(a.amax_out, bits);
     }
   }
 
@@ -521,24 +535,26 @@ extern "C" int qik_block_causal_attention(const qik_attn_args* args, int* status
                 "qik_block_causal_attention: cache strides/alignment must be 16-byte multiples");
   }
   CUtensorMap tq, tk, tv, tck, tcv;
-  int rc = make_bshd_map(&tq, A.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A.B, A.SQ, A.H, A.q_sb, A.q_ss, A.q_sh, 64,
+  const CUtensorMapDataType dt16 =
+      (A.flags & QIK_ATTN_F16) ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  int rc = make_bshd_map(&tq, A.q, dt16, 2, A.B, A.SQ, A.H, A.q_sb, A.q_ss, A.q_sh, 64,
                          CU_TENSOR_MAP_SWIZZLE_128B);
   if (!rc)
-    rc = make_bshd_map(&tk, A.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A.B, A.SN, A.H, A.k_sb, A.k_ss, A.k_sh, 64,
+    rc = make_bshd_map(&tk, A.k, dt16, 2, A.B, A.SN, A.H, A.k_sb, A.k_ss, A.k_sh, 64,
                        CU_TENSOR_MAP_SWIZZLE_128B);
   if (!rc)
-    rc = make_bshd_map(&tv, A.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A.B, A.SN, A.H, A.v_sb, A.v_ss, A.v_sh, 64,
+    rc = make_bshd_map(&tv, A.v, dt16, 2, A.B, A.SN, A.H, A.v_sb, A.v_ss, A.v_sh, 64,
                        CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   if (has_cache) {
-    rc = make_bshd_map(&tck, A.cache_k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A.B, A.P, A.H, A.ck_sb, A.ck_ss, A.ck_sh,
+    rc = make_bshd_map(&tck, A.cache_k, dt16, 2, A.B, A.P, A.H, A.ck_sb, A.ck_ss, A.ck_sh,
                        64, CU_TENSOR_MAP_SWIZZLE_128B);
     if (!rc) {
       if (v_fp8)
         rc = make_bshd_map(&tcv, A.cache_v, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A.B, A.P, A.H, A.cv_sb, A.cv_ss,
                            A.cv_sh, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
       else
-        rc = make_bshd_map(&tcv, A.cache_v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A.B, A.P, A.H, A.cv_sb, A.cv_ss,
+        rc = make_bshd_map(&tcv, A.cache_v, dt16, 2, A.B, A.P, A.H, A.cv_sb, A.cv_ss,
                            A.cv_sh, 64, CU_TENSOR_MAP_SWIZZLE_128B);
     }
     if (rc) return rc;
@@ -550,7 +566,7 @@ extern "C" int qik_block_causal_attention(const qik_attn_args* args, int* status
   d.L = A.L;
   d.key_valid = A.key_valid;
   d.v_scale = A.cache_v_scale;
-  d.out = static_cast<__nv_bfloat16*>(A.out);
+  d.out = static_cast<uint16_t*>(A.out);
   d.o_sb = A.o_sb;
   d.o_ss = A.o_ss;
   d.o_sh = A.o_sh;
@@ -563,13 +579,15 @@ extern "C" int qik_block_causal_attention(const qik_attn_args* args, int* status
   d.flags = A.flags;
   d.status = status;
   d.amax_out = A.amax_out;
-  static bool attr_set[64] = {false};
+  static std::once_flag attr_once[64];
   int dev = 0;
   QIK_TRY_CUDA(cudaGetDevice(&dev));
-  if (dev < 64 && !attr_set[dev]) {
-    QIK_TRY_CUDA(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem::kBytes));
-    attr_set[dev] = true;
-  }
+  QIK_REQUIRE(dev >= 0 && dev < 64, "qik_block_causal_attention: device ordinal %d out of range", dev);
+  cudaError_t attr_rc = cudaSuccess;
+  std::call_once(attr_once[dev], [&] {
+    attr_rc = cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem::kBytes);
+  });
+  QIK_TRY_CUDA(attr_rc);
   // x = (b, h), y = query block (numbered from the last block: heaviest first)
   dim3 grid(static_cast<unsigned>(A.B * A.H), static_cast<unsigned>((A.SQ + kAttnRows - 1) / kAttnRows));
   attn_fwd_kernel<<<grid, kAttnThreads, AttnSmem::kBytes, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, tck, tcv,

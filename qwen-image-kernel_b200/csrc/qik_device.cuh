@@ -461,6 +461,28 @@ __device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// A bf16x2 word (element 0 in the low half) as an fp32 pair, exactly.
+__device__ __forceinline__ uint64_t bf2_to_f2(uint32_t w) {
+  return f2_pack(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+// An fp32 pair rounded to nearest even into a bf16x2 word (element 0 in the low half).
+__device__ __forceinline__ uint32_t f2_to_bf2(uint64_t v) {
+  float lo, hi;
+  f2_unpack(v, lo, hi);
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ float f2_sum(uint64_t v) {
+  float lo, hi;
+  f2_unpack(v, lo, hi);
+  return lo + hi;
+}
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));

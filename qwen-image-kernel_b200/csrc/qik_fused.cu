@@ -6,6 +6,9 @@
 //                    complex RoPE on (even, odd) pairs             (:27-67)
 //   layer_norm_mod   LayerNorm without affine, bf16, times bf16(1 + scale) with the
 //                    per-position modulation row map              (:75-108)
+// The two norms stream their rows through shared memory (bulk copies into a ring,
+// see "row streaming"); RMSNorm + RoPE keeps a register-only form for layouts whose
+// heads are not contiguous within a token.
 //   gate_residual    x + bf16(tanh(gate)) * f                      (:168-196)
 //   swiglu           bf16(silu(g)) * up                            (:227-240)
 // All four are HBM-bound: 16-byte vector loads and stores, grids a multiple of the
@@ -13,6 +16,8 @@
 // amax of their bf16 output (fp32 bit patterns, atomicMax), which is the reduction
 // the next FP8 linear's dynamic quantizer needs, so that linear can skip its own
 // amax pass (qik_quantize_act_from_amax).
+#include <mutex>
+
 #include "qik_device.cuh"
 #include "qik_host.h"
 
@@ -121,74 +126,233 @@ __global__ void __launch_bounds__(kThreads) rms_rope_kernel(const uint16_t* __re
   }
 }
 
-// ---------------------------------------------------------------- LayerNorm + modulate
-// One warp per row of D (D % 8 == 0, D <= 8 * 32 * MAXV): the row stays in
-// registers between the mean, the centred variance and the output pass.
-template <int MAXV>
-__global__ void __launch_bounds__(kThreads) ln_modulate_kernel(const uint16_t* __restrict__ x,
-                                                               const uint16_t* __restrict__ mod, int64_t mod_stride,
-                                                               int64_t scale_off, const uint8_t* __restrict__ tmask,
-                                                               uint16_t* __restrict__ out, int64_t B, int64_t S, int D,
-                                                               float eps, uint32_t* __restrict__ amax_out) {
-  const int lane = threadIdx.x & 31;
-  const int nv = D >> 3;
+// ---------------------------------------------------------------- row streaming
+// Register-resident norms issue a row's loads only when the warp reaches the row, so
+// only a few KB per warp are in flight and they wait on memory latency (~0.5 of HBM).
+// The streaming forms decouple the loads: one CTA per SM, one producer thread issuing
+// bulk copies (cp.async.bulk) of 8-row groups into a ring of shared-memory stages, and
+// two sets of 8 consumer warps taking alternate stages, one row of a stage per warp.
+// The consumers read their row from shared memory in every pass (mean, variance,
+// output), which keeps them at ~40 registers so 16 of them fit beside the producer.  A
+// stage is released once its 8 warps arrive on its empty barrier.  Every wait is
+// bounded.
+constexpr int kStreamWarps = 8;                    // rows per stage = consumer warps per set
+constexpr int kStreamSets = 2;                     // consumer sets, taking alternate stages
+constexpr int kStreamThreads = 32 * (kStreamWarps * kStreamSets + 1);
+constexpr int kStreamMaxStages = 8;
+constexpr int kStreamRingBytes = 216 * 1024;  // ring + table, below the 227 KB per CTA
+
+__device__ __forceinline__ void stream_bars_init(uint64_t* full, uint64_t* empty, int stages, int* abort_flag) {
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < stages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kStreamWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kStreamThreads, 1)
+    ln_modulate_stream_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ mod, int64_t mod_stride,
+                              int64_t scale_off, const uint8_t* __restrict__ tmask, uint16_t* __restrict__ out,
+                              int64_t B, int64_t S, int D, float eps, uint32_t* __restrict__ amax_out, int stages,
+                              int mod_rows) {
+  // [stages][kStreamWarps rows][nv] ring, then bf16(1 + scale) for each used modulation row
+  extern __shared__ __align__(128) uint4 ring[];
+  __shared__ __align__(8) uint64_t full[kStreamMaxStages], empty[kStreamMaxStages];
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nv = D >> 3;  // 16-byte vectors per row; a stage holds kStreamWarps rows = 8 nv vectors
+  uint4* table = ring + static_cast<int64_t>(stages) * kStreamWarps * nv;
+  for (int e = threadIdx.x; e < mod_rows * nv; e += blockDim.x) {
+    const int r = e / nv, c = e - r * nv;
+    const uint4 m = ldg16(mod + r * mod_stride + scale_off + c * 8);
+    const uint32_t w[4] = {m.x, m.y, m.z, m.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o[k] = f2_to_bf2(fadd2(bf2_to_f2(w[k]), f2_pack(1.0f, 1.0f)));
+    table[e] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  stream_bars_init(full, empty, stages, &abort_flag);  // (its barrier also publishes the table)
   const int64_t nrows = B * S;
-  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  uint32_t am2 = 0;  // two running bf16 |y| maxima
-  for (int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); row < nrows;
-       row += warps_total) {
-    const int64_t b = row / S, s = row % S;
-    const uint16_t* xr = x + row * D;
-    uint4 xv[MAXV];
-    float sum = 0.0f;
-#pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-      const int idx = lane + 32 * i;
-      xv[i] = idx < nv ? ldg16(xr + idx * 8) : make_uint4(0u, 0u, 0u, 0u);
-      const uint32_t u[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) sum += bf_lo(u[j]) + bf_hi(u[j]);
-    }
-    sum = warp_sum(sum);
-    const float mean = sum / static_cast<float>(D);
-    float var = 0.0f;
-#pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-      if (lane + 32 * i < nv) {
-        const uint32_t u[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float a = bf_lo(u[j]) - mean, c = bf_hi(u[j]) - mean;
-          var = fmaf(a, a, var);
-          var = fmaf(c, c, var);
-        }
+  const int64_t ngroups = (nrows + kStreamWarps - 1) / kStreamWarps;
+  uint32_t am2 = 0;
+  if (warp == 0) {
+    if (lane == 0) {
+      int i = 0;
+      for (int64_t g = blockIdx.x; g < ngroups; g += gridDim.x, ++i) {
+        const int st = i % stages;
+        if (!mbar_wait(&empty[st], ((i / stages) & 1) ^ 1u, &abort_flag, nullptr)) break;
+        const int64_t r0 = g * kStreamWarps;
+        const int64_t rows = min(static_cast<int64_t>(kStreamWarps), nrows - r0);
+        const uint32_t bytes = static_cast<uint32_t>(rows * D * 2);
+        mbar_arrive_expect_tx(&full[st], bytes);
+        bulk_load(ring + static_cast<int64_t>(st) * kStreamWarps * nv, x + r0 * D, bytes, &full[st]);
       }
     }
-    var = warp_sum(var) / static_cast<float>(D);
-    const float rstd = rsqrtf(var + eps);
-    // target positions use their own sample's row b, the others row B + b
-    const int64_t mrow = (tmask == nullptr || tmask[s] != 0) ? b : B + b;
-    const uint16_t* sc = mod + mrow * mod_stride + scale_off;
-    uint16_t* orow = out + row * D;
-#pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-      const int idx = lane + 32 * i;
-      if (idx < nv) {
-        const uint4 sv = ldg16(sc + idx * 8);
-        const uint32_t u[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
-        const uint32_t m[4] = {sv.x, sv.y, sv.z, sv.w};
-        uint32_t o[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float y0 = round_bf16((bf_lo(u[j]) - mean) * rstd), y1 = round_bf16((bf_hi(u[j]) - mean) * rstd);
-          o[j] = pack_bf16x2(y0 * round_bf16(1.0f + bf_lo(m[j])), y1 * round_bf16(1.0f + bf_hi(m[j])));
-          am2 = absmax_bf16x2(am2, o[j]);
+  } else {
+    const int set = (warp - 1) / kStreamWarps, cw = (warp - 1) % kStreamWarps;
+    int i = set;
+    for (int64_t g = blockIdx.x + static_cast<int64_t>(set) * gridDim.x; g < ngroups;
+         g += static_cast<int64_t>(kStreamSets) * gridDim.x, i += kStreamSets) {
+      const int st = i % stages;
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[st], (i / stages) & 1, &abort_flag, nullptr))) break;
+      const int64_t row = g * kStreamWarps + cw;
+      if (row < nrows) {
+        const uint4* xr = ring + (static_cast<int64_t>(st) * kStreamWarps + cw) * nv;
+        const int64_t b = row / S, s = row % S;
+        uint64_t acc = 0ull;  // (0.f, 0.f)
+        for (int idx = lane; idx < nv; idx += 32) {
+          const uint4 v = xr[idx];
+          acc = fadd2(fadd2(acc, bf2_to_f2(v.x)), bf2_to_f2(v.y));
+          acc = fadd2(fadd2(acc, bf2_to_f2(v.z)), bf2_to_f2(v.w));
         }
-        *reinterpret_cast<uint4*>(orow + idx * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+        const float mean = warp_sum(f2_sum(acc)) / static_cast<float>(D);
+        const uint64_t nm2 = f2_pack(-mean, -mean);
+        acc = 0ull;
+        for (int idx = lane; idx < nv; idx += 32) {
+          const uint4 v = xr[idx];
+          const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t d = fadd2(bf2_to_f2(u[k]), nm2);
+            acc = ffma2(d, d, acc);
+          }
+        }
+        const float var = warp_sum(f2_sum(acc)) / static_cast<float>(D);
+        const uint64_t r2 = f2_pack(rsqrtf(var + eps), rsqrtf(var + eps));
+        // target positions use their own sample's row b, the others row B + b
+        const int64_t mrow = (tmask == nullptr || tmask[s] != 0) ? b : B + b;
+        const uint4* tr = table + mrow * nv;
+        uint16_t* orow = out + row * D;
+#pragma unroll 2
+        for (int idx = lane; idx < nv; idx += 32) {
+          const uint4 v = xr[idx], sv = tr[idx];
+          const uint32_t u[4] = {v.x, v.y, v.z, v.w}, m[4] = {sv.x, sv.y, sv.z, sv.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            // y = bf16((x - mean) * rstd); out = bf16(y * bf16(1 + scale))
+            const uint32_t y = f2_to_bf2(fmul2(fadd2(bf2_to_f2(u[k]), nm2), r2));
+            o[k] = f2_to_bf2(fmul2(bf2_to_f2(y), bf2_to_f2(m[k])));
+            am2 = absmax_bf16x2(am2, o[k]);
+          }
+          *reinterpret_cast<uint4*>(orow + idx * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
     }
   }
   if (amax_out) block_atomic_max(max(am2 & 0xFFFFu, am2 >> 16) << 16, amax_out);
+}
+
+// RMSNorm + RoPE over tokens whose heads are contiguous (x_sh == D, as in the strided
+// q / k views of the fused QKV output): a stage holds 8 tokens' H x D elements (one
+// bulk copy per token), a consumer warp walks its token's heads 32 / G at a time with
+// the token's cos / sin rows loaded once.
+template <int G>
+__global__ void __launch_bounds__(kStreamThreads, 1)
+    rms_rope_stream_kernel(const uint16_t* __restrict__ x, int64_t x_sb, int64_t x_ss, uint16_t* __restrict__ out,
+                           int64_t o_sb, int64_t o_ss, int64_t o_sh, const float* __restrict__ w,
+                           const float* __restrict__ cs, const float* __restrict__ sn, int64_t B, int64_t S, int H,
+                           float eps, int stages) {
+  constexpr int D = 8 * G, HALF = D / 2, RPW = 32 / G;
+  extern __shared__ __align__(128) uint4 ring[];
+  __shared__ __align__(8) uint64_t full[kStreamMaxStages], empty[kStreamMaxStages];
+  __shared__ int abort_flag;
+  stream_bars_init(full, empty, stages, &abort_flag);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tok_vecs = H * G;  // 16-byte vectors per token
+  const int64_t ntok = B * S;
+  const int64_t ngroups = (ntok + kStreamWarps - 1) / kStreamWarps;
+  if (warp == 0) {
+    if (lane == 0) {
+      int i = 0;
+      for (int64_t g = blockIdx.x; g < ngroups; g += gridDim.x, ++i) {
+        const int st = i % stages;
+        if (!mbar_wait(&empty[st], ((i / stages) & 1) ^ 1u, &abort_flag, nullptr)) break;
+        const int64_t t0 = g * kStreamWarps;
+        const int toks = static_cast<int>(min(static_cast<int64_t>(kStreamWarps), ntok - t0));
+        const uint32_t bytes = static_cast<uint32_t>(tok_vecs) * 16u;
+        mbar_arrive_expect_tx(&full[st], bytes * static_cast<uint32_t>(toks));
+        for (int k = 0; k < toks; ++k) {
+          const int64_t t = t0 + k, b = t / S, s = t - b * S;
+          bulk_load(ring + (static_cast<int64_t>(st) * kStreamWarps + k) * tok_vecs, x + b * x_sb + s * x_ss, bytes,
+                    &full[st]);
+        }
+      }
+    }
+    return;
+  }
+  const int set = (warp - 1) / kStreamWarps, cw = (warp - 1) % kStreamWarps;
+  const int sub = lane / G, gl = lane % G;
+  const float4 w0 = ldg16f(w + gl * 8), w1 = ldg16f(w + gl * 8 + 4);
+  const uint64_t w2[4] = {f2_pack(w0.x, w0.y), f2_pack(w0.z, w0.w), f2_pack(w1.x, w1.y), f2_pack(w1.z, w1.w)};
+  int i = set;
+  for (int64_t g = blockIdx.x + static_cast<int64_t>(set) * gridDim.x; g < ngroups;
+       g += static_cast<int64_t>(kStreamSets) * gridDim.x, i += kStreamSets) {
+    const int st = i % stages;
+    if (!__all_sync(0xffffffffu, mbar_wait(&full[st], (i / stages) & 1, &abort_flag, nullptr))) break;
+    const int64_t t = g * kStreamWarps + cw;
+    if (t < ntok) {
+      const int64_t b = t / S, s = t - b * S;
+      const float4 c4 = ldg16f(cs + s * HALF + gl * 4), s4 = ldg16f(sn + s * HALF + gl * 4);
+      // (e + i o)(c + i s): the pair (e c - o s, e s + o c) = e (c, s) + o (-s, c)
+      const uint64_t cs2[4] = {f2_pack(c4.x, s4.x), f2_pack(c4.y, s4.y), f2_pack(c4.z, s4.z), f2_pack(c4.w, s4.w)};
+      const uint64_t sc2[4] = {f2_pack(-s4.x, c4.x), f2_pack(-s4.y, c4.y), f2_pack(-s4.z, c4.z),
+                               f2_pack(-s4.w, c4.w)};
+      const uint4* xt = ring + (static_cast<int64_t>(st) * kStreamWarps + cw) * tok_vecs;
+      uint16_t* ot = out + b * o_sb + s * o_ss;
+#pragma unroll 2
+      for (int h0 = 0; h0 < H; h0 += RPW) {
+        const int h = h0 + sub;
+        const bool live = h < H;
+        const uint4 v = live ? xt[h * G + gl] : make_uint4(0u, 0u, 0u, 0u);
+        const uint64_t x2[4] = {bf2_to_f2(v.x), bf2_to_f2(v.y), bf2_to_f2(v.z), bf2_to_f2(v.w)};
+        uint64_t ss2 = 0ull;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) ss2 = ffma2(x2[k], x2[k], ss2);
+        float ss = f2_sum(ss2);
+#pragma unroll
+        for (int o = G / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float rrms = rsqrtf(ss / static_cast<float>(D) + eps);
+        const uint64_t rr2 = f2_pack(rrms, rrms);
+        uint32_t o4[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          // fp32 norm and weight, one rounding to bf16, the rotation in fp32
+          const uint32_t nb = f2_to_bf2(fmul2(fmul2(x2[k], rr2), w2[k]));
+          const float ne = bf_lo(nb), no = bf_hi(nb);
+          o4[k] = f2_to_bf2(ffma2(f2_pack(ne, ne), cs2[k], fmul2(f2_pack(no, no), sc2[k])));
+        }
+        if (live) *reinterpret_cast<uint4*>(ot + h * o_sh + gl * 8) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+  }
+}
+
+// Shared memory ring of a streaming kernel: stages of `stage_bytes`, at least 2 and at
+// most kStreamMaxStages within kStreamRingBytes; 0 when a stage does not fit twice.
+int stream_stages(int64_t stage_bytes) {
+  const int64_t n = kStreamRingBytes / stage_bytes;
+  return n < 2 ? 0 : static_cast<int>(n < kStreamMaxStages ? n : kStreamMaxStages);
+}
+
+template <typename Kernel>
+int stream_smem_attr(Kernel kernel, std::once_flag* once, const char* what) {
+  int dev = 0;
+  QIK_TRY_CUDA(cudaGetDevice(&dev));
+  QIK_REQUIRE(dev >= 0 && dev < 64, "%s: device ordinal %d out of range", what, dev);
+  cudaError_t rc = cudaSuccess;
+  std::call_once(once[dev], [&] {
+    rc = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamRingBytes);
+  });
+  return cuda_status(rc, what);
 }
 
 // ---------------------------------------------------------------- gate + residual
@@ -347,6 +511,34 @@ int qik_rms_norm_rope(const void* x, int64_t B, int64_t S, int64_t H, int64_t D,
                   aligned_elems(o_ss) && aligned_elems(o_sh),
               "qik_rms_norm_rope: strides must be multiples of 8 elements");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t ntok = B * S;
+  const int stages = x_sh == D ? stream_stages(static_cast<int64_t>(kStreamWarps) * H * D * 2) : 0;
+  if (stages > 0 && H <= 65535) {
+    // heads of a token contiguous: stream 8-token groups through shared memory
+    static std::once_flag once8[64], once16[64], once32[64];
+    const int grid = grid_cap((ntok + kStreamWarps - 1) / kStreamWarps, 1);
+    const size_t smem = static_cast<size_t>(stages) * kStreamWarps * H * D * 2;
+    const uint16_t* xs = static_cast<const uint16_t*>(x);
+    uint16_t* os = static_cast<uint16_t*>(out);
+    int rc;
+    if (D == 64) {
+      if ((rc = stream_smem_attr(rms_rope_stream_kernel<8>, once8, "rms_rope_stream_kernel"))) return rc;
+      rms_rope_stream_kernel<8><<<grid, kStreamThreads, smem, st>>>(xs, x_sb, x_ss, os, o_sb, o_ss, o_sh, weight,
+                                                                    cos_tab, sin_tab, B, S, static_cast<int>(H), eps,
+                                                                    stages);
+    } else if (D == 128) {
+      if ((rc = stream_smem_attr(rms_rope_stream_kernel<16>, once16, "rms_rope_stream_kernel"))) return rc;
+      rms_rope_stream_kernel<16><<<grid, kStreamThreads, smem, st>>>(xs, x_sb, x_ss, os, o_sb, o_ss, o_sh, weight,
+                                                                     cos_tab, sin_tab, B, S, static_cast<int>(H), eps,
+                                                                     stages);
+    } else {
+      if ((rc = stream_smem_attr(rms_rope_stream_kernel<32>, once32, "rms_rope_stream_kernel"))) return rc;
+      rms_rope_stream_kernel<32><<<grid, kStreamThreads, smem, st>>>(xs, x_sb, x_ss, os, o_sb, o_ss, o_sh, weight,
+                                                                     cos_tab, sin_tab, B, S, static_cast<int>(H), eps,
+                                                                     stages);
+    }
+    return check_launch("rms_rope_stream_kernel");
+  }
   const int rows_per_cta = (kThreads / 32) * (32 / static_cast<int>(D / 8)) * kRopeUnroll;
   const int grid = grid_cap((nrows + rows_per_cta - 1) / rows_per_cta, 8);
   const uint16_t* xs = static_cast<const uint16_t*>(x);
@@ -380,23 +572,29 @@ int qik_layer_norm_modulate(const void* x, int64_t B, int64_t S, int64_t D, cons
               static_cast<long long>(B), target_mask ? "2B (rows B..2B-1 are the t = 0 rows)" : "B");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t rows = B * S;
-  // two CTAs per SM, warps walking rows (measured: 36.5 us at the t2i shape against 38.5
-  // with one row per warp and 39.4 with four CTAs per SM)
-  const int grid = grid_cap((rows + 7) / 8, 2);
-  const int nv = static_cast<int>(D / 8);
   const uint16_t* xs = static_cast<const uint16_t*>(x);
   const uint16_t* ms = static_cast<const uint16_t*>(modulation);
   uint16_t* os = static_cast<uint16_t*>(out);
-  if (nv <= 32 * 4)
-    ln_modulate_kernel<4><<<grid, kThreads, 0, st>>>(xs, ms, mod_stride, scale_off, target_mask, os, B, S,
-                                                     static_cast<int>(D), eps, amax_out);
-  else if (nv <= 32 * 12)
-    ln_modulate_kernel<12><<<grid, kThreads, 0, st>>>(xs, ms, mod_stride, scale_off, target_mask, os, B, S,
-                                                      static_cast<int>(D), eps, amax_out);
-  else
-    ln_modulate_kernel<16><<<grid, kThreads, 0, st>>>(xs, ms, mod_stride, scale_off, target_mask, os, B, S,
-                                                      static_cast<int>(D), eps, amax_out);
-  return check_launch("ln_modulate_kernel");
+  // bf16(1 + scale) of every modulation row in use sits in shared memory beside the ring
+  const int mod_used = static_cast<int>(target_mask ? 2 * B : B);
+  const int64_t table_bytes = static_cast<int64_t>(mod_used) * D * 2;
+  const int64_t stage_bytes = static_cast<int64_t>(kStreamWarps) * D * 2;
+  const int64_t fit = (kStreamRingBytes - table_bytes) / stage_bytes;  // stages that fit beside the table
+  const int stages = fit < 2 ? 0 : static_cast<int>(fit < kStreamMaxStages ? fit : kStreamMaxStages);
+  if (stages > 0) {
+    // rows streamed through shared memory, 8 per stage
+    static std::once_flag once[64];
+    const int grid = grid_cap((rows + kStreamWarps - 1) / kStreamWarps, 1);
+    const size_t smem = static_cast<size_t>(stages) * stage_bytes + static_cast<size_t>(table_bytes);
+    int rc;
+    if ((rc = stream_smem_attr(ln_modulate_stream_kernel, once, "ln_modulate_stream_kernel"))) return rc;
+    ln_modulate_stream_kernel<<<grid, kStreamThreads, smem, st>>>(xs, ms, mod_stride, scale_off, target_mask, os, B, S,
+                                                                 static_cast<int>(D), eps, amax_out, stages, mod_used);
+    return check_launch("ln_modulate_stream_kernel");
+  }
+  return set_error(QIK_ERR_UNSUPPORTED,
+                   "qik_layer_norm_modulate: width %lld with %d modulation rows does not fit the row ring",
+                   static_cast<long long>(D), mod_used);
 }
 
 int qik_gate_residual(const void* x, const void* f, int64_t B, int64_t S, int64_t D, const void* modulation,

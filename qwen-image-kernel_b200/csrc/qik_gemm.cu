@@ -23,6 +23,8 @@
 // The epilogue of tile i overlaps the MMAs of tile i+1.
 #include <string.h>
 
+#include <mutex>
+
 #include "qik_device.cuh"
 #include "qik_host.h"
 
@@ -434,14 +436,16 @@ static int launch_gemm(const uint8_t* A, const uint8_t* B, const GemmParams& p, 
     rc = make_tmap_2d(&tc, p.C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<uint64_t>(p.N),
                       static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.ldc) * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
   if (rc) return rc;
-  static bool attr_set[64] = {false};
+  static std::once_flag attr_once[64];
   int dev = 0;
   QIK_TRY_CUDA(cudaGetDevice(&dev));
-  if (dev < 64 && !attr_set[dev]) {
-    QIK_TRY_CUDA(cudaFuncSetAttribute(fp8_gemm_kernel<BN, STAGES, TWO_SM>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kSmemBytes));
-    attr_set[dev] = true;
-  }
+  QIK_REQUIRE(dev >= 0 && dev < 64, "qik_fp8_gemm: device ordinal %d out of range", dev);
+  cudaError_t attr_rc = cudaSuccess;
+  std::call_once(attr_once[dev], [&] {
+    attr_rc = cudaFuncSetAttribute(fp8_gemm_kernel<BN, STAGES, TWO_SM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   Lay::kSmemBytes);
+  });
+  QIK_TRY_CUDA(attr_rc);
   constexpr int kTileM = TWO_SM ? 2 * kGemmBM : kGemmBM;
   const int tiles = ((p.M + kTileM - 1) / kTileM) * ((p.N + BN - 1) / BN);
   if constexpr (TWO_SM) {

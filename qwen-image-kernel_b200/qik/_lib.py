@@ -19,7 +19,7 @@ DTYPE_BF16, DTYPE_F32, DTYPE_E4M3 = 0, 1, 2
 EPI_SCALE, EPI_GELU_TANH, EPI_SCATTER = 0, 1, 2
 GEMM_TILE_AUTO, GEMM_TILE_PAIR_256, GEMM_TILE_SINGLE_256, GEMM_TILE_SINGLE_128, GEMM_TILE_SINGLE_64 = range(5)
 TP_MAX_WORLD = 8
-ATTN_HAS_CACHE, ATTN_HAS_KEY_VALID, ATTN_UNIFORM, ATTN_V_FP8 = 1, 2, 4, 8
+ATTN_HAS_CACHE, ATTN_HAS_KEY_VALID, ATTN_UNIFORM, ATTN_V_FP8, ATTN_F16 = 1, 2, 4, 8, 16
 STATUS_OK, STATUS_TIMEOUT = 0, 1
 
 _i64, _i32, _f32, _vp, _u64 = ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_uint64
@@ -175,3 +175,4 @@ def reset_quant_state() -> None:
     """Zero every cached quantizer workspace (needed after a call that failed)."""
     for t in _quant_state.values():
         t.zero_()
+

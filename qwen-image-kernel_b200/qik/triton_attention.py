@@ -8,7 +8,8 @@ tcgen05 kernel ``qik_block_causal_attention`` of libqik.so.
 
 The allowed set of query row r is the prefix interval kv <= L[r] of the virtual
 concatenation [cache ; fresh] (triton_attention.py:3-18); the e4m3 cache V is
-dequantized in the loop as bf16(fl32(v8) * scale[b, h]).
+dequantized in the loop as bf16(fl32(v8) * scale[b, h]).  bf16 and fp16 tensors are
+both accepted, as in the reference (P is rounded to the tensors' type before P.V).
 """
 from __future__ import annotations
 
@@ -43,8 +44,7 @@ def block_causal_flash_attention(
     (``FP8Linear.forward_from_amax``) without another pass over ``out``.
     """
     assert query.dtype in (torch.bfloat16, torch.float16), "fp16/bf16 only"
-    if query.dtype != torch.bfloat16:
-        raise NotImplementedError("qik attention: bf16 activations only (the DiT runs bf16)")
+    assert key.dtype == query.dtype and value.dtype == query.dtype, "q, k, v must share one dtype"
     B, SQ, H, D = query.shape
     if cache_k is not None:
         P = cache_k.shape[1]
@@ -70,6 +70,10 @@ def block_causal_flash_attention(
     v_fp8 = cache_v_scale is not None
     if v_fp8:
         assert cache_v is not None and cache_v.dtype == torch.float8_e4m3fn
+    elif P > 0:
+        assert cache_v.dtype == key.dtype
+    if query.dtype == torch.float16:
+        flags |= L.ATTN_F16
     if P > 0:
         ck, cv = unit_d(cache_k), unit_d(cache_v)
         flags |= L.ATTN_HAS_CACHE

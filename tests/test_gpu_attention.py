@@ -304,3 +304,44 @@ def test_amax_out_is_max_abs_of_the_output():
     torch.cuda.synchronize()
     want = np.array([out.float().abs().max().item()], np.float32).view(np.int32)[0]
     assert int(amax.item()) == int(want)
+
+
+@pytest.mark.parametrize("name", ["t2i_prefill", "edit_prefill", "padded_prompt", "batch2", "decode_bf16_slab",
+                                  "decode_fp8_slab"])
+def test_fp16_tensors(attn, golden_dir, name):
+    """The reference accepts fp16 as well as bf16 (triton_attention.py:190): the golden
+    layouts with fp16 q / k / v (and fp16 cache K / V, or the golden e4m3 slab V with its
+    scales), fp16 output, against the fp32 oracle on the same fp16 values."""
+    c = GI.attention_cases()[name]
+    h = lambda t: None if t is None else t.to(torch.float16)  # noqa: E731
+    q, k, v, ck = h(c["q"]), h(c["k"]), h(c["v"]), h(c["cache_k"])
+    L, kv = c["L"], c["key_valid"]
+    if c.get("slab_fp8"):
+        g = np.load(golden_dir / "attention.npz")
+        cv = torch.from_numpy(g[f"{name}__v8"]).view(torch.float8_e4m3fn)
+        vsc = torch.from_numpy(g[f"{name}__vsc"])
+        out = attn.block_causal_flash_attention(q.cuda(), k.cuda(), v.cuda(), L.cuda(), _cuda(kv), ck.cuda(),
+                                                cv.cuda(), vsc.cuda(), uniform_full=True)
+        ref32 = O.block_causal_attention(q, k, v, L, kv, ck, cv, vsc, out_dtype=torch.float32, slab_v_bf16=False)
+    else:
+        cv = h(c["cache_v"])
+        out = attn.block_causal_flash_attention(q.cuda(), k.cuda(), v.cuda(), L.cuda(), _cuda(kv), _cuda(ck),
+                                                _cuda(cv))
+        ref32 = O.block_causal_attention(q, k, v, L, kv, ck, cv, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float16 and out.shape == q.shape
+    _check(out, ref32, tag=f"fp16 {name}")
+
+
+def test_fp16_amax_out_and_dtype_checks(attn):
+    """amax_out for fp16 output holds the fp32 bits of max|out|; mixed q / k / v types
+    are refused, as the reference's single-dtype kernel requires."""
+    q, k, v = (GI.randn_bf16(300 + i, (1, 300, 2, 128), 0.5).to(torch.float16).cuda() for i in range(3))
+    L = torch.full((300,), 299, dtype=torch.int32, device="cuda")
+    amax = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = attn.block_causal_flash_attention(q, k, v, L, None, uniform_full=True, amax_out=amax)
+    torch.cuda.synchronize()
+    got = np.array([amax.item()], dtype=np.int32).view(np.float32)[0]
+    assert got == out.float().abs().max().item()
+    with pytest.raises(AssertionError):
+        attn.block_causal_flash_attention(q, k.to(torch.bfloat16), v, L, None)

@@ -153,3 +153,30 @@ def test_swiglu_fused_up_halves_and_amax(F):
     torch.cuda.synchronize()
     _gate(out, O.swiglu(g_cpu, p_cpu), "swiglu halves")
     assert int(amax.item()) == int(out.float().abs().max().view(torch.int32).item())
+
+
+def test_rms_rope_head_major_layout(F):
+    """A [B, H, S, D] tensor seen as [B, S, H, D] (heads not contiguous within a token):
+    the register-only kernel, same gate."""
+    B, S, H, D = 2, 50, 5, 128
+    base = GI.randn_bf16(420, (B, H, S, D), 0.7)
+    x_cpu = base.transpose(1, 2)
+    x = base.cuda().transpose(1, 2)
+    w = GI.randn_bf16(421, (D,), 0.3) + 1.0
+    fr = _freqs(S, D)
+    out = F.fused_rms_norm_rope(x, w.cuda(), fr.cuda(), 1e-6)
+    torch.cuda.synchronize()
+    _gate(out, O.rms_norm_rope(x_cpu, w, fr.real.float(), fr.imag.float(), 1e-6), "rms_rope head-major")
+
+
+def test_ln_modulate_full_t2i_block_shape(F):
+    """The DiT block's shape (B = 2, S = 4352, D = 3072: 8704 rows streamed through the
+    shared-memory ring, several rounds of every stage) with the amax output."""
+    B, S, D = 2, 4352, 3072
+    x = GI.randn_bf16(422, (B, S, D), 1.5)
+    mod = GI.randn_bf16(423, (B, 4 * D), 0.3)
+    amax = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = F.fused_layer_norm_modulate(x.cuda(), mod.cuda(), 0, 4 * D, None, 1e-6, amax_out=amax)
+    torch.cuda.synchronize()
+    _gate(out, O.layer_norm_modulate(x, mod, 0, None, 1e-6), "ln_modulate t2i")
+    assert int(amax.item()) == int(out.float().abs().max().view(torch.int32).item())
