@@ -1010,6 +1010,86 @@ def sweep(device: torch.device, iters: int = 20, tiles: bool = False) -> list[di
     return rows
 
 
+def load_reference_gpu_modules() -> dict:
+    """The reference's own leaf modules (fp8.py with its Triton cast kernel,
+    triton_attention.py with _qwen21_attn_fwd) from the copy of its package under
+    baseline/_ref, loaded by file path under a synthetic package (its __init__ needs
+    the diffusers runtime).  Used only by --reference-bars."""
+    import importlib.util
+    import types
+    ref_dir = ROOT / "baseline" / "_ref" / "qwen_image_kernel"
+    if not (ref_dir / "fp8.py").exists():
+        raise SystemExit(f"--reference-bars needs the reference package under {ref_dir}")
+    pkg = types.ModuleType("qwen_image_kernel")
+    pkg.__path__ = [str(ref_dir)]
+    sys.modules["qwen_image_kernel"] = pkg
+    mods = {}
+    for name in ("fp8", "triton_attention"):
+        spec = importlib.util.spec_from_file_location(f"qwen_image_kernel.{name}", ref_dir / f"{name}.py")
+        m = importlib.util.module_from_spec(spec)
+        sys.modules[f"qwen_image_kernel.{name}"] = m
+        spec.loader.exec_module(m)
+        mods[name] = m
+    return mods
+
+
+def reference_bars(device: torch.device) -> dict:
+    """The reference's own GPU kernels on this B200 beside qik's, same inputs (the bars
+    of the reference's paths that run here): quantize_tensorwise (aten amax + the
+    Triton _scale_cast_fp8_kernel, fp8.py:24-53) at configs[4] row counts, with the
+    bytes and scale compared, and block_causal_flash_attention (Triton
+    _qwen21_attn_fwd recompiled for sm_100, triton_attention.py:35-260) at config 4 in
+    both forms.  CUDA events, L2 flushed between launches."""
+    from qik import fp8 as F
+    from qik.kv_cache import ContiguousKVCache
+    from qik.triton_attention import block_causal_flash_attention as qattn
+    import triton
+    mods = load_reference_gpu_modules()
+    rattn = mods["triton_attention"].block_causal_flash_attention
+    flush = L2Flush(device)
+    st = torch.cuda.current_stream(device)
+    res = {"triton": triton.__version__}
+    for M in (4352, 9472, 16384):
+        x = torch.randn(M, 3072, device=device).to(torch.bfloat16)
+        for nm, fn in (("reference", lambda: mods["fp8"].quantize_tensorwise(x)), ("qik", lambda: F.quantize_tensorwise(x))):
+            for _ in range(3):
+                fn()
+            ms = _time_ms(fn, 20, flush, st)
+            res[f"quantizer_{M}_{nm}_us"] = round(ms * 1e3, 2)
+            res[f"quantizer_{M}_{nm}_gbs"] = round(3 * M * 3072 / ms / 1e6, 1)
+        qr, sr = mods["fp8"].quantize_tensorwise(x)
+        qq, sq = F.quantize_tensorwise(x)
+        res[f"quantizer_{M}_bytes_and_scale_equal"] = bool(torch.equal(qr.view(torch.uint8), qq.view(torch.uint8))
+                                                           and torch.equal(sr.reshape(-1), sq.reshape(-1)))
+    g = torch.Generator(device=device).manual_seed(9)
+    H, D, S = 24, 128, 6656
+    q, k, v = (torch.randn(1, S, H, D, device=device, generator=g, dtype=torch.bfloat16) for _ in range(3))
+    Lp = torch.arange(S, dtype=torch.int32, device=device)
+    Lp[256:2560] = 2559
+    Lp[2560:] = S - 1
+    fl_p = 4.0 * D * H * float((Lp.long() + 1).sum())
+    P, T = 2560, 4096
+    kp, vp = (torch.randn(1, P, H, D, device=device, generator=g, dtype=torch.bfloat16) for _ in range(2))
+    cache = ContiguousKVCache(1, 1, P, H, D, v_fp8=True, device=device)
+    cache.get_layer(0).store(kp, vp)
+    ck, cv, vs = cache.get_layer(0).views()
+    qd, kn, vn = (torch.randn(1, T, H, D, device=device, generator=g, dtype=torch.bfloat16) for _ in range(3))
+    Ld = torch.full((T,), P + T - 1, dtype=torch.int32, device=device)
+    fl_d = 4.0 * D * H * T * (P + T)
+    forms = {"attention_cfg4_prefill": ((q, k, v, Lp, None), {}, fl_p),
+             "attention_cfg4_decode_fp8_slab": ((qd, kn, vn, Ld, None, ck, cv, vs), {"uniform_full": True}, fl_d)}
+    for name, (a, kw, fl) in forms.items():
+        for nm, fn in (("reference", lambda: rattn(*a, **kw)), ("qik", lambda: qattn(*a, **kw))):
+            for _ in range(3):
+                fn()
+            ms = _time_ms(fn, 10, flush, st)
+            res[f"{name}_{nm}_ms"] = round(ms, 4)
+            res[f"{name}_{nm}_tflops"] = round(fl / ms / 1e9, 1)
+        o_r, o_q = rattn(*a, **kw).float(), qattn(*a, **kw).float()
+        res[f"{name}_relF_qik_vs_reference"] = float(f"{((o_q - o_r).norm() / o_r.norm()).item():.3e}")
+    return res
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1021,6 +1101,8 @@ def main() -> int:
                     help="print the configs[4] GEMM / quantizer sweep (one JSON line per shape) instead of the bench")
     ap.add_argument("--sweep-tiles", action="store_true",
                     help="--sweep with every GEMM tile configuration forced beside the default")
+    ap.add_argument("--reference-bars", action="store_true",
+                    help="time the reference's own GPU kernels (from the copy under baseline/_ref) beside qik's")
     ap.add_argument("--profile-case", choices=PROFILE_CASES,
                     help="run one extras workload three times and exit (the launches an ncu capture selects from)")
     args = ap.parse_args()
@@ -1040,6 +1122,9 @@ def main() -> int:
     torch.cuda.set_device(device)
     if args.profile_case:
         profile_case(device, args.profile_case)
+        return 0
+    if args.reference_bars:
+        print(json.dumps(reference_bars(device)), flush=True)
         return 0
     if args.sweep or args.sweep_tiles:
         for row in sweep(device, tiles=args.sweep_tiles):
