@@ -404,12 +404,13 @@ def _time_ms(fn, iters: int, flush: L2Flush, stream) -> float:
 
 
 def fused_ops_cases(device: torch.device, x: torch.Tensor, mod: torch.Tensor) -> dict:
-    """The four fused elementwise ops at the t2i block shapes (B = 2, S = 4352, width
-    3072, 24 heads of 128, MLP 12288): {name: (callable, algorithmic bytes)}.
-    Algorithmic bytes: every input element read once and every output element written
-    once (bf16), the modulation rows and RoPE tables (L2-resident, shared by all rows)
-    excluded."""
-    from qik.triton_fused import fused_gate_residual, fused_layer_norm_modulate, fused_rms_norm_rope, fused_swiglu
+    """The fused elementwise ops at the t2i block shapes (B = 2, S = 4352, width 3072,
+    24 heads of 128, MLP 12288): {name: (callable, algorithmic bytes)}.  Algorithmic
+    bytes: every input element read once and every output element written once (bf16;
+    e4m3 codes for the layer norm that emits its FP8 linear's input), the modulation
+    rows and RoPE tables (L2-resident, shared by all rows) excluded."""
+    from qik.triton_fused import (fused_gate_residual, fused_layer_norm_modulate, fused_layer_norm_modulate_e4m3,
+                                  fused_rms_norm_rope, fused_swiglu)
     B, S, K = x.shape
     H, D = 24, 128
     g = torch.Generator(device=device).manual_seed(11)
@@ -424,6 +425,8 @@ def fused_ops_cases(device: torch.device, x: torch.Tensor, mod: torch.Tensor) ->
     n_x = x.numel()
     return {
         "layer_norm_modulate": (lambda: fused_layer_norm_modulate(x, mod, 0, mod.stride(0), None, 1e-6, amax), 4 * n_x),
+        "layer_norm_modulate_e4m3": (lambda: fused_layer_norm_modulate_e4m3(x, mod, 0, mod.stride(0), None, 1e-6),
+                                     3 * n_x),
         "rms_norm_rope_q": (lambda: fused_rms_norm_rope(q, wn, freqs, 1e-6), 4 * q.numel()),
         "gate_residual": (lambda: fused_gate_residual(x, f, mod, K, None), 6 * n_x),
         "swiglu_12288": (lambda: fused_swiglu(gate, up, amax), 6 * gate.numel()),
@@ -475,16 +478,15 @@ def attention_cfg4_cases(device: torch.device, g: torch.Generator) -> dict:
 
 def dit_block_case(device: torch.device, g: torch.Generator) -> dict:
     """DiT block @1024 px, CFG batch 2: M = 2 x 4352, the whole block --
-    timestep modulation linear (M = 2), LayerNorm + modulate (its amax feeds the QKV
-    quantizer), fused QKV, per-head RMSNorm + RoPE of q and k, block-causal attention
+    timestep modulation linear (M = 2), LayerNorm + modulate emitting the QKV linear's
+    e4m3 input, fused QKV, per-head RMSNorm + RoPE of q and k, block-causal attention
     (256 text causal + 4096 image; its amax feeds the out-proj quantizer), out-proj, gated
-    residual, LayerNorm + modulate (its
-    amax feeds the FFN's quantizer), FFN (GELU-tanh) and the second
-    gated residual; random-init
-    FP8 weights, synthetic activations."""
+    residual, LayerNorm + modulate emitting the FFN's e4m3 input, FFN (GELU-tanh,
+    BASELINE configs[2]) and the second gated residual; random-init FP8 weights,
+    synthetic activations."""
     from qik import fp8 as F
     from qik.triton_attention import block_causal_flash_attention as attn
-    from qik.triton_fused import fused_gate_residual, fused_layer_norm_modulate, fused_rms_norm_rope
+    from qik.triton_fused import fused_gate_residual, fused_layer_norm_modulate_e4m3, fused_rms_norm_rope
     H, D = 24, 128
     B2, S2 = 2, 4352
     M, K = B2 * S2, 3072
@@ -504,20 +506,20 @@ def dit_block_case(device: torch.device, g: torch.Generator) -> dict:
                         torch.outer(torch.arange(S2, device=device).float(), inv))
     Lt = torch.arange(S2, dtype=torch.int32, device=device)
     Lt[256:] = S2 - 1
-    amax = torch.zeros(3, dtype=torch.int32, device=device)
+    amax = torch.zeros(1, dtype=torch.int32, device=device)
 
     def block():
         mod = lin["mod"](temb) * 0.05  # [B, 6 x 3072]: scale / gate rows of the two sub-blocks
         amax.zero_()
-        hm = fused_layer_norm_modulate(x, mod, 0, mod.stride(0), None, 1e-6, amax_out=amax[0:1])
-        qkv = lin["qkv"].forward_from_amax(hm, amax[0:1]).unflatten(-1, (3 * H, D))
+        hq, hs = fused_layer_norm_modulate_e4m3(x, mod, 0, mod.stride(0), None, 1e-6)
+        qkv = lin["qkv"].forward_e4m3(hq, hs).unflatten(-1, (3 * H, D))
         q, k, v = qkv.chunk(3, dim=-2)
         q = fused_rms_norm_rope(q, wn, freqs, 1e-6)
         k = fused_rms_norm_rope(k, wn, freqs, 1e-6)
-        o = attn(q, k, v, Lt, None, amax_out=amax[2:3])
-        h = fused_gate_residual(x, lin["out"].forward_from_amax(o.flatten(2, 3), amax[2:3]), mod, K, None)
-        hm2 = fused_layer_norm_modulate(h, mod, 2 * K, mod.stride(0), None, 1e-6, amax_out=amax[1:2])
-        f2 = F.fp8_ffn_gelu(hm2.reshape(M, K), lin["up"], lin["down"], x_amax=amax[1:2]).view(B2, S2, K)
+        o = attn(q, k, v, Lt, None, amax_out=amax)
+        h = fused_gate_residual(x, lin["out"].forward_from_amax(o.flatten(2, 3), amax), mod, K, None)
+        hq2, hs2 = fused_layer_norm_modulate_e4m3(h, mod, 2 * K, mod.stride(0), None, 1e-6)
+        f2 = F.fp8_ffn_gelu(hq2.reshape(M, K), lin["up"], lin["down"], x_scale=hs2).view(B2, S2, K)
         return fused_gate_residual(h, f2, mod, 3 * K, None)
 
     lin_fl = 2.0 * M * K * (9216 + 3072 + 12288) + 2.0 * M * 12288 * K + 2.0 * B2 * K * 18432
@@ -608,7 +610,7 @@ PROFILE_CASES = ("attention_cfg4_prefill", "attention_cfg4_decode_fp8_slab", "di
 
 def profile_case(device: torch.device, name: str) -> None:
     """Runs one workload three times (the launches an ncu capture selects from); for
-    fused_ops_t2i each of the four ops three times, for modulation_linear the FP8 linear
+    fused_ops_t2i each of the fused ops three times, for modulation_linear the FP8 linear
     and for quantizer_<M> the activation quantizer three times, an L2 flush before every
     launch."""
     g = torch.Generator(device=device).manual_seed(7)
@@ -672,7 +674,8 @@ def extras(device: torch.device, flush: L2Flush, iters: int = 10) -> dict:
         "ms": round(ms, 4), "tflops": round((lin_fl + at_fl) / ms / 1e9, 1),
         "linear_gflop": round(lin_fl / 1e9, 1), "attention_gflop": round(at_fl / 1e9, 1),
         "api": "qik.processors.QwenImage21KernelBlock.forward (+ the timestep-modulation FP8Linear)",
-        "includes": "modulation GEMV (M=2, 3072->18432), 2x LayerNorm+modulate, fused QKV 3072->9216, "
+        "includes": "modulation GEMV (M=2, 3072->18432), 2x LayerNorm+modulate (each emitting its FP8 linear's "
+                    "e4m3 input), fused QKV 3072->9216, "
                     "RMSNorm+RoPE (q, k), block-causal attention, out-proj, SwiGLU MLP (fused up 3072->12288, "
                     "down 6144->3072), 2x gated residual"}
     case = dit_block_case(device, g)

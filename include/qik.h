@@ -151,12 +151,17 @@ int qik_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64
 #define QIK_GEMM_TILE_SINGLE_256 2  /* single CTAs, 128 x 256 tiles */
 #define QIK_GEMM_TILE_SINGLE_128 3  /* single CTAs, 128 x 128 tiles */
 #define QIK_GEMM_TILE_SINGLE_64 4   /* single CTAs, 128 x 64 tiles */
+/* Tile raster, or-ed into tile_cfg: output tiles walked in groups of g (1..255) row
+ * tiles, each group column tile by column tile (g = 1: row-major); 0 = what
+ * qik_fp8_gemm picks. */
+#define QIK_GEMM_RASTER(g) ((g) << 8)
 
 /*
- * qik_fp8_gemm with the tile configuration forced (QIK_GEMM_TILE_*; AUTO = what
- * qik_fp8_gemm picks).  Every configuration computes the same result; this entry
- * point exists for measurement and for tests that cover each configuration.  No
- * counterpart in the reference (its GEMM is cuBLASLt's choice).
+ * qik_fp8_gemm with the tile configuration forced (QIK_GEMM_TILE_*, optionally or-ed
+ * with QIK_GEMM_RASTER(g); AUTO = what qik_fp8_gemm picks).  Every configuration
+ * computes the same result; this entry point exists for measurement and for tests that
+ * cover each configuration.  No counterpart in the reference (its GEMM is cuBLASLt's
+ * choice).
  */
 int qik_fp8_gemm_tiled(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda,
                        int64_t ldb, const float* scale_a, const float* scale_b, const void* bias, void* C,
@@ -193,6 +198,17 @@ int qik_fp8_ffn_from_amax(const void* x, const uint32_t* x_amax_bits, int64_t M,
                           const uint8_t* w_up, const float* s_up, const void* b_up, const uint8_t* w_down,
                           const float* s_down, const void* b_down, void* y, void* ws, size_t ws_bytes, int* status,
                           void* stream);
+
+/*
+ * qik_fp8_ffn with x already quantized by its producer: xq holds the [M, K] e4m3 codes
+ * of x (16-byte aligned) and x_scale their dynamic scale (as
+ * qik_layer_norm_modulate_e4m3 emits them), so the chain starts at the up-projection
+ * GEMM.  Same result as qik_fp8_ffn on the x those codes quantize.
+ */
+int qik_fp8_ffn_e4m3(const uint8_t* xq, const float* x_scale, int64_t M, int64_t K, int64_t hidden,
+                     const uint8_t* w_up, const float* s_up, const void* b_up, const uint8_t* w_down,
+                     const float* s_down, const void* b_down, void* y, void* ws, size_t ws_bytes, int* status,
+                     void* stream);
 
 /* Attention flags. */
 #define QIK_ATTN_HAS_CACHE 1     /* keys/values = virtual concat [cache ; fresh] */
@@ -283,6 +299,26 @@ int qik_rms_norm_rope(const void* x, int64_t B, int64_t S, int64_t H, int64_t D,
 int qik_layer_norm_modulate(const void* x, int64_t B, int64_t S, int64_t D, const void* modulation,
                             int64_t mod_rows, int64_t mod_stride, int64_t scale_off, const uint8_t* target_mask,
                             float eps, void* out, uint32_t* amax_out, void* stream);
+
+/*
+ * qik_layer_norm_modulate feeding an FP8 linear: the same bf16 outputs, quantized
+ * with their own dynamic per-tensor scale exactly as qik_quantize_act would quantize
+ * them (same codes, same scale), without the bf16 tensor ever being written.
+ * Replaces fused_layer_norm_modulate (qwen_image_kernel/triton_fused.py:111-160)
+ * followed by the quantize_tensorwise of the next FP8Linear.forward
+ * (qwen_image_kernel/fp8.py:44-53, 85-86).  One cooperative kernel: the rows are
+ * normalized twice, once for max|out| and, after a grid-wide exchange, once for the
+ * codes (the second read of x comes from L2 while x fits there).
+ *   q: [B, S, D] e4m3 (16-byte aligned); scale_out: 1 fp32 (device).
+ *   ws: qik_quant_workspace_bytes() bytes with the qik_quantize_act contract (zero
+ *       once, then reuse in stream order; zero again after a failed call).
+ *   status: NULL or a device int set to QIK_STATUS_TIMEOUT on a failed wait (the
+ *       scale is then NaN).
+ * Other arguments and limits as qik_layer_norm_modulate.
+ */
+int qik_layer_norm_modulate_e4m3(const void* x, int64_t B, int64_t S, int64_t D, const void* modulation,
+                                 int64_t mod_rows, int64_t mod_stride, int64_t scale_off, const uint8_t* target_mask,
+                                 float eps, uint8_t* q, float* scale_out, void* ws, int* status, void* stream);
 
 /*
  * Gated residual out = x + bf16(tanh(gate)) * f in bf16 arithmetic, the gate row

@@ -478,6 +478,15 @@ __device__ __forceinline__ uint32_t f2_to_bf2(uint64_t v) {
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
 }
+// bf16x2 product rounded once to nearest even.  The fp32 product of two bf16 values is
+// exact (8-bit significands) above the fp32 normal range's floor, so this equals
+// bf16(fl32(a) * fl32(b)); only products below 2^-126 (where an fp32 multiply would
+// round to a subnormal first) can differ, by the fp32 multiply's double rounding.
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 __device__ __forceinline__ float f2_sum(uint64_t v) {
   float lo, hi;
   f2_unpack(v, lo, hi);
@@ -516,6 +525,111 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
 }
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Eight bf16 (one 16-byte vector) -> eight e4m3 codes of fl32(x) * inv: the activation
+// cast (fp8.py:36-41).  Returns bytes 0-3, bytes 4-7 in hi_word.
+__device__ __forceinline__ uint32_t pack8_e4m3(const uint4 a, float inv, uint32_t& hi_word) {
+  const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+  const uint64_t inv2 = f2_pack(inv, inv);
+  uint32_t o[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    float a0, a1, b0, b1;
+    f2_unpack(fmul2(bf2_to_f2(w[2 * j]), inv2), a0, a1);  // each lane an fp32 multiply, as fl32(x) * inv
+    f2_unpack(fmul2(bf2_to_f2(w[2 * j + 1]), inv2), b0, b1);
+    o[j] = static_cast<uint32_t>(cvt_e4m3x2(a0, a1)) | (static_cast<uint32_t>(cvt_e4m3x2(b0, b1)) << 16);
+  }
+  hi_word = o[1];
+  return o[0];
+}
+
+// ---------------------------------------------------------------- L2 cache policies
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint4 ld_nc_hint(const uint4* p, uint64_t pol) {
+  uint4 r;
+  asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p), "l"(pol));
+  return r;
+}
+__device__ __forceinline__ void st_v2_hint(void* p, uint32_t a, uint32_t b, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.v2.b32 [%0], {%1, %2}, %3;" ::"l"(p), "r"(a), "r"(b), "l"(pol) : "memory");
+}
+// bulk_load with an L2 cache policy for the source lines.
+__device__ __forceinline__ void bulk_load_hint(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar,
+                                               uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+
+// ---------------------------------------------------------------- grid-wide amax
+// Workspace of the kernels that must know max|x| over the whole tensor before they
+// write a single e4m3 code (the single-pass activation quantizer, the layer norm that
+// emits codes).  `bar` is a grid barrier: a generation in the high 32 bits and the
+// arrivals of the running call in the low 32.  The last CTA to arrive returns the
+// arrivals to 0 and advances the generation in one atomic add, so a workspace that
+// was zeroed once serves any number of calls in stream order without being cleared
+// again.  partial[i] holds CTA i's max|x| bits for the running call: written before
+// the CTA arrives, read by every CTA after the barrier, so stale contents never
+// matter.  amax_bits belongs to the two-pass form (amax kernel, then pack), which
+// clears it itself.  Kernels using the barrier are launched cooperatively (every CTA
+// resident), with at most kQuantMaxCtas CTAs.
+constexpr int kQuantMaxCtas = 252;
+struct QuantWs {
+  unsigned long long bar;
+  uint32_t amax_bits;
+  uint32_t pad;
+  uint32_t partial[kQuantMaxCtas];
+};
+static_assert(sizeof(QuantWs) == 1024, "QuantWs layout");
+constexpr uint32_t kQuantAbortMark = 0xFFFFFFFFu;  // a partial above every |x| bit pattern: a CTA gave up
+
+// One thread per CTA: publish this CTA's max (bits; kQuantAbortMark when the CTA gave
+// up) in its slot and wait until every CTA of the grid has published.  The arrival
+// releases the slot write; the last arrival acquires every earlier one (they form one
+// release sequence) and publishes the next generation.  Returns false when the wait
+// ran out (QIK_WAIT_NS).
+__device__ __forceinline__ bool grid_max_publish_wait(QuantWs* ws, uint32_t m) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(&ws->partial[blockIdx.x]), "r"(m) : "memory");
+  unsigned long long old;
+  asm volatile("atom.add.acq_rel.gpu.global.u64 %0, [%1], 1;" : "=l"(old) : "l"(&ws->bar) : "memory");
+  const uint32_t gen = static_cast<uint32_t>(old >> 32);
+  if (static_cast<uint32_t>(old) == gridDim.x - 1) {
+    const unsigned long long step = (1ull << 32) - gridDim.x;  // generation + 1, arrivals back to 0
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(&ws->bar), "l"(step) : "memory");
+    return true;
+  }
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 0;; ++it) {
+    unsigned long long cur;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(cur) : "l"(&ws->bar) : "memory");
+    if (static_cast<uint32_t>(cur >> 32) != gen) return true;
+    if ((it & 255u) == 255u && globaltimer() - t0 > QIK_WAIT_NS) return false;
+  }
+}
+// One full warp, after its CTA passed grid_max_publish_wait: the max over every CTA's
+// slot (kQuantAbortMark when any CTA gave up), in every lane.
+__device__ __forceinline__ uint32_t grid_max_collect(const QuantWs* ws) {
+  uint32_t g = 0;
+  for (uint32_t i = threadIdx.x & 31u; i < gridDim.x; i += 32) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(&ws->partial[i]) : "memory");
+    g = max(g, v);
+  }
+  return __reduce_max_sync(0xffffffffu, g);
 }
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   __half2 v = __floats2half2_rn(lo, hi);

@@ -15,7 +15,8 @@
 // SM count with grid-stride loops.  Layer norm and SwiGLU can also accumulate the
 // amax of their bf16 output (fp32 bit patterns, atomicMax), which is the reduction
 // the next FP8 linear's dynamic quantizer needs, so that linear can skip its own
-// amax pass (qik_quantize_act_from_amax).
+// amax pass (qik_quantize_act_from_amax); the layer norm can also emit that linear's
+// e4m3 input itself (ln_modulate_e4m3_kernel, qik_layer_norm_modulate_e4m3).
 #include <mutex>
 
 #include "qik_device.cuh"
@@ -154,6 +155,64 @@ __device__ __forceinline__ void stream_bars_init(uint64_t* full, uint64_t* empty
   __syncthreads();
 }
 
+// bf16(1 + scale) of the first mod_rows modulation rows into `table` (nv vectors a row).
+__device__ __forceinline__ void ln_modulate_table(uint4* table, const uint16_t* __restrict__ mod, int64_t mod_stride,
+                                                  int64_t scale_off, int mod_rows, int nv) {
+  for (int e = threadIdx.x; e < mod_rows * nv; e += blockDim.x) {
+    const int r = e / nv, c = e - r * nv;
+    const uint4 m = ldg16(mod + r * mod_stride + scale_off + c * 8);
+    const uint32_t w[4] = {m.x, m.y, m.z, m.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o[k] = f2_to_bf2(fadd2(bf2_to_f2(w[k]), f2_pack(1.0f, 1.0f)));
+    table[e] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// LayerNorm + modulation of one row held in shared memory, by one warp, in two steps:
+// ln_row_stats gives (-mean, -mean) and (rstd, rstd) as fp32 pairs (fp32 mean and
+// centred variance), ln_row_out computes y = bf16((x - mean) * rstd) and out =
+// bf16(y * bf16(1 + scale)) -- one packed bf16 multiply, the product of two bf16 values
+// being exact in fp32 -- and hands emit(idx, o) the 8 outputs of vector idx as four
+// bf16x2 words.
+__device__ __forceinline__ void ln_row_stats(const uint4* xr, int nv, int D, float eps, int lane, uint64_t& nm2,
+                                             uint64_t& r2) {
+  uint64_t acc = 0ull;  // (0.f, 0.f)
+  for (int idx = lane; idx < nv; idx += 32) {
+    const uint4 v = xr[idx];
+    acc = fadd2(fadd2(acc, bf2_to_f2(v.x)), bf2_to_f2(v.y));
+    acc = fadd2(fadd2(acc, bf2_to_f2(v.z)), bf2_to_f2(v.w));
+  }
+  const float mean = warp_sum(f2_sum(acc)) / static_cast<float>(D);
+  nm2 = f2_pack(-mean, -mean);
+  acc = 0ull;
+  for (int idx = lane; idx < nv; idx += 32) {
+    const uint4 v = xr[idx];
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint64_t d = fadd2(bf2_to_f2(u[k]), nm2);
+      acc = ffma2(d, d, acc);
+    }
+  }
+  const float var = warp_sum(f2_sum(acc)) / static_cast<float>(D);
+  r2 = f2_pack(rsqrtf(var + eps), rsqrtf(var + eps));
+}
+
+template <typename Emit>
+__device__ __forceinline__ void ln_row_out(const uint4* xr, const uint4* tr, int nv, uint64_t nm2, uint64_t r2,
+                                           int lane, Emit emit) {
+#pragma unroll 2
+  for (int idx = lane; idx < nv; idx += 32) {
+    const uint4 v = xr[idx], sv = tr[idx];
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w}, m[4] = {sv.x, sv.y, sv.z, sv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o[k] = mul_bf16x2(f2_to_bf2(fmul2(fadd2(bf2_to_f2(u[k]), nm2), r2)), m[k]);
+    emit(idx, o);
+  }
+}
+
 __global__ void __launch_bounds__(kStreamThreads, 1)
     ln_modulate_stream_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ mod, int64_t mod_stride,
                               int64_t scale_off, const uint8_t* __restrict__ tmask, uint16_t* __restrict__ out,
@@ -166,15 +225,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nv = D >> 3;  // 16-byte vectors per row; a stage holds kStreamWarps rows = 8 nv vectors
   uint4* table = ring + static_cast<int64_t>(stages) * kStreamWarps * nv;
-  for (int e = threadIdx.x; e < mod_rows * nv; e += blockDim.x) {
-    const int r = e / nv, c = e - r * nv;
-    const uint4 m = ldg16(mod + r * mod_stride + scale_off + c * 8);
-    const uint32_t w[4] = {m.x, m.y, m.z, m.w};
-    uint32_t o[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) o[k] = f2_to_bf2(fadd2(bf2_to_f2(w[k]), f2_pack(1.0f, 1.0f)));
-    table[e] = make_uint4(o[0], o[1], o[2], o[3]);
-  }
+  ln_modulate_table(table, mod, mod_stride, scale_off, mod_rows, nv);
   stream_bars_init(full, empty, stages, &abort_flag);  // (its barrier also publishes the table)
   const int64_t nrows = B * S;
   const int64_t ngroups = (nrows + kStreamWarps - 1) / kStreamWarps;
@@ -201,52 +252,146 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       if (!__all_sync(0xffffffffu, mbar_wait(&full[st], (i / stages) & 1, &abort_flag, nullptr))) break;
       const int64_t row = g * kStreamWarps + cw;
       if (row < nrows) {
-        const uint4* xr = ring + (static_cast<int64_t>(st) * kStreamWarps + cw) * nv;
         const int64_t b = row / S, s = row % S;
-        uint64_t acc = 0ull;  // (0.f, 0.f)
-        for (int idx = lane; idx < nv; idx += 32) {
-          const uint4 v = xr[idx];
-          acc = fadd2(fadd2(acc, bf2_to_f2(v.x)), bf2_to_f2(v.y));
-          acc = fadd2(fadd2(acc, bf2_to_f2(v.z)), bf2_to_f2(v.w));
-        }
-        const float mean = warp_sum(f2_sum(acc)) / static_cast<float>(D);
-        const uint64_t nm2 = f2_pack(-mean, -mean);
-        acc = 0ull;
-        for (int idx = lane; idx < nv; idx += 32) {
-          const uint4 v = xr[idx];
-          const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint64_t d = fadd2(bf2_to_f2(u[k]), nm2);
-            acc = ffma2(d, d, acc);
-          }
-        }
-        const float var = warp_sum(f2_sum(acc)) / static_cast<float>(D);
-        const uint64_t r2 = f2_pack(rsqrtf(var + eps), rsqrtf(var + eps));
         // target positions use their own sample's row b, the others row B + b
         const int64_t mrow = (tmask == nullptr || tmask[s] != 0) ? b : B + b;
-        const uint4* tr = table + mrow * nv;
         uint16_t* orow = out + row * D;
-#pragma unroll 2
-        for (int idx = lane; idx < nv; idx += 32) {
-          const uint4 v = xr[idx], sv = tr[idx];
-          const uint32_t u[4] = {v.x, v.y, v.z, v.w}, m[4] = {sv.x, sv.y, sv.z, sv.w};
-          uint32_t o[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            // y = bf16((x - mean) * rstd); out = bf16(y * bf16(1 + scale))
-            const uint32_t y = f2_to_bf2(fmul2(fadd2(bf2_to_f2(u[k]), nm2), r2));
-            o[k] = f2_to_bf2(fmul2(bf2_to_f2(y), bf2_to_f2(m[k])));
-            am2 = absmax_bf16x2(am2, o[k]);
-          }
+        const uint4* xr = ring + (static_cast<int64_t>(st) * kStreamWarps + cw) * nv;
+        uint64_t nm2, r2;
+        ln_row_stats(xr, nv, D, eps, lane, nm2, r2);
+        ln_row_out(xr, table + mrow * nv, nv, nm2, r2, lane, [&](int idx, const uint32_t(&o)[4]) {
+          am2 = absmax_bf16x2(absmax_bf16x2(am2, o[0]), o[1]);
+          am2 = absmax_bf16x2(absmax_bf16x2(am2, o[2]), o[3]);
           *reinterpret_cast<uint4*>(orow + idx * 8) = make_uint4(o[0], o[1], o[2], o[3]);
-        }
+        });
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
     }
   }
   if (amax_out) block_atomic_max(max(am2 & 0xFFFFu, am2 >> 16) << 16, amax_out);
+}
+
+// LayerNorm + modulation emitting e4m3 codes with the output's own dynamic per-tensor
+// scale (fused_layer_norm_modulate followed by quantize_tensorwise, without the bf16
+// output ever reaching memory).  The scale needs max|out| over the whole tensor before
+// the first code, so the kernel makes two passes over the same rows, launched
+// cooperatively (one CTA per SM, every CTA resident): pass 0 streams the CTA's row
+// groups through the ring (L2 evict-last), reduces max|out| and keeps each row's mean
+// and rstd in shared memory; a grid-wide exchange (grid_max_publish_wait) gives every
+// CTA the global amax; pass 1 streams the same groups again (evict-first, from L2 while
+// they are there), recomputes the identical outputs from the kept statistics and
+// stores fl32(out) * (1/s) as e4m3.  The producer runs straight on into
+// pass 1 while the consumers wait at the exchange.  HBM traffic: x once (2 B per
+// element while x fits in L2) and the codes (1 B).  On a failed wait every CTA skips
+// its stores (still draining the ring), CTA 0 writes a NaN scale and `status` records
+// the timeout; the workspace must then be zeroed again before reuse.
+constexpr int kStreamConsumerThreads = 32 * kStreamWarps * kStreamSets;
+
+__global__ void __launch_bounds__(kStreamThreads, 1)
+    ln_modulate_e4m3_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ mod, int64_t mod_stride,
+                            int64_t scale_off, const uint8_t* __restrict__ tmask, uint8_t* __restrict__ q,
+                            float* __restrict__ scale_out, int64_t B, int64_t S, int D, float eps, int stages,
+                            int mod_rows, QuantWs* __restrict__ ws, int* __restrict__ status) {
+  extern __shared__ __align__(128) uint4 ring[];
+  __shared__ __align__(8) uint64_t full[kStreamMaxStages], empty[kStreamMaxStages];
+  __shared__ int abort_flag;
+  __shared__ uint32_t warp_max[kStreamWarps * kStreamSets];
+  __shared__ uint32_t amax_all;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nv = D >> 3;
+  // [stages][8 rows][nv] ring, the modulation table, then (-mean, rstd) of each row of
+  // this CTA (pass 0 computes them, pass 1 reuses them)
+  uint4* table = ring + static_cast<int64_t>(stages) * kStreamWarps * nv;
+  uint4* stats = table + static_cast<int64_t>(mod_rows) * nv;
+  ln_modulate_table(table, mod, mod_stride, scale_off, mod_rows, nv);
+  stream_bars_init(full, empty, stages, &abort_flag);
+  const int64_t nrows = B * S;
+  const int64_t ngroups = (nrows + kStreamWarps - 1) / kStreamWarps;
+  // this CTA's groups: blockIdx.x + k * gridDim.x, k < mine; item j of the ring is
+  // group j % mine of pass j / mine
+  const int64_t mine = ngroups > blockIdx.x ? (ngroups - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol_keep = l2_evict_last_policy(), pol_once = l2_evict_first_policy();
+      for (int64_t j = 0; j < 2 * mine; ++j) {
+        const int st = static_cast<int>(j % stages);
+        if (!mbar_wait(&empty[st], static_cast<uint32_t>((j / stages) & 1) ^ 1u, &abort_flag, status)) break;
+        const int64_t r0 = (blockIdx.x + (j % mine) * gridDim.x) * kStreamWarps;
+        const int64_t rows = min(static_cast<int64_t>(kStreamWarps), nrows - r0);
+        const uint32_t bytes = static_cast<uint32_t>(rows * D * 2);
+        mbar_arrive_expect_tx(&full[st], bytes);
+        bulk_load_hint(ring + static_cast<int64_t>(st) * kStreamWarps * nv, x + r0 * D, bytes, &full[st],
+                       j < mine ? pol_keep : pol_once);
+      }
+    }
+    return;
+  }
+  const int cwarp = warp - 1;
+  const int set = cwarp / kStreamWarps, cw = cwarp % kStreamWarps;
+  uint32_t am2 = 0;
+  float inv = 0.0f;
+  bool skip = false;  // pass 1 without stores: some CTA gave up
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass == 1) {
+      // grid-wide max|out|: warp maxima -> CTA max -> every CTA's slot
+      const uint32_t m = __reduce_max_sync(0xffffffffu, max(am2 & 0xFFFFu, am2 >> 16) << 16);
+      if (lane == 0) warp_max[cwarp] = m;
+      named_bar_sync(1, kStreamConsumerThreads);
+      if (cwarp == 0) {
+        uint32_t c = lane < kStreamWarps * kStreamSets ? warp_max[lane] : 0u;
+        c = __reduce_max_sync(0xffffffffu, c);
+        bool ok = true;
+        if (lane == 0) {
+          ok = grid_max_publish_wait(ws, abort_flag ? kQuantAbortMark : c);
+          if (!ok && status) atomicExch(status, QIK_DEV_TIMEOUT);
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        __syncwarp();  // lane 0's acquire of the barrier before every lane's slot reads
+        const uint32_t g = grid_max_collect(ws);
+        if (lane == 0) amax_all = ok ? g : kQuantAbortMark;
+      }
+      named_bar_sync(1, kStreamConsumerThreads);
+      skip = amax_all == kQuantAbortMark;
+      const float s = skip ? __int_as_float(0x7fc00000) : scale_from_amax_bits(amax_all);
+      inv = act_inverse(s);
+      if (blockIdx.x == 0 && cwarp == 0 && lane == 0) scale_out[0] = s;
+    }
+    for (int64_t j = pass * mine + set; j < (pass + 1) * mine; j += kStreamSets) {
+      const int st = static_cast<int>(j % stages);
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[st], static_cast<uint32_t>((j / stages) & 1), &abort_flag, status)))
+        break;
+      const int64_t row = (blockIdx.x + (j % mine) * gridDim.x) * kStreamWarps + cw;
+      if (row < nrows) {
+        const int64_t b = row / S, s = row % S;
+        const int64_t mrow = (tmask == nullptr || tmask[s] != 0) ? b : B + b;
+        const uint4* xr = ring + (static_cast<int64_t>(st) * kStreamWarps + cw) * nv;
+        uint4* rs = stats + (j % mine) * kStreamWarps + cw;  // the row's (-mean, rstd) pairs
+        if (pass == 0) {
+          uint64_t nm2, r2;
+          ln_row_stats(xr, nv, D, eps, lane, nm2, r2);
+          if (lane == 0) *rs = make_uint4(static_cast<uint32_t>(nm2), static_cast<uint32_t>(nm2 >> 32),
+                                          static_cast<uint32_t>(r2), static_cast<uint32_t>(r2 >> 32));
+          ln_row_out(xr, table + mrow * nv, nv, nm2, r2, lane, [&](int, const uint32_t(&o)[4]) {
+            am2 = absmax_bf16x2(absmax_bf16x2(am2, o[0]), o[1]);
+            am2 = absmax_bf16x2(absmax_bf16x2(am2, o[2]), o[3]);
+          });
+        } else if (!skip) {
+          const uint4 sv = *rs;  // written by this warp's lane 0 in pass 0
+          const uint64_t nm2 = (static_cast<uint64_t>(sv.y) << 32) | sv.x;
+          const uint64_t r2 = (static_cast<uint64_t>(sv.w) << 32) | sv.z;
+          uint2* qrow = reinterpret_cast<uint2*>(q + row * D);
+          ln_row_out(xr, table + mrow * nv, nv, nm2, r2, lane, [&](int idx, const uint32_t(&o)[4]) {
+            uint32_t hi;
+            const uint32_t lo = pack8_e4m3(make_uint4(o[0], o[1], o[2], o[3]), inv, hi);
+            qrow[idx] = make_uint2(lo, hi);
+          });
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+  }
 }
 
 // RMSNorm + RoPE over tokens whose heads are contiguous (x_sh == D, as in the strided
@@ -337,23 +482,31 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 }
 
 // Shared memory ring of a streaming kernel: stages of `stage_bytes`, at least 2 and at
-// most kStreamMaxStages within kStreamRingBytes; 0 when a stage does not fit twice.
-int stream_stages(int64_t stage_bytes) {
-  const int64_t n = kStreamRingBytes / stage_bytes;
-  return n < 2 ? 0 : static_cast<int>(n < kStreamMaxStages ? n : kStreamMaxStages);
+// most kStreamMaxStages within kStreamRingBytes less `reserved` bytes; 0 when a stage
+// does not fit twice.  The count is even: the two consumer sets take alternate ring
+// items, so a stage's previous item then belongs to the same set, which has consumed
+// it before it waits on the stage's next phase (with an odd count the other set's
+// previous item could still be in flight, and a parity wait would see a stale phase).
+int stream_stages(int64_t stage_bytes, int64_t reserved = 0) {
+  int64_t n = (kStreamRingBytes - reserved) / stage_bytes;
+  n = n < kStreamMaxStages ? n : kStreamMaxStages;
+  return n < 2 ? 0 : static_cast<int>(n & ~int64_t{1});
 }
 
 template <typename Kernel>
-int stream_smem_attr(Kernel kernel, std::once_flag* once, const char* what) {
+int stream_smem_attr(Kernel kernel, std::once_flag* once, const char* what, int bytes = kStreamRingBytes) {
   int dev = 0;
   QIK_TRY_CUDA(cudaGetDevice(&dev));
   QIK_REQUIRE(dev >= 0 && dev < 64, "%s: device ordinal %d out of range", what, dev);
   cudaError_t rc = cudaSuccess;
   std::call_once(once[dev], [&] {
-    rc = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamRingBytes);
+    rc = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   });
   return cuda_status(rc, what);
 }
+// Dynamic shared memory of ln_modulate_e4m3_kernel: the ring and table as the other
+// streaming kernels, plus 16 bytes of row statistics for each row of its CTA.
+constexpr int kLnE4m3SmemBytes = 224 * 1024;
 
 // ---------------------------------------------------------------- gate + residual
 // Thread = one 8-column vector of the width, walking kGateRows consecutive rows
@@ -555,46 +708,103 @@ int qik_rms_norm_rope(const void* x, int64_t B, int64_t S, int64_t H, int64_t D,
   return check_launch("rms_rope_kernel");
 }
 
+static int check_ln_args(const char* what, const void* x, int64_t B, int64_t S, int64_t D, const void* modulation,
+                         int64_t mod_rows, int64_t mod_stride, int64_t scale_off, const uint8_t* target_mask,
+                         const void* out) {
+  QIK_REQUIRE(x && modulation && out, "%s: NULL pointer", what);
+  QIK_REQUIRE(D % 8 == 0 && D <= 4096, "%s: D must be a multiple of 8 and at most 4096", what);
+  QIK_REQUIRE(B * S < (int64_t{1} << 31), "%s: more than 2^31 rows", what);
+  QIK_REQUIRE(aligned16(x) && aligned16(out) && aligned16(modulation), "%s: pointers must be 16-byte aligned", what);
+  QIK_REQUIRE(aligned_elems(mod_stride) && aligned_elems(scale_off) && scale_off >= 0 && scale_off + D <= mod_stride,
+              "%s: modulation stride/offset must be multiples of 8 with offset + D <= stride", what);
+  QIK_REQUIRE(mod_rows >= (target_mask ? 2 * B : B), "%s: %lld modulation rows; B = %lld needs %s", what,
+              static_cast<long long>(mod_rows), static_cast<long long>(B),
+              target_mask ? "2B (rows B..2B-1 are the t = 0 rows)" : "B");
+  return QIK_OK;
+}
+
+// Ring geometry of the layer-norm kernels: 8-row stages beside the table of bf16(1 +
+// scale) for every modulation row in use.  Returns the stage count (0: does not fit).
+static int ln_ring(int64_t B, int64_t D, const uint8_t* target_mask, int* mod_used, size_t* smem) {
+  *mod_used = static_cast<int>(target_mask ? 2 * B : B);
+  const int64_t table_bytes = static_cast<int64_t>(*mod_used) * D * 2;
+  const int64_t stage_bytes = static_cast<int64_t>(kStreamWarps) * D * 2;
+  const int stages = table_bytes < kStreamRingBytes ? stream_stages(stage_bytes, table_bytes) : 0;
+  *smem = static_cast<size_t>(stages) * stage_bytes + static_cast<size_t>(table_bytes);
+  return stages;
+}
+
 int qik_layer_norm_modulate(const void* x, int64_t B, int64_t S, int64_t D, const void* modulation,
                             int64_t mod_rows, int64_t mod_stride, int64_t scale_off, const uint8_t* target_mask,
                             float eps, void* out, uint32_t* amax_out, void* stream) {
   QIK_REQUIRE(B >= 0 && S >= 0 && D > 0, "qik_layer_norm_modulate: bad sizes");
   if (B * S == 0) return QIK_OK;
-  QIK_REQUIRE(x && modulation && out, "qik_layer_norm_modulate: NULL pointer");
-  QIK_REQUIRE(D % 8 == 0 && D <= 4096, "qik_layer_norm_modulate: D must be a multiple of 8 and at most 4096");
-  QIK_REQUIRE(B * S < (int64_t{1} << 31), "qik_layer_norm_modulate: more than 2^31 rows");
-  QIK_REQUIRE(aligned16(x) && aligned16(out) && aligned16(modulation),
-              "qik_layer_norm_modulate: pointers must be 16-byte aligned");
-  QIK_REQUIRE(aligned_elems(mod_stride) && aligned_elems(scale_off) && scale_off >= 0 && scale_off + D <= mod_stride,
-              "qik_layer_norm_modulate: modulation stride/offset must be multiples of 8 with offset + D <= stride");
-  QIK_REQUIRE(mod_rows >= (target_mask ? 2 * B : B),
-              "qik_layer_norm_modulate: %lld modulation rows; B = %lld needs %s", static_cast<long long>(mod_rows),
-              static_cast<long long>(B), target_mask ? "2B (rows B..2B-1 are the t = 0 rows)" : "B");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int64_t rows = B * S;
-  const uint16_t* xs = static_cast<const uint16_t*>(x);
-  const uint16_t* ms = static_cast<const uint16_t*>(modulation);
-  uint16_t* os = static_cast<uint16_t*>(out);
-  // bf16(1 + scale) of every modulation row in use sits in shared memory beside the ring
-  const int mod_used = static_cast<int>(target_mask ? 2 * B : B);
-  const int64_t table_bytes = static_cast<int64_t>(mod_used) * D * 2;
-  const int64_t stage_bytes = static_cast<int64_t>(kStreamWarps) * D * 2;
-  const int64_t fit = (kStreamRingBytes - table_bytes) / stage_bytes;  // stages that fit beside the table
-  const int stages = fit < 2 ? 0 : static_cast<int>(fit < kStreamMaxStages ? fit : kStreamMaxStages);
-  if (stages > 0) {
-    // rows streamed through shared memory, 8 per stage
-    static std::once_flag once[64];
-    const int grid = grid_cap((rows + kStreamWarps - 1) / kStreamWarps, 1);
-    const size_t smem = static_cast<size_t>(stages) * stage_bytes + static_cast<size_t>(table_bytes);
-    int rc;
-    if ((rc = stream_smem_attr(ln_modulate_stream_kernel, once, "ln_modulate_stream_kernel"))) return rc;
-    ln_modulate_stream_kernel<<<grid, kStreamThreads, smem, st>>>(xs, ms, mod_stride, scale_off, target_mask, os, B, S,
-                                                                 static_cast<int>(D), eps, amax_out, stages, mod_used);
-    return check_launch("ln_modulate_stream_kernel");
+  int rc = check_ln_args("qik_layer_norm_modulate", x, B, S, D, modulation, mod_rows, mod_stride, scale_off,
+                         target_mask, out);
+  if (rc) return rc;
+  int mod_used = 0;
+  size_t smem = 0;
+  const int stages = ln_ring(B, D, target_mask, &mod_used, &smem);
+  if (stages == 0)
+    return set_error(QIK_ERR_UNSUPPORTED,
+                     "qik_layer_norm_modulate: width %lld with %d modulation rows does not fit the row ring",
+                     static_cast<long long>(D), mod_used);
+  // rows streamed through shared memory, 8 per stage
+  static std::once_flag once[64];
+  if ((rc = stream_smem_attr(ln_modulate_stream_kernel, once, "ln_modulate_stream_kernel"))) return rc;
+  const int grid = grid_cap((B * S + kStreamWarps - 1) / kStreamWarps, 1);
+  ln_modulate_stream_kernel<<<grid, kStreamThreads, smem, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(modulation), mod_stride, scale_off, target_mask,
+      static_cast<uint16_t*>(out), B, S, static_cast<int>(D), eps, amax_out, stages, mod_used);
+  return check_launch("ln_modulate_stream_kernel");
+}
+
+int qik_layer_norm_modulate_e4m3(const void* x, int64_t B, int64_t S, int64_t D, const void* modulation,
+                                 int64_t mod_rows, int64_t mod_stride, int64_t scale_off, const uint8_t* target_mask,
+                                 float eps, uint8_t* q, float* scale_out, void* ws, int* status, void* stream) {
+  QIK_REQUIRE(B >= 0 && S >= 0 && D > 0, "qik_layer_norm_modulate_e4m3: bad sizes");
+  QIK_REQUIRE(scale_out && ws, "qik_layer_norm_modulate_e4m3: scale_out/ws is NULL");
+  QIK_REQUIRE(aligned16(ws), "qik_layer_norm_modulate_e4m3: ws must be 16-byte aligned");
+  if (B * S == 0) return QIK_OK;
+  int rc = check_ln_args("qik_layer_norm_modulate_e4m3", x, B, S, D, modulation, mod_rows, mod_stride, scale_off,
+                         target_mask, q);
+  if (rc) return rc;
+  int mod_used = 0;
+  size_t smem = 0;
+  int stages = ln_ring(B, D, target_mask, &mod_used, &smem);
+  // cooperative: every CTA resident (one per SM) for the grid-wide amax exchange
+  const int64_t ngroups = (B * S + kStreamWarps - 1) / kStreamWarps;
+  const int64_t cap = sm_count() < kQuantMaxCtas ? sm_count() : kQuantMaxCtas;
+  const int64_t grid = ngroups < cap ? ngroups : cap;
+  const size_t stats_bytes = static_cast<size_t>((ngroups + grid - 1) / grid) * kStreamWarps * 16;
+  const size_t stage_bytes = static_cast<size_t>(kStreamWarps) * D * 2;
+  while (stages > 2 && smem + stats_bytes > static_cast<size_t>(kLnE4m3SmemBytes)) {
+    stages -= 2;  // even, as stream_stages keeps it
+    smem -= 2 * stage_bytes;
   }
-  return set_error(QIK_ERR_UNSUPPORTED,
-                   "qik_layer_norm_modulate: width %lld with %d modulation rows does not fit the row ring",
-                   static_cast<long long>(D), mod_used);
+  if (stages == 0 || smem + stats_bytes > static_cast<size_t>(kLnE4m3SmemBytes))
+    return set_error(QIK_ERR_UNSUPPORTED,
+                     "qik_layer_norm_modulate_e4m3: width %lld with %d modulation rows and %lld rows does not fit "
+                     "shared memory",
+                     static_cast<long long>(D), mod_used, static_cast<long long>(B * S));
+  smem += stats_bytes;
+  static std::once_flag once[64];
+  if ((rc = stream_smem_attr(ln_modulate_e4m3_kernel, once, "ln_modulate_e4m3_kernel", kLnE4m3SmemBytes))) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kStreamThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  QIK_TRY_CUDA(cudaLaunchKernelEx(&cfg, ln_modulate_e4m3_kernel, static_cast<const uint16_t*>(x),
+                                  static_cast<const uint16_t*>(modulation), mod_stride, scale_off, target_mask, q,
+                                  scale_out, B, S, static_cast<int>(D), eps, stages, mod_used,
+                                  static_cast<QuantWs*>(ws), status));
+  return check_launch("ln_modulate_e4m3_kernel");
 }
 
 int qik_gate_residual(const void* x, const void* f, int64_t B, int64_t S, int64_t D, const void* modulation,

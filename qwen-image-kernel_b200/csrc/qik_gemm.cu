@@ -52,7 +52,23 @@ struct GemmParams {
   float* scat_dst[QIK_TP_MAX_WORLD];
   uint32_t* scat_cnt[QIK_TP_MAX_WORLD];
   int scat_rows;
+  int group_m;  // raster: row tiles per group (1 = row-major), see tile_coords
 };
+
+// Output tile `tile` of the raster: groups of group_m row tiles, each group walked
+// column tile by column tile with its row tiles fastest.  Consecutive tiles (the CTAs
+// of one wave) then share a few row bands of A and a few column bands of B instead of
+// one row band and all of B, so a B larger than what L2 keeps between waves is read
+// from HBM once per group rather than once per wave.  group_m = 1 is row-major.
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int group_m, int& mb, int& nb) {
+  const int per_group = group_m * num_n;
+  const int g = tile / per_group;
+  const int first = g * group_m;
+  const int gm = min(num_m - first, group_m);
+  const int r = tile - g * per_group;
+  mb = first + r % gm;
+  nb = r / gm;
+}
 
 // TWO_SM: the CTA is half of a 2-CTA cluster computing 256 x BN tiles with
 // tcgen05.mma.cta_group::2 -- it loads 128 rows of A and BN / 2 rows of B per stage.
@@ -156,7 +172,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // expects the bytes of the pair
       const uint32_t full_leader = TWO_SM ? mapa_shared(full, 0) : 0u;
       for (int tile = tile0; tile < tiles; tile += tile_step) {
-        const int mb = tile / num_n, nb = tile % num_n;
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, p.group_m, mb, nb);
         for (int kb = 0; kb < num_k; ++kb) {
           if constexpr (TWO_SM) {
             if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, p.status)) goto producer_done;
@@ -253,7 +270,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!got) break;
       tc_fence_after();
       if (tile + tile_step >= tiles) pdl_trigger();  // last tile of this CTA
-      const int mb = tile / num_n, nb = tile % num_n;
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, p.group_m, mb, nb);
       const int row0 = mb * kTileM + static_cast<int>(rank) * kGemmBM + quarter * 32;
       const bool row_ok = row0 + lane < p.M;
 #pragma unroll 1
@@ -415,6 +433,14 @@ static int gemm_pick_cfg(int64_t M, int64_t N) {
   return (N + 127) / 128 >= sm_count() / 2 ? QIK_GEMM_TILE_SINGLE_128 : QIK_GEMM_TILE_SINGLE_64;
 }
 
+// Raster group (row tiles per group, tile_coords).  Measured on the configs[4] shapes
+// and the DiT block's (1 x B200, groups of 1, 2, 4, 8 and 16 row tiles forced): 16 is
+// the best or within 0.5% of it everywhere but 16384 x 9216 (313.7 against 308.5 us
+// row-major), and it gains most where B is re-read every wave in row-major order: the
+// FFN's down projection 4352 x 3072 x 12288 124.5 -> 113.2 us, 16384 x 18432 677.5 ->
+// 644.9 us, 9472 x 18432 374.2 -> 359.9 us.
+static int gemm_pick_raster(int /*cfg*/) { return 16; }
+
 template <int BN, int STAGES, bool TWO_SM>
 static int launch_gemm(const uint8_t* A, const uint8_t* B, const GemmParams& p, int64_t lda, int64_t ldb,
                        cudaStream_t st, bool pdl) {
@@ -513,7 +539,10 @@ int launch_fp8_gemm_ex(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N,
   p.epilogue = epilogue;
   p.amax_out = amax_out;
   p.status = status;
-  const int cfg = tile_cfg == QIK_GEMM_TILE_AUTO ? gemm_pick_cfg(M, N) : tile_cfg;
+  const int sel = tile_cfg & 0xFF;
+  const int cfg = sel == QIK_GEMM_TILE_AUTO ? gemm_pick_cfg(M, N) : sel;
+  const int raster = (tile_cfg >> 8) & 0xFF;
+  p.group_m = raster != 0 ? raster : gemm_pick_raster(cfg);
   switch (cfg) {
     case QIK_GEMM_TILE_PAIR_256:
       return launch_gemm<256, 6, true>(A, B, p, lda, ldb, stream, pdl);
@@ -598,9 +627,10 @@ extern "C" int qik_fp8_gemm_tiled(const uint8_t* A, const uint8_t* B, int64_t M,
                                   int64_t ldb, const float* scale_a, const float* scale_b, const void* bias, void* C,
                                   int64_t ldc, int out_dtype, int epilogue, uint32_t* amax_out, int tile_cfg,
                                   int* status, void* stream) {
-  QIK_REQUIRE(tile_cfg == QIK_GEMM_TILE_AUTO || tile_cfg == QIK_GEMM_TILE_PAIR_256 ||
-                  tile_cfg == QIK_GEMM_TILE_SINGLE_256 || tile_cfg == QIK_GEMM_TILE_SINGLE_128 ||
-                  tile_cfg == QIK_GEMM_TILE_SINGLE_64,
+  const int sel = tile_cfg & 0xFF;
+  QIK_REQUIRE((tile_cfg & ~0xFFFF) == 0 &&
+                  (sel == QIK_GEMM_TILE_AUTO || sel == QIK_GEMM_TILE_PAIR_256 || sel == QIK_GEMM_TILE_SINGLE_256 ||
+                   sel == QIK_GEMM_TILE_SINGLE_128 || sel == QIK_GEMM_TILE_SINGLE_64),
               "qik_fp8_gemm_tiled: unknown tile configuration %d", tile_cfg);
   return qik::launch_fp8_gemm_ex(A, B, M, N, K, lda, ldb, scale_a, scale_b, bias, C, ldc, out_dtype, epilogue,
                                  amax_out, status, static_cast<cudaStream_t>(stream), false, nullptr, tile_cfg);

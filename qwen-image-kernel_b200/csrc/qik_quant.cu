@@ -18,24 +18,7 @@
 
 namespace qik {
 
-// Workspace of the activation quantizers.  `bar` is the single-pass kernel's grid
-// barrier: a generation in the high 32 bits and the arrivals of the running call in
-// the low 32.  The last CTA to arrive returns the arrivals to 0 and advances the
-// generation in one atomic add, so a workspace that was zeroed once serves any number
-// of calls in stream order without being cleared again.  partial[i] holds CTA i's
-// max|x| bits for the running call: written before the CTA arrives, read by every CTA
-// after the barrier, so stale contents never matter.  amax_bits belongs to the
-// two-pass form (amax kernel, then pack), which clears it itself.
-constexpr int kQuantMaxCtas = 252;
-struct QuantWs {
-  unsigned long long bar;
-  uint32_t amax_bits;
-  uint32_t pad;
-  uint32_t partial[kQuantMaxCtas];
-};
-static_assert(sizeof(QuantWs) == 1024, "QuantWs layout");
-constexpr uint32_t kQuantAbortMark = 0xFFFFFFFFu;  // a partial above every |x| bit pattern: a CTA gave up
-
+// The workspace (QuantWs) and its grid-wide amax exchange are in qik_device.cuh.
 constexpr int kQuantThreads = 256;
 
 __device__ __forceinline__ uint32_t block_max_u32(uint32_t v) {
@@ -135,16 +118,10 @@ __global__ void __launch_bounds__(kQuantThreads) pack_act_kernel(const uint16_t*
     uint4* qv = reinterpret_cast<uint4*>(q);
     for (int64_t i = tid; i < nvec; i += nthreads) {
       const uint4 a = __ldg(xv + 2 * i), b = __ldg(xv + 2 * i + 1);
-      const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-      uint32_t o[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t u0 = w[2 * j], u1 = w[2 * j + 1];
-        const uint16_t lo = cvt_e4m3x2(__uint_as_float(u0 << 16) * inv, __uint_as_float(u0 & 0xFFFF0000u) * inv);
-        const uint16_t hi = cvt_e4m3x2(__uint_as_float(u1 << 16) * inv, __uint_as_float(u1 & 0xFFFF0000u) * inv);
-        o[j] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
-      }
-      qv[i] = make_uint4(o[0], o[1], o[2], o[3]);
+      uint4 o;
+      o.x = pack8_e4m3(a, inv, o.y);
+      o.z = pack8_e4m3(b, inv, o.w);
+      qv[i] = o;
     }
     done = nvec << 4;
   }
@@ -268,49 +245,6 @@ constexpr int kQfChunks = 14;
 constexpr int kQfSmemVecs = kQfChunkVecs * kQfChunks;
 constexpr int kQfSmemBytes = kQfSmemVecs * 16;
 
-__device__ __forceinline__ uint64_t l2_evict_first_policy() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
-__device__ __forceinline__ uint64_t l2_evict_last_policy() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
-__device__ __forceinline__ uint4 ld_nc_hint(const uint4* p, uint64_t pol) {
-  uint4 r;
-  asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p), "l"(pol));
-  return r;
-}
-__device__ __forceinline__ void st_v2_hint(void* p, uint32_t a, uint32_t b, uint64_t pol) {
-  asm volatile("st.global.L2::cache_hint.v2.b32 [%0], {%1, %2}, %3;" ::"l"(p), "r"(a), "r"(b), "l"(pol) : "memory");
-}
-__device__ __forceinline__ void bulk_load_hint(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar,
-                                               uint64_t pol) {
-  asm volatile(
-      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
-          smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
-      : "memory");
-}
-
-__device__ __forceinline__ uint32_t pack8_e4m3(const uint4 a, float inv, uint32_t& hi_word) {
-  const uint32_t w[4] = {a.x, a.y, a.z, a.w};
-  uint32_t o[2];
-#pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    const uint32_t u0 = w[2 * j], u1 = w[2 * j + 1];
-    const uint16_t lo = cvt_e4m3x2(__uint_as_float(u0 << 16) * inv, __uint_as_float(u0 & 0xFFFF0000u) * inv);
-    const uint16_t hi = cvt_e4m3x2(__uint_as_float(u1 << 16) * inv, __uint_as_float(u1 & 0xFFFF0000u) * inv);
-    o[j] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
-  }
-  hi_word = o[1];
-  return o[0];
-}
-
 __device__ __forceinline__ uint32_t absmax8(uint32_t m2, const uint4 a) {
   return __vmaxu2(m2, __vmaxu2(__vmaxu2(a.x & 0x7FFF7FFFu, a.y & 0x7FFF7FFFu),
                                __vmaxu2(a.z & 0x7FFF7FFFu, a.w & 0x7FFF7FFFu)));
@@ -375,38 +309,12 @@ __global__ void __launch_bounds__(kQfThreads, 1) quant_act_single_pass_kernel(co
   uint32_t m = block_max_u32(max(m2 & 0xFFFFu, m2 >> 16)) << 16;
   if (threadIdx.x == 0) {
     if (abort_cta) m = kQuantAbortMark;  // a chunk never landed: poison the amax
-    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(&ws->partial[blockIdx.x]), "r"(m) : "memory");
-    // the arrival releases the slot write; the last arrival acquires every earlier one
-    // (they form one release sequence) and publishes the next generation
-    unsigned long long old;
-    asm volatile("atom.add.acq_rel.gpu.global.u64 %0, [%1], 1;" : "=l"(old) : "l"(&ws->bar) : "memory");
-    const uint32_t gen = static_cast<uint32_t>(old >> 32);
-    if (static_cast<uint32_t>(old) == gridDim.x - 1) {
-      const unsigned long long step = (1ull << 32) - gridDim.x;  // generation + 1, arrivals back to 0
-      asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(&ws->bar), "l"(step) : "memory");
-    } else {
-      // grid barrier: every CTA is resident (cooperative launch); the wait is bounded
-      const uint64_t t0 = globaltimer();
-      for (uint32_t it = 0;; ++it) {
-        unsigned long long cur;
-        asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(cur) : "l"(&ws->bar) : "memory");
-        if (static_cast<uint32_t>(cur >> 32) != gen) break;
-        if ((it & 255u) == 255u && globaltimer() - t0 > QIK_WAIT_NS) {
-          abort_cta = 1;
-          break;
-        }
-      }
-    }
+    // grid barrier: every CTA is resident (cooperative launch); the wait is bounded
+    if (!grid_max_publish_wait(ws, m)) abort_cta = 1;
   }
   __syncthreads();
   if (threadIdx.x < 32) {  // the global amax from every CTA's slot
-    uint32_t g = 0;
-    for (uint32_t i = threadIdx.x; i < gridDim.x; i += 32) {
-      uint32_t v;
-      asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(&ws->partial[i]) : "memory");
-      g = max(g, v);
-    }
-    g = __reduce_max_sync(0xffffffffu, g);
+    const uint32_t g = grid_max_collect(ws);
     if (threadIdx.x == 0) amax_all = abort_cta ? kQuantAbortMark : g;
   }
   __syncthreads();

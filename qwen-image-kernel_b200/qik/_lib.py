@@ -64,6 +64,8 @@ SIGNATURES = {
                            _vp]),
     "qik_fp8_ffn_from_amax": (_i32, [_vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                      ctypes.c_size_t, _vp, _vp]),
+    "qik_fp8_ffn_e4m3": (_i32, [_vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                ctypes.c_size_t, _vp, _vp]),
     "qik_block_causal_attention": (_i32, [ctypes.POINTER(AttnArgs), _vp, _vp]),
     "qik_kv_store": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _i64,
                             _i32, _vp, _vp, _vp]),
@@ -71,6 +73,8 @@ SIGNATURES = {
                                  _i64, _i64, _vp]),
     "qik_layer_norm_modulate": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _f32, _vp, _vp,
                                        _vp]),
+    "qik_layer_norm_modulate_e4m3": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _f32, _vp, _vp,
+                                            _vp, _vp, _vp]),
     "qik_gate_residual": (_i32, [_vp, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _vp]),
     "qik_swiglu": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),
     "qik_selftest_wait_timeout": (_i32, [_vp, _u64, _vp]),

@@ -209,6 +209,18 @@ class FP8Linear(nn.Module):
         out = out.reshape(*x.shape[:-1], self.out_features)
         return out.to(x.dtype) if out.dtype != x.dtype else out
 
+    def forward_e4m3(self, xq: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+        """forward(x) for an input already quantized as forward(x) would quantize it:
+        ``xq`` e4m3 [..., in_features] with its dynamic scale ``scale`` (fp32 [1] on the
+        device), e.g. from ``fused_layer_norm_modulate_e4m3``.  Returns bf16."""
+        if xq.dtype != torch.float8_e4m3fn or xq.shape[-1] != self.in_features:
+            raise ValueError(f"FP8Linear.forward_e4m3: expected float8_e4m3fn [..., {self.in_features}], "
+                             f"got {xq.dtype} {tuple(xq.shape)}")
+        if self.in_features < 256:
+            raise ValueError("FP8Linear.forward_e4m3: linears with in_features < 256 take bf16 input (forward)")
+        out = fp8_gemm(xq.reshape(-1, self.in_features), scale, self.weight, self.weight_scale, self.bias)
+        return out.reshape(*xq.shape[:-1], self.out_features)
+
     def forward_fp32(self, x: torch.Tensor) -> torch.Tensor:
         """Same computation with the fp32 GEMM output before the bf16 cast (parity mode)."""
         x2 = x.reshape(-1, x.shape[-1])
@@ -266,7 +278,8 @@ def fp8_state_dict(model: nn.Module) -> dict[str, torch.Tensor]:
 
 
 def fp8_ffn_gelu(x: torch.Tensor, up: FP8Linear, down: FP8Linear, workspace: torch.Tensor | None = None,
-                 out: torch.Tensor | None = None, x_amax: torch.Tensor | None = None) -> torch.Tensor:
+                 out: torch.Tensor | None = None, x_amax: torch.Tensor | None = None,
+                 x_scale: torch.Tensor | None = None) -> torch.Tensor:
     """DiT FFN pair: down(gelu_tanh(up(x))) with both linears FP8 per-tensor and the
     hidden activation re-quantized dynamically between them (qik_fp8_ffn: one chain
     of four kernels with programmatic dependent launches).
@@ -277,10 +290,12 @@ def fp8_ffn_gelu(x: torch.Tensor, up: FP8Linear, down: FP8Linear, workspace: tor
     avoid an allocation per call, ``out`` (contiguous bf16, x's shape) to write the
     result into a buffer the caller owns, ``x_amax`` (int32 [1] on x's device: the
     fp32 bits of max|x|, as fused_layer_norm_modulate's ``amax_out`` accumulates them)
-    to skip the chain's own max pass."""
+    to skip the chain's own max pass.  With ``x_scale`` (fp32 [1] on x's device), x is
+    already the e4m3 input of the up projection quantized with that scale (as
+    fused_layer_norm_modulate_e4m3 returns them) and the chain starts at its GEMM."""
     _require_cuda(x, "x")
-    if x.dtype != torch.bfloat16:
-        raise TypeError("qik.fp8_ffn_gelu: bf16 activations only")
+    if x.dtype != (torch.float8_e4m3fn if x_scale is not None else torch.bfloat16):
+        raise TypeError("qik.fp8_ffn_gelu: bf16 activations, or float8_e4m3fn ones with x_scale")
     lib = L.load()
     K = x.shape[-1]
     hidden = up.out_features
@@ -302,7 +317,15 @@ def fp8_ffn_gelu(x: torch.Tensor, up: FP8Linear, down: FP8Linear, workspace: tor
     b_down = None if down.bias is None else down.bias.to(torch.bfloat16).contiguous()
     status = L.status_word(x.device)
     with torch.cuda.device(x.device):
-        if x_amax is None:
+        if x_scale is not None:
+            if x_scale.dtype != torch.float32 or x_scale.device != x.device:
+                raise ValueError("qik.fp8_ffn_gelu: x_scale must be an fp32 tensor on x's device")
+            L.check(lib.qik_fp8_ffn_e4m3(x2.data_ptr(), x_scale.data_ptr(), M, K, hidden, up.weight.data_ptr(),
+                                         up.weight_scale.data_ptr(), L.ptr(b_up), down.weight.data_ptr(),
+                                         down.weight_scale.data_ptr(), L.ptr(b_down), y.data_ptr(),
+                                         workspace.data_ptr(), workspace.numel(), status.data_ptr(),
+                                         L.stream_ptr()), "qik_fp8_ffn_e4m3")
+        elif x_amax is None:
             L.check(lib.qik_fp8_ffn(x2.data_ptr(), M, K, hidden, up.weight.data_ptr(), up.weight_scale.data_ptr(),
                                     L.ptr(b_up), down.weight.data_ptr(), down.weight_scale.data_ptr(), L.ptr(b_down),
                                     y.data_ptr(), workspace.data_ptr(), workspace.numel(), status.data_ptr(),

@@ -18,9 +18,11 @@ Same names and call signatures as ``qwen_image_kernel/processors.py``
 
 Where the data layout allows, tensors stay in place instead of being copied: q / k /
 v are strided views of the fused QKV output, gate / up the two halves of the fused
-up projection, and the slab store reads the key / value views directly.  The fused
-layer-norm and SwiGLU kernels also reduce the amax of their output, which the next
-FP8 linear uses instead of its own amax pass (same bytes and scale).
+up projection, and the slab store reads the key / value views directly.  A layer norm
+whose only consumers are FP8 linears emits their e4m3 input and scale itself
+(``fused_layer_norm_modulate_e4m3``: the bf16 output is never written); SwiGLU and the
+attention reduce the amax of their output, which the next FP8 linear uses instead of
+its own amax pass (same bytes and scale).
 """
 from __future__ import annotations
 
@@ -28,7 +30,8 @@ import torch
 
 from .fp8 import FP8Linear
 from .triton_attention import block_causal_flash_attention
-from .triton_fused import fused_gate_residual, fused_layer_norm_modulate, fused_rms_norm_rope, fused_swiglu
+from .triton_fused import (fused_gate_residual, fused_layer_norm_modulate, fused_layer_norm_modulate_e4m3,
+                           fused_rms_norm_rope, fused_swiglu)
 
 
 def _build_prefix_lengths(segments: list[tuple[int, int, bool]], prefix_len: int, seq_len: int,
@@ -42,11 +45,20 @@ def _build_prefix_lengths(segments: list[tuple[int, int, bool]], prefix_len: int
     return L
 
 
-def _linear(mod, x: torch.Tensor, amax: torch.Tensor | None) -> torch.Tensor:
-    """mod(x), with the producer's amax of x when mod is an FP8 linear."""
+def _linear(mod, x: torch.Tensor, amax: torch.Tensor | None, scale: torch.Tensor | None = None) -> torch.Tensor:
+    """mod(x), with the producer's amax of x when mod is an FP8 linear; with ``scale``,
+    x is already the e4m3 input of the FP8 linear mod and ``scale`` its dynamic scale."""
+    if scale is not None:
+        return mod.forward_e4m3(x, scale)
     if amax is not None and isinstance(mod, FP8Linear):
         return mod.forward_from_amax(x, amax)
     return mod(x)
+
+
+def _takes_e4m3(*mods) -> bool:
+    """Every module is an FP8 linear on the tensor-core path (in_features >= 256), so a
+    producer may hand them its output already quantized."""
+    return all(isinstance(m, FP8Linear) and m.in_features >= 256 for m in mods)
 
 
 def _new_amax(x: torch.Tensor) -> torch.Tensor:
@@ -55,8 +67,8 @@ def _new_amax(x: torch.Tensor) -> torch.Tensor:
 
 class QwenImage21KernelProcessor:
     """Drop-in for ``QwenImage21AttnProcessor``: same call signature (plus the optional
-    ``hidden_states_amax`` the fused block passes), one attention kernel for both the
-    prefill and the decode form."""
+    ``hidden_states_amax`` / ``hidden_states_scale`` the fused block passes), one
+    attention kernel for both the prefill and the decode form."""
 
     _attention_backend = None
     _parallel_config = None
@@ -73,20 +85,23 @@ class QwenImage21KernelProcessor:
         segments=None,
         key_valid=None,
         hidden_states_amax: torch.Tensor | None = None,
+        hidden_states_scale: torch.Tensor | None = None,
     ) -> torch.Tensor:
+        # hidden_states_scale: hidden_states is then the e4m3 input of the QKV linears
+        # (fused_layer_norm_modulate_e4m3), quantized with this scale
         B, S, _ = hidden_states.shape
         H = attn.heads
         fused_qkv = getattr(attn, "fused_qkv", None)
         if fused_qkv is not None:
             # one quantization + one GEMM for Q, K and V; the splits are views
             D = fused_qkv.out_features // (3 * H)
-            qkv = _linear(fused_qkv, hidden_states, hidden_states_amax)
+            qkv = _linear(fused_qkv, hidden_states, hidden_states_amax, hidden_states_scale)
             query, key, value = qkv.unflatten(-1, (3 * H, D)).chunk(3, dim=-2)
         else:
             D = attn.to_q.out_features // H
-            query = _linear(attn.to_q, hidden_states, hidden_states_amax).unflatten(-1, (H, D))
-            key = _linear(attn.to_k, hidden_states, hidden_states_amax).unflatten(-1, (H, D))
-            value = _linear(attn.to_v, hidden_states, hidden_states_amax).unflatten(-1, (H, D))
+            query = _linear(attn.to_q, hidden_states, hidden_states_amax, hidden_states_scale).unflatten(-1, (H, D))
+            key = _linear(attn.to_k, hidden_states, hidden_states_amax, hidden_states_scale).unflatten(-1, (H, D))
+            value = _linear(attn.to_v, hidden_states, hidden_states_amax, hidden_states_scale).unflatten(-1, (H, D))
 
         query = fused_rms_norm_rope(query, attn.norm_q.weight, rotary_emb, attn.norm_q.eps)
         key = fused_rms_norm_rope(key, attn.norm_k.weight, rotary_emb, attn.norm_k.eps)
@@ -162,26 +177,42 @@ class QwenImage21KernelBlock(torch.nn.Module):
         fused_qkv = getattr(self.attn, "fused_qkv", None)
         inner = fused_qkv.out_features // 3 if fused_qkv is not None else self.attn.to_q.out_features
         # mod1.scale @ 0, mod1.gate @ inner, mod2.scale @ 2 inner, mod2.gate @ 3 inner
-        amax1 = _new_amax(hidden_states)
-        img_mod = fused_layer_norm_modulate(hidden_states, modulation, 0, mod_stride, target_token_mask, self._eps,
-                                            amax_out=amax1)
-        attn_kwargs = dict(hidden_states=img_mod, attention_mask=attention_mask, rotary_emb=rotary_emb,
-                           layer_cache=layer_cache, kv_cache_mode=kv_cache_mode, cache_write_slice=cache_write_slice,
-                           segments=segments, key_valid=key_valid)
+        attn_kwargs = dict(attention_mask=attention_mask, rotary_emb=rotary_emb, layer_cache=layer_cache,
+                           kv_cache_mode=kv_cache_mode, cache_write_slice=cache_write_slice, segments=segments,
+                           key_valid=key_valid)
+        qkv_mods = (fused_qkv,) if fused_qkv is not None else (self.attn.to_q, self.attn.to_k, self.attn.to_v)
         if isinstance(getattr(self.attn, "processor", None), QwenImage21KernelProcessor):
-            attn_kwargs["hidden_states_amax"] = amax1
-        attn_out = self.attn(**attn_kwargs)
+            if _takes_e4m3(*qkv_mods):
+                # the norm's only consumers are FP8 linears: it emits their e4m3 input
+                img_mod, scale1 = fused_layer_norm_modulate_e4m3(hidden_states, modulation, 0, mod_stride,
+                                                                 target_token_mask, self._eps)
+                attn_kwargs["hidden_states_scale"] = scale1
+            else:
+                amax1 = _new_amax(hidden_states)
+                img_mod = fused_layer_norm_modulate(hidden_states, modulation, 0, mod_stride, target_token_mask,
+                                                    self._eps, amax_out=amax1)
+                attn_kwargs["hidden_states_amax"] = amax1
+        else:
+            img_mod = fused_layer_norm_modulate(hidden_states, modulation, 0, mod_stride, target_token_mask,
+                                                self._eps)
+        attn_out = self.attn(hidden_states=img_mod, **attn_kwargs)
         hidden_states = fused_gate_residual(hidden_states, attn_out, modulation, inner, target_token_mask)
 
-        amax2 = _new_amax(hidden_states)
-        img_mod2 = fused_layer_norm_modulate(hidden_states, modulation, 2 * inner, mod_stride, target_token_mask,
-                                             self._eps, amax_out=amax2)
         fused_up = getattr(self.img_mlp, "fused_up", None)
-        if fused_up is not None:
-            gate, up = _linear(fused_up, img_mod2, amax2).chunk(2, dim=-1)
+        up_mods = (fused_up,) if fused_up is not None else (self.img_mlp.gate_layer, self.img_mlp.proj)
+        amax2 = scale2 = None
+        if _takes_e4m3(*up_mods):
+            img_mod2, scale2 = fused_layer_norm_modulate_e4m3(hidden_states, modulation, 2 * inner, mod_stride,
+                                                              target_token_mask, self._eps)
         else:
-            gate = _linear(self.img_mlp.gate_layer, img_mod2, amax2)
-            up = _linear(self.img_mlp.proj, img_mod2, amax2)
+            amax2 = _new_amax(hidden_states)
+            img_mod2 = fused_layer_norm_modulate(hidden_states, modulation, 2 * inner, mod_stride, target_token_mask,
+                                                 self._eps, amax_out=amax2)
+        if fused_up is not None:
+            gate, up = _linear(fused_up, img_mod2, amax2, scale2).chunk(2, dim=-1)
+        else:
+            gate = _linear(self.img_mlp.gate_layer, img_mod2, amax2, scale2)
+            up = _linear(self.img_mlp.proj, img_mod2, amax2, scale2)
         amax3 = _new_amax(hidden_states)
         mlp_mid = fused_swiglu(gate, up, amax_out=amax3)
         mlp_out = _linear(self.img_mlp.out, mlp_mid, amax3)

@@ -16,7 +16,9 @@ reference kernel's rounding points:
 ``fused_layer_norm_modulate`` and ``fused_swiglu`` take an optional ``amax_out``
 (int32 [1] on the device, zeroed by the caller): the kernel accumulates the fp32
 bit pattern of max|out| into it, which is what the next FP8 linear's dynamic
-quantizer reduces (``qik.fp8.quantize_from_amax``).
+quantizer reduces (``qik.fp8.quantize_from_amax``).  ``fused_layer_norm_modulate_e4m3``
+goes one step further for a layer norm whose only consumers are FP8 linears: it
+returns that linear's e4m3 input and scale directly (``FP8Linear.forward_e4m3``).
 """
 from __future__ import annotations
 
@@ -126,6 +128,32 @@ def fused_layer_norm_modulate(x: torch.Tensor, modulation: torch.Tensor, scale_o
                                         L.stream_ptr(x.device)),
             "qik_layer_norm_modulate")
     return out
+
+
+def fused_layer_norm_modulate_e4m3(x: torch.Tensor, modulation: torch.Tensor, scale_offset: int,
+                                   modulation_stride: int, target_token_mask: torch.Tensor | None,
+                                   eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """fused_layer_norm_modulate followed by the next FP8 linear's dynamic quantizer,
+    in one kernel: returns (e4m3 [B, S, D], scale fp32 [1]) -- the same codes and scale
+    as ``quantize_tensorwise(fused_layer_norm_modulate(...))`` -- without writing the
+    bf16 output (qik_layer_norm_modulate_e4m3)."""
+    _require_bf16(x=x, modulation=modulation)
+    B, S, D = x.shape
+    x = x.contiguous()
+    if modulation.stride(-1) != 1:
+        raise ValueError("modulation must have a unit column stride")
+    q = torch.empty(x.shape, dtype=torch.float8_e4m3fn, device=x.device)
+    s = torch.empty(1, dtype=torch.float32, device=x.device)
+    mask = _u8_mask(target_token_mask, S, x.device)
+    lib = L.load()
+    with torch.cuda.device(x.device):
+        stream = L.stream_ptr()
+        L.check(lib.qik_layer_norm_modulate_e4m3(x.data_ptr(), B, S, D, modulation.data_ptr(), modulation.shape[0],
+                                                 int(modulation_stride), int(scale_offset), L.ptr(mask), float(eps),
+                                                 q.data_ptr(), s.data_ptr(), L.quant_state(x.device, stream).data_ptr(),
+                                                 L.status_word(x.device).data_ptr(), stream),
+                "qik_layer_norm_modulate_e4m3")
+    return q, s
 
 
 def fused_gate_residual(x: torch.Tensor, f: torch.Tensor, modulation: torch.Tensor, gate_offset: int,

@@ -7,13 +7,16 @@ Every kernel call the block makes is recorded (inputs and output) by wrapping th
 module-level functions qik.processors calls; each recorded stage is then recomputed by
 the oracle from the recorded inputs:
 
-* fused LayerNorm + modulate, RMSNorm + RoPE, gated residual, SwiGLU: the fused-op
-  gate of test_gpu_fused.py (<= 0.5% of outputs differ, none by more than 2^-6 of the
-  largest output, relF <= 1e-3), and each amax output equal to the max |output|;
+* RMSNorm + RoPE, gated residual, SwiGLU: the fused-op gate of test_gpu_fused.py
+  (<= 0.5% of outputs differ, none by more than 2^-6 of the largest output, relF <=
+  1e-3), and each amax output equal to the max |output|;
+* the two LayerNorm + modulate stages, which emit the next linear's e4m3 input: codes
+  and scale bit-identical to the bf16 layer-norm kernel followed by the oracle's
+  quantizer on the same recorded input, and that bf16 output at the fused-op gate;
 * every FP8 linear: its bf16 output within max-abs 2e-2 + half a bf16 ulp and relF
   <= 5e-3 of the fp32 dequant oracle on the same input, quantized by the oracle
   (bit-exact with the product's quantizer, tested elsewhere) with the amax the
-  product's producer handed over;
+  product's producer handed over, or on the e4m3 input and scale it was handed;
 * the attention: max-abs <= 2e-2 and relF <= 5e-3 against the fp32 oracle on the q /
   k / v the processor passed, all 48 (sample, head) pairs.
 
@@ -70,7 +73,11 @@ def recorder(monkeypatch):
     """Wraps the kernels qik.processors calls and records (name, inputs, output)."""
     import qik.processors as PR
     calls = []
-    cpu = lambda t: t.detach().cpu() if isinstance(t, torch.Tensor) else t  # noqa: E731
+
+    def cpu(t):
+        if isinstance(t, torch.Tensor):
+            return t.detach().cpu()
+        return tuple(cpu(x) for x in t) if isinstance(t, tuple) else t
 
     def wrap(name, fn):
         def inner(*a, **kw):
@@ -87,7 +94,8 @@ def recorder(monkeypatch):
             return out
         return inner
 
-    for name, attr in (("ln_mod", "fused_layer_norm_modulate"), ("rms_rope", "fused_rms_norm_rope"),
+    for name, attr in (("ln_mod", "fused_layer_norm_modulate"), ("ln_mod_e4m3", "fused_layer_norm_modulate_e4m3"),
+                       ("rms_rope", "fused_rms_norm_rope"),
                        ("gate_res", "fused_gate_residual"), ("swiglu", "fused_swiglu"),
                        ("attention", "block_causal_flash_attention"), ("linear", "_linear")):
         monkeypatch.setattr(PR, attr, wrap(name, getattr(PR, attr)))
@@ -131,8 +139,8 @@ def test_dit_block_cfg2_full_size_stage_by_stage(recorder):
     out = block(x, mod, rotary_emb=freqs, segments=[(0, 256, True)])
     torch.cuda.synchronize()
     names = [c["name"] for c in recorder]
-    assert names == ["ln_mod", "linear", "rms_rope", "rms_rope", "attention", "linear", "gate_res", "ln_mod",
-                     "linear", "swiglu", "linear", "gate_res"], names
+    assert names == ["ln_mod_e4m3", "linear", "rms_rope", "rms_rope", "attention", "linear", "gate_res",
+                     "ln_mod_e4m3", "linear", "swiglu", "linear", "gate_res"], names
     assert recorder[-1]["out"].shape == (B, S, K) and torch.equal(recorder[-1]["out"], out.cpu())
     torch.set_num_threads(max(1, torch.get_num_threads()))
     cos, sin = freqs.real.float().cpu(), freqs.imag.float().cpu()
@@ -143,6 +151,14 @@ def test_dit_block_cfg2_full_size_stage_by_stage(recorder):
             xin, m, off = a[0], a[1], a[2]
             _fused_gate(o, O.layer_norm_modulate(xin, m, off, a[4], a[5]), tag)
             assert int(kw["amax_out"][0]) == _amax_bits_of(o), tag
+        elif c["name"] == "ln_mod_e4m3":
+            from qik.triton_fused import fused_layer_norm_modulate
+            xin, m, off = a[0], a[1], a[2]
+            ref = fused_layer_norm_modulate(xin.cuda(), m.cuda(), off, a[3], a[4], a[5]).cpu()
+            q_o, s_o = O.quantize_act(ref)
+            assert np.array_equal(o[0].view(torch.uint8).numpy().reshape(q_o.shape), q_o), tag
+            assert np.float32(s_o) == np.float32(o[1].item()), tag
+            _fused_gate(ref, O.layer_norm_modulate(xin, m, off, a[4], a[5]), tag)
         elif c["name"] == "rms_rope":
             _fused_gate(o, O.rms_norm_rope(a[0], a[1], cos, sin, a[3]), tag)
         elif c["name"] == "gate_res":
@@ -153,9 +169,12 @@ def test_dit_block_cfg2_full_size_stage_by_stage(recorder):
         elif c["name"] == "linear":
             lin, xin, amax = c["mod"], a[1], a[2]
             x2 = xin.reshape(-1, xin.shape[-1]).contiguous()
-            if amax is not None:  # the producer's amax is max|x| itself
-                assert int(amax[0]) == _amax_bits_of(x2), tag
-            q, s = O.quantize_act(x2)
+            if xin.dtype == torch.float8_e4m3fn:  # handed its e4m3 input and scale
+                q, s = x2.view(torch.uint8).numpy(), float(a[3].item())
+            else:
+                if amax is not None:  # the producer's amax is max|x| itself
+                    assert int(amax[0]) == _amax_bits_of(x2), tag
+                q, s = O.quantize_act(x2)
             ref = O.fp8_linear(q, s, lin.weight.cpu(), float(lin.weight_scale.item()),
                                None if lin.bias is None else lin.bias.cpu())
             y = o.reshape(-1, o.shape[-1]).float()

@@ -180,3 +180,84 @@ def test_ln_modulate_full_t2i_block_shape(F):
     torch.cuda.synchronize()
     _gate(out, O.layer_norm_modulate(x, mod, 0, None, 1e-6), "ln_modulate t2i")
     assert int(amax.item()) == int(out.float().abs().max().view(torch.int32).item())
+
+
+# ---------------------------------------------------------------- layer norm -> e4m3
+def _ln_e4m3_check(F, x, mod, off, tm, tag):
+    """fused_layer_norm_modulate_e4m3 against the composition it replaces: the bf16
+    layer-norm kernel followed by the activation quantizer (codes and scale
+    bit-identical), and the oracle's quantizer on that bf16 output (bit-exact); the
+    bf16 output itself passes the fused-op gate against the oracle."""
+    from qik.fp8 import quantize_tensorwise
+    xd, md = x.cuda(), mod.cuda()
+    tmd = None if tm is None else tm.cuda()
+    q, s = F.fused_layer_norm_modulate_e4m3(xd, md, off, mod.shape[1], tmd, 1e-6)
+    ref = F.fused_layer_norm_modulate(xd, md, off, mod.shape[1], tmd, 1e-6)
+    q_ref, s_ref = quantize_tensorwise(ref)
+    torch.cuda.synchronize()
+    qb = q.view(torch.uint8).cpu()
+    mism = (qb != q_ref.view(torch.uint8).cpu()).sum().item()
+    print(f"{tag}: scale {s.item():.6g} code mismatches {mism}")
+    assert mism == 0, tag
+    assert s.cpu().view(torch.int32).item() == s_ref.cpu().view(torch.int32).item(), tag
+    q_o, s_o = O.quantize_act(ref.cpu())
+    assert np.array_equal(qb.numpy().reshape(q_o.shape), q_o), tag
+    assert np.float32(s_o) == np.float32(s.item()), tag
+    _gate(ref, O.layer_norm_modulate(x, mod, off, tm, 1e-6), tag)
+    return q, s
+
+
+@pytest.mark.parametrize("mask", [False, True])
+def test_ln_modulate_e4m3_batch2_ragged(F, mask):
+    """B = 2, S = 333 (666 rows: the last 8-row group partial), D = 3072, the second
+    modulation's scale with and without the t = 0 rows."""
+    B, S, D = 2, 333, 3072
+    x = GI.randn_bf16(430, (B, S, D), 2.0)
+    mod = GI.randn_bf16(431, (2 * B, 4 * D), 0.3)
+    tm = torch.from_numpy(np.random.default_rng(432).random(S) > 0.3) if mask else None
+    _ln_e4m3_check(F, x, mod, 2 * D, tm, f"ln_e4m3 B=2 mask={mask}")
+
+
+def test_ln_modulate_e4m3_reference_case_width_4096(F):
+    """tests/test_fused.py:61-75's shape (B = 1, S = 500, D = 4096, random mask): a
+    64 KB stage, so only two stages fit beside the table."""
+    B, S, D = 1, 500, 4096
+    x = GI.randn_bf16(433, (B, S, D))
+    mod = GI.randn_bf16(434, (B + 1, 4 * D), 0.2)
+    tm = torch.from_numpy(np.random.default_rng(435).random(S) > 0.5)
+    _ln_e4m3_check(F, x, mod, 0, tm, "ln_e4m3 D=4096")
+
+
+def test_ln_modulate_e4m3_tiny(F):
+    """Fewer row groups than SMs (a grid of one CTA) and a narrow row."""
+    x = GI.randn_bf16(436, (1, 3, 64))
+    mod = GI.randn_bf16(437, (1, 256), 0.2)
+    _ln_e4m3_check(F, x, mod, 64, None, "ln_e4m3 tiny")
+
+
+def test_ln_modulate_e4m3_full_t2i_block_shape_calls_in_a_row(F):
+    """The DiT block's shape (B = 2, S = 4352, D = 3072; each CTA makes two passes over
+    7 or 8 groups), three calls in a row on one workspace with the amplitude changing
+    (large, small, large): each call's grid barrier and amax slots start from what the
+    last call left."""
+    from qik import _lib as L
+    B, S, D = 2, 4352, 3072
+    mod = GI.randn_bf16(439, (B, 4 * D), 0.3)
+    for i, amp in enumerate((3.0, 0.25, 1.5)):
+        x = GI.randn_bf16(440 + i, (B, S, D), amp)
+        _ln_e4m3_check(F, x, mod, 0, None, f"ln_e4m3 t2i call {i}")
+    assert L.device_status(torch.device("cuda", 0)) == 0
+
+
+def test_ln_modulate_e4m3_rejects_unaligned_codes(F):
+    from qik import _lib as L
+    lib = L.load()
+    x = torch.zeros(1, 8, 64, dtype=torch.bfloat16, device="cuda")
+    mod = torch.zeros(1, 256, dtype=torch.bfloat16, device="cuda")
+    q = torch.empty(8 * 64 + 16, dtype=torch.uint8, device="cuda")
+    s = torch.empty(1, dtype=torch.float32, device="cuda")
+    ws = torch.zeros(lib.qik_quant_workspace_bytes(), dtype=torch.uint8, device="cuda")
+    rc = lib.qik_layer_norm_modulate_e4m3(x.data_ptr(), 1, 8, 64, mod.data_ptr(), 1, 256, 0, None, 1e-6,
+                                          q.data_ptr() + 8, s.data_ptr(), ws.data_ptr(), None,
+                                          L.stream_ptr())
+    assert rc == 1 and b"16-byte aligned" in lib.qik_last_error()

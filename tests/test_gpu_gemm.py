@@ -67,6 +67,22 @@ def test_gemm_every_tile_config_exact(fp8, cfg, M, N, K):
     assert torch.equal(yb.cpu(), ref.to(torch.bfloat16))
 
 
+@pytest.mark.parametrize("cfg", [1, 3])
+@pytest.mark.parametrize("raster", [1, 3, 16, 255])
+def test_gemm_raster_groups_exact(fp8, cfg, raster):
+    """The tile raster (QIK_GEMM_RASTER(g): groups of g row tiles walked column by
+    column) only reorders tiles: exact small-integer products for group sizes that
+    divide the row tiles unevenly (4352 rows = 17 pair tiles, 34 single tiles), equal
+    them, and exceed them."""
+    M, N, K = 4352, 1280, 256
+    a = _e4m3_small_ints(M + 3 * K, (M, K)).cuda()
+    b = _e4m3_small_ints(N + 11 * K, (N, K)).cuda()
+    ref = a.cpu().float() @ b.cpu().float().t()
+    y = fp8.fp8_gemm(a, _one(), b, _one(), out_dtype=torch.float32, tile_cfg=cfg | (raster << 8))
+    torch.cuda.synchronize()
+    assert torch.equal(y.cpu(), ref)
+
+
 def test_gemm_deterministic(fp8):
     """Repeated launches give bitwise-identical results (fixed schedule, no atomics)."""
     M, N, K = 640, 768, 6144
@@ -265,6 +281,29 @@ def test_ffn_pair_from_layer_norm_amax(fp8):
     y_plain = fp8.fp8_ffn_gelu(hm.reshape(M, K), up, down)
     torch.cuda.synchronize()
     assert torch.equal(y_fused, y_plain)
+
+
+def test_ffn_pair_from_layer_norm_e4m3(fp8):
+    """The DiT block's second half with the LayerNorm emitting the FFN's e4m3 input
+    (qik_layer_norm_modulate_e4m3 -> qik_fp8_ffn_e4m3): identical to the chain on the
+    bf16 LayerNorm output."""
+    from qik.triton_fused import fused_layer_norm_modulate, fused_layer_norm_modulate_e4m3
+    M, K, Hd = 384, 3072, 12288
+    h = GI.randn_bf16(99, (1, M, K)).cuda()
+    mod = GI.randn_bf16(100, (1, 4 * K), 0.2).cuda()
+    up = fp8.FP8Linear(K, Hd).cuda()
+    down = fp8.FP8Linear(Hd, K).cuda()
+    for lin, seed in ((up, 101), (down, 102)):
+        wq, sw = fp8.quantize_weight_tensorwise(GI.randn_bf16(seed, (lin.out_features, lin.in_features), 0.02).cuda())
+        lin.weight.copy_(wq)
+        lin.weight_scale.copy_(sw)
+    hq, hs = fused_layer_norm_modulate_e4m3(h, mod, 2 * K, 4 * K, None, 1e-6)
+    y_e4m3 = fp8.fp8_ffn_gelu(hq.reshape(M, K), up, down, x_scale=hs)
+    y_plain = fp8.fp8_ffn_gelu(fused_layer_norm_modulate(h, mod, 2 * K, 4 * K, None, 1e-6).reshape(M, K), up, down)
+    torch.cuda.synchronize()
+    assert torch.equal(y_e4m3, y_plain)
+    # an FP8 linear handed the same codes and scale (FP8Linear.forward_e4m3) equals forward
+    assert torch.equal(up.forward_e4m3(hq, hs), up(fused_layer_norm_modulate(h, mod, 2 * K, 4 * K, None, 1e-6)))
 
 
 def test_gemm_rejects_bad_shapes(fp8):
