@@ -16,9 +16,8 @@
 // of each dequantized V element is below half a bf16 ulp of V.
 //
 // One CTA per (256-query block, b, h): two 128-row query tiles, A and B, share every
-// K/V tile, and each has its own softmax warpgroup, so the tensor core computes one
-// tile's S and P.V while the other tile's softmax runs (and two softmax warps share
-// each SM sub-partition, hiding each other's latencies).
+// K/V tile, and each has its own 8 softmax warps, so the tensor core computes one
+// tile's S and P.V while the other tile's softmax runs.
 //   warp 0      TMA producer: Q_A and Q_B once (64-column halves, 128-byte swizzle),
 //               K tiles into a 2-stage ring (freed once S_A and S_B are computed), V
 //               tiles (bf16, or e4m3 raw for the fp8 slab) into a 2-stage ring (freed
@@ -31,12 +30,17 @@
 //               been consumed: P_g(t+1) can overwrite S_g's columns and O_g can be
 //               rescaled without another barrier;
 //   warps 2-3   e4m3 -> f16 V converters for slab tiles when V is fp8 (exact);
-//   warps 4-7   softmax of tile A, warps 8-11 softmax of tile B: thread = query row;
-//               reads S_g(t) from TMEM, masks, online max/sum (O_g is rescaled in
-//               TMEM only when the running max grows by more than 2^8, which leaves
-//               the final O/l unchanged), writes P_g(t) as bf16 over S_g's first 64
-//               columns; finally O_g / l -> bf16 -> global.
-// TMEM columns: S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512); P_g over S_g.
+//   warps 4-11  softmax of tile A, warps 12-19 softmax of tile B: two threads per
+//               query row (16x32bx2 TMEM accesses), each with 64 of its 128 scores,
+//               so a tile's softmax takes half the time of one thread per row and
+//               fits inside the other tile's MMAs; each thread reads its half of
+//               S_g(t) from TMEM, masks, takes the row max with one shuffle, keeps an
+//               online half-row sum (O_g is rescaled in TMEM only when the running
+//               max grows by more than 2^8, which leaves the final O/l unchanged),
+//               writes its half of P_g(t) as bf16 over the first 32 of its own S
+//               columns; finally O_g / l -> bf16 -> global, each thread 64 columns.
+// TMEM columns: S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512); P_g(keys 0-63)
+// over S_g columns 0-31, P_g(keys 64-127) over S_g columns 64-95.
 // CTAs are numbered heaviest-first (the last query blocks, which see the most keys
 // under a block-causal mask, start first) so the short blocks fill the tail.
 #include <mutex>
@@ -51,13 +55,14 @@ constexpr int kAttnTiles = 2;                       // query tiles per CTA
 constexpr int kAttnRows = kAttnBM * kAttnTiles;     // query rows per CTA
 constexpr int kAttnBN = 128;
 constexpr int kAttnD = 128;
-constexpr int kAttnThreads = 128 + 128 * kAttnTiles;  // producer, MMA, 2 converters, softmax warpgroups
+constexpr int kAttnHalf = kAttnBN / 2;              // scores per softmax thread: half a row
+constexpr int kAttnSoftmaxWarps = 8;                // per query tile: two threads per row
+constexpr int kAttnThreads = 128 + 32 * kAttnSoftmaxWarps * kAttnTiles;  // producer, MMA, 2 converters, softmax
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when the max grows by > 2^8
-// Softmax exponentials: pairs j >= kPolyFromPair of a row (on tiles where every key
-// is allowed) use the FMA-pipe 2^x, the others MUFU ex2.  The FMA-pipe pairs come
-// last, where most scores of the row are consumed and its constants fit the 168
-// registers of a 384-thread CTA.
-constexpr int kPolyFromPair = 46;
+// Softmax exponentials: pairs j >= kPolyFromPair of a half row (on tiles where every
+// key is allowed) use the FMA-pipe 2^x, the others MUFU ex2 (9 of the 32 pairs, the
+// share measured best for the two pipes).
+constexpr int kPolyFromPair = 23;
 
 struct AttnSmem {
   static constexpr int kQ = 0;                          // per tile 32 KB: two 16 KB halves (d 0-63, 64-127)
@@ -91,18 +96,22 @@ __device__ __forceinline__ void load_bf16_tile(const CUtensorMap* tm, void* dst,
   tma_load_4d(static_cast<uint8_t*>(dst) + 16384, tm, 64, key0, h, b, bar);
 }
 
-// P row of one 128-key tile: p = 2^(s * scale - m) computed in pairs (f32x2), packed
-// (f16 for fp8-slab tiles, else bf16) and written to TMEM at tP; returns the fp32
-// row sum.  kPoly (tiles where every key of the row is allowed): pairs
-// j >= kPolyFromPair take 2^x on the FMA pipe (exp2_poly2), the rest MUFU ex2, so
-// the two pipes share the 128 exponentials of the row.
+// P half row of one 128-key tile: the thread's 64 scores (columns 64 hc .. 64 hc + 63
+// of its row), p = 2^(s * scale - m) computed in pairs (f32x2), packed (f16 for
+// fp8-slab tiles, else bf16) and written to TMEM at tP with the 16x32bx2 shape: the
+// hc = 0 thread's 32 packed words at columns 0-31 of S_g, the hc = 1 thread's at 64-95,
+// each over scores that thread has already read.  Returns the half row's fp32 sum.
+// kPoly (tiles where every key of the row is allowed): pairs j >= kPolyFromPair take
+// 2^x on the FMA pipe (exp2_poly2), the rest MUFU ex2, so the two pipes share the
+// exponentials.
 template <bool kPoly, bool kF16>
-__device__ __forceinline__ float softmax_row(const float (&sv)[kAttnBN], float scale, float neg_m, uint32_t tP) {
+__device__ __forceinline__ float softmax_half_row(const float (&sv)[kAttnHalf], float scale, float neg_m,
+                                                  uint32_t tP) {
   const uint64_t sc2 = f2_pack(scale, scale), nm2 = f2_pack(neg_m, neg_m);
   uint64_t acc[2] = {0ull, 0ull};  // (0.f, 0.f) pairs
-  uint32_t pk[kAttnBN / 2];
+  uint32_t pk[kAttnHalf / 2];
 #pragma unroll
-  for (int j = 0; j < kAttnBN / 2; ++j) {
+  for (int j = 0; j < kAttnHalf / 2; ++j) {
     const uint64_t x2 = ffma2(f2_pack(sv[2 * j], sv[2 * j + 1]), sc2, nm2);
     uint64_t p2;
     if (kPoly && j >= kPolyFromPair) {
@@ -118,7 +127,7 @@ __device__ __forceinline__ float softmax_row(const float (&sv)[kAttnBN], float s
     pk[j] = kF16 ? pack_f16x2(p0, p1) : pack_bf16x2(p0, p1);
   }
   __syncwarp();
-  tmem_st64(tP, pk);
+  tmem_st_2x32(tP, pk);
   float a0, a1, b0, b1;
   f2_unpack(acc[0], a0, a1);
   f2_unpack(acc[1], b0, b1);
@@ -140,7 +149,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* v8_full = bars + 7;   // [2] raw e4m3 V landed
   uint64_t* v_empty = bars + 9;   // [2] V stage free (after P_B.V)
   uint64_t* s_full = bars + 11;   // [tile] S_g(t) computed (and everything before it)
-  uint64_t* p_full = bars + 13;   // [tile] P_g(t) written (4 softmax warps)
+  uint64_t* p_full = bars + 13;   // [tile] P_g(t) written (its 8 softmax warps)
   uint64_t* o_full = bars + 15;   // [tile] last P_g.V done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -168,7 +177,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&v8_full[s], 1);
       mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&p_full[s], 4);
+      mbar_init(&p_full[s], kAttnSoftmaxWarps);
       mbar_init(&o_full[s], 1);
     }
     *abort_flag = 0;
@@ -182,7 +191,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   // per-row limits; the largest L of the block decides how many key tiles exist
   int my_L = -1;
   if (warp >= 4) {
-    const int r = m0 + (threadIdx.x - 128);
+    const int sw = warp - 4;  // softmax warp: tile sw / 8, rows 32 (sw % 4) + 16 ((sw / 4) % 2) + lane % 16
+    const int r = m0 + (sw >> 3) * kAttnBM + (sw & 3) * 32 + ((sw >> 2) & 1) * 16 + (lane & 15);
     if (r < a.SQ) my_L = uniform ? kv_total - 1 : min(__ldg(a.L + r), kv_total - 1);
   }
   tc_fence_before();
@@ -250,15 +260,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint32_t idesc_o = f16 ? idesc_o16 : idesc_o_bf16;
       // S_g at column 128 g (P_g over its first 64 columns), O_g at 256 + 128 g
       bool ok = mbar_wait(q_full, 0, abort_flag, a.status);
-      const uint32_t q_addr = smem_u32(sQ);
+      // Shared-memory descriptors of the Q tiles and of ring stage 0; another tile,
+      // stage or K step is the same descriptor plus its byte offset / 16 (the 14-bit
+      // address field never carries: every address is below 256 KB).  One 32 KB tile
+      // or stage = 2048 in the field.  This keeps the single issuing thread to a few
+      // instructions per MMA: it shares its sub-partition with four softmax warps.
+      const uint64_t q_desc = sdesc_sw128(smem_u32(sQ), 16, 1024);
+      const uint64_t k_desc = sdesc_sw128(smem_u32(k_ptr(0)), 16, 1024);
+      const uint64_t v_desc = sdesc_sw128(smem_u32(v_ptr(0)), 16384, 1024);
       auto issue_s = [&](int g, int t) {  // K_t resident (k_full waited)
-        const uint32_t k_addr = smem_u32(k_ptr(t & 1));
+        const uint64_t qd0 = q_desc + static_cast<uint64_t>(g) * 2048u;
+        const uint64_t kd0 = k_desc + static_cast<uint64_t>(t & 1) * 2048u;
 #pragma unroll
         for (int k = 0; k < kAttnD / 16; ++k) {
-          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-          const uint64_t qd = sdesc_sw128(q_addr + g * 32768 + off, 16, 1024);
-          const uint64_t kd = sdesc_sw128(k_addr + off, 16, 1024);
-          umma_f16_ss(tmem + 128u * g, qd, kd, idesc_s, k > 0 ? 1u : 0u);
+          const uint32_t off16 = ((k >> 2) * 16384 + (k & 3) * 32) >> 4;
+          umma_f16_ss(tmem + 128u * g, qd0 + off16, kd0 + off16, idesc_s, k > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[g]);
       };
@@ -272,13 +288,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (!mbar_wait(&p_full[g], t & 1, abort_flag, a.status)) return false;
         if (g == 0 && !mbar_wait(&v_full[vs], (t >> 1) & 1, abort_flag, a.status)) return false;
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(v_ptr(vs));
+        const uint64_t vd0 = v_desc + static_cast<uint64_t>(vs) * 2048u;
         const uint32_t idesc = (v_fp8 && t < n_slab) ? idesc_o16 : idesc_o;
 #pragma unroll
         for (int k = 0; k < kAttnBN / 16; ++k) {
           // 16 keys per step: V rows [16k, 16k+16) (2048 B); d halves 16 KB apart
-          const uint64_t vd = sdesc_sw128(v_addr + k * 2048, 16384, 1024);
-          umma_f16_ts(tmem + 256u + 128u * g, tmem + 128u * g + k * 8, vd, idesc, (t > 0 || k > 0) ? 1u : 0u);
+          // P of keys 16k .. 16k+15: 8 packed columns, keys 64-127 at S_g's columns 64-95
+          const uint32_t p_col = 128u * g + k * 8 + (k >= kAttnBN / 32 ? 32u : 0u);
+          umma_f16_ts(tmem + 256u + 128u * g, tmem + p_col, vd0 + k * 128u, idesc, (t > 0 || k > 0) ? 1u : 0u);
         }
         if (t == n_tiles - 1) umma_commit(&o_full[g]);
         if (g == kAttnTiles - 1) umma_commit(&v_empty[vs]);
@@ -332,14 +349,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax (tile g)
-    const int g = (warp - 4) >> 2;
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = quarter * 32 + lane;
-    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t tS = tmem + lane_base + 128u * g;  // S_g; P_g over its first 64 columns
+    // 8 warps per query tile; a warp covers 16 rows of its TMEM lane quarter with two
+    // threads per row (16x32bx2 accesses): thread (row, hc) reads, masks and
+    // exponentiates the scores of columns 64 hc .. 64 hc + 63, the row max is one
+    // shuffle away (lane ^ 16), and the row sum is combined only at the end.
+    const int sw = warp - 4;
+    const int g = sw >> 3;
+    const int quarter = sw & 3;      // TMEM lane quarter this warp may access (warp % 4)
+    const int sub = (sw >> 2) & 1;   // its lower or upper 16 lanes
+    const int hc = lane >> 4;        // column half of the row
+    const int row = quarter * 32 + sub * 16 + (lane & 15);
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32 + sub * 16) << 16;
+    const uint32_t tS = tmem + lane_base + 128u * g;  // S_g; P_g over the first half of each thread's scores
     const uint32_t tO = tmem + lane_base + 256u + 128u * g;
     const uint8_t* kvb = has_kv ? a.key_valid + static_cast<int64_t>(b) * a.kv_sb : nullptr;
-    float m_run = -INFINITY, l_run = 0.0f;
+    float m_run = -INFINITY, l_run = 0.0f;  // l_run: this thread's half of the row sum
     bool ok = true;
     // fp8 slab: the per-(b, h) V scale is applied to O once, after the last slab tile
     const bool slab_f16 = v_fp8 && n_slab > 0;
@@ -355,34 +379,39 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const bool slab = t < n_slab;
       const int kv0 = slab ? t * kAttnBN : P + (t - n_slab) * kAttnBN;
       const int seg_end = slab ? P : kv_total;
-      const int lim_rel = min(my_L, seg_end - 1) - kv0;  // column c allowed iff c <= lim_rel (and key valid)
-      // key-valid bits of this tile: bit i of kvm[j] <-> column 32 j + i (4 warp ballots)
-      uint32_t kvm[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
+      // column c of the tile allowed iff c <= lim_rel (and key valid); this thread's
+      // columns are 64 hc + j
+      const int lim_rel = min(my_L, seg_end - 1) - kv0 - kAttnHalf * hc;
+      // key-valid bits of this thread's columns: bit i of kvm[j] <-> column 64 hc + 32 j + i
+      uint32_t kvm[2] = {0xffffffffu, 0xffffffffu};
       if (has_kv) {
+        uint32_t all[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int kv = kv0 + 32 * j + lane;
           const bool valid = kv < seg_end && __ldg(kvb + kv) != 0;
-          kvm[j] = __ballot_sync(0xffffffffu, valid);
+          all[j] = __ballot_sync(0xffffffffu, valid);
         }
+        kvm[0] = hc ? all[2] : all[0];
+        kvm[1] = hc ? all[3] : all[1];
       }
-      float sv[kAttnBN];
+      float sv[kAttnHalf];
       {
-        uint32_t r[kAttnBN];
-        tmem_ld128(tS, r);
+        uint32_t r[kAttnHalf];
+        tmem_ld_2x64(tS, r);
 #pragma unroll
-        for (int j = 0; j < kAttnBN; ++j) sv[j] = __uint_as_float(r[j]);
+        for (int j = 0; j < kAttnHalf; ++j) sv[j] = __uint_as_float(r[j]);
       }
       // raw scores stay unscaled; the scale is folded into the exponent below
       // every key of the tile allowed for every row of the warp (warp-uniform: the
       // branches below end in warp-collective TMEM stores)
-      const bool full = __all_sync(0xffffffffu, lim_rel >= kAttnBN - 1 && !has_kv);
+      const bool full = __all_sync(0xffffffffu, lim_rel + kAttnHalf * hc >= kAttnBN - 1 && !has_kv);
       float mx[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) mx[i] = -INFINITY;
       if (full) {
 #pragma unroll
-        for (int c = 0; c < kAttnBN; c += 8) {
+        for (int c = 0; c < kAttnHalf; c += 8) {
           mx[0] = fmax3(mx[0], sv[c], sv[c + 1]);
           mx[1] = fmax3(mx[1], sv[c + 2], sv[c + 3]);
           mx[2] = fmax3(mx[2], sv[c + 4], sv[c + 5]);
@@ -390,15 +419,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       } else {
 #pragma unroll
-        for (int c = 0; c < kAttnBN; ++c) {
+        for (int c = 0; c < kAttnHalf; ++c) {
           const bool allowed = (c <= lim_rel) && ((kvm[c >> 5] >> (c & 31)) & 1u);
           sv[c] = allowed ? sv[c] : -INFINITY;
           mx[c & 3] = fmaxf(mx[c & 3], sv[c]);
         }
       }
-      const float raw_max = fmax3(mx[0], mx[1], fmaxf(mx[2], mx[3]));
+      float raw_max = fmax3(mx[0], mx[1], fmaxf(mx[2], mx[3]));
+      raw_max = fmaxf(raw_max, __shfl_xor_sync(0xffffffffu, raw_max, 16));  // the row's other half
       const float tmax = raw_max * a.qk_scale_log2;  // scale > 0: max commutes with it
-      // the running max moves (and O, l are rescaled) only when it grows by > 2^8
+      // the running max moves (and O, l are rescaled) only when it grows by > 2^8; both
+      // threads of a row see the same values and decide alike
       float alpha = 1.0f;
       bool rescale_o = false;
       if (tmax > m_run + kRescaleThreshold || (m_run == -INFINITY && tmax > -INFINITY)) {
@@ -407,15 +438,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         m_run = tmax;
       }
       const float neg_m = (m_run == -INFINITY) ? 0.0f : -m_run;
-      // S_g(t) is in registers: P_g(t) overwrites its first 64 columns
+      // S_g(t) is in registers: P_g(t) overwrites the first 32 of each thread's columns
       const bool f16p = f16 || (slab_f16 && slab);
       float psum;
       if (full)
-        psum = f16p ? softmax_row<true, true>(sv, a.qk_scale_log2, neg_m, tS)
-                    : softmax_row<true, false>(sv, a.qk_scale_log2, neg_m, tS);
+        psum = f16p ? softmax_half_row<true, true>(sv, a.qk_scale_log2, neg_m, tS)
+                    : softmax_half_row<true, false>(sv, a.qk_scale_log2, neg_m, tS);
       else
-        psum = f16p ? softmax_row<false, true>(sv, a.qk_scale_log2, neg_m, tS)
-                    : softmax_row<false, false>(sv, a.qk_scale_log2, neg_m, tS);
+        psum = f16p ? softmax_half_row<false, true>(sv, a.qk_scale_log2, neg_m, tS)
+                    : softmax_half_row<false, false>(sv, a.qk_scale_log2, neg_m, tS);
       l_run = l_run * alpha + psum;
       // O_g holds the sum up to tile t-1 (P_g(t-1).V completed before S_g(t)): it is
       // touched only when some row of the warp rescales (or at the slab boundary);
@@ -425,12 +456,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (t >= 1 && __any_sync(0xffffffffu, rescale_o || boundary)) {
         const float f = (rescale_o ? alpha : 1.0f) * (boundary ? vsc : 1.0f);
 #pragma unroll
-        for (int c = 0; c < kAttnD / 32; ++c) {
+        for (int c = 0; c < kAttnHalf / 32; ++c) {
           uint32_t r[32];
-          tmem_ld32(tO + c * 32, r);
+          tmem_ld_2x32(tO + c * 32, r);
 #pragma unroll
           for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * f);
-          tmem_st32(tO + c * 32, r);
+          tmem_st_2x32(tO + c * 32, r);
         }
         if (boundary) vsc_applied = true;
       }
@@ -439,27 +470,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[g]);
     }
-    // epilogue: O / l -> bf16
+    // epilogue: O / l -> bf16, each thread its row's half (columns 64 hc ..)
+    const float l_row = l_run + __shfl_xor_sync(0xffffffffu, l_run, 16);
     const int grow = m0 + g * kAttnBM + row;
-    float o[kAttnD];
+    float o[kAttnHalf];
     bool have_o = false;
     const bool o_ready = ok && n_tiles > 0 && mbar_wait(&o_full[g], 0, abort_flag, a.status);
     if (__all_sync(0xffffffffu, o_ready)) {  // warp-uniform: tcgen05.ld is warp-collective
       tc_fence_after();
-      uint32_t r[kAttnD];
-      tmem_ld128(tO, r);
+      uint32_t r[kAttnHalf];
+      tmem_ld_2x64(tO, r);
 #pragma unroll
-      for (int j = 0; j < kAttnD; ++j) o[j] = __uint_as_float(r[j]);
+      for (int j = 0; j < kAttnHalf; ++j) o[j] = __uint_as_float(r[j]);
       have_o = true;
     }
     uint32_t am2 = 0;  // two running bf16 |out| maxima (amax_out)
     if (grow < a.SQ) {
-      const bool nz = have_o && l_run > 0.0f;
-      const float inv = nz ? (vsc_applied ? 1.0f : vsc) / l_run : 0.0f;
+      const bool nz = have_o && l_row > 0.0f;
+      const float inv = nz ? (vsc_applied ? 1.0f : vsc) / l_row : 0.0f;
       uint16_t* dst = a.out + static_cast<int64_t>(b) * a.o_sb + static_cast<int64_t>(grow) * a.o_ss +
-                      static_cast<int64_t>(h) * a.o_sh;
+                      static_cast<int64_t>(h) * a.o_sh + kAttnHalf * hc;
 #pragma unroll
-      for (int c = 0; c < kAttnD; c += 8) {
+      for (int c = 0; c < kAttnHalf; c += 8) {
         uint4 w = make_uint4(0u, 0u, 0u, 0u);
         if (nz && f16)
           w = make_uint4(pack_f16x2(o[c] * inv, o[c + 1] * inv), pack_f16x2(o[c + 2] * inv, o[c + 3] * inv),
