@@ -434,12 +434,14 @@ static int gemm_pick_cfg(int64_t M, int64_t N) {
 }
 
 // Raster group (row tiles per group, tile_coords).  Measured on the configs[4] shapes
-// and the DiT block's (1 x B200, groups of 1, 2, 4, 8 and 16 row tiles forced): 16 is
-// the best or within 0.5% of it everywhere but 16384 x 9216 (313.7 against 308.5 us
-// row-major), and it gains most where B is re-read every wave in row-major order: the
-// FFN's down projection 4352 x 3072 x 12288 124.5 -> 113.2 us, 16384 x 18432 677.5 ->
-// 644.9 us, 9472 x 18432 374.2 -> 359.9 us.
-static int gemm_pick_raster(int /*cfg*/) { return 16; }
+// and the DiT block's (1 x B200, groups of 1, 2, 4, 8 and 16 row tiles forced): for a B
+// of 18432 x 3072 (56.6 MB, more than L2 keeps from one wave to the next in row-major
+// order) groups of 16 gain 2-5% (16384 x 18432 677.5 -> 644.9 us, 9472 x 18432 374.2
+// -> 359.9, 4352 x 18432 171.3 -> 167.1); where B is smaller they are within 1% either
+// way but read more: the FFN's down projection (4352 x 3072 x 12288) ran faster alone
+// with groups of 16 (113.2 against 124.5 us, L2 flushed) yet read 200 MB of DRAM instead
+// of 118 MB, and inside the FFN chain, whose pack leaves A in L2, it was no faster.
+static int gemm_pick_raster(int64_t N, int64_t K) { return N * K > (int64_t{48} << 20) ? 16 : 1; }
 
 template <int BN, int STAGES, bool TWO_SM>
 static int launch_gemm(const uint8_t* A, const uint8_t* B, const GemmParams& p, int64_t lda, int64_t ldb,
@@ -542,7 +544,7 @@ int launch_fp8_gemm_ex(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N,
   const int sel = tile_cfg & 0xFF;
   const int cfg = sel == QIK_GEMM_TILE_AUTO ? gemm_pick_cfg(M, N) : sel;
   const int raster = (tile_cfg >> 8) & 0xFF;
-  p.group_m = raster != 0 ? raster : gemm_pick_raster(cfg);
+  p.group_m = raster != 0 ? raster : gemm_pick_raster(N, K);
   switch (cfg) {
     case QIK_GEMM_TILE_PAIR_256:
       return launch_gemm<256, 6, true>(A, B, p, lda, ldb, stream, pdl);
