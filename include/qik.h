@@ -151,6 +151,7 @@ int qik_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64
 #define QIK_GEMM_TILE_SINGLE_256 2  /* single CTAs, 128 x 256 tiles */
 #define QIK_GEMM_TILE_SINGLE_128 3  /* single CTAs, 128 x 128 tiles */
 #define QIK_GEMM_TILE_SINGLE_64 4   /* single CTAs, 128 x 64 tiles */
+#define QIK_GEMM_TILE_SWAP_16 5     /* M <= 16 only: operands swapped, 128 weight rows x 16 activation rows */
 /* Tile raster, or-ed into tile_cfg: output tiles walked in groups of g (1..255) row
  * tiles, each group column tile by column tile (g = 1: row-major); 0 = what
  * qik_fp8_gemm picks. */

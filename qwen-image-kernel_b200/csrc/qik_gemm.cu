@@ -8,7 +8,9 @@
 //       by tcgen05.mma.cta_group::2 -- each CTA loads 128 rows of A and 128 rows of B
 //       per stage, so a CTA moves 32 KB instead of 48 KB per 128-deep K step for the
 //       same 128 x 256 share of the output, with 6 pipeline stages;
-//     - single CTAs with 128 x BN tiles (BN = 256, 128 or 64) for skinny M;
+//     - single CTAs with 128 x BN tiles (BN = 256, 128 or 64) for skinny M, and for at
+//       most 16 rows the operands swapped (BN = 16: 128 weight rows x 16 activation
+//       rows per tile, stored transposed by the epilogue);
 //   * warp 0: TMA producer -- 128-byte swizzle, no cluster multicast (each CTA loads
 //     its own tiles; in a pair both CTAs' loads complete on the leader's barrier);
 //   * warp 1: one thread (of the leader CTA in a pair) issues tcgen05.mma.kind::f8f6f4
@@ -79,7 +81,8 @@ struct GemmLayout {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStageOutOffset = STAGES * kStageBytes;  // 8 warps x 2 buffers x 2 KB
   static constexpr int kOutBufBytes = 2048;                      // 32 rows x 64 bytes
-  static constexpr int kBarOffset = kStageOutOffset + kGemmEpiWarps * 2 * kOutBufBytes;
+  // the transposed tiny-M form (BN = 16) stores straight from registers: no staging
+  static constexpr int kBarOffset = kStageOutOffset + (BN == 16 ? 0 : kGemmEpiWarps * 2 * kOutBufBytes);
   static constexpr int kBarBytes = (2 * STAGES + 4) * 8 + 16;
   static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;  // + alignment slack
   // two accumulators of BN columns each (BN a power of two, as the TMEM allocation is)
@@ -274,6 +277,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tile_coords(tile, num_m, num_n, p.group_m, mb, nb);
       const int row0 = mb * kTileM + static_cast<int>(rank) * kGemmBM + quarter * 32;
       const bool row_ok = row0 + lane < p.M;
+      if constexpr (BN == 16) {
+        // transposed tiny-M form: kernel row r = output column (a weight row), kernel
+        // column c = output row (an activation row); one warp per lane quarter stores
+        // its 32 output columns of each of the 16 (valid) output rows, 64 contiguous
+        // bytes per row and store
+        if (half == 0) {
+          uint32_t r[16];
+          tmem_ld16(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                        static_cast<uint32_t>(acc * Lay::kAccStride),
+                    r);
+          const int n = row0 + lane;
+          if (row_ok) {
+            const float bn = p.bias ? __bfloat162float(p.bias[n]) : 0.0f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int m = nb * 16 + j;
+              if (m >= p.N) break;
+              float v = __uint_as_float(r[j]) * s + bn;
+              if (p.out_f32) {
+                static_cast<float*>(p.C)[static_cast<int64_t>(m) * p.ldc + n] = v;
+              } else {
+                if (p.epilogue == QIK_EPI_GELU_TANH) v = gelu_tanh_f32(__bfloat162float(__float2bfloat16_rn(v)));
+                const __nv_bfloat16 o = __float2bfloat16_rn(v);
+                static_cast<__nv_bfloat16*>(p.C)[static_cast<int64_t>(m) * p.ldc + n] = o;
+                amax_local = max(amax_local, static_cast<uint32_t>(__bfloat16_as_ushort(o) & 0x7FFFu));
+              }
+            }
+          }
+        }
+      }
 #pragma unroll 1
       for (int c = half; c < BN / 32; c += 2) {
         uint32_t r[32];
@@ -427,9 +460,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // at every configs[4] shape and at the FFN's (4352 x 12288: 120.7 and 139.3 us against
 // 116.4): a 240-wide tile took about as long as a 256-wide one, and 192-wide tiles read
 // ~17% more operand bytes per FLOP.
-static int gemm_pick_cfg(int64_t M, int64_t N) {
+// At most 16 rows (the DiT's timestep-modulation linear: M = 2), the operands swap
+// (QIK_GEMM_TILE_SWAP_16): 128 weight rows per tile against the 16-row activation tile,
+// 18 KB per pipeline stage instead of 32 KB, so 11 stages of the weight stream are in
+// flight per SM instead of 6; the scatter (tensor-parallel) epilogue keeps the
+// untransposed tiles.
+static int gemm_pick_cfg(int64_t M, int64_t N, bool scatter = false) {
   if (M > 2 * kGemmBM) return QIK_GEMM_TILE_PAIR_256;
   if (M > kGemmBM) return N >= 12288 ? QIK_GEMM_TILE_PAIR_256 : QIK_GEMM_TILE_SINGLE_128;
+  if (M <= 16 && !scatter) return QIK_GEMM_TILE_SWAP_16;
   return (N + 127) / 128 >= sm_count() / 2 ? QIK_GEMM_TILE_SINGLE_128 : QIK_GEMM_TILE_SINGLE_64;
 }
 
@@ -457,12 +496,16 @@ static int launch_gemm(const uint8_t* A, const uint8_t* B, const GemmParams& p, 
                     static_cast<uint64_t>(ldb), kGemmBK, kBRows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   CUtensorMap tc;
+  // the output [rows, cols]: the kernel's [M, N], or [N, M] in the transposed tiny-M
+  // form (whose epilogue stores without the map)
+  const uint64_t c_cols = static_cast<uint64_t>(BN == 16 ? p.M : p.N);
+  const uint64_t c_rows = static_cast<uint64_t>(BN == 16 ? p.N : p.M);
   if (p.out_f32)
-    rc = make_tmap_2d(&tc, p.C, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, static_cast<uint64_t>(p.N),
-                      static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.ldc) * 4, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    rc = make_tmap_2d(&tc, p.C, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, c_cols, c_rows, static_cast<uint64_t>(p.ldc) * 4, 16,
+                      32, CU_TENSOR_MAP_SWIZZLE_64B);
   else
-    rc = make_tmap_2d(&tc, p.C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<uint64_t>(p.N),
-                      static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.ldc) * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    rc = make_tmap_2d(&tc, p.C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, c_cols, c_rows, static_cast<uint64_t>(p.ldc) * 2, 32,
+                      32, CU_TENSOR_MAP_SWIZZLE_64B);
   if (rc) return rc;
   static std::once_flag attr_once[64];
   int dev = 0;
@@ -542,7 +585,7 @@ int launch_fp8_gemm_ex(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N,
   p.amax_out = amax_out;
   p.status = status;
   const int sel = tile_cfg & 0xFF;
-  const int cfg = sel == QIK_GEMM_TILE_AUTO ? gemm_pick_cfg(M, N) : sel;
+  const int cfg = sel == QIK_GEMM_TILE_AUTO ? gemm_pick_cfg(M, N, scatter != nullptr) : sel;
   const int raster = (tile_cfg >> 8) & 0xFF;
   p.group_m = raster != 0 ? raster : gemm_pick_raster(N, K);
   switch (cfg) {
@@ -554,6 +597,17 @@ int launch_fp8_gemm_ex(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N,
       return launch_gemm<64, 8, false>(A, B, p, lda, ldb, stream, pdl);
     case QIK_GEMM_TILE_SINGLE_256:
       return launch_gemm<256, 4, false>(A, B, p, lda, ldb, stream, pdl);
+    case QIK_GEMM_TILE_SWAP_16: {
+      // C^T = B . A^T: the weights are the tile rows, the (at most 16) activation rows
+      // the tile columns; the epilogue stores C untransposed
+      QIK_REQUIRE(M <= 16 && !scatter, "qik_fp8_gemm: the swapped tiny-M configuration needs M <= 16, got %lld",
+                  static_cast<long long>(M));
+      GemmParams q = p;
+      q.M = p.N;
+      q.N = p.M;
+      q.group_m = 1;
+      return launch_gemm<16, 11, false>(B, A, q, ldb, lda, stream, pdl);
+    }
     default:
       return set_error(QIK_ERR_INVALID, "qik_fp8_gemm: unknown tile configuration %d", cfg);
   }
@@ -571,7 +625,7 @@ int launch_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, in
 namespace qik {
 // Tile height and width of the configuration launch_fp8_gemm picks for (M, N).
 static void gemm_tile_shape(int64_t M, int64_t N, int* tile_m, int* tile_n, int* ctas_per_tile) {
-  const int cfg = gemm_pick_cfg(M, N);
+  const int cfg = gemm_pick_cfg(M, N, true);  // the scatter epilogue's tiles
   const bool pair = cfg == QIK_GEMM_TILE_PAIR_256;
   *tile_m = pair ? 2 * kGemmBM : kGemmBM;
   *tile_n = (pair || cfg == QIK_GEMM_TILE_SINGLE_256) ? 256 : (cfg == QIK_GEMM_TILE_SINGLE_128 ? 128 : 64);
@@ -632,7 +686,7 @@ extern "C" int qik_fp8_gemm_tiled(const uint8_t* A, const uint8_t* B, int64_t M,
   const int sel = tile_cfg & 0xFF;
   QIK_REQUIRE((tile_cfg & ~0xFFFF) == 0 &&
                   (sel == QIK_GEMM_TILE_AUTO || sel == QIK_GEMM_TILE_PAIR_256 || sel == QIK_GEMM_TILE_SINGLE_256 ||
-                   sel == QIK_GEMM_TILE_SINGLE_128 || sel == QIK_GEMM_TILE_SINGLE_64),
+                   sel == QIK_GEMM_TILE_SINGLE_128 || sel == QIK_GEMM_TILE_SINGLE_64 || sel == QIK_GEMM_TILE_SWAP_16),
               "qik_fp8_gemm_tiled: unknown tile configuration %d", tile_cfg);
   return qik::launch_fp8_gemm_ex(A, B, M, N, K, lda, ldb, scale_a, scale_b, bias, C, ldc, out_dtype, epilogue,
                                  amax_out, status, static_cast<cudaStream_t>(stream), false, nullptr, tile_cfg);

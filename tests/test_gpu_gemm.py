@@ -67,6 +67,43 @@ def test_gemm_every_tile_config_exact(fp8, cfg, M, N, K):
     assert torch.equal(yb.cpu(), ref.to(torch.bfloat16))
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 128, 128), (2, 18432, 3072), (5, 736, 384), (16, 1936, 256), (2, 3072, 12288)])
+def test_gemm_swapped_tiny_m_exact(fp8, M, N, K):
+    """The tiny-M configuration (QIK_GEMM_TILE_SWAP_16, the default for M <= 16: weights
+    as the tile rows, the activation rows as a 16-wide tile, the output stored
+    transposed): exact small-integer products in fp32 and bf16, equal to the untransposed
+    128 x 64 configuration, with bias, GELU and the amax output."""
+    from qik import _lib as L
+    a = _e4m3_small_ints(M + 13 * K, (M, K)).cuda()
+    b = _e4m3_small_ints(N + 17 * K, (N, K)).cuda()
+    ref = a.cpu().float() @ b.cpu().float().t()
+    y = fp8.fp8_gemm(a, _one(), b, _one(), out_dtype=torch.float32, tile_cfg=L.GEMM_TILE_SWAP_16)
+    yb = fp8.fp8_gemm(a, _one(), b, _one(), tile_cfg=L.GEMM_TILE_SWAP_16)
+    y_auto = fp8.fp8_gemm(a, _one(), b, _one())  # the default for M <= 16
+    torch.cuda.synchronize()
+    assert torch.equal(y.cpu(), ref)
+    assert torch.equal(yb.cpu(), ref.to(torch.bfloat16))
+    assert torch.equal(y_auto.cpu(), ref.to(torch.bfloat16))
+    bias = (torch.randn(N, generator=torch.Generator().manual_seed(N)) * 4).to(torch.bfloat16).cuda()
+    for epi in (L.EPI_SCALE, L.EPI_GELU_TANH):
+        am_s, am_u = (torch.zeros(1, dtype=torch.int32, device="cuda") for _ in range(2))
+        ys = fp8.fp8_gemm(a, _one(), b, _one(), bias=bias, epilogue=epi, amax_out=am_s,
+                          tile_cfg=L.GEMM_TILE_SWAP_16)
+        yu = fp8.fp8_gemm(a, _one(), b, _one(), bias=bias, epilogue=epi, amax_out=am_u,
+                          tile_cfg=L.GEMM_TILE_SINGLE_64)
+        torch.cuda.synchronize()
+        assert torch.equal(ys, yu), epi
+        assert int(am_s.item()) == int(am_u.item()) == int(ys.float().abs().max().view(torch.int32).item())
+
+
+def test_gemm_swapped_tiny_m_rejects_larger_m(fp8):
+    from qik import _lib as L
+    a = torch.zeros(17, 128, dtype=torch.float8_e4m3fn, device="cuda")
+    b = torch.zeros(128, 128, dtype=torch.float8_e4m3fn, device="cuda")
+    with pytest.raises(L.QikError, match="M <= 16"):
+        fp8.fp8_gemm(a, _one(), b, _one(), tile_cfg=L.GEMM_TILE_SWAP_16)
+
+
 @pytest.mark.parametrize("cfg", [1, 3])
 @pytest.mark.parametrize("raster", [1, 3, 16, 255])
 def test_gemm_raster_groups_exact(fp8, cfg, raster):
