@@ -252,7 +252,8 @@ typedef struct qik_attn_args {
  * (QIK_ATTN_F16) fp16 tensors as the reference accepts both
  * (triton_attention.py:190): P is rounded to the tensors' type before P.V
  * (triton_attention.py:162-163), fp32 accumulation.
- * Requires D == 128 and unit stride along D; rows with no allowed key give 0.
+ * Requires D == 128 and unit stride along D; rows with no allowed key give 0.  SN may be
+ * 0 (the rows attend to the cache alone; k and v are then not read and may be NULL).
  */
 int qik_block_causal_attention(const qik_attn_args* args, int* status, void* stream);
 

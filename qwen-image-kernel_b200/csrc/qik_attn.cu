@@ -543,10 +543,12 @@ extern "C" int qik_block_causal_attention(const qik_attn_args* args, int* status
   QIK_REQUIRE(A.D == kAttnD, "qik_block_causal_attention: head_dim %lld unsupported (128 only)", (long long)A.D);
   QIK_REQUIRE(A.B >= 0 && A.SQ >= 0 && A.SN >= 0 && A.P >= 0 && A.H > 0, "qik_block_causal_attention: bad sizes");
   if (A.B == 0 || A.SQ == 0) return QIK_OK;
-  QIK_REQUIRE(A.SN > 0, "qik_block_causal_attention: no fresh keys (SN == 0)");
   QIK_REQUIRE(A.B * A.H <= 65535 && (A.SQ + kAttnRows - 1) / kAttnRows <= 65535 && A.SN + A.P <= (1ll << 30),
               "qik_block_causal_attention: size out of range");
-  QIK_REQUIRE(A.q && A.k && A.v && A.out, "qik_block_causal_attention: NULL q/k/v/out");
+  // SN == 0: the rows attend to the cache alone (or, without one, to no key: zeros);
+  // k and v are then never read and may be empty
+  const bool fresh = A.SN > 0;
+  QIK_REQUIRE(A.q && A.out && (!fresh || (A.k && A.v)), "qik_block_causal_attention: NULL q/k/v/out");
   const bool has_cache = (A.flags & QIK_ATTN_HAS_CACHE) && A.P > 0;
   const bool v_fp8 = has_cache && (A.flags & QIK_ATTN_V_FP8);
   QIK_REQUIRE(!has_cache || (A.cache_k && A.cache_v), "qik_block_causal_attention: cache pointers missing");
@@ -556,10 +558,10 @@ extern "C" int qik_block_causal_attention(const qik_attn_args* args, int* status
   auto ok_strides = [](int64_t sb, int64_t ss, int64_t sh, int esize) {
     return (sb * esize) % 16 == 0 && (ss * esize) % 16 == 0 && (sh * esize) % 16 == 0 && sb >= 0 && ss > 0 && sh > 0;
   };
-  QIK_REQUIRE(ok_strides(A.q_sb, A.q_ss, A.q_sh, 2) && ok_strides(A.k_sb, A.k_ss, A.k_sh, 2) &&
-                  ok_strides(A.v_sb, A.v_ss, A.v_sh, 2) && ok_strides(A.o_sb, A.o_ss, A.o_sh, 2),
+  QIK_REQUIRE(ok_strides(A.q_sb, A.q_ss, A.q_sh, 2) && ok_strides(A.o_sb, A.o_ss, A.o_sh, 2) &&
+                  (!fresh || (ok_strides(A.k_sb, A.k_ss, A.k_sh, 2) && ok_strides(A.v_sb, A.v_ss, A.v_sh, 2))),
               "qik_block_causal_attention: q/k/v/out strides must be multiples of 16 bytes (unit stride on D)");
-  QIK_REQUIRE(aligned16(A.q) && aligned16(A.k) && aligned16(A.v) && aligned16(A.out),
+  QIK_REQUIRE(aligned16(A.q) && aligned16(A.out) && (!fresh || (aligned16(A.k) && aligned16(A.v))),
               "qik_block_causal_attention: q/k/v/out must be 16-byte aligned");
   if (has_cache) {
     QIK_REQUIRE(ok_strides(A.ck_sb, A.ck_ss, A.ck_sh, 2) && ok_strides(A.cv_sb, A.cv_ss, A.cv_sh, v_fp8 ? 1 : 2) &&
@@ -571,13 +573,14 @@ extern "C" int qik_block_causal_attention(const qik_attn_args* args, int* status
       (A.flags & QIK_ATTN_F16) ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   int rc = make_bshd_map(&tq, A.q, dt16, 2, A.B, A.SQ, A.H, A.q_sb, A.q_ss, A.q_sh, 64,
                          CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc)
+  if (!rc && fresh)
     rc = make_bshd_map(&tk, A.k, dt16, 2, A.B, A.SN, A.H, A.k_sb, A.k_ss, A.k_sh, 64,
                        CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc)
+  if (!rc && fresh)
     rc = make_bshd_map(&tv, A.v, dt16, 2, A.B, A.SN, A.H, A.v_sb, A.v_ss, A.v_sh, 64,
                        CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
+  if (!fresh) tk = tv = tq;  // never read: no fresh key tile exists
   if (has_cache) {
     rc = make_bshd_map(&tck, A.cache_k, dt16, 2, A.B, A.P, A.H, A.ck_sb, A.ck_ss, A.ck_sh,
                        64, CU_TENSOR_MAP_SWIZZLE_128B);

@@ -123,6 +123,31 @@ def test_reference_decode_layouts(attn, P, T):
         _check(out, ref32, tag=f"decode P={P} T={T} uniform={uniform}")
 
 
+@pytest.mark.parametrize("P", [0, 300])
+def test_no_fresh_keys(attn, P):
+    """SN == 0: the query rows attend to the cache alone (P > 0, uniform and per-row
+    limits), or to no key at all (P == 0: zeros); the empty fresh K / V are never read."""
+    H, T = 2, 200
+    q = GI.randn_bf16(70 + P, (1, T, H, 128), 0.3)
+    kn = torch.empty(1, 0, H, 128, dtype=torch.bfloat16)
+    vn = torch.empty(1, 0, H, 128, dtype=torch.bfloat16)
+    if P == 0:
+        L = torch.full((T,), -1, dtype=torch.int32)
+        out = attn.block_causal_flash_attention(q.cuda(), kn.cuda(), vn.cuda(), L.cuda(), None)
+        torch.cuda.synchronize()
+        assert torch.count_nonzero(out).item() == 0
+        return
+    ck = GI.randn_bf16(71 + P, (1, P, H, 128), 0.3)
+    cv = GI.randn_bf16(72 + P, (1, P, H, 128), 0.3)
+    for L, uniform in ((torch.full((T,), P - 1, dtype=torch.int32), True),
+                       (torch.arange(T, dtype=torch.int32) + (P - T), False)):
+        ref32 = O.block_causal_attention(q, kn, vn, L, None, ck, cv, out_dtype=torch.float32)
+        out = attn.block_causal_flash_attention(q.cuda(), kn.cuda(), vn.cuda(), L.cuda(), None, ck.cuda(),
+                                                cv.cuda(), uniform_full=uniform)
+        torch.cuda.synchronize()
+        _check(out, ref32, tag=f"no fresh keys P={P} uniform={uniform}")
+
+
 def test_fp8_slab_through_kv_cache(attn):
     """tests/test_kv_cache.py:40-60: fp8-V slab stored by ContiguousKVCache, attention
     vs the oracle with the same dequantized V, and vs the bf16-V result (rel < 0.03)."""
