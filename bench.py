@@ -676,8 +676,8 @@ def extras(device: torch.device, flush: L2Flush, iters: int = 10) -> dict:
         "api": "qik.processors.QwenImage21KernelBlock.forward (+ the timestep-modulation FP8Linear)",
         "includes": "modulation GEMV (M=2, 3072->18432), 2x LayerNorm+modulate (each emitting its FP8 linear's "
                     "e4m3 input), fused QKV 3072->9216, "
-                    "RMSNorm+RoPE (q, k), block-causal attention, out-proj, SwiGLU MLP (fused up 3072->12288, "
-                    "down 6144->3072), 2x gated residual"}
+                    "RMSNorm+RoPE (q, k), block-causal attention, out-proj, SwiGLU MLP (fused up 3072->12288 with "
+                    "the SwiGLU in its GEMM epilogue, down 6144->3072), 2x gated residual"}
     case = dit_block_case(device, g)
     block = case["block"]
     for _ in range(3):

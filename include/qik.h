@@ -125,6 +125,10 @@ int qik_quantize_weight(const void* w, int dtype, int64_t n, uint8_t* q, float* 
 #define QIK_EPI_SCALE 0      /* y = acc * sa * sb (+ bias) */
 #define QIK_EPI_GELU_TANH 1  /* y = gelu_tanh(bf16(acc * sa * sb (+ bias))) */
 #define QIK_EPI_SCATTER 2    /* fp32 acc * sa * sb rows to their owner rank (qik_fp8_gemm_scatter) */
+#define QIK_EPI_SWIGLU 3     /* SwiGLU of the fused gate / up linear (B rows [0, N/2) gate, [N/2, N)
+                                up, as fused_swiglu's chunk(2) splits them): C[:, j] =
+                                bf16(bf16(silu(g_j)) * u_j), g_j, u_j the bf16 outputs of B rows j
+                                and N/2 + j (+ bias); C has N / 2 columns; N % 256 == 0, BF16 */
 
 /*
  * FP8 GEMM on tcgen05: C[M,N] = epilogue(A[M,K] . B[N,K]^T), e4m3 x e4m3 with
@@ -135,8 +139,9 @@ int qik_quantize_weight(const void* w, int dtype, int64_t n, uint8_t* q, float* 
  *   scale_a, scale_b: 1 fp32 each (device)
  *   bias: N bf16 or NULL
  *   C: row-major [M, N] of out_dtype (BF16 or F32), row pitch ldc elements
- *      (N % 16 == 0, ldc % 8 == 0, C 16-byte aligned)
- *   epilogue: QIK_EPI_*
+ *      (N % 16 == 0, ldc % 8 == 0, C 16-byte aligned); [M, N / 2] for QIK_EPI_SWIGLU
+ *   epilogue: QIK_EPI_*; QIK_EPI_SWIGLU always runs on CTA-pair 256 x 256 tiles
+ *      (a tile holds 128 gate and the matching 128 up columns)
  *   amax_out: NULL, or a u32 that receives atomicMax of the fp32 bit patterns of
  *      |C| (BF16 output only): the amax of the next dynamic quantization.
  *   status: NULL or a device int set to QIK_STATUS_TIMEOUT on a failed wait.
@@ -275,7 +280,7 @@ int qik_kv_store(const void* k, const void* v, int64_t B, int64_t P, int64_t H, 
  * Per-head RMSNorm + rotary embedding of one of q / k: for every (b, s, h) row of D,
  * rrms = rsqrt(sum(x^2) / D + eps), n = bf16(x * rrms * weight), then each pair
  * (n[2i], n[2i+1]) is rotated by (cos[s, i], sin[s, i]); bf16 out.  Replaces
- * fused_rms_norm_rope + rms_rope_kernel (qwen_image_kernel/triton_fused.py:27-117);
+ * fused_rms_norm_rope + rms_rope_kernel (qwen_image_kernel/triton_fused.py:28-105);
  * unlike the reference it reads strided q / k views of the fused QKV output directly.
  *   x: [B, S, H, D] bf16, element strides (x_sb, x_ss, x_sh), unit D stride
  *   weight: D fp32; cos_tab, sin_tab: [S, D/2] fp32 (rows contiguous)
@@ -291,7 +296,7 @@ int qik_rms_norm_rope(const void* x, int64_t B, int64_t S, int64_t H, int64_t D,
  * bf16(1 + scale), the scale row chosen per position: row b where target_mask[s]
  * is non-zero (or target_mask is NULL), row B + b elsewhere (the t = 0 rows).
  * Replaces fused_layer_norm_modulate + ln_modulate_kernel and _modulation_row_map
- * (qwen_image_kernel/triton_fused.py:75-160).
+ * (qwen_image_kernel/triton_fused.py:111-177).
  *   x, out: [B, S, D] bf16 contiguous; modulation: mod_rows rows of mod_stride bf16
  *   (at least B rows, 2B with a target_mask), scale at column scale_off;
  *   target_mask: S bytes or NULL; D % 8 == 0, D <= 4096.
@@ -306,7 +311,7 @@ int qik_layer_norm_modulate(const void* x, int64_t B, int64_t S, int64_t D, cons
  * qik_layer_norm_modulate feeding an FP8 linear: the same bf16 outputs, quantized
  * with their own dynamic per-tensor scale exactly as qik_quantize_act would quantize
  * them (same codes, same scale), without the bf16 tensor ever being written.
- * Replaces fused_layer_norm_modulate (qwen_image_kernel/triton_fused.py:111-160)
+ * Replaces fused_layer_norm_modulate (qwen_image_kernel/triton_fused.py:111-177)
  * followed by the quantize_tensorwise of the next FP8Linear.forward
  * (qwen_image_kernel/fp8.py:44-53, 85-86).  One cooperative kernel: the rows are
  * normalized twice, once for max|out| and, after a grid-wide exchange, once for the
@@ -325,7 +330,7 @@ int qik_layer_norm_modulate_e4m3(const void* x, int64_t B, int64_t S, int64_t D,
 /*
  * Gated residual out = x + bf16(tanh(gate)) * f in bf16 arithmetic, the gate row
  * chosen per position as in qik_layer_norm_modulate.  Replaces fused_gate_residual
- * + gate_residual_kernel (qwen_image_kernel/triton_fused.py:168-218).
+ * + gate_residual_kernel (qwen_image_kernel/triton_fused.py:183-231).
  *   x, f, out: [B, S, D] bf16 contiguous, out distinct from x and f; gate at column gate_off.
  */
 int qik_gate_residual(const void* x, const void* f, int64_t B, int64_t S, int64_t D, const void* modulation,
@@ -334,7 +339,7 @@ int qik_gate_residual(const void* x, const void* f, int64_t B, int64_t S, int64_
 
 /*
  * SwiGLU out = bf16(bf16(silu(gate)) * up).  Replaces fused_swiglu + swiglu_kernel
- * (qwen_image_kernel/triton_fused.py:227-262); gate and up may be the two halves of
+ * (qwen_image_kernel/triton_fused.py:237-263); gate and up may be the two halves of
  * the fused up-projection output (row pitches ld_*, in elements), read in place.
  *   [M, N] bf16 each; N and the pitches multiples of 8; amax_out as in
  *   qik_layer_norm_modulate (for the down projection's quantizer).

@@ -325,8 +325,8 @@ def _rb(t: torch.Tensor) -> torch.Tensor:
 
 def modulation_rows(target_token_mask: torch.Tensor | None, B: int, S: int) -> torch.Tensor:
     """[B, S] modulation row of each (sample, position): the row map of
-    _modulation_row_map (triton_fused.py:128-139, 0 for target positions, B
-    otherwise) plus the sample index, as the kernels add it (triton_fused.py:111,188)."""
+    _modulation_row_map (triton_fused.py:141-151, 0 for target positions, B
+    otherwise) plus the sample index, as the kernels add it (triton_fused.py:127,199)."""
     if target_token_mask is None:
         base = torch.zeros(S, dtype=torch.int64)
     else:
@@ -336,7 +336,7 @@ def modulation_rows(target_token_mask: torch.Tensor | None, B: int, S: int) -> t
 
 def rms_norm_rope(x: torch.Tensor, weight: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                   eps: float) -> torch.Tensor:
-    """rms_rope_kernel (triton_fused.py:27-67): per (b, s, h) row of D,
+    """rms_rope_kernel (triton_fused.py:28-69): per (b, s, h) row of D,
     rrms = rsqrt(sum(x^2) / D + eps); n = bf16((x * rrms) * w) in fp32; the pairs
     (n[2i], n[2i+1]) rotate by (cos[s, i], sin[s, i]); bf16 out.
     x: [B, S, H, D] bf16 (any strides); weight: [D]; cos, sin: [S, D/2] fp32."""
@@ -355,7 +355,7 @@ def rms_norm_rope(x: torch.Tensor, weight: torch.Tensor, cos: torch.Tensor, sin:
 
 def layer_norm_modulate(x: torch.Tensor, modulation: torch.Tensor, scale_off: int,
                         target_token_mask: torch.Tensor | None, eps: float) -> torch.Tensor:
-    """ln_modulate_kernel (triton_fused.py:75-108): LayerNorm without affine in fp32
+    """ln_modulate_kernel (triton_fused.py:111-138): LayerNorm without affine in fp32
     (mean, then the centred variance), y = bf16(xc * rsqrt(var + eps)), then
     bf16(y * bf16(1 + scale)) with scale = modulation[row, scale_off : scale_off + D].
     x: [B, S, D] bf16; modulation: [R, >= scale_off + D] bf16."""
@@ -372,7 +372,7 @@ def layer_norm_modulate(x: torch.Tensor, modulation: torch.Tensor, scale_off: in
 
 def gate_residual(x: torch.Tensor, f: torch.Tensor, modulation: torch.Tensor, gate_off: int,
                   target_token_mask: torch.Tensor | None) -> torch.Tensor:
-    """gate_residual_kernel (triton_fused.py:168-196): g = bf16(tanh(gate)) with gate =
+    """gate_residual_kernel (triton_fused.py:183-209): g = bf16(tanh(gate)) with gate =
     modulation[row, gate_off : gate_off + D]; y = x + g * f in bf16 arithmetic (the
     product rounded to bf16, then the sum), as the stock expression rounds."""
     x = x.cpu().float()
@@ -384,7 +384,7 @@ def gate_residual(x: torch.Tensor, f: torch.Tensor, modulation: torch.Tensor, ga
 
 
 def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
-    """swiglu_kernel (triton_fused.py:227-240): s = bf16(g * sigmoid(g)) in fp32, then
+    """swiglu_kernel (triton_fused.py:237-249): s = bf16(g * sigmoid(g)) in fp32, then
     bf16(s * up)."""
     g = gate.cpu().float()
     s = _rb(g * torch.sigmoid(g))

@@ -515,6 +515,15 @@ __device__ __forceinline__ uint32_t f2_to_bf2(uint64_t v) {
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
 }
+// bf16(silu(g)) of the SwiGLU (triton_fused.py:237-249): g / (1 + e^-g) with the
+// reciprocal from rcp.approx (an error of about one fp32 ulp, far below the bf16
+// rounding of the result; 1 / inf = 0 gives silu(-large) = -0).  Shared by the SwiGLU
+// kernel and the GEMM's SwiGLU epilogue, so both give the same bytes.
+__device__ __forceinline__ float silu_bf16(float g) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + __expf(-g)));
+  return __bfloat162float(__float2bfloat16_rn(g * r));
+}
 // bf16x2 product rounded once to nearest even.  The fp32 product of two bf16 values is
 // exact (8-bit significands) above the fp32 normal range's floor, so this equals
 // bf16(fl32(a) * fl32(b)); only products below 2^-126 (where an fp32 multiply would

@@ -3,14 +3,14 @@
 // Restatements of the reference's fused Triton kernels
 // (qwen_image_kernel/triton_fused.py) with the same rounding points:
 //   rms_norm_rope    per-head RMSNorm (fp32 weight multiply, one bf16 rounding) +
-//                    complex RoPE on (even, odd) pairs             (:27-67)
+//                    complex RoPE on (even, odd) pairs             (:28-69)
 //   layer_norm_mod   LayerNorm without affine, bf16, times bf16(1 + scale) with the
-//                    per-position modulation row map              (:75-108)
+//                    per-position modulation row map              (:111-138)
 // The two norms stream their rows through shared memory (bulk copies into a ring,
 // see "row streaming"); RMSNorm + RoPE keeps a register-only form for layouts whose
 // heads are not contiguous within a token.
-//   gate_residual    x + bf16(tanh(gate)) * f                      (:168-196)
-//   swiglu           bf16(silu(g)) * up                            (:227-240)
+//   gate_residual    x + bf16(tanh(gate)) * f                      (:183-209)
+//   swiglu           bf16(silu(g)) * up                            (:237-249)
 // All four are HBM-bound: 16-byte vector loads and stores, grids a multiple of the
 // SM count with grid-stride loops.  Layer norm and SwiGLU can also accumulate the
 // amax of their bf16 output (fp32 bit patterns, atomicMax), which is the reduction
@@ -583,14 +583,7 @@ __global__ void __launch_bounds__(kGateThreads, 7) gate_residual_kernel(
 }
 
 // ---------------------------------------------------------------- SwiGLU
-// silu(g) = g / (1 + e^-g) with the reciprocal from rcp.approx (an error of about one
-// fp32 ulp, far below the bf16 rounding of the result; 1 / inf = 0 gives
-// silu(-large) = -0).
-__device__ __forceinline__ float silu_bf16(float g) {
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + __expf(-g)));
-  return round_bf16(g * r);
-}
+// silu_bf16 (qik_device.cuh): bf16(g / (1 + e^-g)), shared with the GEMM's SwiGLU epilogue.
 
 __global__ void __launch_bounds__(kThreads) swiglu_kernel(const uint16_t* __restrict__ g, int64_t ld_g,
                                                           const uint16_t* __restrict__ p, int64_t ld_p,

@@ -20,6 +20,9 @@
 //   * warps 2-9: epilogue -- tcgen05.ld of the CTA's own accumulator rows, scale by
 //     sa*sb, optional bias and GELU-tanh, bf16/fp32 via swizzled staging and TMA
 //     stores, optional amax of the bf16 output for the next dynamic quantization;
+//     or (QIK_EPI_SWIGLU) silu(gate) * up of a CTA-pair tile whose leader loaded 128
+//     gate rows of the fused up-projection weight and whose peer the matching 128 up
+//     rows, so each tile's TMEM holds both operands of 128 output columns;
 //     or (QIK_EPI_SCATTER) fp32 rows stored from the staging buffer straight into the
 //     owner rank's receive slot in peer memory, each finished tile counted there.
 // The epilogue of tile i overlaps the MMAs of tile i+1.
@@ -104,6 +107,23 @@ __device__ __forceinline__ float gelu_tanh_f32(float x) {
   return x * r;
 }
 
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// v[j] += bias[j] for j < ncols (16 or 32), the bias row 16-byte aligned
+__device__ __forceinline__ void add_bias32(float (&v)[32], const __nv_bfloat16* bias, int ncols = 32) {
+  const uint4* bp = reinterpret_cast<const uint4*>(bias);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 bb = (q * 8 < ncols) ? __ldg(bp + q) : make_uint4(0u, 0u, 0u, 0u);
+    const uint32_t bw[4] = {bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      v[q * 8 + 2 * t] += __uint_as_float(bw[t] << 16);
+      v[q * 8 + 2 * t + 1] += __uint_as_float(bw[t] & 0xFFFF0000u);
+    }
+  }
+}
+
 template <int BN, int STAGES, bool TWO_SM>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -174,9 +194,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // TWO_SM: both CTAs' loads complete on the leader's full barrier, which alone
       // expects the bytes of the pair
       const uint32_t full_leader = TWO_SM ? mapa_shared(full, 0) : 0u;
+      // QIK_EPI_SWIGLU: the leader loads gate rows nb * 128 + [0, 128), the peer the up
+      // rows N / 2 + nb * 128 + [0, 128), so tile columns 0-127 are gate outputs and
+      // 128-255 the matching up outputs
+      const bool swiglu = TWO_SM && p.epilogue == QIK_EPI_SWIGLU;
       for (int tile = tile0; tile < tiles; tile += tile_step) {
         int mb, nb;
         tile_coords(tile, num_m, num_n, p.group_m, mb, nb);
+        const int brow = swiglu ? (rank ? p.N / 2 : 0) + nb * (BN / 2) : nb * BN + static_cast<int>(rank) * (BN / 2);
         for (int kb = 0; kb < num_k; ++kb) {
           if constexpr (TWO_SM) {
             if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, p.status)) goto producer_done;
@@ -184,8 +209,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t bar = full_leader + static_cast<uint32_t>(stage) * 8u;
             tma_load_2d_cg2(sA + stage * Lay::kABytes, &tmA, kb * kGemmBK,
                             mb * kTileM + static_cast<int>(rank) * kGemmBM, bar);
-            tma_load_2d_cg2(sB + stage * Lay::kBBytes, &tmB, kb * kGemmBK,
-                            nb * BN + static_cast<int>(rank) * (BN / 2), bar);
+            tma_load_2d_cg2(sB + stage * Lay::kBBytes, &tmB, kb * kGemmBK, brow, bar);
           } else {
             if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status)) goto producer_done;
             mbar_arrive_expect_tx(&full[stage], Lay::kStageBytes);
@@ -307,8 +331,69 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       }
+      // 32 rows x 32 bf16 output columns from registers: swizzled staging buffer -> one TMA store
+      auto store_bf16 = [&](const uint32_t (&w)[16], int col0) {
+        // the staging buffer is free once at most one store (the other buffer's) reads smem
+        if (lane == 0) bulk_wait_read_1();
+        __syncwarp();
+        uint8_t* sb = stage_out + buf * Lay::kOutBufBytes;
+        // 64-byte rows, 64-byte swizzle: 16-byte chunk q of row l at chunk q ^ ((l >> 1) & 3)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(sb + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) =
+              make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && row0 < p.M) {
+          tma_store_2d(&tmC, col0, row0, sb);
+          bulk_commit_group();
+        }
+        buf ^= 1;
+      };
+      int chunks = BN / 32;
+      if constexpr (TWO_SM && BN == 256) {
+        if (p.epilogue == QIK_EPI_SWIGLU) {
+          // tile columns c * 32 + [0, 32) (gate) and 128 + c * 32 + [0, 32) (up) give output
+          // columns nb * 128 + c * 32 + [0, 32); N % 256 == 0, so every chunk is whole
+          chunks = 0;
+          const int h = p.N >> 1;
 #pragma unroll 1
-      for (int c = half; c < BN / 32; c += 2) {
+          for (int c = half; c < 4; c += 2) {
+            uint32_t rg[32], ru[32];
+            const uint32_t ta = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                static_cast<uint32_t>(acc * Lay::kAccStride + c * 32);
+            tmem_ld32(ta, rg);
+            tmem_ld32(ta + 128, ru);
+            const int col0 = nb * 128 + c * 32;
+            float g[32], u[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              g[j] = __uint_as_float(rg[j]) * s;
+              u[j] = __uint_as_float(ru[j]) * s;
+            }
+            if (p.bias) {
+              add_bias32(g, p.bias + col0);
+              add_bias32(u, p.bias + h + col0);
+            }
+            uint32_t w[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float lo = silu_bf16(bf16_round(g[2 * j])) * bf16_round(u[2 * j]);
+              const float hi = silu_bf16(bf16_round(g[2 * j + 1])) * bf16_round(u[2 * j + 1]);
+              w[j] = pack_bf16x2(lo, hi);
+            }
+            if (p.amax_out && row_ok) {
+              uint32_t m2 = 0;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) m2 = __vmaxu2(m2, w[j] & 0x7FFF7FFFu);
+              amax_local = max(amax_local, max(m2 & 0xFFFFu, m2 >> 16));
+            }
+            store_bf16(w, col0);
+          }
+        }
+      }
+#pragma unroll 1
+      for (int c = half; c < chunks; c += 2) {
         uint32_t r[32];
         tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                       static_cast<uint32_t>(acc * Lay::kAccStride + c * 32),
@@ -319,19 +404,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * s;
-        if (p.bias) {
-          const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col0);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint4 bb = (q * 8 < ncols) ? __ldg(bp + q) : make_uint4(0u, 0u, 0u, 0u);
-            const uint32_t bw[4] = {bb.x, bb.y, bb.z, bb.w};
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              v[q * 8 + 2 * t] += __uint_as_float(bw[t] << 16);
-              v[q * 8 + 2 * t + 1] += __uint_as_float(bw[t] & 0xFFFF0000u);
-            }
-          }
-        }
+        if (p.bias) add_bias32(v, p.bias + col0, ncols);
         if (p.out_f32) {
           // two 16-column blocks of 64-byte rows, 64-byte swizzle
 #pragma unroll
@@ -390,22 +463,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               if (2 * j < ncols) m2 = __vmaxu2(m2, w[j] & 0x7FFF7FFFu);
             amax_local = max(amax_local, max(m2 & 0xFFFFu, m2 >> 16));
           }
-          // the staging buffer is free once at most one store (the other buffer's) reads smem
-          if (lane == 0) bulk_wait_read_1();
-          __syncwarp();
-          uint8_t* sb = stage_out + buf * Lay::kOutBufBytes;
-          // 64-byte rows, 64-byte swizzle: 16-byte chunk q of row l at chunk q ^ ((l >> 1) & 3)
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4*>(sb + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) =
-                make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0 && row0 < p.M) {
-            tma_store_2d(&tmC, col0, row0, sb);
-            bulk_commit_group();
-          }
-          buf ^= 1;
+          store_bf16(w, col0);
         }
       }
       tc_fence_before();
@@ -498,7 +556,7 @@ static int launch_gemm(const uint8_t* A, const uint8_t* B, const GemmParams& p, 
   CUtensorMap tc;
   // the output [rows, cols]: the kernel's [M, N], or [N, M] in the transposed tiny-M
   // form (whose epilogue stores without the map)
-  const uint64_t c_cols = static_cast<uint64_t>(BN == 16 ? p.M : p.N);
+  const uint64_t c_cols = static_cast<uint64_t>(BN == 16 ? p.M : (p.epilogue == QIK_EPI_SWIGLU ? p.N / 2 : p.N));
   const uint64_t c_rows = static_cast<uint64_t>(BN == 16 ? p.N : p.M);
   if (p.out_f32)
     rc = make_tmap_2d(&tc, p.C, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, c_cols, c_rows, static_cast<uint64_t>(p.ldc) * 4, 16,
@@ -559,11 +617,16 @@ int launch_fp8_gemm_ex(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N,
               "qik_fp8_gemm: lda/ldb must be >= K and multiples of 16 bytes");
   QIK_REQUIRE(aligned16(A) && aligned16(B) && aligned16(C), "qik_fp8_gemm: A, B, C must be 16-byte aligned");
   QIK_REQUIRE(N % 16 == 0, "qik_fp8_gemm: N=%lld must be a multiple of 16", (long long)N);
-  QIK_REQUIRE(ldc >= N && ldc % 8 == 0, "qik_fp8_gemm: ldc must be >= N and a multiple of 8");
+  const bool swiglu = epilogue == QIK_EPI_SWIGLU;
+  const int64_t c_cols = swiglu ? N / 2 : N;
+  QIK_REQUIRE(ldc >= c_cols && ldc % 8 == 0, "qik_fp8_gemm: ldc must be >= the output width and a multiple of 8");
   QIK_REQUIRE(out_dtype == QIK_DTYPE_BF16 || out_dtype == QIK_DTYPE_F32, "qik_fp8_gemm: out_dtype must be BF16/F32");
   QIK_REQUIRE(epilogue == QIK_EPI_SCALE || epilogue == QIK_EPI_GELU_TANH ||
-                  (epilogue == QIK_EPI_SCATTER && scatter && out_dtype == QIK_DTYPE_F32 && !bias),
+                  (epilogue == QIK_EPI_SCATTER && scatter && out_dtype == QIK_DTYPE_F32 && !bias) ||
+                  (swiglu && !scatter),
               "qik_fp8_gemm: unknown epilogue");
+  QIK_REQUIRE(!swiglu || (N % 256 == 0 && out_dtype == QIK_DTYPE_BF16),
+              "qik_fp8_gemm: the SwiGLU epilogue needs N %% 256 == 0 (N=%lld) and BF16 output", (long long)N);
   QIK_REQUIRE(!(out_dtype == QIK_DTYPE_F32 && ((epilogue != QIK_EPI_SCALE && epilogue != QIK_EPI_SCATTER) || amax_out)),
               "qik_fp8_gemm: GELU and amax need BF16 output");
   QIK_REQUIRE(!bias || aligned16(bias), "qik_fp8_gemm: bias must be 16-byte aligned");
@@ -585,7 +648,11 @@ int launch_fp8_gemm_ex(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N,
   p.amax_out = amax_out;
   p.status = status;
   const int sel = tile_cfg & 0xFF;
-  const int cfg = sel == QIK_GEMM_TILE_AUTO ? gemm_pick_cfg(M, N, scatter != nullptr) : sel;
+  // SwiGLU: a CTA-pair tile holds the gate and the up columns of the same 128 outputs
+  const int cfg = swiglu ? QIK_GEMM_TILE_PAIR_256
+                         : (sel == QIK_GEMM_TILE_AUTO ? gemm_pick_cfg(M, N, scatter != nullptr) : sel);
+  QIK_REQUIRE(!swiglu || sel == QIK_GEMM_TILE_AUTO || sel == QIK_GEMM_TILE_PAIR_256,
+              "qik_fp8_gemm: the SwiGLU epilogue runs on CTA-pair tiles only (tile configuration %d)", sel);
   const int raster = (tile_cfg >> 8) & 0xFF;
   p.group_m = raster != 0 ? raster : gemm_pick_raster(N, K);
   switch (cfg) {

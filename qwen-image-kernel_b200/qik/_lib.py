@@ -16,7 +16,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libqik.so"
 
 QIK_OK = 0
 DTYPE_BF16, DTYPE_F32, DTYPE_E4M3 = 0, 1, 2
-EPI_SCALE, EPI_GELU_TANH, EPI_SCATTER = 0, 1, 2
+EPI_SCALE, EPI_GELU_TANH, EPI_SCATTER, EPI_SWIGLU = 0, 1, 2, 3
 GEMM_TILE_AUTO, GEMM_TILE_PAIR_256, GEMM_TILE_SINGLE_256, GEMM_TILE_SINGLE_128, GEMM_TILE_SINGLE_64, GEMM_TILE_SWAP_16 = range(6)
 TP_MAX_WORLD = 8
 ATTN_HAS_CACHE, ATTN_HAS_KEY_VALID, ATTN_UNIFORM, ATTN_V_FP8, ATTN_F16 = 1, 2, 4, 8, 16

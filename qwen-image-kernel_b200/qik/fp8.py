@@ -131,7 +131,9 @@ def fp8_gemm(xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: torch.Ten
     parity output.  ``amax_out`` (int32 [1], zeroed by the caller) receives the
     amax of the bf16 output for the next dynamic quantization.  ``tile_cfg`` forces a
     tile configuration (``qik._lib.GEMM_TILE_*``, for measurements and tests; the
-    result is the same)."""
+    result is the same).  ``epilogue=EPI_SWIGLU`` takes wq as the fused gate / up
+    weight (rows [0, N/2) gate, [N/2, N) up) and returns silu(gate) * up, [M, N/2]
+    bf16, the bytes fused_swiglu gives on the two halves of the plain GEMM's output."""
     lib = L.load()
     if xq.dtype != torch.float8_e4m3fn or wq.dtype != torch.float8_e4m3fn:
         raise TypeError("qik.fp8_gemm: operands must be float8_e4m3fn")
@@ -144,7 +146,7 @@ def fp8_gemm(xq: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: torch.Ten
     if K2 != K:
         raise ValueError(f"qik.fp8_gemm: K mismatch {K} vs {K2}")
     if out is None:
-        out = torch.empty(M, N, dtype=out_dtype, device=xq.device)
+        out = torch.empty(M, N // 2 if epilogue == L.EPI_SWIGLU else N, dtype=out_dtype, device=xq.device)
     if bias is not None:
         bias = bias.to(torch.bfloat16).contiguous()
     status = L.status_word(xq.device)
@@ -220,6 +222,21 @@ class FP8Linear(nn.Module):
             raise ValueError("FP8Linear.forward_e4m3: linears with in_features < 256 take bf16 input (forward)")
         out = fp8_gemm(xq.reshape(-1, self.in_features), scale, self.weight, self.weight_scale, self.bias)
         return out.reshape(*xq.shape[:-1], self.out_features)
+
+    def forward_swiglu_e4m3(self, xq: torch.Tensor, scale: torch.Tensor,
+                            amax_out: torch.Tensor | None = None) -> torch.Tensor:
+        """fused_swiglu(*forward_e4m3(xq, scale).chunk(2, -1)) for the fused gate / up
+        linear of the MLP, in one GEMM whose epilogue applies the SwiGLU: returns bf16
+        [..., out_features / 2].  ``amax_out`` (int32 [1], zeroed) receives the amax of
+        the result, as fused_swiglu's does.  Needs out_features % 256 == 0."""
+        if xq.dtype != torch.float8_e4m3fn or xq.shape[-1] != self.in_features:
+            raise ValueError(f"FP8Linear.forward_swiglu_e4m3: expected float8_e4m3fn [..., {self.in_features}], "
+                             f"got {xq.dtype} {tuple(xq.shape)}")
+        if self.in_features < 256 or self.out_features % 256:
+            raise ValueError("FP8Linear.forward_swiglu_e4m3: needs in_features >= 256 and out_features % 256 == 0")
+        out = fp8_gemm(xq.reshape(-1, self.in_features), scale, self.weight, self.weight_scale, self.bias,
+                       epilogue=L.EPI_SWIGLU, amax_out=amax_out)
+        return out.reshape(*xq.shape[:-1], self.out_features // 2)
 
     def forward_fp32(self, x: torch.Tensor) -> torch.Tensor:
         """Same computation with the fp32 GEMM output before the bf16 cast (parity mode)."""

@@ -20,9 +20,11 @@ Where the data layout allows, tensors stay in place instead of being copied: q /
 v are strided views of the fused QKV output, gate / up the two halves of the fused
 up projection, and the slab store reads the key / value views directly.  A layer norm
 whose only consumers are FP8 linears emits their e4m3 input and scale itself
-(``fused_layer_norm_modulate_e4m3``: the bf16 output is never written); SwiGLU and the
-attention reduce the amax of their output, which the next FP8 linear uses instead of
-its own amax pass (same bytes and scale).
+(``fused_layer_norm_modulate_e4m3``: the bf16 output is never written); the fused
+up projection then applies the SwiGLU in its GEMM epilogue (``_swiglu_linear``: the
+gate / up output is never written either).  SwiGLU and the attention reduce the amax
+of their output, which the next FP8 linear uses instead of its own amax pass (same
+bytes and scale).
 """
 from __future__ import annotations
 
@@ -53,6 +55,13 @@ def _linear(mod, x: torch.Tensor, amax: torch.Tensor | None, scale: torch.Tensor
     if amax is not None and isinstance(mod, FP8Linear):
         return mod.forward_from_amax(x, amax)
     return mod(x)
+
+
+def _swiglu_linear(mod: FP8Linear, xq: torch.Tensor, scale: torch.Tensor, amax_out: torch.Tensor) -> torch.Tensor:
+    """fused_swiglu(*mod(x).chunk(2, -1)) for the fused gate / up FP8 linear ``mod`` handed
+    its e4m3 input ``xq`` with scale ``scale``: one GEMM with the SwiGLU in its epilogue
+    (the gate / up output is never written); ``amax_out`` receives the result's amax."""
+    return mod.forward_swiglu_e4m3(xq, scale, amax_out=amax_out)
 
 
 def _takes_e4m3(*mods) -> bool:
@@ -208,13 +217,16 @@ class QwenImage21KernelBlock(torch.nn.Module):
             amax2 = _new_amax(hidden_states)
             img_mod2 = fused_layer_norm_modulate(hidden_states, modulation, 2 * inner, mod_stride, target_token_mask,
                                                  self._eps, amax_out=amax2)
-        if fused_up is not None:
-            gate, up = _linear(fused_up, img_mod2, amax2, scale2).chunk(2, dim=-1)
-        else:
-            gate = _linear(self.img_mlp.gate_layer, img_mod2, amax2, scale2)
-            up = _linear(self.img_mlp.proj, img_mod2, amax2, scale2)
         amax3 = _new_amax(hidden_states)
-        mlp_mid = fused_swiglu(gate, up, amax_out=amax3)
+        if fused_up is not None and scale2 is not None and fused_up.out_features % 256 == 0:
+            mlp_mid = _swiglu_linear(fused_up, img_mod2, scale2, amax3)
+        else:
+            if fused_up is not None:
+                gate, up = _linear(fused_up, img_mod2, amax2, scale2).chunk(2, dim=-1)
+            else:
+                gate = _linear(self.img_mlp.gate_layer, img_mod2, amax2, scale2)
+                up = _linear(self.img_mlp.proj, img_mod2, amax2, scale2)
+            mlp_mid = fused_swiglu(gate, up, amax_out=amax3)
         mlp_out = _linear(self.img_mlp.out, mlp_mid, amax3)
         return fused_gate_residual(hidden_states, mlp_out, modulation, 3 * inner, target_token_mask)
 

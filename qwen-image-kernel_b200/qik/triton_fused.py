@@ -5,12 +5,12 @@ Each function launches one qik CUDA kernel (``csrc/qik_fused.cu``) with the
 reference kernel's rounding points:
 
 * ``fused_rms_norm_rope`` -- per-head RMSNorm (fp32 weight multiply, one bf16
-  rounding) + complex RoPE (triton_fused.py:27-117).  Strided q / k views of the
+  rounding) + complex RoPE (triton_fused.py:28-105).  Strided q / k views of the
   fused QKV output are read in place; the reference copies them to contiguous.
 * ``fused_layer_norm_modulate`` -- LayerNorm (no affine) then ``* (1 + scale)`` with
-  the per-position modulation row map (triton_fused.py:75-160).
-* ``fused_gate_residual`` -- ``x + tanh(gate) * f`` (triton_fused.py:168-218).
-* ``fused_swiglu`` -- ``silu(gate) * up`` (triton_fused.py:227-262); the two halves of
+  the per-position modulation row map (triton_fused.py:111-177).
+* ``fused_gate_residual`` -- ``x + tanh(gate) * f`` (triton_fused.py:183-231).
+* ``fused_swiglu`` -- ``silu(gate) * up`` (triton_fused.py:237-263); the two halves of
   the fused up-projection output are read in place.
 
 ``fused_layer_norm_modulate`` and ``fused_swiglu`` take an optional ``amax_out``
@@ -53,7 +53,7 @@ def _u8_mask(target_token_mask: torch.Tensor | None, S: int, device: torch.devic
 def _modulation_row_map(target_token_mask: torch.Tensor | None, B: int, S: int,
                         device: torch.device) -> torch.Tensor:
     """Per-position modulation row offset: 0 = own sample's timestep row, B = the
-    t = 0 rows (triton_fused.py:128-139).  The kernels add the sample index."""
+    t = 0 rows (triton_fused.py:141-151).  The kernels add the sample index."""
     if target_token_mask is not None:
         return torch.where(target_token_mask.to(torch.bool),
                            torch.zeros(S, dtype=torch.int32, device=device),

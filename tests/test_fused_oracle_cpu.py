@@ -91,7 +91,7 @@ def test_swiglu_oracle_vs_stock():
 
 
 def test_modulation_rows_follow_row_map_plus_sample():
-    """Row map 0 / B (triton_fused.py:128-139) plus the sample index the kernels add."""
+    """Row map 0 / B (triton_fused.py:141-151) plus the sample index the kernels add."""
     mask = torch.tensor([True, False, True])
     rows = O.modulation_rows(mask, 2, 3)
     assert rows.tolist() == [[0, 2, 0], [1, 3, 1]]

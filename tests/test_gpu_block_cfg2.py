@@ -18,7 +18,10 @@ the oracle from the recorded inputs:
   (bit-exact with the product's quantizer, tested elsewhere) with the amax the
   product's producer handed over, or on the e4m3 input and scale it was handed;
 * the attention: max-abs <= 2e-2 and relF <= 5e-3 against the fp32 oracle on the q /
-  k / v the processor passed, all 48 (sample, head) pairs.
+  k / v the processor passed, all 48 (sample, head) pairs;
+* the fused up projection with the SwiGLU in its epilogue: bit-identical (values and
+  amax) to the plain GEMM's gate / up halves through the SwiGLU kernel, and at the
+  fused-op gate against the oracle's SwiGLU of the bf16-rounded fp32 dequant GEMM.
 
 The structure is the reference block's (processors.py:129-187): fused QKV 3072 -> 9216,
 out-projection 3072 -> 3072, SwiGLU MLP with its fused up projection at BASELINE's
@@ -83,13 +86,15 @@ def recorder(monkeypatch):
         def inner(*a, **kw):
             out = fn(*a, **kw)
             rec = {"name": name, "args": [cpu(x) for x in a], "kw": {k: cpu(v) for k, v in kw.items()}}
-            if name == "linear":
+            if name in ("linear", "swiglu_linear"):
                 rec["mod"] = a[0]
             torch.cuda.synchronize()
             rec["out"] = cpu(out)
             for k in ("amax_out",):
                 if isinstance(kw.get(k), torch.Tensor):
                     rec["kw"][k] = kw[k].detach().cpu()
+            if name == "swiglu_linear":
+                rec["kw"]["amax_out"] = a[3].detach().cpu()  # positional, filled by the call
             calls.append(rec)
             return out
         return inner
@@ -97,7 +102,8 @@ def recorder(monkeypatch):
     for name, attr in (("ln_mod", "fused_layer_norm_modulate"), ("ln_mod_e4m3", "fused_layer_norm_modulate_e4m3"),
                        ("rms_rope", "fused_rms_norm_rope"),
                        ("gate_res", "fused_gate_residual"), ("swiglu", "fused_swiglu"),
-                       ("attention", "block_causal_flash_attention"), ("linear", "_linear")):
+                       ("attention", "block_causal_flash_attention"), ("linear", "_linear"),
+                       ("swiglu_linear", "_swiglu_linear")):
         monkeypatch.setattr(PR, attr, wrap(name, getattr(PR, attr)))
     return calls
 
@@ -140,7 +146,7 @@ def test_dit_block_cfg2_full_size_stage_by_stage(recorder):
     torch.cuda.synchronize()
     names = [c["name"] for c in recorder]
     assert names == ["ln_mod_e4m3", "linear", "rms_rope", "rms_rope", "attention", "linear", "gate_res",
-                     "ln_mod_e4m3", "linear", "swiglu", "linear", "gate_res"], names
+                     "ln_mod_e4m3", "swiglu_linear", "linear", "gate_res"], names
     assert recorder[-1]["out"].shape == (B, S, K) and torch.equal(recorder[-1]["out"], out.cpu())
     torch.set_num_threads(max(1, torch.get_num_threads()))
     cos, sin = freqs.real.float().cpu(), freqs.imag.float().cpu()
@@ -166,6 +172,24 @@ def test_dit_block_cfg2_full_size_stage_by_stage(recorder):
         elif c["name"] == "swiglu":
             _fused_gate(o, O.swiglu(a[0], a[1]), tag)
             assert int(kw["amax_out"][0]) == _amax_bits_of(o), tag
+        elif c["name"] == "swiglu_linear":
+            # bit-identical to the plain GEMM's halves through the SwiGLU kernel, and
+            # within the linear + elementwise gates of the oracle's composition
+            from qik.fp8 import fp8_gemm
+            from qik.triton_fused import fused_swiglu
+            lin, xq, sx = c["mod"], a[1], a[2]
+            x2 = xq.reshape(-1, xq.shape[-1]).cuda()
+            gu = fp8_gemm(x2, sx.cuda(), lin.weight, lin.weight_scale, lin.bias)
+            am = torch.zeros(1, dtype=torch.int32, device="cuda")
+            ref = fused_swiglu(*gu.chunk(2, dim=-1), amax_out=am).cpu()
+            y = o.reshape(-1, o.shape[-1])
+            assert torch.equal(y, ref), tag
+            assert int(kw["amax_out"][0]) == int(am[0]) == _amax_bits_of(y), tag
+            q, s = x2.view(torch.uint8).cpu().numpy(), float(sx.item())
+            gu_ref = O.fp8_linear(q, s, lin.weight.cpu(), float(lin.weight_scale.item()),
+                                  None if lin.bias is None else lin.bias.cpu())
+            h = gu_ref.shape[-1] // 2
+            _fused_gate(y, O.swiglu(gu_ref[:, :h].to(torch.bfloat16), gu_ref[:, h:].to(torch.bfloat16)), tag)
         elif c["name"] == "linear":
             lin, xin, amax = c["mod"], a[1], a[2]
             x2 = xin.reshape(-1, xin.shape[-1]).contiguous()

@@ -104,6 +104,42 @@ def test_gemm_swapped_tiny_m_rejects_larger_m(fp8):
         fp8.fp8_gemm(a, _one(), b, _one(), tile_cfg=L.GEMM_TILE_SWAP_16)
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 256, 128), (300, 512, 256), (513, 12288, 3072), (4352, 24576, 3072)])
+def test_gemm_swiglu_epilogue_matches_gemm_then_swiglu(fp8, M, N, K):
+    """QIK_EPI_SWIGLU (the fused gate / up projection with silu(gate) * up applied in the
+    epilogue, the gate / up output never written) is bit-identical, values and amax, to
+    the plain GEMM on the same CTA-pair tiles followed by the SwiGLU kernel on its two
+    halves; with and without bias, ragged M (a partial last 256-row tile)."""
+    from qik import _lib as L
+    from qik.triton_fused import fused_swiglu
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    wq, sw = fp8.quantize_weight_tensorwise(torch.randn(N, K, device="cuda", generator=g) * 0.02)
+    xq, sx = fp8.quantize_tensorwise(torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16))
+    bias = (torch.randn(N, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+    for b in (None, bias):
+        gu = fp8.fp8_gemm(xq, sx, wq, sw, b, tile_cfg=L.GEMM_TILE_PAIR_256)
+        am_ref, am = (torch.zeros(1, dtype=torch.int32, device="cuda") for _ in range(2))
+        ref = fused_swiglu(*gu.chunk(2, dim=-1), amax_out=am_ref)
+        y = fp8.fp8_gemm(xq, sx, wq, sw, b, epilogue=L.EPI_SWIGLU, amax_out=am)
+        torch.cuda.synchronize()
+        assert y.shape == (M, N // 2)
+        assert torch.equal(y, ref), b is None
+        assert int(am.item()) == int(am_ref.item()) == int(y.float().abs().max().view(torch.int32).item())
+
+
+def test_gemm_swiglu_epilogue_rejects(fp8):
+    from qik import _lib as L
+    a = torch.zeros(64, 128, dtype=torch.float8_e4m3fn, device="cuda")
+    b = torch.zeros(384, 128, dtype=torch.float8_e4m3fn, device="cuda")
+    with pytest.raises(L.QikError, match="N % 256 == 0"):
+        fp8.fp8_gemm(a, _one(), b, _one(), epilogue=L.EPI_SWIGLU)
+    b = torch.zeros(512, 128, dtype=torch.float8_e4m3fn, device="cuda")
+    with pytest.raises(L.QikError, match="CTA-pair tiles only"):
+        fp8.fp8_gemm(a, _one(), b, _one(), epilogue=L.EPI_SWIGLU, tile_cfg=L.GEMM_TILE_SINGLE_128)
+    with pytest.raises(L.QikError, match="BF16 output"):
+        fp8.fp8_gemm(a, _one(), b, _one(), epilogue=L.EPI_SWIGLU, out_dtype=torch.float32)
+
+
 @pytest.mark.parametrize("cfg", [1, 3])
 @pytest.mark.parametrize("raster", [1, 3, 16, 255])
 def test_gemm_raster_groups_exact(fp8, cfg, raster):
