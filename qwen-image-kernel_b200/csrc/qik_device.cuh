@@ -668,13 +668,21 @@ __device__ __forceinline__ bool grid_max_publish_wait(QuantWs* ws, uint32_t m) {
 }
 // One full warp, after its CTA passed grid_max_publish_wait: the max over every CTA's
 // slot (kQuantAbortMark when any CTA gave up), in every lane.
+// All of a lane's slot loads are issued before the first is used, so the collect costs
+// one L2 round trip rather than one per 32 slots.
 __device__ __forceinline__ uint32_t grid_max_collect(const QuantWs* ws) {
-  uint32_t g = 0;
-  for (uint32_t i = threadIdx.x & 31u; i < gridDim.x; i += 32) {
-    uint32_t v;
-    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(&ws->partial[i]) : "memory");
-    g = max(g, v);
+  constexpr int kPerLane = (kQuantMaxCtas + 31) / 32;
+  const uint32_t lane = threadIdx.x & 31u;
+  uint32_t v[kPerLane];
+#pragma unroll
+  for (int k = 0; k < kPerLane; ++k) {
+    const uint32_t i = lane + 32u * static_cast<uint32_t>(k);
+    v[k] = 0u;
+    if (i < gridDim.x) asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v[k]) : "l"(&ws->partial[i]) : "memory");
   }
+  uint32_t g = 0;
+#pragma unroll
+  for (int k = 0; k < kPerLane; ++k) g = max(g, v[k]);
   return __reduce_max_sync(0xffffffffu, g);
 }
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {

@@ -284,16 +284,18 @@ __global__ void __launch_bounds__(kQfThreads, 1) quant_act_single_pass_kernel(co
   // shared memory first, so its loads overlap the bulk copies in flight
   uint32_t m2 = 0;
   if (has_rem) {
+    // 16 loads of 16 B in flight per thread (128 KB per CTA) keep HBM busy once the
+    // bulk copies have landed
     const uint64_t pol_keep = l2_evict_last_policy();
-    for (int64_t base = nkeep; base < cnt; base += 8 * kQfThreads) {
-      uint4 r[8];
+    for (int64_t base = nkeep; base < cnt; base += 16 * kQfThreads) {
+      uint4 r[16];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < 16; ++k) {
         const int64_t i = base + k * kQfThreads + threadIdx.x;
         r[k] = i < cnt ? ld_nc_hint(xv + i, pol_keep) : make_uint4(0u, 0u, 0u, 0u);
       }
 #pragma unroll
-      for (int k = 0; k < 8; ++k) m2 = absmax8(m2, r[k]);
+      for (int k = 0; k < 16; ++k) m2 = absmax8(m2, r[k]);
     }
   }
   bool ok = true;
