@@ -129,6 +129,8 @@ int qik_quantize_weight(const void* w, int dtype, int64_t n, uint8_t* q, float* 
                                 up, as fused_swiglu's chunk(2) splits them): C[:, j] =
                                 bf16(bf16(silu(g_j)) * u_j), g_j, u_j the bf16 outputs of B rows j
                                 and N/2 + j (+ bias); C has N / 2 columns; N % 256 == 0, BF16 */
+#define QIK_EPI_RMS_ROPE 4   /* the fused QKV linear with per-head RMSNorm + RoPE of q and k
+                                (qik_fp8_gemm_qkv_rms_rope only) */
 
 /*
  * FP8 GEMM on tcgen05: C[M,N] = epilogue(A[M,K] . B[N,K]^T), e4m3 x e4m3 with
@@ -173,6 +175,21 @@ int qik_fp8_gemm_tiled(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N,
                        int64_t ldb, const float* scale_a, const float* scale_b, const void* bias, void* C,
                        int64_t ldc, int out_dtype, int epilogue, uint32_t* amax_out, int tile_cfg, int* status,
                        void* stream);
+
+/*
+ * The fused QKV linear followed by the per-head RMSNorm + RoPE of its q and k heads, in
+ * one GEMM: replaces fused_qkv(hidden_states) and the two fused_rms_norm_rope calls of
+ * QwenImage21AttnProcessor.__call__ (qwen_image_kernel/processors.py:64-79).  B is the
+ * fused weight [3 heads head_dim, K] (q rows, then k, then v), C bf16 [M, 3 heads
+ * head_dim] with row pitch ldc: the q and k columns hold rms_norm_rope(bf16 GEMM output)
+ * exactly as qik_rms_norm_rope computes it on that output (w_q / w_k fp32 [head_dim],
+ * rope_cos / rope_sin fp32 [seq, head_dim / 2] at position row % seq, eps), the v
+ * columns the bf16 GEMM output.  head_dim == 128, M % seq == 0; runs on CTA-pair tiles.
+ */
+int qik_fp8_gemm_qkv_rms_rope(const uint8_t* A, const uint8_t* B, int64_t M, int64_t K, int64_t lda, int64_t ldb,
+                              const float* scale_a, const float* scale_b, const void* bias, void* C, int64_t ldc,
+                              int heads, int head_dim, const float* w_q, const float* w_k, const float* rope_cos,
+                              const float* rope_sin, int64_t seq, float eps, int* status, void* stream);
 
 /*
  * Bytes of workspace qik_fp8_ffn needs for an [M, K] input and a hidden width.

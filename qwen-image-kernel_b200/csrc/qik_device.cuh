@@ -538,6 +538,37 @@ __device__ __forceinline__ float f2_sum(uint64_t v) {
   f2_unpack(v, lo, hi);
   return lo + hi;
 }
+// Per-head RMSNorm + RoPE arithmetic (rms_rope_kernel, triton_fused.py:28-69), shared by
+// the RMSNorm + RoPE kernel and the fused QKV GEMM's epilogue so both give the same
+// bytes.  A head of D elements is summed in groups of 8: each group's squares by
+// rms_ss8 (even and odd elements in two fp32 fma chains, then added), the D / 8 group
+// sums by an xor butterfly over groups (rms_ss_tree16 restates it for D = 128).
+__device__ __forceinline__ float rms_ss8(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
+  uint64_t ss2 = 0ull;
+  ss2 = ffma2(bf2_to_f2(w0), bf2_to_f2(w0), ss2);
+  ss2 = ffma2(bf2_to_f2(w1), bf2_to_f2(w1), ss2);
+  ss2 = ffma2(bf2_to_f2(w2), bf2_to_f2(w2), ss2);
+  ss2 = ffma2(bf2_to_f2(w3), bf2_to_f2(w3), ss2);
+  return f2_sum(ss2);
+}
+// The value every lane holds after `ss += shfl_xor(ss, o)` for o = 8, 4, 2, 1 over 16
+// group sums (fp32 addition is commutative, so lanes i and i ^ o add the same pair).
+__device__ __forceinline__ float rms_ss_tree16(const float (&g)[16]) {
+  float a[8], b[4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a[i] = g[i] + g[i + 8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) b[i] = a[i] + a[i + 4];
+  return (b[0] + b[2]) + (b[1] + b[3]);
+}
+__device__ __forceinline__ float rms_rstd(float ss, int d, float eps) { return rsqrtf(ss / static_cast<float>(d) + eps); }
+// One (even, odd) pair: bf16(x * rstd * w) in fp32 with one rounding, then the rotation
+// (e + i o)(c + i s) = e (c, s) + o (-s, c) in fp32, rounded to bf16.
+__device__ __forceinline__ uint32_t rms_rope_pair(uint32_t xw, uint64_t rr2, uint64_t w2, uint64_t cs2, uint64_t sc2) {
+  const uint32_t nb = f2_to_bf2(fmul2(fmul2(bf2_to_f2(xw), rr2), w2));
+  const float ne = __uint_as_float(nb << 16), no = __uint_as_float(nb & 0xFFFF0000u);
+  return f2_to_bf2(ffma2(f2_pack(ne, ne), cs2, fmul2(f2_pack(no, no), sc2)));
+}
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));

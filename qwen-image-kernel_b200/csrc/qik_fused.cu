@@ -456,23 +456,16 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         const int h = h0 + sub;
         const bool live = h < H;
         const uint4 v = live ? xt[h * G + gl] : make_uint4(0u, 0u, 0u, 0u);
-        const uint64_t x2[4] = {bf2_to_f2(v.x), bf2_to_f2(v.y), bf2_to_f2(v.z), bf2_to_f2(v.w)};
-        uint64_t ss2 = 0ull;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) ss2 = ffma2(x2[k], x2[k], ss2);
-        float ss = f2_sum(ss2);
+        float ss = rms_ss8(v.x, v.y, v.z, v.w);
 #pragma unroll
         for (int o = G / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float rrms = rsqrtf(ss / static_cast<float>(D) + eps);
+        const float rrms = rms_rstd(ss, D, eps);
         const uint64_t rr2 = f2_pack(rrms, rrms);
-        uint32_t o4[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          // fp32 norm and weight, one rounding to bf16, the rotation in fp32
-          const uint32_t nb = f2_to_bf2(fmul2(fmul2(x2[k], rr2), w2[k]));
-          const float ne = bf_lo(nb), no = bf_hi(nb);
-          o4[k] = f2_to_bf2(ffma2(f2_pack(ne, ne), cs2[k], fmul2(f2_pack(no, no), sc2[k])));
-        }
+        // fp32 norm and weight, one rounding to bf16, the rotation in fp32
+        const uint32_t o4[4] = {rms_rope_pair(v.x, rr2, w2[0], cs2[0], sc2[0]),
+                                rms_rope_pair(v.y, rr2, w2[1], cs2[1], sc2[1]),
+                                rms_rope_pair(v.z, rr2, w2[2], cs2[2], sc2[2]),
+                                rms_rope_pair(v.w, rr2, w2[3], cs2[3], sc2[3])};
         if (live) *reinterpret_cast<uint4*>(ot + h * o_sh + gl * 8) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
       }
     }

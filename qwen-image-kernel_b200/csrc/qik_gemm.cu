@@ -23,6 +23,10 @@
 //     or (QIK_EPI_SWIGLU) silu(gate) * up of a CTA-pair tile whose leader loaded 128
 //     gate rows of the fused up-projection weight and whose peer the matching 128 up
 //     rows, so each tile's TMEM holds both operands of 128 output columns;
+//     or (QIK_EPI_RMS_ROPE, the fused QKV linear) the per-head RMSNorm + RoPE of the q
+//     and k heads, one head per warp: the squares of the bf16 outputs summed in the
+//     RMSNorm + RoPE kernel's order, then the accumulator read again and normalised,
+//     rotated and stored (bit-identical to GEMM -> qik_rms_norm_rope);
 //     or (QIK_EPI_SCATTER) fp32 rows stored from the staging buffer straight into the
 //     owner rank's receive slot in peer memory, each finished tile counted there.
 // The epilogue of tile i overlaps the MMAs of tile i+1.
@@ -58,6 +62,16 @@ struct GemmParams {
   uint32_t* scat_cnt[QIK_TP_MAX_WORLD];
   int scat_rows;
   int group_m;  // raster: row tiles per group (1 = row-major), see tile_coords
+  // QIK_EPI_RMS_ROPE (the fused QKV linear): columns [0, rms_cols) are the q heads then
+  // the k heads, 128 columns each, normalised with rms_w[0] (the first rms_cols / 2
+  // columns) or rms_w[1] and rotated by rope_cos / rope_sin [rope_seq, 64] at position
+  // row % rope_seq; the columns after them (v) as QIK_EPI_SCALE
+  const float* rms_w[2];
+  const float* rope_cos;
+  const float* rope_sin;
+  int rope_seq;
+  int rms_cols;
+  float rms_eps;
 };
 
 // Output tile `tile` of the raster: groups of group_m row tiles, each group walked
@@ -352,6 +366,81 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       };
       int chunks = BN / 32;
       if constexpr (TWO_SM && BN == 256) {
+        if (p.epilogue == QIK_EPI_RMS_ROPE && nb * 256 < p.rms_cols) {
+          // a q or k tile: warp half h takes head h (tile columns 128 h + [0, 128)) whole,
+          // so each thread holds its row of the head; pass 1 sums the squares of the bf16
+          // outputs in groups of 8 as the RMSNorm + RoPE kernel's lanes do, pass 2 reloads
+          // the accumulator, normalises, rotates and stores
+          chunks = 0;
+          const int hc0 = nb * 256 + half * 128;
+          const float* wv = p.rms_w[hc0 >= (p.rms_cols >> 1) ? 1 : 0];
+          const uint32_t ta = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                              static_cast<uint32_t>(acc * Lay::kAccStride + half * 128);
+          const int srow = (row0 + lane) % p.rope_seq;
+          const float4* cs_row = reinterpret_cast<const float4*>(p.rope_cos + static_cast<int64_t>(srow) * 64);
+          const float4* sn_row = reinterpret_cast<const float4*>(p.rope_sin + static_cast<int64_t>(srow) * 64);
+          // each chunk's 16 cos / sin pairs of this row are loaded one chunk ahead (the
+          // first before pass 1), so their L2 latency overlaps the previous chunk's work
+          float4 c_nx[4], s_nx[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            c_nx[q] = __ldg(cs_row + q);
+            s_nx[q] = __ldg(sn_row + q);
+          }
+          auto chunk_words = [&](int j, uint32_t (&w)[16]) {
+            uint32_t r[32];
+            tmem_ld32(ta + static_cast<uint32_t>(j * 32), r);
+            float v[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]) * s;
+            if (p.bias) add_bias32(v, p.bias + hc0 + j * 32);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) w[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
+          };
+          float part[16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t w[16];
+            chunk_words(j, w);
+#pragma unroll
+            for (int gi = 0; gi < 4; ++gi)
+              part[4 * j + gi] = rms_ss8(w[4 * gi], w[4 * gi + 1], w[4 * gi + 2], w[4 * gi + 3]);
+          }
+          const float rrms = rms_rstd(rms_ss_tree16(part), 128, p.rms_eps);
+          const uint64_t rr2 = f2_pack(rrms, rrms);
+#pragma unroll 1
+          for (int j = 0; j < 4; ++j) {
+            float4 c_cur[4], s_cur[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              c_cur[q] = c_nx[q];
+              s_cur[q] = s_nx[q];
+            }
+            if (j < 3) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                c_nx[q] = __ldg(cs_row + (j + 1) * 4 + q);
+                s_nx[q] = __ldg(sn_row + (j + 1) * 4 + q);
+              }
+            }
+            uint32_t w[16];
+            chunk_words(j, w);
+            const float4* wp = reinterpret_cast<const float4*>(wv + j * 32);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float4 wa = __ldg(wp + 2 * q), wb = __ldg(wp + 2 * q + 1);
+              const float4 c4 = c_cur[q], s4 = s_cur[q];
+              w[4 * q] = rms_rope_pair(w[4 * q], rr2, f2_pack(wa.x, wa.y), f2_pack(c4.x, s4.x), f2_pack(-s4.x, c4.x));
+              w[4 * q + 1] =
+                  rms_rope_pair(w[4 * q + 1], rr2, f2_pack(wa.z, wa.w), f2_pack(c4.y, s4.y), f2_pack(-s4.y, c4.y));
+              w[4 * q + 2] =
+                  rms_rope_pair(w[4 * q + 2], rr2, f2_pack(wb.x, wb.y), f2_pack(c4.z, s4.z), f2_pack(-s4.z, c4.z));
+              w[4 * q + 3] =
+                  rms_rope_pair(w[4 * q + 3], rr2, f2_pack(wb.z, wb.w), f2_pack(c4.w, s4.w), f2_pack(-s4.w, c4.w));
+            }
+            store_bf16(w, hc0 + j * 32);
+          }
+        }
         if (p.epilogue == QIK_EPI_SWIGLU) {
           // tile columns c * 32 + [0, 32) (gate) and 128 + c * 32 + [0, 32) (up) give output
           // columns nb * 128 + c * 32 + [0, 32); N % 256 == 0, so every chunk is whole
@@ -621,10 +710,12 @@ int launch_fp8_gemm_ex(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N,
   const int64_t c_cols = swiglu ? N / 2 : N;
   QIK_REQUIRE(ldc >= c_cols && ldc % 8 == 0, "qik_fp8_gemm: ldc must be >= the output width and a multiple of 8");
   QIK_REQUIRE(out_dtype == QIK_DTYPE_BF16 || out_dtype == QIK_DTYPE_F32, "qik_fp8_gemm: out_dtype must be BF16/F32");
+  const bool rms = epilogue == QIK_EPI_RMS_ROPE;
   QIK_REQUIRE(epilogue == QIK_EPI_SCALE || epilogue == QIK_EPI_GELU_TANH ||
                   (epilogue == QIK_EPI_SCATTER && scatter && out_dtype == QIK_DTYPE_F32 && !bias) ||
-                  (swiglu && !scatter),
-              "qik_fp8_gemm: unknown epilogue");
+                  (swiglu && !scatter) ||
+                  (rms && scatter && scatter->rms_cols > 0 && out_dtype == QIK_DTYPE_BF16 && !amax_out),
+              "qik_fp8_gemm: unknown epilogue (QIK_EPI_RMS_ROPE only through qik_fp8_gemm_qkv_rms_rope)");
   QIK_REQUIRE(!swiglu || (N % 256 == 0 && out_dtype == QIK_DTYPE_BF16),
               "qik_fp8_gemm: the SwiGLU epilogue needs N %% 256 == 0 (N=%lld) and BF16 output", (long long)N);
   QIK_REQUIRE(!(out_dtype == QIK_DTYPE_F32 && ((epilogue != QIK_EPI_SCALE && epilogue != QIK_EPI_SCATTER) || amax_out)),
@@ -649,8 +740,8 @@ int launch_fp8_gemm_ex(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N,
   p.status = status;
   const int sel = tile_cfg & 0xFF;
   // SwiGLU: a CTA-pair tile holds the gate and the up columns of the same 128 outputs
-  const int cfg = swiglu ? QIK_GEMM_TILE_PAIR_256
-                         : (sel == QIK_GEMM_TILE_AUTO ? gemm_pick_cfg(M, N, scatter != nullptr) : sel);
+  const int cfg = (swiglu || rms) ? QIK_GEMM_TILE_PAIR_256
+                                  : (sel == QIK_GEMM_TILE_AUTO ? gemm_pick_cfg(M, N, scatter != nullptr) : sel);
   QIK_REQUIRE(!swiglu || sel == QIK_GEMM_TILE_AUTO || sel == QIK_GEMM_TILE_PAIR_256,
               "qik_fp8_gemm: the SwiGLU epilogue runs on CTA-pair tiles only (tile configuration %d)", sel);
   const int raster = (tile_cfg >> 8) & 0xFF;
@@ -736,6 +827,33 @@ extern "C" int qik_fp8_gemm_scatter(const uint8_t* A, const uint8_t* B, int64_t 
   extra.scat_rows = static_cast<int>(rows_per_owner);
   return launch_fp8_gemm_ex(A, B, M, N, K, lda, ldb, scale_a, scale_b, nullptr, dst[0], N, QIK_DTYPE_F32,
                             QIK_EPI_SCATTER, nullptr, status, static_cast<cudaStream_t>(stream), false, &extra);
+}
+
+extern "C" int qik_fp8_gemm_qkv_rms_rope(const uint8_t* A, const uint8_t* B, int64_t M, int64_t K, int64_t lda,
+                                         int64_t ldb, const float* scale_a, const float* scale_b, const void* bias,
+                                         void* C, int64_t ldc, int heads, int head_dim, const float* w_q,
+                                         const float* w_k, const float* rope_cos, const float* rope_sin, int64_t seq,
+                                         float eps, int* status, void* stream) {
+  using namespace qik;
+  QIK_REQUIRE(head_dim == 128, "qik_fp8_gemm_qkv_rms_rope: head_dim must be 128, got %d", head_dim);
+  QIK_REQUIRE(heads >= 1 && heads <= 4096, "qik_fp8_gemm_qkv_rms_rope: heads %d out of range", heads);
+  QIK_REQUIRE(w_q && w_k && rope_cos && rope_sin, "qik_fp8_gemm_qkv_rms_rope: NULL norm weight / rotary table");
+  QIK_REQUIRE(aligned16(w_q) && aligned16(w_k) && aligned16(rope_cos) && aligned16(rope_sin),
+              "qik_fp8_gemm_qkv_rms_rope: norm weights and rotary tables must be 16-byte aligned");
+  QIK_REQUIRE(seq >= 1 && seq <= (1ll << 31) - 1 && M % seq == 0,
+              "qik_fp8_gemm_qkv_rms_rope: M=%lld must be a multiple of seq=%lld", (long long)M, (long long)seq);
+  GemmParams extra;
+  memset(&extra, 0, sizeof(extra));
+  extra.rms_w[0] = w_q;
+  extra.rms_w[1] = w_k;
+  extra.rope_cos = rope_cos;
+  extra.rope_sin = rope_sin;
+  extra.rope_seq = static_cast<int>(seq);
+  extra.rms_cols = 2 * heads * head_dim;
+  extra.rms_eps = eps;
+  const int64_t N = 3ll * heads * head_dim;
+  return launch_fp8_gemm_ex(A, B, M, N, K, lda, ldb, scale_a, scale_b, bias, C, ldc, QIK_DTYPE_BF16, QIK_EPI_RMS_ROPE,
+                            nullptr, status, static_cast<cudaStream_t>(stream), false, &extra, QIK_GEMM_TILE_PAIR_256);
 }
 
 extern "C" int qik_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda,

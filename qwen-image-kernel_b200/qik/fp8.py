@@ -238,6 +238,39 @@ class FP8Linear(nn.Module):
                        epilogue=L.EPI_SWIGLU, amax_out=amax_out)
         return out.reshape(*xq.shape[:-1], self.out_features // 2)
 
+    def forward_qkv_rms_rope_e4m3(self, xq: torch.Tensor, scale: torch.Tensor, heads: int, w_q: torch.Tensor,
+                                  w_k: torch.Tensor, freqs_cis: torch.Tensor | None, eps: float) -> torch.Tensor:
+        """The fused QKV linear (weight rows q, k, v of ``heads`` x 128 each) on its e4m3
+        input [B, S, in_features], with the per-head RMSNorm (fp32 weights ``w_q`` /
+        ``w_k``) + RoPE of the q and k heads applied in the GEMM epilogue: returns bf16
+        [B, S, 3 heads, 128] whose q / k heads equal fused_rms_norm_rope of
+        forward_e4m3's output bit for bit and whose v heads equal that output."""
+        from .triton_fused import _fp32_weight, rope_tables
+        if xq.dtype != torch.float8_e4m3fn or xq.dim() != 3 or xq.shape[-1] != self.in_features:
+            raise ValueError(f"FP8Linear.forward_qkv_rms_rope_e4m3: expected float8_e4m3fn [B, S, {self.in_features}]"
+                             f", got {xq.dtype} {tuple(xq.shape)}")
+        D = 128
+        if self.out_features != 3 * heads * D or self.in_features < 256:
+            raise ValueError(f"FP8Linear.forward_qkv_rms_rope_e4m3: out_features {self.out_features} is not "
+                             f"3 x {heads} heads x {D}")
+        B, S, K = xq.shape
+        x2 = xq.reshape(B * S, K)
+        if x2.stride(-1) != 1 or x2.stride(0) % 16:
+            x2 = x2.contiguous()
+        cos, sin = rope_tables(freqs_cis, S, D, xq.device)
+        wq, wk = _fp32_weight(w_q, xq.device), _fp32_weight(w_k, xq.device)
+        out = torch.empty(B * S, self.out_features, dtype=torch.bfloat16, device=xq.device)
+        lib = L.load()
+        bias = None if self.bias is None else self.bias.to(torch.bfloat16).contiguous()
+        with torch.cuda.device(xq.device):
+            L.check(lib.qik_fp8_gemm_qkv_rms_rope(x2.data_ptr(), self.weight.data_ptr(), B * S, K, x2.stride(0),
+                                                  self.weight.stride(0), scale.data_ptr(), self.weight_scale.data_ptr(),
+                                                  L.ptr(bias), out.data_ptr(), out.stride(0), heads, D, wq.data_ptr(),
+                                                  wk.data_ptr(), cos.data_ptr(), sin.data_ptr(), S, float(eps),
+                                                  L.status_word(xq.device).data_ptr(), L.stream_ptr()),
+                    "qik_fp8_gemm_qkv_rms_rope")
+        return out.view(B, S, 3 * heads, D)
+
     def forward_fp32(self, x: torch.Tensor) -> torch.Tensor:
         """Same computation with the fp32 GEMM output before the bf16 cast (parity mode)."""
         x2 = x.reshape(-1, x.shape[-1])

@@ -20,9 +20,10 @@ Where the data layout allows, tensors stay in place instead of being copied: q /
 v are strided views of the fused QKV output, gate / up the two halves of the fused
 up projection, and the slab store reads the key / value views directly.  A layer norm
 whose only consumers are FP8 linears emits their e4m3 input and scale itself
-(``fused_layer_norm_modulate_e4m3``: the bf16 output is never written); the fused
-up projection then applies the SwiGLU in its GEMM epilogue (``_swiglu_linear``: the
-gate / up output is never written either).  SwiGLU and the attention reduce the amax
+(``fused_layer_norm_modulate_e4m3``: the bf16 output is never written); the fused QKV
+linear then applies the q / k RMSNorm + RoPE in its GEMM epilogue (``_qkv_rms_rope``)
+and the fused up projection the SwiGLU (``_swiglu_linear``: the gate / up output is
+never written).  SwiGLU and the attention reduce the amax
 of their output, which the next FP8 linear uses instead of its own amax pass (same
 bytes and scale).
 """
@@ -64,6 +65,26 @@ def _swiglu_linear(mod: FP8Linear, xq: torch.Tensor, scale: torch.Tensor, amax_o
     return mod.forward_swiglu_e4m3(xq, scale, amax_out=amax_out)
 
 
+def _qkv_fuses_rms_rope(mod, attn, D: int, rotary_emb, S: int) -> bool:
+    """The fused QKV linear can apply the q / k RMSNorm + RoPE in its epilogue: an FP8
+    linear on the tensor-core path, heads of 128, both norms with fp32-convertible weights
+    and one eps, and a rotary table of the sequence's shape (or none)."""
+    nq, nk = getattr(attn, "norm_q", None), getattr(attn, "norm_k", None)
+    return (isinstance(mod, FP8Linear) and mod.in_features >= 256 and D == 128
+            and getattr(nq, "weight", None) is not None and getattr(nk, "weight", None) is not None
+            and nq.weight.numel() == D and nk.weight.numel() == D and nq.eps is not None and nq.eps == nk.eps
+            and (rotary_emb is None or tuple(rotary_emb.shape) == (S, D // 2)))
+
+
+def _qkv_rms_rope(mod: FP8Linear, xq: torch.Tensor, scale: torch.Tensor, heads: int, attn,
+                  rotary_emb) -> torch.Tensor:
+    """The fused QKV linear on its e4m3 input with the q / k RMSNorm + RoPE in the GEMM
+    epilogue: [B, S, 3 heads, 128] bf16, q and k heads equal to fused_rms_norm_rope of
+    the plain linear's output, v heads equal to that output."""
+    return mod.forward_qkv_rms_rope_e4m3(xq, scale, heads, attn.norm_q.weight, attn.norm_k.weight, rotary_emb,
+                                         attn.norm_q.eps)
+
+
 def _takes_e4m3(*mods) -> bool:
     """Every module is an FP8 linear on the tensor-core path (in_features >= 256), so a
     producer may hand them its output already quantized."""
@@ -101,19 +122,26 @@ class QwenImage21KernelProcessor:
         B, S, _ = hidden_states.shape
         H = attn.heads
         fused_qkv = getattr(attn, "fused_qkv", None)
+        normed = False
         if fused_qkv is not None:
             # one quantization + one GEMM for Q, K and V; the splits are views
             D = fused_qkv.out_features // (3 * H)
-            qkv = _linear(fused_qkv, hidden_states, hidden_states_amax, hidden_states_scale)
-            query, key, value = qkv.unflatten(-1, (3 * H, D)).chunk(3, dim=-2)
+            if hidden_states_scale is not None and _qkv_fuses_rms_rope(fused_qkv, attn, D, rotary_emb, S):
+                # the GEMM epilogue normalises and rotates q and k (same bytes)
+                qkv = _qkv_rms_rope(fused_qkv, hidden_states, hidden_states_scale, H, attn, rotary_emb)
+                normed = True
+            else:
+                qkv = _linear(fused_qkv, hidden_states, hidden_states_amax, hidden_states_scale).unflatten(-1, (3 * H, D))
+            query, key, value = qkv.chunk(3, dim=-2)
         else:
             D = attn.to_q.out_features // H
             query = _linear(attn.to_q, hidden_states, hidden_states_amax, hidden_states_scale).unflatten(-1, (H, D))
             key = _linear(attn.to_k, hidden_states, hidden_states_amax, hidden_states_scale).unflatten(-1, (H, D))
             value = _linear(attn.to_v, hidden_states, hidden_states_amax, hidden_states_scale).unflatten(-1, (H, D))
 
-        query = fused_rms_norm_rope(query, attn.norm_q.weight, rotary_emb, attn.norm_q.eps)
-        key = fused_rms_norm_rope(key, attn.norm_k.weight, rotary_emb, attn.norm_k.eps)
+        if not normed:
+            query = fused_rms_norm_rope(query, attn.norm_q.weight, rotary_emb, attn.norm_q.eps)
+            key = fused_rms_norm_rope(key, attn.norm_k.weight, rotary_emb, attn.norm_k.eps)
 
         if kv_cache_mode == "extract" and layer_cache is not None and cache_write_slice is not None:
             # the slab store copies (and quantizes V) on the stream: the views suffice

@@ -74,6 +74,27 @@ def _fp32_weight(weight: torch.Tensor, device: torch.device) -> torch.Tensor:
     return hit[1]
 
 
+def rope_tables(freqs_cis: torch.Tensor | None, S: int, D: int, device: torch.device) -> tuple:
+    """fp32 cos / sin tables [S, D/2] of the complex rotary frequencies (the identity
+    rotation for None), cached per frequency tensor."""
+    key = (S, D, device, None if freqs_cis is None else (freqs_cis.data_ptr(), freqs_cis._version, freqs_cis.device))
+    cached = _cos_sin_cache.get(key)
+    if cached is not None:
+        return cached[1], cached[2]
+    if freqs_cis is None:  # no rotary embedding: the identity rotation
+        cos = torch.ones(S, D // 2, dtype=torch.float32, device=device)
+        sin = torch.zeros(S, D // 2, dtype=torch.float32, device=device)
+    else:
+        if tuple(freqs_cis.shape) != (S, D // 2):
+            raise ValueError(f"freqs_cis has shape {tuple(freqs_cis.shape)}, expected ({S}, {D // 2})")
+        cos = freqs_cis.real.float().to(device).contiguous()
+        sin = freqs_cis.imag.float().to(device).contiguous()
+    if len(_cos_sin_cache) > 8:
+        _cos_sin_cache.clear()
+    _cos_sin_cache[key] = (freqs_cis, cos, sin)
+    return cos, sin
+
+
 def fused_rms_norm_rope(x: torch.Tensor, weight: torch.Tensor, freqs_cis: torch.Tensor, eps: float) -> torch.Tensor:
     """x: [B, S, H, D] bf16 (any strides with a unit D stride); weight: [D];
     freqs_cis: complex [S, D/2] (None: no rotation).  Returns a contiguous
@@ -82,23 +103,7 @@ def fused_rms_norm_rope(x: torch.Tensor, weight: torch.Tensor, freqs_cis: torch.
     B, S, H, D = x.shape
     if x.stride(-1) != 1 or any(s % 8 for s in x.stride()[:3]) or x.data_ptr() % 16:
         x = x.contiguous()
-    key = (S, D, x.device,
-           None if freqs_cis is None else (freqs_cis.data_ptr(), freqs_cis._version, freqs_cis.device))
-    cached = _cos_sin_cache.get(key)
-    if cached is None:
-        if freqs_cis is None:  # no rotary embedding: the identity rotation
-            cos = torch.ones(S, D // 2, dtype=torch.float32, device=x.device)
-            sin = torch.zeros(S, D // 2, dtype=torch.float32, device=x.device)
-        else:
-            if tuple(freqs_cis.shape) != (S, D // 2):
-                raise ValueError(f"freqs_cis has shape {tuple(freqs_cis.shape)}, expected ({S}, {D // 2})")
-            cos = freqs_cis.real.float().to(x.device).contiguous()
-            sin = freqs_cis.imag.float().to(x.device).contiguous()
-        if len(_cos_sin_cache) > 8:
-            _cos_sin_cache.clear()
-        _cos_sin_cache[key] = (freqs_cis, cos, sin)
-    else:
-        _, cos, sin = cached
+    cos, sin = rope_tables(freqs_cis, S, D, x.device)
     w = _fp32_weight(weight, x.device)
     out = torch.empty((B, S, H, D), dtype=torch.bfloat16, device=x.device)
     lib = L.load()

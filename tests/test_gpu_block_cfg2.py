@@ -7,7 +7,7 @@ Every kernel call the block makes is recorded (inputs and output) by wrapping th
 module-level functions qik.processors calls; each recorded stage is then recomputed by
 the oracle from the recorded inputs:
 
-* RMSNorm + RoPE, gated residual, SwiGLU: the fused-op gate of test_gpu_fused.py
+* gated residual (and RMSNorm + RoPE, SwiGLU where they run as kernels): the fused-op gate of test_gpu_fused.py
   (<= 0.5% of outputs differ, none by more than 2^-6 of the largest output, relF <=
   1e-3), and each amax output equal to the max |output|;
 * the two LayerNorm + modulate stages, which emit the next linear's e4m3 input: codes
@@ -19,6 +19,11 @@ the oracle from the recorded inputs:
   product's producer handed over, or on the e4m3 input and scale it was handed;
 * the attention: max-abs <= 2e-2 and relF <= 5e-3 against the fp32 oracle on the q /
   k / v the processor passed, all 48 (sample, head) pairs;
+* the fused QKV linear with the q / k RMSNorm + RoPE in its epilogue: bit-identical to
+  the plain GEMM followed by the RMSNorm + RoPE kernel; against the oracle's dequant GEMM
+  -> bf16 -> RMSNorm + RoPE, v within the linear gate, q and k within relF <= 5e-3 and
+  no error above 2^-6 of the largest output (a last-bit change of a GEMM output moves
+  its normalised value by up to two bf16 ulps);
 * the fused up projection with the SwiGLU in its epilogue: bit-identical (values and
   amax) to the plain GEMM's gate / up halves through the SwiGLU kernel, and at the
   fused-op gate against the oracle's SwiGLU of the bf16-rounded fp32 dequant GEMM.
@@ -86,8 +91,10 @@ def recorder(monkeypatch):
         def inner(*a, **kw):
             out = fn(*a, **kw)
             rec = {"name": name, "args": [cpu(x) for x in a], "kw": {k: cpu(v) for k, v in kw.items()}}
-            if name in ("linear", "swiglu_linear"):
+            if name in ("linear", "swiglu_linear", "qkv_rms_rope"):
                 rec["mod"] = a[0]
+            if name == "qkv_rms_rope":
+                rec["attn"] = a[4]
             torch.cuda.synchronize()
             rec["out"] = cpu(out)
             for k in ("amax_out",):
@@ -103,7 +110,7 @@ def recorder(monkeypatch):
                        ("rms_rope", "fused_rms_norm_rope"),
                        ("gate_res", "fused_gate_residual"), ("swiglu", "fused_swiglu"),
                        ("attention", "block_causal_flash_attention"), ("linear", "_linear"),
-                       ("swiglu_linear", "_swiglu_linear")):
+                       ("swiglu_linear", "_swiglu_linear"), ("qkv_rms_rope", "_qkv_rms_rope")):
         monkeypatch.setattr(PR, attr, wrap(name, getattr(PR, attr)))
     return calls
 
@@ -145,7 +152,7 @@ def test_dit_block_cfg2_full_size_stage_by_stage(recorder):
     out = block(x, mod, rotary_emb=freqs, segments=[(0, 256, True)])
     torch.cuda.synchronize()
     names = [c["name"] for c in recorder]
-    assert names == ["ln_mod_e4m3", "linear", "rms_rope", "rms_rope", "attention", "linear", "gate_res",
+    assert names == ["ln_mod_e4m3", "qkv_rms_rope", "attention", "linear", "gate_res",
                      "ln_mod_e4m3", "swiglu_linear", "linear", "gate_res"], names
     assert recorder[-1]["out"].shape == (B, S, K) and torch.equal(recorder[-1]["out"], out.cpu())
     torch.set_num_threads(max(1, torch.get_num_threads()))
@@ -172,6 +179,37 @@ def test_dit_block_cfg2_full_size_stage_by_stage(recorder):
         elif c["name"] == "swiglu":
             _fused_gate(o, O.swiglu(a[0], a[1]), tag)
             assert int(kw["amax_out"][0]) == _amax_bits_of(o), tag
+        elif c["name"] == "qkv_rms_rope":
+            # bit-identical to the plain GEMM + the RMSNorm + RoPE kernel on its q / k views,
+            # and within the linear gate of the oracle's linear -> bf16 -> RMSNorm + RoPE
+            from qik.fp8 import fp8_gemm
+            from qik.triton_fused import fused_rms_norm_rope
+            lin, xq, sx, heads, at = c["mod"], a[1], a[2], a[3], c["attn"]
+            Bq, Sq, Kq = xq.shape
+            x2 = xq.reshape(-1, Kq).cuda()
+            plain = fp8_gemm(x2, sx.cuda(), lin.weight, lin.weight_scale, lin.bias).view(Bq, Sq, 3 * heads, D)
+            pq, pk, pv = plain.chunk(3, dim=-2)
+            rq = fused_rms_norm_rope(pq, at.norm_q.weight, freqs, at.norm_q.eps).cpu()
+            rk = fused_rms_norm_rope(pk, at.norm_k.weight, freqs, at.norm_k.eps).cpu()
+            oq, ok_, ov = o.chunk(3, dim=-2)
+            assert torch.equal(oq, rq) and torch.equal(ok_, rk) and torch.equal(ov, pv.cpu()), tag
+            q8, s8 = x2.view(torch.uint8).cpu().numpy(), float(sx.item())
+            y = O.fp8_linear(q8, s8, lin.weight.cpu(), float(lin.weight_scale.item()),
+                             None if lin.bias is None else lin.bias.cpu()).to(torch.bfloat16).view(Bq, Sq, 3 * heads, D)
+            yq, yk, yv = y.chunk(3, dim=-2)
+            refs = (O.rms_norm_rope(yq, at.norm_q.weight.detach().cpu(), cos, sin, at.norm_q.eps),
+                    O.rms_norm_rope(yk, at.norm_k.weight.detach().cpu(), cos, sin, at.norm_k.eps), yv)
+            for part, (got, ref) in zip("qkv", zip((oq, ok_, ov), refs)):
+                gf, rf = got.float(), ref.float()
+                r = O.relf(gf, rf)
+                if part == "v":  # the linear's own output: the linear gate
+                    d = ((gf - rf).abs() - 0.5 * O.bf16_ulp(rf)).max().item()
+                    print(f"{tag} {part}: max-abs over half an ulp {d:.3e} relF {r:.3e}")
+                    assert d <= LIN_MAX_ABS and r <= LIN_RELF, (tag, part)
+                else:  # normalised heads (|out| up to ~5): errors relative to the largest output
+                    d = (gf - rf).abs().max().item() / rf.abs().max().item()
+                    print(f"{tag} {part}: max-abs / max|ref| {d:.3e} relF {r:.3e}")
+                    assert d <= 2.0 ** -6 and r <= LIN_RELF, (tag, part)
         elif c["name"] == "swiglu_linear":
             # bit-identical to the plain GEMM's halves through the SwiGLU kernel, and
             # within the linear + elementwise gates of the oracle's composition

@@ -127,6 +127,54 @@ def test_gemm_swiglu_epilogue_matches_gemm_then_swiglu(fp8, M, N, K):
         assert int(am.item()) == int(am_ref.item()) == int(y.float().abs().max().view(torch.int32).item())
 
 
+@pytest.mark.parametrize("B,S,H,rope", [(2, 4352, 24, True), (1, 300, 2, True), (3, 77, 3, True), (1, 256, 4, False)])
+def test_qkv_rms_rope_epilogue_matches_gemm_then_rms_rope(fp8, B, S, H, rope):
+    """qik_fp8_gemm_qkv_rms_rope (the fused QKV linear with the per-head RMSNorm + RoPE of
+    q and k in its epilogue) is bit-identical to the plain GEMM on the same CTA-pair tiles
+    followed by the RMSNorm + RoPE kernel on its q and k views, its v columns equal to the
+    GEMM's: the configs[2] shape, ragged M (a partial last 256-row tile), an odd head
+    count (a tile holding the last q head and the first k head, a partial last v tile),
+    and no rotary table (the identity rotation)."""
+    from qik import _lib as L
+    from qik.triton_fused import fused_rms_norm_rope
+    D, K = 128, 384 if H < 8 else 3072
+    g = torch.Generator(device="cuda").manual_seed(B * S + H)
+    lin = fp8.FP8Linear(K, 3 * H * D, bias=True).cuda()
+    wq8, sw = fp8.quantize_weight_tensorwise(torch.randn(3 * H * D, K, device="cuda", generator=g) * 0.05)
+    lin.weight.copy_(wq8)
+    lin.weight_scale.copy_(sw)
+    lin.bias.copy_((torch.randn(3 * H * D, device="cuda", generator=g) * 0.3).to(torch.bfloat16))
+    xq, sx = fp8.quantize_tensorwise(torch.randn(B * S, K, device="cuda", generator=g).to(torch.bfloat16))
+    xq = xq.view(B, S, K)
+    w_q = 1.0 + 0.2 * torch.randn(D, device="cuda", generator=g)
+    w_k = 1.0 + 0.2 * torch.randn(D, device="cuda", generator=g)
+    freqs = None
+    if rope:
+        inv = 1.0 / (10000 ** (torch.arange(0, D, 2, device="cuda").float() / D))
+        freqs = torch.polar(torch.ones(S, D // 2, device="cuda"),
+                            torch.outer(torch.arange(S, device="cuda").float(), inv))
+    out = lin.forward_qkv_rms_rope_e4m3(xq, sx, H, w_q, w_k, freqs, 1e-6)
+    plain = fp8.fp8_gemm(xq.view(B * S, K), sx, lin.weight, lin.weight_scale, lin.bias,
+                         tile_cfg=L.GEMM_TILE_PAIR_256).view(B, S, 3 * H, D)
+    q, k, v = plain.chunk(3, dim=-2)
+    ref_q = fused_rms_norm_rope(q, w_q, freqs, 1e-6)
+    ref_k = fused_rms_norm_rope(k, w_k, freqs, 1e-6)
+    torch.cuda.synchronize()
+    oq, ok, ov = out.chunk(3, dim=-2)
+    assert out.shape == (B, S, 3 * H, D)
+    assert torch.equal(oq, ref_q), "q"
+    assert torch.equal(ok, ref_k), "k"
+    assert torch.equal(ov, v), "v"
+
+
+def test_qkv_rms_rope_rejects(fp8):
+    lin = fp8.FP8Linear(256, 3 * 2 * 64).cuda()
+    xq = torch.zeros(1, 16, 256, dtype=torch.float8_e4m3fn, device="cuda")
+    w = torch.ones(128, device="cuda")
+    with pytest.raises(ValueError, match="heads"):
+        lin.forward_qkv_rms_rope_e4m3(xq, _one(), 2, w, w, None, 1e-6)
+
+
 def test_gemm_swiglu_epilogue_rejects(fp8):
     from qik import _lib as L
     a = torch.zeros(64, 128, dtype=torch.float8_e4m3fn, device="cuda")
