@@ -131,6 +131,8 @@ int qik_quantize_weight(const void* w, int dtype, int64_t n, uint8_t* q, float* 
                                 and N/2 + j (+ bias); C has N / 2 columns; N % 256 == 0, BF16 */
 #define QIK_EPI_RMS_ROPE 4   /* the fused QKV linear with per-head RMSNorm + RoPE of q and k
                                 (qik_fp8_gemm_qkv_rms_rope only) */
+#define QIK_EPI_GATE_RES 5   /* gated residual x + bf16(bf16(tanh(gate)) * y) of the bf16 output y
+                                (qik_fp8_gemm_gate_residual only) */
 
 /*
  * FP8 GEMM on tcgen05: C[M,N] = epilogue(A[M,K] . B[N,K]^T), e4m3 x e4m3 with
@@ -190,6 +192,32 @@ int qik_fp8_gemm_qkv_rms_rope(const uint8_t* A, const uint8_t* B, int64_t M, int
                               const float* scale_a, const float* scale_b, const void* bias, void* C, int64_t ldc,
                               int heads, int head_dim, const float* w_q, const float* w_k, const float* rope_cos,
                               const float* rope_sin, int64_t seq, float eps, int* status, void* stream);
+
+/*
+ * bf16(tanh(modulation[r, gate_off + c])) for r < mod_rows, c < D, as the gated residual
+ * computes it (qik_gate_residual): the table qik_fp8_gemm_gate_residual reads, [mod_rows,
+ * D] bf16 contiguous.  Part of the reference's fused_gate_residual
+ * (qwen_image_kernel/triton_fused.py:183-231).
+ */
+int qik_gate_table(const void* modulation, int64_t mod_rows, int64_t mod_stride, int64_t gate_off, int64_t D,
+                   void* table, void* stream);
+
+/*
+ * An FP8 linear followed by the DiT block's gated residual, in one GEMM: replaces
+ * attn.to_out[0](...) / img_mlp.out(...) and the fused_gate_residual call after it
+ * (qwen_image_kernel/processors.py:172-187, triton_fused.py:183-231).  C [M, N] bf16 =
+ * x + bf16(T[t] * y), y the bf16 linear output (qik_fp8_gemm with QIK_EPI_SCALE), x
+ * bf16 [M, N] (row pitch ldx), T the qik_gate_table output (row pitch ldt) and, for row
+ * b * seq + s, t = b when target_mask is NULL or target_mask[s] != 0, else batch + b (the
+ * table then has 2 batch rows).  The bytes equal qik_gate_residual on y, except where a
+ * product T * y lies below 2^-126 in magnitude (rounded once here, twice there).
+ * M == batch * seq; C must not alias x.
+ */
+int qik_fp8_gemm_gate_residual(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda,
+                               int64_t ldb, const float* scale_a, const float* scale_b, const void* bias,
+                               const void* x, int64_t ldx, const void* gate_table, int64_t ldt,
+                               const uint8_t* target_mask, int64_t batch, int64_t seq, void* C, int64_t ldc,
+                               int* status, void* stream);
 
 /*
  * Bytes of workspace qik_fp8_ffn needs for an [M, K] input and a hidden width.

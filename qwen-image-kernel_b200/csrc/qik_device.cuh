@@ -533,6 +533,14 @@ __device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
   asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
+// bf16x2 sum rounded once to nearest even: for bf16 operands this equals
+// bf16(fl32(a) + fl32(b)) (the fp32 sum is exact unless the exponents differ by more
+// than 16, and then the smaller operand is far below half a bf16 ulp of the result).
+__device__ __forceinline__ uint32_t add_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 __device__ __forceinline__ float f2_sum(uint64_t v) {
   float lo, hi;
   f2_unpack(v, lo, hi);

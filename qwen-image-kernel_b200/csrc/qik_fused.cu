@@ -793,6 +793,38 @@ int qik_layer_norm_modulate_e4m3(const void* x, int64_t B, int64_t S, int64_t D,
   return check_launch("ln_modulate_e4m3_kernel");
 }
 
+// bf16(tanh(gate)) of every modulation row, as gate_fill computes it: the table the
+// FP8 GEMM's gated-residual epilogue reads.
+__global__ void __launch_bounds__(kThreads) gate_table_kernel(const uint16_t* __restrict__ mod, int64_t mod_stride,
+                                                              int64_t gate_off, int64_t rows, int64_t D,
+                                                              uint16_t* __restrict__ table) {
+  const int64_t nv = D >> 3, total = rows * nv;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / nv, v = i - r * nv;
+    GateCache c;
+    gate_fill(c, r, mod, mod_stride, gate_off + v * 8);
+    *reinterpret_cast<uint4*>(table + r * D + v * 8) =
+        make_uint4(pack_bf16x2(c.t[0], c.t[1]), pack_bf16x2(c.t[2], c.t[3]), pack_bf16x2(c.t[4], c.t[5]),
+                   pack_bf16x2(c.t[6], c.t[7]));
+  }
+}
+
+int qik_gate_table(const void* modulation, int64_t mod_rows, int64_t mod_stride, int64_t gate_off, int64_t D,
+                   void* table, void* stream) {
+  QIK_REQUIRE(mod_rows >= 0 && D > 0, "qik_gate_table: bad sizes");
+  if (mod_rows == 0) return QIK_OK;
+  QIK_REQUIRE(modulation && table, "qik_gate_table: NULL pointer");
+  QIK_REQUIRE(D % 8 == 0 && aligned16(modulation) && aligned16(table),
+              "qik_gate_table: D must be a multiple of 8 and the pointers 16-byte aligned");
+  QIK_REQUIRE(aligned_elems(mod_stride) && aligned_elems(gate_off) && gate_off >= 0 && gate_off + D <= mod_stride,
+              "qik_gate_table: modulation stride/offset must be multiples of 8 with offset + D <= stride");
+  const int grid = grid_cap((mod_rows * (D / 8) + kThreads - 1) / kThreads, 1);
+  gate_table_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(modulation), mod_stride, gate_off, mod_rows, D, static_cast<uint16_t*>(table));
+  return check_launch("gate_table_kernel");
+}
+
 int qik_gate_residual(const void* x, const void* f, int64_t B, int64_t S, int64_t D, const void* modulation,
                       int64_t mod_rows, int64_t mod_stride, int64_t gate_off, const uint8_t* target_mask, void* out,
                       void* stream) {

@@ -72,6 +72,17 @@ struct GemmParams {
   int rope_seq;
   int rms_cols;
   float rms_eps;
+  // QIK_EPI_GATE_RES (the DiT block's gated residual): C = x + bf16(T[t] * f) with f the
+  // bf16 output, x = res_x [M, N] (row pitch res_ld), T the bf16(tanh(gate)) table (row
+  // pitch gate_ld) and t = b + (gate_mask && !gate_mask[s] ? gate_batch : 0) for row
+  // b * gate_seq + s
+  const uint16_t* res_x;
+  int64_t res_ld;
+  const uint16_t* gate_tab;
+  int64_t gate_ld;
+  const uint8_t* gate_mask;
+  int gate_seq;
+  int gate_batch;
 };
 
 // Output tile `tile` of the raster: groups of group_m row tiles, each group walked
@@ -315,6 +326,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tile_coords(tile, num_m, num_n, p.group_m, mb, nb);
       const int row0 = mb * kTileM + static_cast<int>(rank) * kGemmBM + quarter * 32;
       const bool row_ok = row0 + lane < p.M;
+
       if constexpr (BN == 16) {
         // transposed tiny-M form: kernel row r = output column (a weight row), kernel
         // column c = output row (an activation row); one warp per lane quarter stores
@@ -545,6 +557,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             w[j] = pack_bf16x2(lo, hi);
           }
+          if (p.epilogue == QIK_EPI_GATE_RES && row_ok) {
+            // x + bf16(T * f) in bf16x2 arithmetic: the products and sums of bf16 values,
+            // each rounded once, as the gated-residual kernel's fp32 arithmetic rounds them
+            const int grow = row0 + lane, b = grow / p.gate_seq, sq = grow - b * p.gate_seq;
+            const int t = b + ((p.gate_mask != nullptr && p.gate_mask[sq] == 0) ? p.gate_batch : 0);
+            const uint4* xp = reinterpret_cast<const uint4*>(p.res_x + static_cast<int64_t>(grow) * p.res_ld + col0);
+            const uint4* tp = reinterpret_cast<const uint4*>(p.gate_tab + static_cast<int64_t>(t) * p.gate_ld + col0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              if (q * 8 < ncols) {
+                const uint4 xv = __ldg(xp + q), tv = __ldg(tp + q);
+                w[4 * q] = add_bf16x2(xv.x, mul_bf16x2(tv.x, w[4 * q]));
+                w[4 * q + 1] = add_bf16x2(xv.y, mul_bf16x2(tv.y, w[4 * q + 1]));
+                w[4 * q + 2] = add_bf16x2(xv.z, mul_bf16x2(tv.z, w[4 * q + 2]));
+                w[4 * q + 3] = add_bf16x2(xv.w, mul_bf16x2(tv.w, w[4 * q + 3]));
+              }
+            }
+          }
           if (p.amax_out && row_ok) {
             uint32_t m2 = 0;
 #pragma unroll
@@ -711,11 +741,14 @@ int launch_fp8_gemm_ex(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N,
   QIK_REQUIRE(ldc >= c_cols && ldc % 8 == 0, "qik_fp8_gemm: ldc must be >= the output width and a multiple of 8");
   QIK_REQUIRE(out_dtype == QIK_DTYPE_BF16 || out_dtype == QIK_DTYPE_F32, "qik_fp8_gemm: out_dtype must be BF16/F32");
   const bool rms = epilogue == QIK_EPI_RMS_ROPE;
+  const bool gate = epilogue == QIK_EPI_GATE_RES;
   QIK_REQUIRE(epilogue == QIK_EPI_SCALE || epilogue == QIK_EPI_GELU_TANH ||
                   (epilogue == QIK_EPI_SCATTER && scatter && out_dtype == QIK_DTYPE_F32 && !bias) ||
                   (swiglu && !scatter) ||
-                  (rms && scatter && scatter->rms_cols > 0 && out_dtype == QIK_DTYPE_BF16 && !amax_out),
-              "qik_fp8_gemm: unknown epilogue (QIK_EPI_RMS_ROPE only through qik_fp8_gemm_qkv_rms_rope)");
+                  (rms && scatter && scatter->rms_cols > 0 && out_dtype == QIK_DTYPE_BF16 && !amax_out) ||
+                  (gate && scatter && scatter->res_x && out_dtype == QIK_DTYPE_BF16),
+              "qik_fp8_gemm: unknown epilogue (QIK_EPI_RMS_ROPE and QIK_EPI_GATE_RES only through their entry "
+              "points)");
   QIK_REQUIRE(!swiglu || (N % 256 == 0 && out_dtype == QIK_DTYPE_BF16),
               "qik_fp8_gemm: the SwiGLU epilogue needs N %% 256 == 0 (N=%lld) and BF16 output", (long long)N);
   QIK_REQUIRE(!(out_dtype == QIK_DTYPE_F32 && ((epilogue != QIK_EPI_SCALE && epilogue != QIK_EPI_SCATTER) || amax_out)),
@@ -854,6 +887,32 @@ extern "C" int qik_fp8_gemm_qkv_rms_rope(const uint8_t* A, const uint8_t* B, int
   const int64_t N = 3ll * heads * head_dim;
   return launch_fp8_gemm_ex(A, B, M, N, K, lda, ldb, scale_a, scale_b, bias, C, ldc, QIK_DTYPE_BF16, QIK_EPI_RMS_ROPE,
                             nullptr, status, static_cast<cudaStream_t>(stream), false, &extra, QIK_GEMM_TILE_PAIR_256);
+}
+
+extern "C" int qik_fp8_gemm_gate_residual(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K,
+                                          int64_t lda, int64_t ldb, const float* scale_a, const float* scale_b,
+                                          const void* bias, const void* x, int64_t ldx, const void* gate_table,
+                                          int64_t ldt, const uint8_t* target_mask, int64_t batch, int64_t seq,
+                                          void* C, int64_t ldc, int* status, void* stream) {
+  using namespace qik;
+  QIK_REQUIRE(x && gate_table, "qik_fp8_gemm_gate_residual: NULL residual / gate table");
+  QIK_REQUIRE(aligned16(x) && aligned16(gate_table) && ldx % 8 == 0 && ldt % 8 == 0 && ldx >= N && ldt >= N,
+              "qik_fp8_gemm_gate_residual: residual and gate table must be 16-byte aligned with row pitches >= N "
+              "and multiples of 8");
+  QIK_REQUIRE(batch >= 1 && seq >= 1 && batch * seq == M && M <= (1ll << 31) - 1,
+              "qik_fp8_gemm_gate_residual: M=%lld is not batch=%lld x seq=%lld", (long long)M, (long long)batch,
+              (long long)seq);
+  GemmParams extra;
+  memset(&extra, 0, sizeof(extra));
+  extra.res_x = static_cast<const uint16_t*>(x);
+  extra.res_ld = ldx;
+  extra.gate_tab = static_cast<const uint16_t*>(gate_table);
+  extra.gate_ld = ldt;
+  extra.gate_mask = target_mask;
+  extra.gate_seq = static_cast<int>(seq);
+  extra.gate_batch = static_cast<int>(batch);
+  return launch_fp8_gemm_ex(A, B, M, N, K, lda, ldb, scale_a, scale_b, bias, C, ldc, QIK_DTYPE_BF16, QIK_EPI_GATE_RES,
+                            nullptr, status, static_cast<cudaStream_t>(stream), false, &extra, QIK_GEMM_TILE_AUTO);
 }
 
 extern "C" int qik_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda,

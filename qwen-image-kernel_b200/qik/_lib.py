@@ -61,6 +61,9 @@ SIGNATURES = {
                                   _vp, _i32, _vp, _vp]),
     "qik_fp8_gemm_qkv_rms_rope": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i32, _i32,
                                          _vp, _vp, _vp, _vp, _i64, _f32, _vp, _vp]),
+    "qik_gate_table": (_i32, [_vp, _i64, _i64, _i64, _i64, _vp, _vp]),
+    "qik_fp8_gemm_gate_residual": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _i64,
+                                          _vp, _i64, _i64, _vp, _i64, _vp, _vp]),
     "qik_fp8_ffn_workspace_bytes": (ctypes.c_size_t, [_i64, _i64, _i64]),
     "qik_fp8_ffn": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp,
                            _vp]),

@@ -271,6 +271,38 @@ class FP8Linear(nn.Module):
                     "qik_fp8_gemm_qkv_rms_rope")
         return out.view(B, S, 3 * heads, D)
 
+    def forward_gate_residual(self, x: torch.Tensor, amax: torch.Tensor | None, residual: torch.Tensor,
+                              table: torch.Tensor, target_token_mask: torch.Tensor | None) -> torch.Tensor:
+        """fused_gate_residual(residual, forward_from_amax(x, amax), ...) in one GEMM whose
+        epilogue applies the gated residual: x [B, S, in_features] bf16 (``amax`` its
+        max|x| from the producer, or None), residual [B, S, out_features] bf16, ``table``
+        the gate_table rows (B, or 2B with a target mask).  Same bytes as the two steps
+        (up to products below 2^-126, rounded once here)."""
+        from .triton_fused import _u8_mask
+        B, S, K = x.shape
+        if K != self.in_features or self.in_features < 256 or residual.shape != (B, S, self.out_features):
+            raise ValueError(f"FP8Linear.forward_gate_residual: x {tuple(x.shape)} / residual "
+                             f"{tuple(residual.shape)} do not fit [{self.in_features} -> {self.out_features}]")
+        x2 = x.reshape(B * S, K)
+        xq, s_a = quantize_tensorwise(x2) if amax is None else quantize_from_amax(x2, amax)
+        res = residual.contiguous()
+        tab = table.contiguous()
+        if tab.shape[0] < (2 * B if target_token_mask is not None else B) or tab.shape[1] != self.out_features:
+            raise ValueError(f"FP8Linear.forward_gate_residual: gate table {tuple(tab.shape)} too small")
+        mask = _u8_mask(target_token_mask, S, x.device)
+        out = torch.empty(B, S, self.out_features, dtype=torch.bfloat16, device=x.device)
+        bias = None if self.bias is None else self.bias.to(torch.bfloat16).contiguous()
+        lib = L.load()
+        with torch.cuda.device(x.device):
+            L.check(lib.qik_fp8_gemm_gate_residual(xq.data_ptr(), self.weight.data_ptr(), B * S, self.out_features, K,
+                                                   xq.stride(0), self.weight.stride(0), s_a.data_ptr(),
+                                                   self.weight_scale.data_ptr(), L.ptr(bias), res.data_ptr(),
+                                                   self.out_features, tab.data_ptr(), self.out_features, L.ptr(mask),
+                                                   B, S, out.data_ptr(), self.out_features,
+                                                   L.status_word(x.device).data_ptr(), L.stream_ptr()),
+                    "qik_fp8_gemm_gate_residual")
+        return out
+
     def forward_fp32(self, x: torch.Tensor) -> torch.Tensor:
         """Same computation with the fp32 GEMM output before the bf16 cast (parity mode)."""
         x2 = x.reshape(-1, x.shape[-1])

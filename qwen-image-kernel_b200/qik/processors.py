@@ -23,7 +23,9 @@ whose only consumers are FP8 linears emits their e4m3 input and scale itself
 (``fused_layer_norm_modulate_e4m3``: the bf16 output is never written); the fused QKV
 linear then applies the q / k RMSNorm + RoPE in its GEMM epilogue (``_qkv_rms_rope``)
 and the fused up projection the SwiGLU (``_swiglu_linear``: the gate / up output is
-never written).  SwiGLU and the attention reduce the amax
+never written); the out-projection and the down projection add their gated output
+to the residual in their GEMM epilogues (``_gate_linear``, with the bf16(tanh(gate))
+rows from ``gate_table``).  SwiGLU and the attention reduce the amax
 of their output, which the next FP8 linear uses instead of its own amax pass (same
 bytes and scale).
 """
@@ -34,7 +36,7 @@ import torch
 from .fp8 import FP8Linear
 from .triton_attention import block_causal_flash_attention
 from .triton_fused import (fused_gate_residual, fused_layer_norm_modulate, fused_layer_norm_modulate_e4m3,
-                           fused_rms_norm_rope, fused_swiglu)
+                           fused_rms_norm_rope, fused_swiglu, gate_table)
 
 
 def _build_prefix_lengths(segments: list[tuple[int, int, bool]], prefix_len: int, seq_len: int,
@@ -85,6 +87,22 @@ def _qkv_rms_rope(mod: FP8Linear, xq: torch.Tensor, scale: torch.Tensor, heads: 
                                          attn.norm_q.eps)
 
 
+def _gate_linear(mod: FP8Linear, x: torch.Tensor, amax: torch.Tensor | None, residual: torch.Tensor,
+                 table: torch.Tensor, target_token_mask: torch.Tensor | None) -> torch.Tensor:
+    """fused_gate_residual(residual, mod(x), ...) in one GEMM whose epilogue applies the
+    gated residual with the bf16(tanh(gate)) rows of ``table`` (gate_table); same bytes."""
+    return mod.forward_gate_residual(x, amax, residual, table, target_token_mask)
+
+
+def _fuses_gate(lin, after=None) -> bool:
+    """An FP8 linear on the tensor-core path (followed by nothing but an identity or an
+    inactive dropout) can apply the gated residual in its GEMM epilogue."""
+    if not (isinstance(lin, FP8Linear) and lin.in_features >= 256 and lin.out_features % 8 == 0):
+        return False
+    return (after is None or isinstance(after, torch.nn.Identity)
+            or (isinstance(after, torch.nn.Dropout) and (after.p == 0 or not after.training)))
+
+
 def _takes_e4m3(*mods) -> bool:
     """Every module is an FP8 linear on the tensor-core path (in_features >= 256), so a
     producer may hand them its output already quantized."""
@@ -116,6 +134,7 @@ class QwenImage21KernelProcessor:
         key_valid=None,
         hidden_states_amax: torch.Tensor | None = None,
         hidden_states_scale: torch.Tensor | None = None,
+        gate_residual: tuple | None = None,
     ) -> torch.Tensor:
         # hidden_states_scale: hidden_states is then the e4m3 input of the QKV linears
         # (fused_layer_norm_modulate_e4m3), quantized with this scale
@@ -180,6 +199,13 @@ class QwenImage21KernelProcessor:
         out = out.flatten(2, 3).type_as(query)
         # the attention epilogue accumulated max|out|: the out-projection's quantizer
         # skips its own max pass
+        if gate_residual is not None:
+            # (residual, gate table, target mask) from the fused block: the out-projection
+            # returns residual + bf16(tanh(gate)) * to_out(out) from its GEMM epilogue
+            if not _fuses_gate(attn.to_out[0], attn.to_out[1]):
+                raise ValueError("gate_residual needs an FP8 out-projection followed by an identity")
+            residual, table, mask = gate_residual
+            return _gate_linear(attn.to_out[0], out, out_amax, residual, table, mask)
         out = _linear(attn.to_out[0], out, out_amax)
         return attn.to_out[1](out)
 
@@ -218,7 +244,10 @@ class QwenImage21KernelBlock(torch.nn.Module):
                            kv_cache_mode=kv_cache_mode, cache_write_slice=cache_write_slice, segments=segments,
                            key_valid=key_valid)
         qkv_mods = (fused_qkv,) if fused_qkv is not None else (self.attn.to_q, self.attn.to_k, self.attn.to_v)
-        if isinstance(getattr(self.attn, "processor", None), QwenImage21KernelProcessor):
+        ours = isinstance(getattr(self.attn, "processor", None), QwenImage21KernelProcessor)
+        # modulation rows the gates read: the samples' rows, and the t = 0 rows with a mask
+        gate_rows = hidden_states.shape[0] * (2 if target_token_mask is not None else 1)
+        if ours:
             if _takes_e4m3(*qkv_mods):
                 # the norm's only consumers are FP8 linears: it emits their e4m3 input
                 img_mod, scale1 = fused_layer_norm_modulate_e4m3(hidden_states, modulation, 0, mod_stride,
@@ -232,8 +261,14 @@ class QwenImage21KernelBlock(torch.nn.Module):
         else:
             img_mod = fused_layer_norm_modulate(hidden_states, modulation, 0, mod_stride, target_token_mask,
                                                 self._eps)
-        attn_out = self.attn(hidden_states=img_mod, **attn_kwargs)
-        hidden_states = fused_gate_residual(hidden_states, attn_out, modulation, inner, target_token_mask)
+        if ours and _fuses_gate(self.attn.to_out[0], self.attn.to_out[1]):
+            # the out-projection's GEMM epilogue adds the gated attention output to the residual
+            table1 = gate_table(modulation, inner, gate_rows, inner)
+            attn_kwargs["gate_residual"] = (hidden_states, table1, target_token_mask)
+            hidden_states = self.attn(hidden_states=img_mod, **attn_kwargs)
+        else:
+            attn_out = self.attn(hidden_states=img_mod, **attn_kwargs)
+            hidden_states = fused_gate_residual(hidden_states, attn_out, modulation, inner, target_token_mask)
 
         fused_up = getattr(self.img_mlp, "fused_up", None)
         up_mods = (fused_up,) if fused_up is not None else (self.img_mlp.gate_layer, self.img_mlp.proj)
@@ -255,6 +290,9 @@ class QwenImage21KernelBlock(torch.nn.Module):
                 gate = _linear(self.img_mlp.gate_layer, img_mod2, amax2, scale2)
                 up = _linear(self.img_mlp.proj, img_mod2, amax2, scale2)
             mlp_mid = fused_swiglu(gate, up, amax_out=amax3)
+        if _fuses_gate(self.img_mlp.out):
+            table2 = gate_table(modulation, 3 * inner, gate_rows, inner)
+            return _gate_linear(self.img_mlp.out, mlp_mid, amax3, hidden_states, table2, target_token_mask)
         mlp_out = _linear(self.img_mlp.out, mlp_mid, amax3)
         return fused_gate_residual(hidden_states, mlp_out, modulation, 3 * inner, target_token_mask)
 

@@ -180,6 +180,22 @@ def fused_gate_residual(x: torch.Tensor, f: torch.Tensor, modulation: torch.Tens
     return out
 
 
+def gate_table(modulation: torch.Tensor, gate_offset: int, rows: int, D: int) -> torch.Tensor:
+    """bf16(tanh(modulation[r, gate_offset:gate_offset + D])) for r < rows, as
+    fused_gate_residual computes the gate: the table of the FP8 linears' gated-residual
+    epilogue (qik.fp8.FP8Linear.forward_gate_residual)."""
+    _require_bf16(modulation=modulation)
+    if modulation.stride(-1) != 1:
+        raise ValueError("modulation must have a unit column stride")
+    if rows > modulation.shape[0]:
+        raise ValueError(f"gate_table: {rows} rows requested, modulation has {modulation.shape[0]}")
+    out = torch.empty(rows, D, dtype=torch.bfloat16, device=modulation.device)
+    lib = L.load()
+    L.check(lib.qik_gate_table(modulation.data_ptr(), rows, modulation.stride(0), int(gate_offset), D, out.data_ptr(),
+                               L.stream_ptr(modulation.device)), "qik_gate_table")
+    return out
+
+
 def _rows(t: torch.Tensor, M: int, N: int) -> tuple[torch.Tensor, int]:
     """t ([..., N]) as an [M, N] view with one row pitch (elements), copying only when
     the leading dims do not flatten or the pitch / base is not 16-byte aligned."""

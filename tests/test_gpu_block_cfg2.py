@@ -24,6 +24,12 @@ the oracle from the recorded inputs:
   -> bf16 -> RMSNorm + RoPE, v within the linear gate, q and k within relF <= 5e-3 and
   no error above 2^-6 of the largest output (a last-bit change of a GEMM output moves
   its normalised value by up to two bf16 ulps);
+* the out-projection and the down projection with the gated residual in their
+  epilogues: bit-identical to the linear followed by the gated-residual kernel, and
+  against the oracle's dequant GEMM -> bf16 -> gated residual within relF <= 5e-3 and no
+  error above 2^-6 of the largest output (the residual stream grows to |x| ~ 8, where a
+  last-bit change of a linear output moves a sum by one bf16 ulp of 2^-4); the gate
+  tables within 2^-8 of tanh;
 * the fused up projection with the SwiGLU in its epilogue: bit-identical (values and
   amax) to the plain GEMM's gate / up halves through the SwiGLU kernel, and at the
   fused-op gate against the oracle's SwiGLU of the bf16-rounded fp32 dequant GEMM.
@@ -91,7 +97,7 @@ def recorder(monkeypatch):
         def inner(*a, **kw):
             out = fn(*a, **kw)
             rec = {"name": name, "args": [cpu(x) for x in a], "kw": {k: cpu(v) for k, v in kw.items()}}
-            if name in ("linear", "swiglu_linear", "qkv_rms_rope"):
+            if name in ("linear", "swiglu_linear", "qkv_rms_rope", "gate_linear"):
                 rec["mod"] = a[0]
             if name == "qkv_rms_rope":
                 rec["attn"] = a[4]
@@ -110,7 +116,8 @@ def recorder(monkeypatch):
                        ("rms_rope", "fused_rms_norm_rope"),
                        ("gate_res", "fused_gate_residual"), ("swiglu", "fused_swiglu"),
                        ("attention", "block_causal_flash_attention"), ("linear", "_linear"),
-                       ("swiglu_linear", "_swiglu_linear"), ("qkv_rms_rope", "_qkv_rms_rope")):
+                       ("swiglu_linear", "_swiglu_linear"), ("qkv_rms_rope", "_qkv_rms_rope"),
+                       ("gate_linear", "_gate_linear"), ("gate_table", "gate_table")):
         monkeypatch.setattr(PR, attr, wrap(name, getattr(PR, attr)))
     return calls
 
@@ -152,8 +159,8 @@ def test_dit_block_cfg2_full_size_stage_by_stage(recorder):
     out = block(x, mod, rotary_emb=freqs, segments=[(0, 256, True)])
     torch.cuda.synchronize()
     names = [c["name"] for c in recorder]
-    assert names == ["ln_mod_e4m3", "qkv_rms_rope", "attention", "linear", "gate_res",
-                     "ln_mod_e4m3", "swiglu_linear", "linear", "gate_res"], names
+    assert names == ["ln_mod_e4m3", "gate_table", "qkv_rms_rope", "attention", "gate_linear",
+                     "ln_mod_e4m3", "swiglu_linear", "gate_table", "gate_linear"], names
     assert recorder[-1]["out"].shape == (B, S, K) and torch.equal(recorder[-1]["out"], out.cpu())
     torch.set_num_threads(max(1, torch.get_num_threads()))
     cos, sin = freqs.real.float().cpu(), freqs.imag.float().cpu()
@@ -179,6 +186,31 @@ def test_dit_block_cfg2_full_size_stage_by_stage(recorder):
         elif c["name"] == "swiglu":
             _fused_gate(o, O.swiglu(a[0], a[1]), tag)
             assert int(kw["amax_out"][0]) == _amax_bits_of(o), tag
+        elif c["name"] == "gate_table":
+            m, off, rows, width = a[0], a[1], a[2], a[3]
+            ref = torch.tanh(m[:rows, off:off + width].float())
+            assert (o.float() - ref).abs().max().item() <= 2.0 ** -8, tag
+        elif c["name"] == "gate_linear":
+            # bit-identical to the linear + the gated-residual kernel, and within the linear
+            # gate of the oracle's dequant GEMM -> bf16 -> gated residual
+            from qik.triton_fused import fused_gate_residual
+            lin, xin, amax, resid, mask = c["mod"], a[1], a[2], a[3], a[5]
+            off = K if i < 6 else 3 * K
+            f = lin.forward_from_amax(xin.cuda(), None if amax is None else amax.cuda())
+            ref = fused_gate_residual(resid.cuda(), f, mod, off, None if mask is None else mask.cuda()).cpu()
+            assert torch.equal(o, ref), tag
+            x2 = xin.reshape(-1, xin.shape[-1]).contiguous()
+            if amax is not None:
+                assert int(amax[0]) == _amax_bits_of(x2), tag
+            q8, s8 = O.quantize_act(x2)
+            y = O.fp8_linear(q8, s8, lin.weight.cpu(), float(lin.weight_scale.item()),
+                             None if lin.bias is None else lin.bias.cpu()).to(torch.bfloat16).view(o.shape)
+            oref = O.gate_residual(resid, y, mod.cpu(), off, mask).float()
+            gf = o.float()
+            d = (gf - oref).abs().max().item() / oref.abs().max().item()
+            r = O.relf(gf, oref)
+            print(f"{tag}: max-abs / max|ref| {d:.3e} relF {r:.3e}")
+            assert d <= 2.0 ** -6 and r <= LIN_RELF, tag
         elif c["name"] == "qkv_rms_rope":
             # bit-identical to the plain GEMM + the RMSNorm + RoPE kernel on its q / k views,
             # and within the linear gate of the oracle's linear -> bf16 -> RMSNorm + RoPE

@@ -167,6 +167,38 @@ def test_qkv_rms_rope_epilogue_matches_gemm_then_rms_rope(fp8, B, S, H, rope):
     assert torch.equal(ov, v), "v"
 
 
+@pytest.mark.parametrize("B,S,K,N,masked", [(2, 4352, 3072, 3072, False), (2, 4352, 6144, 3072, True),
+                                            (1, 77, 256, 256, True), (3, 50, 384, 144, False)])
+def test_gate_residual_epilogue_matches_linear_then_gate_residual(fp8, B, S, K, N, masked):
+    """qik_fp8_gemm_gate_residual (an FP8 linear with the DiT block's gated residual in
+    its epilogue) is bit-identical to the linear followed by the gated-residual kernel:
+    the configs[2] out-projection and down-projection shapes (with the t = 0 modulation
+    rows of a target mask), and small ragged shapes (partial tiles, a partial column
+    chunk, a bias)."""
+    from qik.triton_fused import fused_gate_residual, gate_table
+    g = torch.Generator(device="cuda").manual_seed(B * S + K + N)
+    lin = fp8.FP8Linear(K, N, bias=True).cuda()
+    wq8, sw = fp8.quantize_weight_tensorwise(torch.randn(N, K, device="cuda", generator=g) * 0.03)
+    lin.weight.copy_(wq8)
+    lin.weight_scale.copy_(sw)
+    lin.bias.copy_((torch.randn(N, device="cuda", generator=g) * 0.2).to(torch.bfloat16))
+    x = torch.randn(B, S, K, device="cuda", generator=g).to(torch.bfloat16)
+    res = (torch.randn(B, S, N, device="cuda", generator=g) * 2).to(torch.bfloat16)
+    mod = (torch.randn(2 * B, 4 * N, device="cuda", generator=g) * 0.8).to(torch.bfloat16)
+    mask = (torch.rand(S, device="cuda", generator=g) < 0.7) if masked else None
+    amax = fp8.amax_bits(x.reshape(-1, K))
+    for off in (N, 3 * N):
+        table = gate_table(mod, off, 2 * B if masked else B, N)
+        out = lin.forward_gate_residual(x, amax, res, table, mask)
+        ref = fused_gate_residual(res, lin.forward_from_amax(x, amax), mod, off, mask)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref), off
+    # the table is bf16(tanh(gate)) (fp32 tanh, one rounding)
+    t = gate_table(mod, N, 2 * B, N).float()
+    r = torch.tanh(mod[:, N:2 * N].float())
+    assert (t - r).abs().max().item() <= 2.0 ** -8
+
+
 def test_qkv_rms_rope_rejects(fp8):
     lin = fp8.FP8Linear(256, 3 * 2 * 64).cuda()
     xq = torch.zeros(1, 16, 256, dtype=torch.float8_e4m3fn, device="cuda")
