@@ -149,7 +149,12 @@ __device__ __forceinline__ void add_bias32(float (&v)[32], const __nv_bfloat16* 
   }
 }
 
-template <int BN, int STAGES, bool TWO_SM>
+// Epilogue kinds compiled into separate kernels, so the plain path carries none of the
+// fused epilogues' code: plain (QIK_EPI_SCALE / GELU_TANH / SCATTER), SwiGLU, RMSNorm +
+// RoPE (CTA pairs only) and gated residual.
+constexpr int kEkPlain = 0, kEkSwiglu = 1, kEkRms = 2, kEkGate = 3;
+
+template <int BN, int STAGES, bool TWO_SM, int EK>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
@@ -222,7 +227,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // QIK_EPI_SWIGLU: the leader loads gate rows nb * 128 + [0, 128), the peer the up
       // rows N / 2 + nb * 128 + [0, 128), so tile columns 0-127 are gate outputs and
       // 128-255 the matching up outputs
-      const bool swiglu = TWO_SM && p.epilogue == QIK_EPI_SWIGLU;
+      constexpr bool swiglu = TWO_SM && EK == kEkSwiglu;
       for (int tile = tile0; tile < tiles; tile += tile_step) {
         int mb, nb;
         tile_coords(tile, num_m, num_n, p.group_m, mb, nb);
@@ -377,8 +382,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         buf ^= 1;
       };
       int chunks = BN / 32;
-      if constexpr (TWO_SM && BN == 256) {
-        if (p.epilogue == QIK_EPI_RMS_ROPE && nb * 256 < p.rms_cols) {
+      if constexpr (TWO_SM && BN == 256 && EK == kEkRms) {
+        if (nb * 256 < p.rms_cols) {
           // a q or k tile: warp half h takes head h (tile columns 128 h + [0, 128)) whole,
           // so each thread holds its row of the head; pass 1 sums the squares of the bf16
           // outputs in groups of 8 as the RMSNorm + RoPE kernel's lanes do, pass 2 reloads
@@ -453,7 +458,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             store_bf16(w, hc0 + j * 32);
           }
         }
-        if (p.epilogue == QIK_EPI_SWIGLU) {
+      }
+      if constexpr (TWO_SM && BN == 256 && EK == kEkSwiglu) {
+        {
           // tile columns c * 32 + [0, 32) (gate) and 128 + c * 32 + [0, 32) (up) give output
           // columns nb * 128 + c * 32 + [0, 32); N % 256 == 0, so every chunk is whole
           chunks = 0;
@@ -557,7 +564,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             w[j] = pack_bf16x2(lo, hi);
           }
-          if (p.epilogue == QIK_EPI_GATE_RES && row_ok) {
+          if (EK == kEkGate && row_ok) {
             // x + bf16(T * f) in bf16x2 arithmetic: the products and sums of bf16 values,
             // each rounded once, as the gated-residual kernel's fp32 arithmetic rounds them
             const int grow = row0 + lane, b = grow / p.gate_seq, sq = grow - b * p.gate_seq;
@@ -659,7 +666,7 @@ static int gemm_pick_cfg(int64_t M, int64_t N, bool scatter = false) {
 // of 118 MB, and inside the FFN chain, whose pack leaves A in L2, it was no faster.
 static int gemm_pick_raster(int64_t N, int64_t K) { return N * K > (int64_t{48} << 20) ? 16 : 1; }
 
-template <int BN, int STAGES, bool TWO_SM>
+template <int BN, int STAGES, bool TWO_SM, int EK = kEkPlain>
 static int launch_gemm(const uint8_t* A, const uint8_t* B, const GemmParams& p, int64_t lda, int64_t ldb,
                        cudaStream_t st, bool pdl) {
   using Lay = GemmLayout<BN, STAGES, TWO_SM>;
@@ -690,7 +697,7 @@ static int launch_gemm(const uint8_t* A, const uint8_t* B, const GemmParams& p, 
   QIK_REQUIRE(dev >= 0 && dev < 64, "qik_fp8_gemm: device ordinal %d out of range", dev);
   cudaError_t attr_rc = cudaSuccess;
   std::call_once(attr_once[dev], [&] {
-    attr_rc = cudaFuncSetAttribute(fp8_gemm_kernel<BN, STAGES, TWO_SM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    attr_rc = cudaFuncSetAttribute(fp8_gemm_kernel<BN, STAGES, TWO_SM, EK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    Lay::kSmemBytes);
   });
   QIK_TRY_CUDA(attr_rc);
@@ -713,10 +720,10 @@ static int launch_gemm(const uint8_t* A, const uint8_t* B, const GemmParams& p, 
     attr[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    QIK_TRY_CUDA(cudaLaunchKernelEx(&cfg, fp8_gemm_kernel<BN, STAGES, TWO_SM>, ta, tb, tc, p));
+    QIK_TRY_CUDA(cudaLaunchKernelEx(&cfg, fp8_gemm_kernel<BN, STAGES, TWO_SM, EK>, ta, tb, tc, p));
   } else {
     const int grid = min(tiles, sm_count());
-    QIK_TRY_CUDA(launch_kernel(fp8_gemm_kernel<BN, STAGES, TWO_SM>, dim3(grid), dim3(kGemmThreads), Lay::kSmemBytes,
+    QIK_TRY_CUDA(launch_kernel(fp8_gemm_kernel<BN, STAGES, TWO_SM, EK>, dim3(grid), dim3(kGemmThreads), Lay::kSmemBytes,
                                st, pdl, ta, tb, tc, p));
   }
   return check_launch("fp8_gemm_kernel");
@@ -779,15 +786,28 @@ int launch_fp8_gemm_ex(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N,
               "qik_fp8_gemm: the SwiGLU epilogue runs on CTA-pair tiles only (tile configuration %d)", sel);
   const int raster = (tile_cfg >> 8) & 0xFF;
   p.group_m = raster != 0 ? raster : gemm_pick_raster(N, K);
+  const int ek = swiglu ? kEkSwiglu : rms ? kEkRms : gate ? kEkGate : kEkPlain;
   switch (cfg) {
     case QIK_GEMM_TILE_PAIR_256:
-      return launch_gemm<256, 6, true>(A, B, p, lda, ldb, stream, pdl);
+      switch (ek) {
+        case kEkSwiglu:
+          return launch_gemm<256, 6, true, kEkSwiglu>(A, B, p, lda, ldb, stream, pdl);
+        case kEkRms:
+          return launch_gemm<256, 6, true, kEkRms>(A, B, p, lda, ldb, stream, pdl);
+        case kEkGate:
+          return launch_gemm<256, 6, true, kEkGate>(A, B, p, lda, ldb, stream, pdl);
+        default:
+          return launch_gemm<256, 6, true>(A, B, p, lda, ldb, stream, pdl);
+      }
     case QIK_GEMM_TILE_SINGLE_128:
-      return launch_gemm<128, 6, false>(A, B, p, lda, ldb, stream, pdl);
+      return ek == kEkGate ? launch_gemm<128, 6, false, kEkGate>(A, B, p, lda, ldb, stream, pdl)
+                           : launch_gemm<128, 6, false>(A, B, p, lda, ldb, stream, pdl);
     case QIK_GEMM_TILE_SINGLE_64:
-      return launch_gemm<64, 8, false>(A, B, p, lda, ldb, stream, pdl);
+      return ek == kEkGate ? launch_gemm<64, 8, false, kEkGate>(A, B, p, lda, ldb, stream, pdl)
+                           : launch_gemm<64, 8, false>(A, B, p, lda, ldb, stream, pdl);
     case QIK_GEMM_TILE_SINGLE_256:
-      return launch_gemm<256, 4, false>(A, B, p, lda, ldb, stream, pdl);
+      return ek == kEkGate ? launch_gemm<256, 4, false, kEkGate>(A, B, p, lda, ldb, stream, pdl)
+                           : launch_gemm<256, 4, false>(A, B, p, lda, ldb, stream, pdl);
     case QIK_GEMM_TILE_SWAP_16: {
       // C^T = B . A^T: the weights are the tile rows, the (at most 16) activation rows
       // the tile columns; the epilogue stores C untransposed
