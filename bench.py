@@ -108,7 +108,7 @@ class L2Flush:
 # step, from `ncu --set full --clock-control none -k regex:fp8_gemm -s 2 -c 2
 # python bench.py --steps 3 --warmup 3 --no-extras` (the algorithmic bytes are 158.1 MB
 # for GEMM1 and 117.9 MB for GEMM2).
-GEMM_DRAM_BYTES_PER_LAUNCH = 136778496
+GEMM_DRAM_BYTES_PER_LAUNCH = 140240512
 GEMM_TRAFFIC_SOURCE = ("ncu capture (dram__bytes_read.sum + dram__bytes_write.sum, mean of the step's two GEMM "
                        "launches): ncu --set full --clock-control none -k regex:fp8_gemm -s 2 -c 2 "
                        "python bench.py --steps 3 --warmup 3 --no-extras")
