@@ -460,6 +460,18 @@ int qik_tp_reduce_gather(const float* recv, const uint32_t* cnt_in, uint32_t cnt
 int qik_tp_wait(const uint32_t* gcnt, uint32_t target, int world, int* status, void* stream);
 
 /*
+ * Sequence-parallel form of the TP stack: after the reduce-scatter of a row-parallel
+ * linear's fp32 partial products, this rank's rows x [rows, N] become
+ * out = bf16(x + bias) (bias bf16 [N] or NULL; fp32 add, one rounding) with max|out|
+ * accumulated into *amax_out (fp32 bits, atomic max; NULL to skip) for the next FP8
+ * linear's dynamic scale.  The bias add and bf16 output of FP8Linear.forward
+ * (qwen_image_kernel/fp8.py:86-90), applied once after the sum over the ranks.
+ * N a multiple of 8; x, out, bias 16-byte aligned.
+ */
+int qik_rows_bias_bf16(const float* x, int64_t rows, int64_t N, const void* bias, void* out, uint32_t* amax_out,
+                       void* stream);
+
+/*
  * Self-test of the bounded-wait machinery: launches one CTA that waits on an
  * mbarrier nothing will ever complete, with a limit of `wait_ns` nanoseconds, and
  * writes QIK_STATUS_TIMEOUT to *status when the wait gives up.  The GPU context

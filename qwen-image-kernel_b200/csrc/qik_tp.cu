@@ -108,6 +108,43 @@ __global__ void __launch_bounds__(kTpThreads) tp_reduce_gather_kernel(const Redu
   }
 }
 
+// out = bf16(x + bias) for the rows of x [rows, N] fp32 (this rank's rows of a summed
+// row-parallel product), and max|out| into *amax_out (fp32 bits, atomic max) for the
+// next FP8 linear's dynamic scale.  8 columns per thread step.
+__global__ void __launch_bounds__(kTpThreads) rows_bias_bf16_kernel(const float* __restrict__ x, int64_t rows, int N,
+                                                                    const __nv_bfloat16* __restrict__ bias,
+                                                                    __nv_bfloat16* __restrict__ out,
+                                                                    uint32_t* __restrict__ amax_out) {
+  const int64_t groups = rows * (N / 8);
+  uint32_t m2 = 0;
+  for (int64_t gi = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; gi < groups;
+       gi += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = gi / (N / 8);
+    const int c = static_cast<int>(gi - r * (N / 8)) * 8;
+    const float4 u = __ldcs(reinterpret_cast<const float4*>(x + r * N + c));
+    const float4 v = __ldcs(reinterpret_cast<const float4*>(x + r * N + c + 4));
+    float acc[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
+    if (bias) {
+      const uint4 bb = __ldg(reinterpret_cast<const uint4*>(bias + c));
+      const uint32_t bw[4] = {bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        acc[2 * t] += __uint_as_float(bw[t] << 16);
+        acc[2 * t + 1] += __uint_as_float(bw[t] & 0xFFFF0000u);
+      }
+    }
+    const uint4 w = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                               pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+    m2 = __vmaxu2(m2, __vmaxu2(__vmaxu2(w.x & 0x7FFF7FFFu, w.y & 0x7FFF7FFFu),
+                               __vmaxu2(w.z & 0x7FFF7FFFu, w.w & 0x7FFF7FFFu)));
+    *reinterpret_cast<uint4*>(out + r * N + c) = w;
+  }
+  if (amax_out) {
+    const uint32_t m = __reduce_max_sync(0xffffffffu, max(m2 & 0xFFFFu, m2 >> 16));
+    if ((threadIdx.x & 31) == 0 && m != 0u) atomicMax(amax_out, m << 16);
+  }
+}
+
 __global__ void tp_wait_kernel(const uint32_t* gcnt, uint32_t target, int world, int* status) {
   if (threadIdx.x == 0) {
     wait_counters(gcnt, world, target, status);
@@ -192,4 +229,22 @@ extern "C" int qik_tp_wait(const uint32_t* gcnt, uint32_t target, int world, int
   QIK_REQUIRE(gcnt && world >= 1 && world <= QIK_TP_MAX_WORLD, "qik_tp_wait: bad arguments");
   tp_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(gcnt, target, world, status);
   return check_launch("tp_wait_kernel");
+}
+
+extern "C" int qik_rows_bias_bf16(const float* x, int64_t rows, int64_t N, const void* bias, void* out,
+                                  uint32_t* amax_out, void* stream) {
+  QIK_REQUIRE(rows >= 0 && N > 0 && N % 8 == 0 && N <= (1ll << 30), "qik_rows_bias_bf16: N=%lld must be a positive "
+              "multiple of 8", (long long)N);
+  if (rows == 0) return QIK_OK;
+  QIK_REQUIRE(x && out, "qik_rows_bias_bf16: NULL x / out");
+  QIK_REQUIRE(aligned16(x) && aligned16(out) && (!bias || aligned16(bias)),
+              "qik_rows_bias_bf16: x, out and bias must be 16-byte aligned");
+  const int64_t groups = rows * (N / 8);
+  const int64_t want = (groups + kTpThreads - 1) / kTpThreads;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+  const int grid = static_cast<int>(want < cap ? want : cap);
+  rows_bias_bf16_kernel<<<grid, kTpThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, rows, static_cast<int>(N), static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(out),
+      amax_out);
+  return check_launch("rows_bias_bf16_kernel");
 }

@@ -93,6 +93,7 @@ SIGNATURES = {
     "qik_tp_reduce_gather": (_i32, [_vp, _vp, ctypes.c_uint32, _i32, _i32, _i64, _i64, _i64, _vp, _vp, _vp, _i32,
                                     _vp, _vp]),
     "qik_tp_wait": (_i32, [_vp, ctypes.c_uint32, _i32, _vp, _vp]),
+    "qik_rows_bias_bf16": (_i32, [_vp, _i64, _i64, _vp, _vp, _vp, _vp]),
 }
 
 _lock = threading.Lock()

@@ -19,6 +19,17 @@ Two layouts (the reference itself is single-GPU; these follow the BASELINE confi
   their fp32 partial products are summed with an NCCL all-reduce, and the bias is
   added once after the sum.
 
+* **Sequence parallel** (``TPBlock(sequence_parallel=True)``) -- the same stack with the
+  activations between the linears kept as row shards: a row-parallel linear's fp32
+  partial products are reduce-scattered (each rank receives the sum of its own rows),
+  the bias add and bf16 cast run on those rows only, and a column-parallel linear
+  quantizes its local rows with the global scale (4-byte all-reduce MAX) and
+  all-gathers the e4m3 bytes (1 byte per element) before its GEMM.  Per row-parallel
+  linear a rank then moves (world-1)/world of the fp32 product once (reduce-scatter)
+  plus (world-1)/world of the e4m3 activation, instead of an fp32 all-reduce (twice
+  the product) followed by a replicated amax and pack of the whole activation; the
+  e4m3 bytes equal the 1-GPU quantization of the whole tensor.
+
 The arithmetic goes through an ``ops`` object: ``QikOps`` (the CUDA kernels, the
 default and the only product path) or a test double with the same methods.
 """
@@ -57,6 +68,17 @@ class QikOps:
         from .triton_attention import block_causal_flash_attention
         return block_causal_flash_attention(q, k, v, L, None)
 
+    def bias_bf16(self, x: torch.Tensor, bias: torch.Tensor | None, amax: torch.Tensor) -> torch.Tensor:
+        """bf16(x + bias) of fp32 rows, max|out| accumulated into ``amax``."""
+        xc = x.contiguous()
+        out = torch.empty(xc.shape, dtype=torch.bfloat16, device=x.device)
+        b = None if bias is None else bias.contiguous()
+        lib = L.load()
+        with torch.cuda.device(x.device):
+            L.check(lib.qik_rows_bias_bf16(xc.data_ptr(), xc.shape[0], xc.shape[1], L.ptr(b), out.data_ptr(),
+                                           amax.data_ptr(), L.stream_ptr()), "qik_rows_bias_bf16")
+        return out
+
 
 _comm_streams: dict[int, torch.cuda.Stream] = {}
 
@@ -89,6 +111,46 @@ def allreduce_amax_(amax: torch.Tensor, group=None) -> torch.Tensor:
     if _world(group)[1] > 1:
         dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=group)
     return amax
+
+
+def _nccl(group) -> bool:
+    return dist.get_backend(group) == "nccl"
+
+
+def reduce_scatter_rows(part: torch.Tensor, group=None) -> torch.Tensor:
+    """This rank's rows [M / world, N] of the sum over the ranks of ``part`` [M, N]
+    (M a multiple of world): NCCL's reduce-scatter; gloo, which has none, sums with an
+    all-reduce and keeps the rank's rows."""
+    rank, world = _world(group)
+    if world == 1:
+        return part
+    M = part.shape[0]
+    if M % world:
+        raise ValueError(f"reduce_scatter_rows: {M} rows do not split evenly over {world} ranks")
+    if _nccl(group):
+        out = torch.empty((M // world,) + tuple(part.shape[1:]), dtype=part.dtype, device=part.device)
+        dist.reduce_scatter_tensor(out, part.contiguous(), op=dist.ReduceOp.SUM, group=group)
+        return out
+    full = part.contiguous().clone()
+    dist.all_reduce(full, op=dist.ReduceOp.SUM, group=group)
+    return full[rank * (M // world):(rank + 1) * (M // world)].contiguous()
+
+
+def all_gather_rows(local: torch.Tensor, group=None) -> torch.Tensor:
+    """The ranks' equal row shards concatenated in rank order (e4m3 moved as bytes)."""
+    _, world = _world(group)
+    if world == 1:
+        return local
+    fp8 = local.dtype == torch.float8_e4m3fn
+    src = (local.view(torch.uint8) if fp8 else local).contiguous()
+    if _nccl(group):
+        full = torch.empty((world * src.shape[0],) + tuple(src.shape[1:]), dtype=src.dtype, device=src.device)
+        dist.all_gather_into_tensor(full, src, group=group)
+    else:
+        parts = [torch.empty_like(src) for _ in range(world)]
+        dist.all_gather(parts, src, group=group)
+        full = torch.cat(parts, 0)
+    return full.view(torch.float8_e4m3fn) if fp8 else full
 
 
 def quantize_sharded(x_local: torch.Tensor, group=None, global_amax: bool = True, ops=None):
@@ -177,6 +239,20 @@ class ColumnParallelFP8Linear(nn.Module):
         x2 = x.reshape(-1, x.shape[-1])
         amax = self.ops.amax_bits(x2)
         xq, sx = self.ops.pack(x2, amax)
+        return self.ops.gemm(xq, sx, self.weight, self.weight_scale, self.bias, epilogue=epilogue, amax_out=amax_out)
+
+    def forward_gathered(self, x_local: torch.Tensor, amax: torch.Tensor | None = None, group=None,
+                         epilogue: int = L.EPI_SCALE, amax_out: torch.Tensor | None = None):
+        """Sequence parallel: the input is this rank's rows.  They are quantized with the
+        scale of the whole input (``amax``: max|x_local| if a producer accumulated it,
+        made global by a 4-byte all-reduce MAX), the e4m3 rows of all ranks gathered,
+        and the GEMM runs over every row for this rank's output features."""
+        x2 = x_local.reshape(-1, x_local.shape[-1])
+        if amax is None:
+            amax = self.ops.amax_bits(x2)
+        allreduce_amax_(amax, group)
+        xq_local, sx = self.ops.pack(x2, amax)
+        xq = all_gather_rows(xq_local, group)
         return self.ops.gemm(xq, sx, self.weight, self.weight_scale, self.bias, epilogue=epilogue, amax_out=amax_out)
 
 
@@ -282,6 +358,16 @@ class RowParallelFP8Linear(nn.Module):
         xq, sx = self.ops.pack(x2, amax)
         return self.forward_quantized(xq, sx)
 
+    def forward_scattered(self, xq: torch.Tensor, sx: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """Sequence parallel: the sum over the ranks of the partial products, reduce-
+        scattered by rows (M a multiple of the world size), so this rank receives its
+        own rows only; the bias is added to them once and their max|.| accumulated for
+        the next FP8 linear.  Returns (bf16 rows [M / world, N], amax bits)."""
+        part = self.ops.gemm(xq, sx, self.weight, self.weight_scale, None, out_dtype=torch.float32)
+        rows = reduce_scatter_rows(part, self.group)
+        amax = self.ops.zeros_amax(xq.device)
+        return self.ops.bias_bf16(rows, self.bias, amax), amax
+
 
 def tp_ffn(x: torch.Tensor, up: ColumnParallelFP8Linear, down: RowParallelFP8Linear) -> torch.Tensor:
     """down(gelu_tanh(up(x))) with up column-parallel and down row-parallel: the GELU
@@ -295,19 +381,38 @@ def tp_ffn(x: torch.Tensor, up: ColumnParallelFP8Linear, down: RowParallelFP8Lin
     return down.forward_quantized(hq, sh)
 
 
+def tp_ffn_sp(h_local: torch.Tensor, h_amax: torch.Tensor | None, up: ColumnParallelFP8Linear,
+              down: RowParallelFP8Linear) -> tuple[torch.Tensor, torch.Tensor]:
+    """Sequence-parallel tp_ffn: this rank's rows in (with their max|.| when known), this
+    rank's rows of down(gelu_tanh(up(h))) out, with their max|.|."""
+    ops = up.ops
+    amax = ops.zeros_amax(h_local.device)
+    hid = up.forward_gathered(h_local, h_amax, down.group, epilogue=L.EPI_GELU_TANH, amax_out=amax)
+    allreduce_amax_(amax, down.group)
+    hq, sh = ops.pack(hid, amax)
+    return down.forward_scattered(hq, sh)
+
+
 class TPBlock(nn.Module):
     """The linears + attention of one DiT block, tensor parallel over heads / hidden
     features: QKV (column, by heads) -> block-causal attention on the local heads ->
-    attention-out (row) -> FFN up (column, GELU-tanh) -> FFN down (row)."""
+    attention-out (row) -> FFN up (column, GELU-tanh) -> FFN down (row).
 
-    def __init__(self, qkv, out, up, down, heads_local: int, head_dim: int):
+    With ``sequence_parallel`` the block's input and output are this rank's token rows
+    (rows [rank * M / world, (rank + 1) * M / world); M a multiple of the world size):
+    the column-parallel linears gather the e4m3 rows of every rank, the row-parallel
+    ones reduce-scatter their partial products (``forward_gathered``,
+    ``forward_scattered``); the NCCL (or gloo) collectives carry both."""
+
+    def __init__(self, qkv, out, up, down, heads_local: int, head_dim: int, sequence_parallel: bool = False):
         super().__init__()
         self.qkv, self.out, self.up, self.down = qkv, out, up, down
         self.hl, self.d = heads_local, head_dim
+        self.sequence_parallel = sequence_parallel
 
     @classmethod
     def from_full(cls, full: dict, heads: int, head_dim: int, rank: int, world: int, group=None, ops=None,
-                  chunks: int = 1, comm: str = "auto"):
+                  chunks: int = 1, comm: str = "auto", sequence_parallel: bool = False):
         """full: name -> (weight e4m3 [N, K], weight_scale [1], bias or None) for
         'qkv', 'out', 'up', 'down' (unsharded, quantized once).  ``chunks``: row blocks of
         the row-parallel GEMMs whose all-reduce overlaps the next block's GEMM;
@@ -318,11 +423,32 @@ class TPBlock(nn.Module):
         out = RowParallelFP8Linear.from_full(*full["out"], rank, world, group, ops, chunks, comm)
         up = ColumnParallelFP8Linear.from_full(*full["up"], rank, world, ops=ops)
         down = RowParallelFP8Linear.from_full(*full["down"], rank, world, group, ops, chunks, comm)
-        return cls(qkv, out, up, down, heads // world, head_dim)
+        return cls(qkv, out, up, down, heads // world, head_dim, sequence_parallel)
 
-    def forward(self, x: torch.Tensor, batch: int, seq: int, prefix_lengths: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, batch: int, seq: int, prefix_lengths: torch.Tensor,
+                x_amax: torch.Tensor | None = None) -> torch.Tensor:
+        """x: the whole activation [batch * seq, width] (replicated), or with
+        ``sequence_parallel`` this rank's rows of it (``x_amax``: their max|.| when the
+        producer accumulated it, e.g. the previous block's ``forward_sp``)."""
+        if self.sequence_parallel:
+            return self.forward_sp(x, batch, seq, prefix_lengths, x_amax)[0]
         M = x.shape[0]
         qkv = self.qkv(x).view(batch, seq, 3, self.hl, self.d)
         o = self.qkv.ops.attention(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2], prefix_lengths)
         h = self.out(o.reshape(M, self.hl * self.d))
         return tp_ffn(h, self.up, self.down)
+
+    def forward_sp(self, x_local: torch.Tensor, batch: int, seq: int, prefix_lengths: torch.Tensor,
+                   x_amax: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """Sequence parallel: this rank's rows in, this rank's rows out with their
+        max|.| (the next block's ``x_amax``)."""
+        group = self.out.group
+        M = batch * seq
+        qkv = self.qkv.forward_gathered(x_local, x_amax, group).view(batch, seq, 3, self.hl, self.d)
+        o = self.qkv.ops.attention(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2], prefix_lengths)
+        o2 = o.reshape(M, self.hl * self.d)
+        amax = self.qkv.ops.amax_bits(o2)
+        allreduce_amax_(amax, group)
+        oq, so = self.qkv.ops.pack(o2, amax)
+        h_local, h_amax = self.out.forward_scattered(oq, so)
+        return tp_ffn_sp(h_local, h_amax, self.up, self.down)

@@ -44,3 +44,10 @@ class OracleOps:
 
     def attention(self, q, k, v, L):
         return O.block_causal_attention(q, k, v, L)
+
+    def bias_bf16(self, x, bias, amax):
+        y = x.float() + (bias.float() if bias is not None else 0.0)
+        y = y.to(torch.bfloat16)
+        cur = _bits_to_float(amax)
+        amax.fill_(_float_to_bits(max(cur, y.float().abs().max().item())))
+        return y

@@ -6,6 +6,9 @@
   out / FFN-down with fp32 partial all-reduce) matches the single-GPU block within
   the BASELINE tolerances, in both forms (one all-reduce, or row blocks whose
   all-reduces run on a side stream);
+* the sequence-parallel block (row shards in and out: reduce-scatter of the partial
+  products, e4m3 rows all-gathered with the global scale) equals the all-reduce form
+  bit for bit on each rank's rows, two blocks in a row;
 * with the row-parallel sums over NVLink peer memory (qik.tp_comm.PeerRowReduce:
   GEMM epilogue stores into the owner's memory, owner reduce + bf16 gather) the block
   is bit-identical to the all-reduce form (same fp32 partial products; for two ranks
@@ -72,6 +75,14 @@ def _worker(rank, world, port, outdir):
         Lp = torch.arange(S, dtype=torch.int32, device=dev)
         Lp[64:] = S - 1
         res["block"] = blk(xb, B, S, Lp).float().cpu().numpy()
+        # sequence parallel: this rank's rows in and out, two blocks in a row
+        bsp = PX.TPBlock.from_full(full, heads, d, rank, world, sequence_parallel=True)
+        lo_r, hi_r = rank * (B * S // world), (rank + 1) * (B * S // world)
+        y1, a1 = bsp.forward_sp(xb[lo_r:hi_r].contiguous(), B, S, Lp)
+        y1c = y1.clone()
+        y2, _ = bsp.forward_sp(y1, B, S, Lp, a1)
+        res["block_sp"] = (lo_r, hi_r, y1c.float().cpu().numpy(), y2.float().cpu().numpy())
+        res["block_twice"] = blk(blk(xb, B, S, Lp), B, S, Lp).float().cpu().numpy()
         # row-parallel GEMMs in 4 row blocks, each all-reduce on a side stream
         blk4 = PX.TPBlock.from_full(full, heads, d, rank, world, chunks=4, comm="nccl")
         res["block4"] = blk4(xb, B, S, Lp).float().cpu().numpy()
@@ -140,4 +151,9 @@ def test_sharded_quantization_and_tp_block_on_two_gpus():
         assert O.relf(torch.from_numpy(r["block4"]), ref) <= 5e-3
         assert r["status"] == 0
         assert all(np.array_equal(yp, r["block"]) for yp in r["block_peer"])
+        # sequence parallel (reduce-scatter + e4m3 all-gather): on two ranks the same
+        # two-term sums and the same e4m3 bytes as the all-reduce form
+        lo_r, hi_r, y1, y2 = r["block_sp"]
+        assert np.array_equal(y1, r["block"][lo_r:hi_r])
+        assert np.array_equal(y2, r["block_twice"][lo_r:hi_r])
         assert r["direct_equal"] == [True, True, True]

@@ -5,7 +5,8 @@ Checks that (1) token-row shards quantized with the 4-byte global-amax all-reduc
 exactly the bytes and scale of the unsharded quantization; (2) the tensor-parallel
 FFN and DiT block (column/row parallel FP8 linears, head-split attention, fp32
 partial all-reduce) reproduce the single-rank result; (3) weight sharding helpers
-cut the fused QKV weight by heads."""
+cut the fused QKV weight by heads; (4) the sequence-parallel block (row shards in and
+out) equals the replicated form."""
 import os
 import pickle
 import socket
@@ -63,6 +64,16 @@ def _worker(rank, world, port, outdir):
         Lp[4:] = S - 1
         res["ffn"] = PX.tp_ffn(xb, blk.up, blk.down).float().numpy()
         res["block"] = blk(xb, B, S, Lp).float().numpy()
+        # (4) the sequence-parallel form: this rank's rows in and out
+        sp = PX.TPBlock.from_full(full, heads, d, rank, world, ops=ops, sequence_parallel=True)
+        lo, hi = rank * (B * S // world), (rank + 1) * (B * S // world)
+        y_sp, amax_sp = sp.forward_sp(xb[lo:hi].contiguous(), B, S, Lp)
+        res["block_sp"] = (lo, hi, y_sp.float().numpy(), int(amax_sp.reshape(-1)[0].item()))
+        y2, _ = sp.forward_sp(y_sp, B, S, Lp, amax_sp)   # a second block fed the first one's amax
+        res["block_sp2"] = y2.float().numpy()
+        res["block2"] = blk(blk(xb, B, S, Lp), B, S, Lp).float().numpy()
+        h_sp, _ = PX.tp_ffn_sp(xb[lo:hi].contiguous(), None, sp.up, sp.down)
+        res["ffn_sp"] = h_sp.float().numpy()
         with open(os.path.join(outdir, f"r{rank}.pkl"), "wb") as f:
             pickle.dump(res, f)
     finally:
@@ -103,6 +114,20 @@ def test_tp_ffn_matches_single_rank(results):
         y = torch.from_numpy(r["ffn"])
         assert O.relf(y, ref) <= 5e-3
         assert (y - ref).abs().max().item() <= 2e-2 + 0.01 * ref.abs().max().item()
+
+
+def test_sequence_parallel_block_equals_replicated_form(results):
+    """Row shards in and out (reduce-scatter, e4m3 all-gather with the global scale):
+    the concatenated rows equal the replicated TP block's output bit for bit on the same
+    ranks (the same sums; the same e4m3 bytes), two blocks in a row included, and the
+    returned amax is max|output| of the rank's rows."""
+    for runs in results:
+        for r in runs:
+            lo, hi, y, amax_bits = r["block_sp"]
+            assert np.array_equal(y, r["block"][lo:hi])
+            assert amax_bits == int(np.float32(np.abs(y).max()).view(np.int32))
+            assert np.array_equal(r["block_sp2"], r["block2"][lo:hi])
+            assert np.array_equal(r["ffn_sp"], r["ffn"][lo:hi])
 
 
 def test_tp_block_matches_single_rank(results):
