@@ -770,9 +770,9 @@ def tp_stack(device: torch.device, rank: int, world: int, flush: L2Flush, iters:
                         red.close()
         return float(t.item())
 
-    def stack_output(comm: str, sp: bool = False) -> torch.Tensor:
+    def stack_output(comm: str, sp: bool = False, n_blocks: int = 4) -> torch.Tensor:
         blocks = [PX.TPBlock.from_full(full, H, D, rank, world, chunks=1, comm=comm, sequence_parallel=sp)
-                  for full in fulls]
+                  for full in fulls[:n_blocks]]
         h = make_stack(blocks, sp)().clone()
         torch.cuda.synchronize(device)
         if world > 1:
@@ -813,6 +813,23 @@ def tp_stack(device: torch.device, rank: int, world: int, flush: L2Flush, iters:
                       "relF": float(same[5].item()),
                       "compared": "each rank's rows of the 4-block stack output, sequence parallel vs the "
                                   "NCCL all-reduce form"}}
+        # one block of every form against the single-GPU block, computed by rank 0 alone
+        # (a group of one rank: no collective) and broadcast
+        g0 = torch.distributed.new_group([0])
+        if rank == 0:
+            ref1 = PX.TPBlock.from_full(fulls[0], H, D, 0, 1, group=g0)(x, B, S, Lt).contiguous()
+        else:
+            ref1 = torch.empty(M, K, dtype=torch.bfloat16, device=device)
+        torch.distributed.broadcast(ref1, src=0)
+        one = torch.tensor([relf(stack_output("peer", n_blocks=1), ref1),
+                            relf(stack_output("nccl", n_blocks=1), ref1),
+                            relf(stack_output("nccl", sp=True, n_blocks=1), ref1[lo_sp:hi_sp])],
+                           dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(one, op=torch.distributed.ReduceOp.MAX)
+        parity["one_block_vs_single_gpu_relF"] = {
+            "peer": float(one[0].item()), "nccl_allreduce": float(one[1].item()),
+            "sequence_parallel": float(one[2].item()), "gate": 5e-3,
+            "pass": bool(one.max().item() <= 5e-3)}
     ms_peer = timed(1, "peer")
     ms_nccl = timed(1, "nccl") if world > 1 else ms_peer
     ms_overlap = timed(4, "nccl") if world > 1 else ms_peer
