@@ -636,7 +636,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // or single CTAs with 128 x BN tiles (BN = 256, 128 or 64).
 //
 // Shape -> tile configuration, from the configs[4] sweep with every configuration
-// forced: CTA pairs from M = 257 up, and at M = 129-256 once N >= 12288; at M = 129-256
+// forced: CTA pairs from M = 257 up (but 128 x 256 single-CTA tiles for 257-1024 rows
+// of an output at most 3072 wide), and at M = 129-256 once N >= 12288; at M = 129-256
 // with a narrower N, 128 x 128 single-CTA tiles (more CTAs on the same work) win; at
 // most 128 rows, a single 128-row tile spans M and the N tiles spread the weight
 // stream over the SMs.  Narrower CTA-pair tiles (256 x 240, 256 x 192), chosen to fill
@@ -650,6 +651,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // flight per SM instead of 6; the scatter (tensor-parallel) epilogue keeps the
 // untransposed tiles.
 static int gemm_pick_cfg(int64_t M, int64_t N, bool scatter = false) {
+  // up to 1024 rows of a narrow output (N <= 3072), 128 x 256 single-CTA tiles: the same
+  // CTA count as pairs at M = 1024 and measured faster there (18.5 vs 20.5 us)
+  if (M > 2 * kGemmBM && M <= 8 * kGemmBM && N <= 3072 && !scatter) return QIK_GEMM_TILE_SINGLE_256;
   if (M > 2 * kGemmBM) return QIK_GEMM_TILE_PAIR_256;
   if (M > kGemmBM) return N >= 12288 ? QIK_GEMM_TILE_PAIR_256 : QIK_GEMM_TILE_SINGLE_128;
   if (M <= 16 && !scatter) return QIK_GEMM_TILE_SWAP_16;

@@ -286,7 +286,9 @@ class FP8Linear(nn.Module):
         x2 = x.reshape(B * S, K)
         xq, s_a = quantize_tensorwise(x2) if amax is None else quantize_from_amax(x2, amax)
         res = residual.contiguous()
-        tab = table.contiguous()
+        # the table may be a column slice of a wider table (row pitch a multiple of 8)
+        tab = table if (table.dim() == 2 and table.stride(-1) == 1 and table.stride(0) % 8 == 0
+                        and table.stride(0) >= table.shape[1] and table.data_ptr() % 16 == 0) else table.contiguous()
         if tab.shape[0] < (2 * B if target_token_mask is not None else B) or tab.shape[1] != self.out_features:
             raise ValueError(f"FP8Linear.forward_gate_residual: gate table {tuple(tab.shape)} too small")
         mask = _u8_mask(target_token_mask, S, x.device)
@@ -297,7 +299,7 @@ class FP8Linear(nn.Module):
             L.check(lib.qik_fp8_gemm_gate_residual(xq.data_ptr(), self.weight.data_ptr(), B * S, self.out_features, K,
                                                    xq.stride(0), self.weight.stride(0), s_a.data_ptr(),
                                                    self.weight_scale.data_ptr(), L.ptr(bias), res.data_ptr(),
-                                                   self.out_features, tab.data_ptr(), self.out_features, L.ptr(mask),
+                                                   self.out_features, tab.data_ptr(), tab.stride(0), L.ptr(mask),
                                                    B, S, out.data_ptr(), self.out_features,
                                                    L.status_word(x.device).data_ptr(), L.stream_ptr()),
                     "qik_fp8_gemm_gate_residual")

@@ -50,6 +50,23 @@ def _build_prefix_lengths(segments: list[tuple[int, int, bool]], prefix_len: int
     return L
 
 
+_prefix_cache: dict = {}
+
+
+def _prefix_lengths_on(segments, prefix_len: int, seq_len: int, device: torch.device) -> torch.Tensor:
+    """_build_prefix_lengths on ``device``, kept per (segments, lengths, device): every
+    block of a forward pass reads the same read-only L, so it is built once (a few
+    entries at most: one per distinct sequence layout, oldest dropped past 16)."""
+    key = (tuple(tuple(x) for x in segments), prefix_len, seq_len, str(device))
+    L = _prefix_cache.get(key)
+    if L is None:
+        if len(_prefix_cache) >= 16:
+            _prefix_cache.pop(next(iter(_prefix_cache)))
+        L = _build_prefix_lengths(segments, prefix_len, seq_len, device)
+        _prefix_cache[key] = L
+    return L
+
+
 def _linear(mod, x: torch.Tensor, amax: torch.Tensor | None, scale: torch.Tensor | None = None) -> torch.Tensor:
     """mod(x), with the producer's amax of x when mod is an FP8 linear; with ``scale``,
     x is already the e4m3 input of the FP8 linear mod and ``scale`` its dynamic scale."""
@@ -135,6 +152,7 @@ class QwenImage21KernelProcessor:
         hidden_states_amax: torch.Tensor | None = None,
         hidden_states_scale: torch.Tensor | None = None,
         gate_residual: tuple | None = None,
+        out_amax: torch.Tensor | None = None,
     ) -> torch.Tensor:
         # hidden_states_scale: hidden_states is then the e4m3 input of the QKV linears
         # (fused_layer_norm_modulate_e4m3), quantized with this scale
@@ -167,12 +185,16 @@ class QwenImage21KernelProcessor:
             layer_cache.store(key[:, cache_write_slice], value[:, cache_write_slice])
 
         # max|attention output| for the FP8 out-projection, accumulated by the kernel
-        out_amax = _new_amax(query) if isinstance(attn.to_out[0], FP8Linear) else None
+        # (out_amax: a zeroed int32 word from the caller, e.g. the fused block's, or a new one)
+        if not isinstance(attn.to_out[0], FP8Linear):
+            out_amax = None
+        elif out_amax is None:
+            out_amax = _new_amax(query)
         if segments is not None:
             # prefill over the full joint sequence
             assert key_valid is None or key_valid.dim() == 2
             prefix_end = segments[-1][1] if segments else 0
-            L = _build_prefix_lengths(segments, prefix_end, S, query.device)
+            L = _prefix_lengths_on(segments, prefix_end, S, query.device)
             out = block_causal_flash_attention(query, key, value, L, key_valid, cache_k=None, cache_v=None,
                                                amax_out=out_amax)
         else:
@@ -247,6 +269,17 @@ class QwenImage21KernelBlock(torch.nn.Module):
         ours = isinstance(getattr(self.attn, "processor", None), QwenImage21KernelProcessor)
         # modulation rows the gates read: the samples' rows, and the t = 0 rows with a mask
         gate_rows = hidden_states.shape[0] * (2 if target_token_mask is not None else 1)
+        fuse_gate1 = ours and _fuses_gate(self.attn.to_out[0], self.attn.to_out[1])
+        fuse_gate2 = _fuses_gate(self.img_mlp.out)
+        table1 = table2 = None
+        if fuse_gate1 and fuse_gate2:
+            # both gates' tables in one launch: columns [inner, 4 inner) of the modulation
+            # (mod1.gate, mod2.scale, mod2.gate), the two gate slices used in place
+            tables = gate_table(modulation, inner, gate_rows, 3 * inner)
+            table1, table2 = tables[:, :inner], tables[:, 2 * inner:]
+        # the max|.| words of the attention output and of the MLP's hidden activation:
+        # one zeroed allocation
+        amaxes = torch.zeros(2, dtype=torch.int32, device=hidden_states.device) if ours else None
         if ours:
             if _takes_e4m3(*qkv_mods):
                 # the norm's only consumers are FP8 linears: it emits their e4m3 input
@@ -261,9 +294,12 @@ class QwenImage21KernelBlock(torch.nn.Module):
         else:
             img_mod = fused_layer_norm_modulate(hidden_states, modulation, 0, mod_stride, target_token_mask,
                                                 self._eps)
-        if ours and _fuses_gate(self.attn.to_out[0], self.attn.to_out[1]):
+        if ours:
+            attn_kwargs["out_amax"] = amaxes[0:1]
+        if fuse_gate1:
             # the out-projection's GEMM epilogue adds the gated attention output to the residual
-            table1 = gate_table(modulation, inner, gate_rows, inner)
+            if table1 is None:
+                table1 = gate_table(modulation, inner, gate_rows, inner)
             attn_kwargs["gate_residual"] = (hidden_states, table1, target_token_mask)
             hidden_states = self.attn(hidden_states=img_mod, **attn_kwargs)
         else:
@@ -280,7 +316,7 @@ class QwenImage21KernelBlock(torch.nn.Module):
             amax2 = _new_amax(hidden_states)
             img_mod2 = fused_layer_norm_modulate(hidden_states, modulation, 2 * inner, mod_stride, target_token_mask,
                                                  self._eps, amax_out=amax2)
-        amax3 = _new_amax(hidden_states)
+        amax3 = amaxes[1:2] if amaxes is not None else _new_amax(hidden_states)
         if fused_up is not None and scale2 is not None and fused_up.out_features % 256 == 0:
             mlp_mid = _swiglu_linear(fused_up, img_mod2, scale2, amax3)
         else:
@@ -290,8 +326,9 @@ class QwenImage21KernelBlock(torch.nn.Module):
                 gate = _linear(self.img_mlp.gate_layer, img_mod2, amax2, scale2)
                 up = _linear(self.img_mlp.proj, img_mod2, amax2, scale2)
             mlp_mid = fused_swiglu(gate, up, amax_out=amax3)
-        if _fuses_gate(self.img_mlp.out):
-            table2 = gate_table(modulation, 3 * inner, gate_rows, inner)
+        if fuse_gate2:
+            if table2 is None:
+                table2 = gate_table(modulation, 3 * inner, gate_rows, inner)
             return _gate_linear(self.img_mlp.out, mlp_mid, amax3, hidden_states, table2, target_token_mask)
         mlp_out = _linear(self.img_mlp.out, mlp_mid, amax3)
         return fused_gate_residual(hidden_states, mlp_out, modulation, 3 * inner, target_token_mask)
