@@ -605,14 +605,14 @@ def dit_block_product_case(device: torch.device, g: torch.Generator) -> dict:
 
 PROFILE_CASES = ("attention_cfg4_prefill", "attention_cfg4_decode_fp8_slab", "dit_block_1024px_cfg2",
                  "dit_block_1024px_cfg2_gelu_ffn", "fused_ops_t2i", "modulation_linear", "quantizer_4352",
-                 "quantizer_9472", "quantizer_16384")
+                 "quantizer_9472", "quantizer_16384", "gemm_256x3072", "gemm_256x12288")
 
 
 def profile_case(device: torch.device, name: str) -> None:
     """Runs one workload three times (the launches an ncu capture selects from); for
-    fused_ops_t2i each of the fused ops three times, for modulation_linear the FP8 linear
-    and for quantizer_<M> the activation quantizer three times, an L2 flush before every
-    launch."""
+    fused_ops_t2i each of the fused ops three times, for modulation_linear and gemm_<M>x<N>
+    the FP8 linear and for quantizer_<M> the activation quantizer three times, an L2 flush
+    before every launch."""
     g = torch.Generator(device=device).manual_seed(7)
     if name.startswith("quantizer_"):
         # the dynamic activation quantizer (qik_quantize_act) on M x 3072 bf16 rows
@@ -622,6 +622,16 @@ def profile_case(device: torch.device, name: str) -> None:
         for r in range(3):
             flush(r)
             F.quantize_tensorwise(x)
+    elif name.startswith("gemm_"):
+        # a configs[4] FP8 linear (K = 3072) at skinny M, default tile configuration
+        from qik import fp8 as F
+        M, N = (int(v) for v in name.split("_")[1].split("x"))
+        wq, sw = F.quantize_weight_tensorwise(torch.randn(N, 3072, device=device, generator=g) * 0.02)
+        xq, sx = F.quantize_tensorwise(torch.randn(M, 3072, device=device, generator=g).to(torch.bfloat16))
+        flush = L2Flush(device)
+        for r in range(3):
+            flush(r)
+            F.fp8_gemm(xq, sx, wq, sw)
     elif name == "modulation_linear":
         # the DiT block's timestep-modulation FP8 linear: M = 2 (CFG batch) x 3072 -> 18432
         from qik import fp8 as F
