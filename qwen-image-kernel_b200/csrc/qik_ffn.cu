@@ -82,7 +82,8 @@ static int fp8_ffn_chain(const void* x, const uint32_t* x_amax, const float* x_s
   if (!rc)
     rc = launch_fp8_gemm(xq, w_up, M, hidden, K, K, K, sx, s_up, b_up, h, hidden, QIK_DTYPE_BF16,
                          QIK_EPI_GELU_TANH, &hdr->amax_h, status, st, x_scale == nullptr);
-  if (!rc) rc = launch_pack_act(h, M * hidden, &hdr->amax_h, hq, &hdr->sh, st, true);
+  // backward: h was just written by GEMM1 in row order and exceeds what L2 keeps of it
+  if (!rc) rc = launch_pack_act(h, M * hidden, &hdr->amax_h, hq, &hdr->sh, st, true, true);
   if (!rc)
     rc = launch_fp8_gemm(hq, w_down, M, K, hidden, hidden, hidden, &hdr->sh, s_down, b_down, y, K, QIK_DTYPE_BF16,
                          QIK_EPI_SCALE, nullptr, status, st, true);

@@ -72,7 +72,7 @@ cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
 // kernel in the stream).
 int launch_amax(const void* x, int dtype, int64_t n, uint32_t* amax_bits, cudaStream_t st, bool pdl);
 int launch_pack_act(const void* x, int64_t n, const uint32_t* amax_bits, uint8_t* q, float* scale_out,
-                    cudaStream_t st, bool pdl);
+                    cudaStream_t st, bool pdl, bool backward = false);
 // Single-pass activation quantizer (one cooperative kernel; x, q and ws 16-byte aligned):
 // ws is its 1 KB workspace (qik_quant_workspace_bytes), whose barrier word must be
 // zero before the first call and is left ready for the next call by each call that

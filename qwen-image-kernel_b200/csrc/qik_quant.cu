@@ -101,10 +101,14 @@ __global__ void scale_finalize_kernel(const uint32_t* __restrict__ amax_bits, fl
 // ---------------------------------------------------------------- packs
 // Activation: 16 bf16 -> 16 e4m3 per thread iteration (two 16-byte loads, one
 // 16-byte store).
+// backward: the 16-element vectors are visited from the last one down (same codes).
+// For an x its producer has just written in row order and that L2 kept only in part,
+// the lines written last are read first, while they are still in L2; a forward walk
+// over such an x misses on nearly every line.
 __global__ void __launch_bounds__(kQuantThreads) pack_act_kernel(const uint16_t* __restrict__ x, int64_t n,
                                                                  const uint32_t* __restrict__ amax_bits,
                                                                  uint8_t* __restrict__ q,
-                                                                 float* __restrict__ scale_out) {
+                                                                 float* __restrict__ scale_out, int backward) {
   pdl_wait();
   const float s = scale_from_amax_bits(__ldg(amax_bits));
   const float inv = act_inverse(s);
@@ -116,7 +120,8 @@ __global__ void __launch_bounds__(kQuantThreads) pack_act_kernel(const uint16_t*
     const int64_t nvec = n >> 4;
     const uint4* xv = reinterpret_cast<const uint4*>(x);
     uint4* qv = reinterpret_cast<uint4*>(q);
-    for (int64_t i = tid; i < nvec; i += nthreads) {
+    for (int64_t k = tid; k < nvec; k += nthreads) {
+      const int64_t i = backward ? nvec - 1 - k : k;
       const uint4 a = __ldg(xv + 2 * i), b = __ldg(xv + 2 * i + 1);
       uint4 o;
       o.x = pack8_e4m3(a, inv, o.y);
@@ -424,9 +429,9 @@ int launch_amax(const void* x, int dtype, int64_t n, uint32_t* amax_bits, cudaSt
 }
 
 int launch_pack_act(const void* x, int64_t n, const uint32_t* amax_bits, uint8_t* q, float* scale_out,
-                    cudaStream_t st, bool pdl) {
+                    cudaStream_t st, bool pdl, bool backward) {
   QIK_TRY_CUDA(launch_kernel(pack_act_kernel, dim3(grid_for(n, 16)), dim3(kQuantThreads), 0, st, pdl,
-                             static_cast<const uint16_t*>(x), n, amax_bits, q, scale_out));
+                             static_cast<const uint16_t*>(x), n, amax_bits, q, scale_out, backward ? 1 : 0));
   return check_launch("pack_act_kernel");
 }
 
@@ -465,7 +470,9 @@ int qik_quantize_act_from_amax(const void* x, int64_t n, const uint32_t* amax_bi
   QIK_REQUIRE((x && q) || n == 0, "qik_quantize_act_from_amax: x/q is NULL");
   QIK_REQUIRE(amax_bits, "qik_quantize_act_from_amax: amax_bits is NULL");
   QIK_REQUIRE(n >= 0, "qik_quantize_act_from_amax: negative n");
-  return launch_pack_act(x, n, amax_bits, q, scale_out, static_cast<cudaStream_t>(stream), false);
+  // backward: x is typically the output its producer (GEMM, attention, SwiGLU) has just
+  // written, and whatever part of it L2 kept is the part written last
+  return launch_pack_act(x, n, amax_bits, q, scale_out, static_cast<cudaStream_t>(stream), false, true);
 }
 
 static int quantize_act_impl(const void* x, int64_t n, uint8_t* q, float* scale_out, void* ws, cudaStream_t st,
