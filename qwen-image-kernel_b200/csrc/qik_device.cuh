@@ -125,6 +125,14 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, int32_t x, in
                "r"(x), "r"(y), "r"(smem_u32(smem_src))
                : "memory");
 }
+// The same store with an L2 cache policy (createpolicy) for the written lines.
+__device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap* m, int32_t x, int32_t y, const void* smem_src,
+                                                  uint64_t policy) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%1, %2}], [%3], %4;" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(x), "r"(y), "r"(smem_u32(smem_src)), "l"(policy)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until at most 1 committed bulk group of this thread still reads shared memory.
 __device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }

@@ -79,9 +79,12 @@ static int fp8_ffn_chain(const void* x, const uint32_t* x_amax, const float* x_s
     rc = launch_amax(x, QIK_DTYPE_BF16, M * K, &hdr->amax_x, st, false);
     if (!rc) rc = launch_pack_act(x, M * K, &hdr->amax_x, xq_ws, &hdr->sx, st, true);
   }
+  // h larger than a few MB: stored with an L2 evict-last policy, so more of it is still
+  // in L2 when the pack below reads it
+  const bool keep_h = static_cast<int64_t>(M) * hidden * 2 > (int64_t{32} << 20);
   if (!rc)
     rc = launch_fp8_gemm(xq, w_up, M, hidden, K, K, K, sx, s_up, b_up, h, hidden, QIK_DTYPE_BF16,
-                         QIK_EPI_GELU_TANH, &hdr->amax_h, status, st, x_scale == nullptr);
+                         QIK_EPI_GELU_TANH, &hdr->amax_h, status, st, x_scale == nullptr, keep_h);
   // backward: h was just written by GEMM1 in row order and exceeds what L2 keeps of it
   if (!rc) rc = launch_pack_act(h, M * hidden, &hdr->amax_h, hq, &hdr->sh, st, true, true);
   if (!rc)

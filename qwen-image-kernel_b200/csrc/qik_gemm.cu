@@ -62,6 +62,7 @@ struct GemmParams {
   uint32_t* scat_cnt[QIK_TP_MAX_WORLD];
   int scat_rows;
   int group_m;  // raster: row tiles per group (1 = row-major), see tile_coords
+  int keep_out_l2;  // bf16 output stored with an L2 evict-last policy (its consumer follows at once)
   // QIK_EPI_RMS_ROPE (the fused QKV linear): columns [0, rms_cols) are the q heads then
   // the k heads, 128 columns each, normalised with rms_w[0] (the first rms_cols / 2
   // columns) or rms_w[1] and rotated by rope_cos / rope_sin [rope_seq, 64] at position
@@ -376,7 +377,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0 && row0 < p.M) {
-          tma_store_2d(&tmC, col0, row0, sb);
+          if (p.keep_out_l2)
+            tma_store_2d_hint(&tmC, col0, row0, sb, l2_evict_last_policy());
+          else
+            tma_store_2d(&tmC, col0, row0, sb);
           bulk_commit_group();
         }
         buf ^= 1;
@@ -830,9 +834,16 @@ int launch_fp8_gemm_ex(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N,
 
 int launch_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
                     const float* scale_a, const float* scale_b, const void* bias, void* C, int64_t ldc, int out_dtype,
-                    int epilogue, uint32_t* amax_out, int* status, cudaStream_t stream, bool pdl) {
+                    int epilogue, uint32_t* amax_out, int* status, cudaStream_t stream, bool pdl, bool keep_out_l2) {
+  if (!keep_out_l2)
+    return launch_fp8_gemm_ex(A, B, M, N, K, lda, ldb, scale_a, scale_b, bias, C, ldc, out_dtype, epilogue, amax_out,
+                              status, stream, pdl, nullptr, QIK_GEMM_TILE_AUTO);
+  GemmParams extra;
+  memset(&extra, 0, sizeof(extra));
+  extra.keep_out_l2 = 1;
+  // (an extras block keeps the scatter-safe tile choice: no operand-swapped tiny-M tiles)
   return launch_fp8_gemm_ex(A, B, M, N, K, lda, ldb, scale_a, scale_b, bias, C, ldc, out_dtype, epilogue, amax_out,
-                            status, stream, pdl, nullptr, QIK_GEMM_TILE_AUTO);
+                            status, stream, pdl, &extra, QIK_GEMM_TILE_AUTO);
 }
 
 }  // namespace qik

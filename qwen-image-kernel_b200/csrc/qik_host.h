@@ -82,6 +82,7 @@ int launch_quant_single_pass(const void* x, int64_t n, uint8_t* q, float* scale_
                              bool clear_bar);
 int launch_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
                     const float* scale_a, const float* scale_b, const void* bias, void* C, int64_t ldc, int out_dtype,
-                    int epilogue, uint32_t* amax_out, int* status, cudaStream_t st, bool pdl);
+                    int epilogue, uint32_t* amax_out, int* status, cudaStream_t st, bool pdl,
+                    bool keep_out_l2 = false);
 
 }  // namespace qik
