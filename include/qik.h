@@ -395,7 +395,7 @@ int qik_swiglu(const void* gate, int64_t ld_gate, const void* up, int64_t ld_up,
 /* ---------------------------------------------------------------- tensor parallel
  * Row-parallel FP8 linear with the reduction over peer memory, replacing the
  * fp32 partial product + NCCL all-reduce of the tensor-parallel block stack
- * (4-block TP; the reference itself is single-GPU: its
+ * (4 DiT blocks tensor parallel over the GPUs; the reference itself is single-GPU: its
  * FP8Linear.forward is qwen_image_kernel/fp8.py:78-90).  One process per GPU; every
  * rank maps its peers' workspaces (CUDA IPC) and calls, in the same order:
  *   qik_fp8_gemm_scatter   (its GEMM's fp32 rows stored straight into the owner

@@ -230,7 +230,7 @@ def block_causal_attention(query, key, value, prefix_lengths, key_valid=None, ca
     produce zeros (the kernel's `l == 0` epilogue, triton_attention.py:166).
     Returns [B,SQ,H,D] in ``out_dtype`` (bf16 like the reference, or fp32 for
     tolerance checks on the pre-cast values).  ``slab_v_bf16=False`` keeps the slab V
-    dequant in fp32 (fl32(v8) * vsc, the BASELINE's fp32 dequant path) instead of
+    dequant in fp32 (fl32(v8) * vsc, the fp32-accumulated dequant path parity is gated on) instead of
     the reference kernel's per-element bf16 rounding.
     """
     B, SQ, H, D = query.shape

@@ -2,7 +2,7 @@
 //
 // y = down(gelu_tanh(up(x))) with both linears FP8 per-tensor: two applications of
 // FP8Linear.forward (qwen_image_kernel/fp8.py:78-90) with GELU-tanh between them
-// (the reference block uses SwiGLU through a fused up
+// (the DiT FFN pair 3072 -> 12288 -> 3072; the reference block uses SwiGLU through a fused up
 // projection, processors.py:180-187), the hidden activation re-quantized
 // dynamically.  Four kernels in one stream (five without the single pass):
 //   quantize(x) -> GEMM1 (+GELU, amax(h)) -> pack(h) -> GEMM2

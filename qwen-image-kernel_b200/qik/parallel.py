@@ -1,6 +1,7 @@
 """Multi-GPU execution of the FP8 DiT hot path: one process per GPU, torch.distributed.
 
-Two layouts (the reference itself is single-GPU; these follow the BASELINE configs):
+Three layouts (the reference itself is single-GPU; these serve the token-row sweep and the
+tensor-parallel layer stack):
 
 * **Shards** -- token rows (or the two CFG branches) are independent work: each rank
   runs the unchanged single-GPU path on its own rows, with no collective on the data

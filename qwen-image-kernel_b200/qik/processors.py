@@ -6,8 +6,8 @@ Same names and call signatures as ``qwen_image_kernel/processors.py``
 * ``_build_prefix_lengths`` (processors.py:22-36): the block-causal mask of a joint
   [prefix ; target] sequence collapses to one inclusive key limit per query row --
   text rows are causal (L = q), image-block rows see the whole prefix up to the end
-  of their block (L = end - 1), target rows see everything (L = S - 1).  BASELINE's
-  "causal length" is the exclusive count L + 1.
+  of their block (L = end - 1), target rows see everything (L = S - 1).  The
+  per-row "causal length" of the block-causal attention is the exclusive count L + 1.
 * ``QwenImage21KernelProcessor`` (processors.py:39-126): fused QKV FP8 GEMM, per-head
   RMSNorm + RoPE, prefill (block-causal over the joint sequence) or decode (target
   rows over [cached prefix ; fresh target] without concatenation), output FP8 GEMM.
