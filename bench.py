@@ -816,8 +816,10 @@ def tp_stack(device: torch.device, rank: int, world: int, flush: L2Flush, iters:
                   "relF": float(same[2].item()), "max_abs_output": float(same[6].item()),
                   "expected": "bit-identical on 2 ranks (two-term fp32 sums commute); on more ranks NCCL's "
                               "summation order differs from the rank-order sum in the last bits, and every "
-                              "later FP8 linear re-quantizes with a dynamic scale, so the 4-block outputs "
-                              "differ at rounding level (relF)",
+                              "later FP8 linear re-quantizes with a dynamic per-tensor scale over a stack "
+                              "with no normalisation, so after 4 blocks the forms can differ well beyond "
+                              "rounding (relF 0.07-0.09 measured on 4 and 8 ranks); one block of every "
+                              "form is gated against the single-GPU block below",
                   "sequence_parallel_vs_allreduce": {
                       "bit_identical_all_ranks": bool(same[3].item() == 1.0), "max_abs_diff": float(same[4].item()),
                       "relF": float(same[5].item()),
