@@ -188,6 +188,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
+  // launched as a programmatic dependent: everything above touches no global memory;
+  // the predecessor's results are read from here on
+  pdl_wait();
   // per-row limits; the largest L of the block decides how many key tiles exist
   int my_L = -1;
   if (warp >= 4) {
@@ -516,6 +519,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  pdl_trigger();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -625,7 +629,9 @@ extern "C" int qik_block_causal_attention(const qik_attn_args* args, int* status
   QIK_TRY_CUDA(attr_rc);
   // x = (b, h), y = query block (numbered from the last block: heaviest first)
   dim3 grid(static_cast<unsigned>(A.B * A.H), static_cast<unsigned>((A.SQ + kAttnRows - 1) / kAttnRows));
-  attn_fwd_kernel<<<grid, kAttnThreads, AttnSmem::kBytes, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, tck, tcv,
-                                                                                                  d);
+  // a programmatic dependent of the previous kernel in the stream (its prologue overlaps
+  // that kernel's tail; the kernel waits for it before reading any input)
+  QIK_TRY_CUDA(launch_kernel(attn_fwd_kernel, grid, dim3(kAttnThreads), AttnSmem::kBytes,
+                             static_cast<cudaStream_t>(stream), true, tq, tk, tv, tck, tcv, d));
   return check_launch("attn_fwd_kernel");
 }

@@ -798,6 +798,7 @@ int qik_layer_norm_modulate_e4m3(const void* x, int64_t B, int64_t S, int64_t D,
 __global__ void __launch_bounds__(kThreads) gate_table_kernel(const uint16_t* __restrict__ mod, int64_t mod_stride,
                                                               int64_t gate_off, int64_t rows, int64_t D,
                                                               uint16_t* __restrict__ table) {
+  pdl_wait();  // the modulation rows come from the previous kernel
   const int64_t nv = D >> 3, total = rows * nv;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -820,8 +821,10 @@ int qik_gate_table(const void* modulation, int64_t mod_rows, int64_t mod_stride,
   QIK_REQUIRE(aligned_elems(mod_stride) && aligned_elems(gate_off) && gate_off >= 0 && gate_off + D <= mod_stride,
               "qik_gate_table: modulation stride/offset must be multiples of 8 with offset + D <= stride");
   const int grid = grid_cap((mod_rows * (D / 8) + kThreads - 1) / kThreads, 1);
-  gate_table_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint16_t*>(modulation), mod_stride, gate_off, mod_rows, D, static_cast<uint16_t*>(table));
+  // a programmatic dependent of the previous kernel (the modulation linear)
+  QIK_TRY_CUDA(launch_kernel(gate_table_kernel, dim3(grid), dim3(kThreads), 0, static_cast<cudaStream_t>(stream), true,
+                             static_cast<const uint16_t*>(modulation), mod_stride, gate_off, mod_rows, D,
+                             static_cast<uint16_t*>(table)));
   return check_launch("gate_table_kernel");
 }
 

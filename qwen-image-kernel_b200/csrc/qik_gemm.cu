@@ -921,7 +921,7 @@ extern "C" int qik_fp8_gemm_qkv_rms_rope(const uint8_t* A, const uint8_t* B, int
   extra.rms_eps = eps;
   const int64_t N = 3ll * heads * head_dim;
   return launch_fp8_gemm_ex(A, B, M, N, K, lda, ldb, scale_a, scale_b, bias, C, ldc, QIK_DTYPE_BF16, QIK_EPI_RMS_ROPE,
-                            nullptr, status, static_cast<cudaStream_t>(stream), false, &extra, QIK_GEMM_TILE_PAIR_256);
+                            nullptr, status, static_cast<cudaStream_t>(stream), true, &extra, QIK_GEMM_TILE_PAIR_256);
 }
 
 extern "C" int qik_fp8_gemm_gate_residual(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K,
@@ -947,7 +947,7 @@ extern "C" int qik_fp8_gemm_gate_residual(const uint8_t* A, const uint8_t* B, in
   extra.gate_seq = static_cast<int>(seq);
   extra.gate_batch = static_cast<int>(batch);
   return launch_fp8_gemm_ex(A, B, M, N, K, lda, ldb, scale_a, scale_b, bias, C, ldc, QIK_DTYPE_BF16, QIK_EPI_GATE_RES,
-                            nullptr, status, static_cast<cudaStream_t>(stream), false, &extra, QIK_GEMM_TILE_AUTO);
+                            nullptr, status, static_cast<cudaStream_t>(stream), true, &extra, QIK_GEMM_TILE_AUTO);
 }
 
 extern "C" int qik_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda,
@@ -955,7 +955,7 @@ extern "C" int qik_fp8_gemm(const uint8_t* A, const uint8_t* B, int64_t M, int64
                             int64_t ldc, int out_dtype, int epilogue, uint32_t* amax_out, int* status,
                             void* stream) {
   return qik::launch_fp8_gemm(A, B, M, N, K, lda, ldb, scale_a, scale_b, bias, C, ldc, out_dtype, epilogue, amax_out,
-                              status, static_cast<cudaStream_t>(stream), false);
+                              status, static_cast<cudaStream_t>(stream), true);
 }
 
 extern "C" int qik_fp8_gemm_tiled(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K, int64_t lda,
@@ -968,5 +968,5 @@ extern "C" int qik_fp8_gemm_tiled(const uint8_t* A, const uint8_t* B, int64_t M,
                    sel == QIK_GEMM_TILE_SINGLE_128 || sel == QIK_GEMM_TILE_SINGLE_64 || sel == QIK_GEMM_TILE_SWAP_16),
               "qik_fp8_gemm_tiled: unknown tile configuration %d", tile_cfg);
   return qik::launch_fp8_gemm_ex(A, B, M, N, K, lda, ldb, scale_a, scale_b, bias, C, ldc, out_dtype, epilogue,
-                                 amax_out, status, static_cast<cudaStream_t>(stream), false, nullptr, tile_cfg);
+                                 amax_out, status, static_cast<cudaStream_t>(stream), true, nullptr, tile_cfg);
 }

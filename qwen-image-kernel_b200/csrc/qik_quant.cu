@@ -472,7 +472,7 @@ int qik_quantize_act_from_amax(const void* x, int64_t n, const uint32_t* amax_bi
   QIK_REQUIRE(n >= 0, "qik_quantize_act_from_amax: negative n");
   // backward: x is typically the output its producer (GEMM, attention, SwiGLU) has just
   // written, and whatever part of it L2 kept is the part written last
-  return launch_pack_act(x, n, amax_bits, q, scale_out, static_cast<cudaStream_t>(stream), false, true);
+  return launch_pack_act(x, n, amax_bits, q, scale_out, static_cast<cudaStream_t>(stream), true, true);
 }
 
 static int quantize_act_impl(const void* x, int64_t n, uint8_t* q, float* scale_out, void* ws, cudaStream_t st,
