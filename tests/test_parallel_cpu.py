@@ -74,6 +74,16 @@ def _worker(rank, world, port, outdir):
         res["block2"] = blk(blk(xb, B, S, Lp), B, S, Lp).float().numpy()
         h_sp, _ = PX.tp_ffn_sp(xb[lo:hi].contiguous(), None, sp.up, sp.down)
         res["ffn_sp"] = h_sp.float().numpy()
+        # row shards that do not split evenly are refused before any collective
+        odd = torch.ones(2 * world + 1, 8)
+        try:
+            PX.reduce_scatter_rows(odd)
+            res["uneven_refused"] = world == 1
+        except ValueError:
+            res["uneven_refused"] = world > 1
+        # e4m3 rows gather as bytes, in rank order
+        mine = torch.full((2, 4), float(rank + 1)).to(torch.float8_e4m3fn)
+        res["gathered"] = PX.all_gather_rows(mine).float().numpy()
         with open(os.path.join(outdir, f"r{rank}.pkl"), "wb") as f:
             pickle.dump(res, f)
     finally:
@@ -128,6 +138,17 @@ def test_sequence_parallel_block_equals_replicated_form(results):
             assert amax_bits == int(np.float32(np.abs(y).max()).view(np.int32))
             assert np.array_equal(r["block_sp2"], r["block2"][lo:hi])
             assert np.array_equal(r["ffn_sp"], r["ffn"][lo:hi])
+
+
+def test_sequence_parallel_helpers(results):
+    """reduce_scatter_rows refuses rows that do not split over the ranks (and is the
+    identity on one rank); all_gather_rows concatenates e4m3 shards in rank order."""
+    for runs in results:
+        world = len(runs)
+        for r in runs:
+            assert r["uneven_refused"]
+            want = np.concatenate([np.full((2, 4), float(k + 1), dtype=np.float32) for k in range(world)], 0)
+            assert np.array_equal(r["gathered"], want)
 
 
 def test_tp_block_matches_single_rank(results):
